@@ -1,0 +1,85 @@
+//===- FusedKernels.h - fused kernels on B200 (sm_100a) ----------*- C++ -*-===//
+//
+// Drop-in replacement for the reference's kernel layer
+// (AVmakeralt/jules include/jules/Kernel/FusedKernels.h).  Same namespace,
+// names, argument order (note (M,K,N) vs (M,N,K)) and defaults; the
+// functions are declared here and defined once in the jules_b200 library,
+// so any number of translation units may include this header.
+//
+// float* arguments are HOST pointers, as in the reference: each call stages
+// its operands to the current GPU, runs an fp32 CUDA kernel and copies the
+// result back before returning.  The device-pointer C ABI in
+// jules_kernels.h is the fast path (bf16 tensor cores, no copies).
+//
+//===----------------------------------------------------------------------===//
+#ifndef JULES_KERNEL_FUSED_KERNELS_H
+#define JULES_KERNEL_FUSED_KERNELS_H
+
+#include <cstddef>
+#include <cstdint>
+
+#include "jules/Kernel/ExecutionArena.h"
+#include "jules/Kernel/TilePlanner.h"
+
+namespace jules {
+namespace kernel {
+
+// FusedKernels.h:61-67
+enum class ActivationType {
+  None,
+  Relu,
+  Sigmoid,
+  Tanh,
+  Gelu,
+};
+
+// C = act(A.B); A [M,K], B [K,N].  FusedKernels.h:69-72, 378-458.
+void tiledMatmulWithActivation(const float* A, const float* B, float* C, int M, int N, int K,
+                               const TileConfig& cfg, ActivationType act = ActivationType::None);
+
+// ReLU(X.W); argument order (M,K,N).  FusedKernels.h:203-259.
+void fusedMatmulRelu(const float* X, const float* W, float* output, int M, int K, int N);
+
+// ReLU(X.W + bias); argument order (M,K,N).  FusedKernels.h:265-372.
+void fusedMatmulBiasRelu(const float* X, const float* W, const float* bias, float* output, int M,
+                         int K, int N);
+
+// GELU(X.W + bias); argument order (M,K,N).  The GELU counterpart the
+// reference lacks (its routing pass has no GELU name, KernelRoutingPass.cpp:88-94).
+void fusedMatmulBiasGelu(const float* X, const float* W, const float* bias, float* output, int M,
+                         int K, int N);
+
+// FusedKernels.h:532-600
+void fusedLayerNorm(float* output, const float* input, const float* gamma, const float* beta,
+                    int M, int N, float epsilon = 1e-5f);
+
+// FusedKernels.h:606-627
+void fusedGelu(float* output, const float* input, int N);
+
+// Row-major SGEMM, C = alpha op(A) op(B) + beta C.  FusedKernels.h:633-644.
+void blasMatmul(const float* A, const float* B, float* C, int M, int N, int K, float alpha = 1.0f,
+                float beta = 0.0f, bool transA = false, bool transB = false);
+
+// FusedKernels.h:650-657
+struct MLPParams {
+  const float* W1;
+  const float* b1;
+  const float* W2;
+  const float* b2;
+  int batch_size;
+  int in_features;
+  int hidden_features;
+  int out_features;
+};
+
+// X.W1 + b1 -> ReLU -> .W2 + b2.  FusedKernels.h:659-760.
+void fusedMLPForward(float* output, const float* X, const MLPParams& params, ExecutionArena& arena,
+                     TilePlanner& planner);
+
+// FusedKernels.h:1085-1115 (same decision rule).
+bool shouldUseFlashAttention(int seq_len, int head_dim, size_t l3_bytes);
+
+}  // namespace kernel
+}  // namespace jules
+
+#endif

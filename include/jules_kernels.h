@@ -1,0 +1,162 @@
+/*
+ * jules_kernels.h - C ABI of the B200 (sm_100a) implementation of the Jules
+ * fused-kernel layer.
+ *
+ * Every entry point takes DEVICE pointers, plain sizes and a CUDA stream
+ * (cudaStream_t passed as void*; NULL = legacy default stream), enqueues its
+ * kernels and returns a status code without synchronising.  Inputs are
+ * dense row-major, like the reference (include/jules/Kernel/*.h of
+ * AVmakeralt/jules).  Outputs are fully overwritten.
+ *
+ * The reference's C++ API (jules::kernel::flashAttention etc., host float*)
+ * is kept verbatim in include/jules/Kernel/*.h and is implemented on top of
+ * these functions.
+ *
+ * Errors: 0 = success; otherwise a JULES_ERR_* code, with a message from
+ * jules_last_error_string() (thread-local).  Shapes are validated (the
+ * reference does no validation and aborts on arena overflow,
+ * ExecutionArena.h:140-143).  Kernels never trap: a pipeline wait that
+ * exceeds its time limit sets a device error word that
+ * jules_device_error() reports.
+ */
+#ifndef JULES_KERNELS_H
+#define JULES_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define JULES_OK 0
+#define JULES_ERR_SHAPE 1       /* invalid or unsupported dimensions */
+#define JULES_ERR_ALIGN 2       /* pointer alignment the kernel needs */
+#define JULES_ERR_DTYPE 3       /* unsupported dtype combination */
+#define JULES_ERR_CUDA 4        /* CUDA runtime / launch error */
+#define JULES_ERR_TIMEOUT 5     /* device pipeline wait timed out */
+#define JULES_ERR_ARG 6         /* NULL pointer or bad enum */
+#define JULES_ERR_UNSUPPORTED 7 /* name known but not implemented */
+#define JULES_ERR_WORKSPACE 8   /* caller workspace too small */
+
+/* Element types. */
+#define JULES_DTYPE_F32 0
+#define JULES_DTYPE_BF16 1
+
+/* Activations: same order as jules::kernel::ActivationType
+ * (include/jules/Kernel/FusedKernels.h:61-67). */
+#define JULES_ACT_NONE 0
+#define JULES_ACT_RELU 1
+#define JULES_ACT_SIGMOID 2
+#define JULES_ACT_TANH 3
+#define JULES_ACT_GELU 4
+
+/* Library version, (major << 16) | minor. */
+int jules_version(void);
+
+/* Message for the last error on this host thread ("" if none). */
+const char* jules_last_error_string(void);
+
+/* Name of a status code. */
+const char* jules_status_string(int status);
+
+/*
+ * Device error word: synchronises the current device, copies the word into
+ * *word (may be NULL) and clears it when clear != 0.  Returns JULES_OK when
+ * the word is zero, JULES_ERR_TIMEOUT when a bounded wait expired.
+ */
+int jules_device_error(uint32_t* word, int clear);
+
+/*
+ * C = act(A . W + bias) (+ residual)
+ *   A [M,K], W [K,N], C and residual [M,N], bias [N] (fp32, nullable),
+ *   residual nullable (same dtype as C).
+ *   in_dtype: dtype of A and W; out_dtype: dtype of C.
+ * bf16 in / bf16 out with N % 8 == 0, K % 8 == 0 and 16-byte aligned
+ * pointers runs on tcgen05 tensor cores (fp32 accumulate); everything else
+ * on CUDA cores in fp32.
+ * Replaces tiledMatmulWithActivation (FusedKernels.h:378-458),
+ * fusedMatmulRelu (:203-259), fusedMatmulBiasRelu (:265-372) and
+ * blasMatmul with alpha=1, beta=0, no transposes (:633-644).
+ */
+int jules_gemm_bias_act(const void* A, const void* W, const float* bias, const void* residual,
+                        void* C, int64_t M, int64_t N, int64_t K, int act, int in_dtype,
+                        int out_dtype, void* stream);
+
+/*
+ * Row-major fp32 SGEMM, C = alpha op(A) op(B) + beta C, with op = transpose
+ * when transA / transB != 0; lda/ldb/ldc in elements.  The cblas_sgemm
+ * contract the reference relies on (FusedKernels.h:633-644,
+ * FlashAttention.h:74,92,184).  CUDA cores, fp32.
+ */
+int jules_sgemm(int transA, int transB, int64_t M, int64_t N, int64_t K, float alpha,
+                const float* A, int64_t lda, const float* B, int64_t ldb, float beta, float* C,
+                int64_t ldc, void* stream);
+
+/*
+ * Flash-attention forward.
+ *   Q, O [B,Hq,S,D]; K, V [B,Hkv,S,D]; lse [B,Hq,S] fp32 (nullable),
+ *   lse = log(sum_j exp(scale * q.k_j)) per query row, natural log.
+ *   Hq % Hkv == 0 (grouped-query heads: kv head = h / (Hq/Hkv)).
+ *   causal != 0 masks key j > query i.  scale <= 0 means 1/sqrt(D).
+ *   dtype F32 (fp32 in/out, CUDA cores) or BF16 (bf16 in/out, fp32
+ *   softmax statistics; D == 128 runs on tcgen05).
+ * Replaces flashAttention (FlashAttention.h:130-309), standardAttention
+ * (:52-100) and attention (:114-124), which are the non-causal, Hq == Hkv,
+ * fp32 special case.
+ */
+int jules_flash_attention_fwd(const void* Q, const void* K, const void* V, void* O, float* lse,
+                              int B, int Hq, int Hkv, int S, int D, float scale, int causal,
+                              int dtype, void* stream);
+
+/*
+ * Row LayerNorm: out = (x - mean) * inv_std * gamma + beta, biased variance,
+ * inv_std = 1/sqrt(var + eps).  in [M,N], gamma/beta [N] fp32, optional
+ * mean_out / rstd_out [M] fp32.
+ * Replaces fusedLayerNorm (FusedKernels.h:532-600).
+ */
+int jules_layernorm(const void* in, const float* gamma, const float* beta, void* out, int64_t M,
+                    int64_t N, float eps, int in_dtype, int out_dtype, float* mean_out,
+                    float* rstd_out, void* stream);
+
+/*
+ * GELU (tanh form) elementwise, n elements.
+ * Replaces fusedGelu (FusedKernels.h:606-627).
+ */
+int jules_gelu(const void* in, void* out, int64_t n, int dtype, void* stream);
+
+/*
+ * Transformer MLP block, bf16:
+ *   out = GELU(LN(X) . W1 + b1) . W2 + b2 + X
+ *   X, out [T,d]; W1 [d,dff]; W2 [dff,d]; gamma, beta, b2 [d] and b1 [dff]
+ *   fp32.  LN statistics, bias, GELU and residual in fp32; LN(X) and the
+ *   hidden activation are stored as bf16 (matmul operands).
+ * workspace: device buffer of at least jules_mlp_block_workspace_bytes().
+ * Generalises fusedMLPForward (FusedKernels.h:650-760).
+ */
+size_t jules_mlp_block_workspace_bytes(int64_t T, int64_t d, int64_t dff);
+int jules_mlp_block(const void* X, const float* gamma, const float* beta, const void* W1,
+                    const float* b1, const void* W2, const float* b2, void* out, int64_t T,
+                    int64_t d, int64_t dff, float eps, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+/*
+ * Kernel registry keyed by the jules.extern_kernel names that
+ * KernelRoutingPass emits (lib/Passes/KernelRoutingPass.cpp:134-419) plus
+ * the documented fusedMLPForward / flashAttention and the GELU variants the
+ * routing pass cannot name (activationToString has no GELU case,
+ * KernelRoutingPass.cpp:88-94).
+ * jules_kernel_by_name returns an id >= 0, or -1 for an unknown name.
+ * jules_kernel_implemented returns 1 when the id has a CUDA implementation.
+ */
+int jules_kernel_by_name(const char* name);
+const char* jules_kernel_name(int id);
+int jules_kernel_count(void);
+int jules_kernel_implemented(int id);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* JULES_KERNELS_H */

@@ -1,0 +1,227 @@
+"""jules_b200 - B200 (sm_100a) implementation of the Jules fused-kernel layer.
+
+The product is the shared library ``jules_b200/_lib/libjules_b200.so``
+(C ABI in ``include/jules_kernels.h``, reference-signature C++ API in
+``include/jules/Kernel/*.h``).  This module loads it with ctypes and offers
+thin torch-tensor wrappers (device memory and streams come from torch; the
+arithmetic is the library's CUDA kernels).
+
+There is no CPU fallback: if the library is missing or no GPU is present the
+calls raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+__all__ = [
+    "lib", "JulesError", "ACT", "gemm_bias_act", "flash_attention_fwd", "layernorm", "gelu",
+    "mlp_block", "mlp_block_workspace_bytes", "sgemm", "device_error", "kernel_by_name",
+    "kernel_names", "LIB_PATH",
+]
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libjules_b200.so")
+
+ACT = {"none": 0, "relu": 1, "sigmoid": 2, "tanh": 3, "gelu": 4}
+DT_F32, DT_BF16 = 0, 1
+
+_c_vp = ctypes.c_void_p
+_c_i64 = ctypes.c_int64
+_c_int = ctypes.c_int
+_c_f = ctypes.c_float
+
+_SIGNATURES = {
+    "jules_version": ([], _c_int),
+    "jules_last_error_string": ([], ctypes.c_char_p),
+    "jules_status_string": ([_c_int], ctypes.c_char_p),
+    "jules_device_error": ([ctypes.POINTER(ctypes.c_uint32), _c_int], _c_int),
+    "jules_gemm_bias_act": ([_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_int,
+                             _c_int, _c_int, _c_vp], _c_int),
+    "jules_sgemm": ([_c_int, _c_int, _c_i64, _c_i64, _c_i64, _c_f, _c_vp, _c_i64, _c_vp, _c_i64,
+                     _c_f, _c_vp, _c_i64, _c_vp], _c_int),
+    "jules_flash_attention_fwd": ([_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int,
+                                   _c_int, _c_int, _c_f, _c_int, _c_int, _c_vp], _c_int),
+    "jules_layernorm": ([_c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_f, _c_int, _c_int, _c_vp,
+                         _c_vp, _c_vp], _c_int),
+    "jules_gelu": ([_c_vp, _c_vp, _c_i64, _c_int, _c_vp], _c_int),
+    "jules_mlp_block_workspace_bytes": ([_c_i64, _c_i64, _c_i64], ctypes.c_size_t),
+    "jules_mlp_block": ([_c_vp] * 8 + [_c_i64, _c_i64, _c_i64, _c_f, _c_vp, ctypes.c_size_t,
+                                       _c_vp], _c_int),
+    "jules_kernel_by_name": ([ctypes.c_char_p], _c_int),
+    "jules_kernel_name": ([_c_int], ctypes.c_char_p),
+    "jules_kernel_count": ([], _c_int),
+    "jules_kernel_implemented": ([_c_int], _c_int),
+}
+
+
+class JulesError(RuntimeError):
+    def __init__(self, status: int, what: str):
+        self.status = status
+        super().__init__(what)
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} missing: build it with `python -m jules_b200.build`")
+        h = ctypes.CDLL(LIB_PATH)
+        for name, (args, res) in _SIGNATURES.items():
+            fn = getattr(h, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = h
+    return _lib
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        h = lib()
+        raise JulesError(rc, f"{what}: {h.jules_status_string(rc).decode()}: "
+                             f"{h.jules_last_error_string().decode()}")
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _dtype_code(t) -> int:
+    import torch
+    if t.dtype == torch.float32:
+        return DT_F32
+    if t.dtype == torch.bfloat16:
+        return DT_BF16
+    raise TypeError(f"unsupported dtype {t.dtype}")
+
+
+def _stream(stream=None):
+    import torch
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _dense(t, name):
+    if not t.is_cuda or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous CUDA tensor")
+    return t
+
+
+def device_error(clear: bool = True) -> int:
+    """Synchronise and return the device error word (0 = no error)."""
+    w = ctypes.c_uint32(0)
+    lib().jules_device_error(ctypes.byref(w), 1 if clear else 0)
+    return int(w.value)
+
+
+def gemm_bias_act(A, W, bias=None, residual=None, act="none", out=None, out_dtype=None,
+                  stream=None):
+    """C = act(A @ W + bias) (+ residual); A [M,K], W [K,N] (same dtype)."""
+    import torch
+    _dense(A, "A"), _dense(W, "W")
+    M, K = A.shape
+    K2, N = W.shape
+    if K2 != K or W.dtype != A.dtype:
+        raise ValueError("A/W shape or dtype mismatch")
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype or A.dtype, device=A.device)
+    if bias is not None:
+        _dense(bias, "bias")
+        assert bias.dtype == torch.float32 and bias.numel() == N
+    if residual is not None:
+        _dense(residual, "residual")
+        assert residual.dtype == out.dtype and residual.shape == out.shape
+    rc = lib().jules_gemm_bias_act(_ptr(A), _ptr(W), _ptr(bias), _ptr(residual), _ptr(out), M, N,
+                                   K, ACT[act] if isinstance(act, str) else int(act),
+                                   _dtype_code(A), _dtype_code(out), _stream(stream))
+    _check(rc, "jules_gemm_bias_act")
+    return out
+
+
+def sgemm(A, B, C=None, alpha=1.0, beta=0.0, transA=False, transB=False, stream=None):
+    """Row-major fp32 C = alpha op(A) op(B) + beta C."""
+    import torch
+    M = A.shape[1] if transA else A.shape[0]
+    K = A.shape[0] if transA else A.shape[1]
+    N = B.shape[0] if transB else B.shape[1]
+    if C is None:
+        C = torch.zeros((M, N), dtype=torch.float32, device=A.device)
+    rc = lib().jules_sgemm(int(transA), int(transB), M, N, K, alpha, _ptr(A), A.shape[1], _ptr(B),
+                           B.shape[1], beta, _ptr(C), C.shape[1], _stream(stream))
+    _check(rc, "jules_sgemm")
+    return C
+
+
+def flash_attention_fwd(Q, K, V, causal=False, scale=0.0, out=None, lse=True, stream=None):
+    """Q [B,Hq,S,D], K/V [B,Hkv,S,D] (fp32 or bf16).  Returns (O, lse|None)."""
+    import torch
+    for t, n in ((Q, "Q"), (K, "K"), (V, "V")):
+        _dense(t, n)
+    B, Hq, S, D = Q.shape
+    Hkv = K.shape[1]
+    if out is None:
+        out = torch.empty_like(Q)
+    l = torch.empty((B, Hq, S), dtype=torch.float32, device=Q.device) if lse else None
+    rc = lib().jules_flash_attention_fwd(_ptr(Q), _ptr(K), _ptr(V), _ptr(out), _ptr(l), B, Hq, Hkv,
+                                         S, D, float(scale), int(bool(causal)), _dtype_code(Q),
+                                         _stream(stream))
+    _check(rc, "jules_flash_attention_fwd")
+    return out, l
+
+
+def layernorm(x, gamma, beta, eps=1e-5, out=None, out_dtype=None, stats=False, stream=None):
+    import torch
+    _dense(x, "x")
+    M, N = x.shape
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype or x.dtype, device=x.device)
+    mean = torch.empty(M, dtype=torch.float32, device=x.device) if stats else None
+    rstd = torch.empty(M, dtype=torch.float32, device=x.device) if stats else None
+    rc = lib().jules_layernorm(_ptr(x), _ptr(gamma), _ptr(beta), _ptr(out), M, N, float(eps),
+                               _dtype_code(x), _dtype_code(out), _ptr(mean), _ptr(rstd),
+                               _stream(stream))
+    _check(rc, "jules_layernorm")
+    return (out, mean, rstd) if stats else out
+
+
+def gelu(x, out=None, stream=None):
+    import torch
+    _dense(x, "x")
+    if out is None:
+        out = torch.empty_like(x)
+    rc = lib().jules_gelu(_ptr(x), _ptr(out), x.numel(), _dtype_code(x), _stream(stream))
+    _check(rc, "jules_gelu")
+    return out
+
+
+def mlp_block_workspace_bytes(T, d, dff) -> int:
+    return int(lib().jules_mlp_block_workspace_bytes(T, d, dff))
+
+
+def mlp_block(X, gamma, beta, W1, b1, W2, b2, eps=1e-5, out=None, workspace=None, stream=None):
+    """out = GELU(LN(X) @ W1 + b1) @ W2 + b2 + X  (bf16)."""
+    import torch
+    T, d = X.shape
+    dff = W1.shape[1]
+    if out is None:
+        out = torch.empty_like(X)
+    need = mlp_block_workspace_bytes(T, d, dff)
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=X.device)
+    rc = lib().jules_mlp_block(_ptr(X), _ptr(gamma), _ptr(beta), _ptr(W1), _ptr(b1), _ptr(W2),
+                               _ptr(b2), _ptr(out), T, d, dff, float(eps), _ptr(workspace),
+                               workspace.numel() * workspace.element_size(), _stream(stream))
+    _check(rc, "jules_mlp_block")
+    return out
+
+
+def kernel_by_name(name: str) -> int:
+    return int(lib().jules_kernel_by_name(name.encode()))
+
+
+def kernel_names():
+    h = lib()
+    return [h.jules_kernel_name(i).decode() for i in range(h.jules_kernel_count())]

@@ -1,0 +1,417 @@
+// C ABI of the jules_b200 library (include/jules_kernels.h): argument
+// validation, path selection (tensor-core vs CUDA-core kernel) and launches.
+//
+// Single translation unit for all device code, so the device error word
+// (jb::g_dev_error) is one symbol without relocatable device code.
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/jules_kernels.h"
+#include "attn_tc.cuh"
+#include "gemm_tc.cuh"
+#include "sm100.cuh"
+#include "simt.cuh"
+
+namespace {
+
+thread_local char g_errbuf[512];
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_errbuf, sizeof(g_errbuf), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(JULES_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int ok() {
+  g_errbuf[0] = 0;
+  return JULES_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---------------------------------------------------------------------------
+// Per-device facts, looked up once.
+// ---------------------------------------------------------------------------
+constexpr int kMaxDevices = 64;
+struct DeviceInfo {
+  int sms = 0;
+  bool gemm_attr = false;
+  bool attn_attr = false;
+};
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int current_device(int* dev) {
+  cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (*dev < 0 || *dev >= kMaxDevices) return fail(JULES_ERR_CUDA, "device index %d", *dev);
+  return JULES_OK;
+}
+
+int device_sms(int dev) {
+  if (g_dev[dev].sms == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    g_dev[dev].sms = v > 0 ? v : 148;
+  }
+  return g_dev[dev].sms;
+}
+
+// ---------------------------------------------------------------------------
+// Tensor maps (driver entry point, so the library needs no -lcuda).
+// ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// rank-2 or rank-3 bf16 map with 128-byte swizzle.
+int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                   const uint64_t* strides_bytes, const uint32_t* box) {
+  auto enc = tmap_encoder();
+  if (!enc) return fail(JULES_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t d[3];
+  cuuint64_t st[2];
+  cuuint32_t bx[3];
+  cuuint32_t es[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+  }
+  for (int i = 0; i < rank - 1; ++i) st[i] = strides_bytes[i];
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, st,
+                   bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(JULES_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return JULES_OK;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return ok();
+}
+
+// ---------------------------------------------------------------------------
+// GEMM paths
+// ---------------------------------------------------------------------------
+constexpr int kGemmBN = 256;
+constexpr int kGemmStages = 4;
+
+int gemm_tc(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
+            const __nv_bfloat16* res, __nv_bfloat16* C, int64_t M, int64_t N, int64_t K, int act,
+            cudaStream_t st) {
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  CUtensorMap ta, tw;
+  {
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)K * 2};
+    const uint32_t box[2] = {64, 128};
+    if (int rc = make_tmap_bf16(&ta, A, 2, dims, strides, box)) return rc;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
+    const uint64_t strides[1] = {(uint64_t)N * 2};
+    const uint32_t box[2] = {64, 64};
+    if (int rc = make_tmap_bf16(&tw, W, 2, dims, strides, box)) return rc;
+  }
+  auto kern = jb::gemm::gemm_bf16_tc_kernel<kGemmBN, kGemmStages>;
+  const size_t smem = sizeof(jb::gemm::Smem<kGemmBN, kGemmStages>) + 1024;
+  if (!g_dev[dev].gemm_attr) {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm)");
+    g_dev[dev].gemm_attr = true;
+  }
+  const int64_t tiles = ((M + 127) / 128) * ((N + kGemmBN - 1) / kGemmBN);
+  const int grid = (int)(tiles < device_sms(dev) ? tiles : device_sms(dev));
+  kern<<<grid, jb::gemm::kThreads, smem, st>>>(ta, tw, bias, res, C, (int)M, (int)N, (int)K, act);
+  return check_launch("gemm_bf16_tc_kernel launch");
+}
+
+template <typename TIn, typename TOut>
+int gemm_simt(const void* A, const void* W, const float* bias, const void* res, void* C, int64_t M,
+              int64_t N, int64_t K, int act, int exact, cudaStream_t st) {
+  dim3 grid((unsigned)((N + jb::simt::GBN - 1) / jb::simt::GBN),
+            (unsigned)((M + jb::simt::GBM - 1) / jb::simt::GBM));
+  if (grid.y > 65535u) return fail(JULES_ERR_SHAPE, "M=%lld too large for the CUDA-core GEMM", (long long)M);
+  jb::simt::gemm_kernel<TIn, TOut><<<grid, 256, 0, st>>>(
+      static_cast<const TIn*>(A), static_cast<const TIn*>(W), bias,
+      static_cast<const TOut*>(res), static_cast<TOut*>(C), (int)M, (int)N, (int)K, act, exact);
+  return check_launch("gemm_kernel launch");
+}
+
+// ---------------------------------------------------------------------------
+// Attention paths
+// ---------------------------------------------------------------------------
+template <typename TIn, typename TOut, int DPL>
+int attn_simt_launch(const void* Q, const void* K, const void* V, void* O, float* lse, int B, int Hq,
+                     int Hkv, int S, int D, float scale, int causal, cudaStream_t st) {
+  constexpr int DMAX = DPL * 32;
+  const size_t smem = sizeof(float) * (jb::simt::ABQ * DMAX + jb::simt::ABK * (DMAX + 1) +
+                                       jb::simt::ABK * DMAX);
+  auto kern = jb::simt::attn_kernel<TIn, TOut, DPL>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn)");
+  }
+  dim3 grid((unsigned)((S + jb::simt::ABQ - 1) / jb::simt::ABQ), (unsigned)(B * Hq));
+  kern<<<grid, 128, smem, st>>>(static_cast<const TIn*>(Q), static_cast<const TIn*>(K),
+                                static_cast<const TIn*>(V), static_cast<TOut*>(O), lse, Hq, Hkv, S,
+                                D, scale, causal);
+  return check_launch("attn_kernel launch");
+}
+
+template <typename T>
+int attn_simt(const void* Q, const void* K, const void* V, void* O, float* lse, int B, int Hq,
+              int Hkv, int S, int D, float scale, int causal, cudaStream_t st) {
+  if (D <= 32) return attn_simt_launch<T, T, 1>(Q, K, V, O, lse, B, Hq, Hkv, S, D, scale, causal, st);
+  if (D <= 64) return attn_simt_launch<T, T, 2>(Q, K, V, O, lse, B, Hq, Hkv, S, D, scale, causal, st);
+  if (D <= 128) return attn_simt_launch<T, T, 4>(Q, K, V, O, lse, B, Hq, Hkv, S, D, scale, causal, st);
+  return attn_simt_launch<T, T, 8>(Q, K, V, O, lse, B, Hq, Hkv, S, D, scale, causal, st);
+}
+
+int attn_tc(const void* Q, const void* K, const void* V, void* O, float* lse, int B, int Hq, int Hkv,
+            int S, int D, float scale, int causal, cudaStream_t st) {
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  CUtensorMap tq, tk, tv;
+  const uint32_t box[3] = {64, (uint32_t)jb::attn::BQ, 1};
+  const uint32_t boxkv[3] = {64, (uint32_t)jb::attn::BKV, 1};
+  {
+    const uint64_t dims[3] = {(uint64_t)D, (uint64_t)S, (uint64_t)B * Hq};
+    const uint64_t strides[2] = {(uint64_t)D * 2, (uint64_t)S * D * 2};
+    if (int rc = make_tmap_bf16(&tq, Q, 3, dims, strides, box)) return rc;
+  }
+  {
+    const uint64_t dims[3] = {(uint64_t)D, (uint64_t)S, (uint64_t)B * Hkv};
+    const uint64_t strides[2] = {(uint64_t)D * 2, (uint64_t)S * D * 2};
+    if (int rc = make_tmap_bf16(&tk, K, 3, dims, strides, boxkv)) return rc;
+    if (int rc = make_tmap_bf16(&tv, V, 3, dims, strides, boxkv)) return rc;
+  }
+  auto kern = jb::attn::attn_fwd_tc_kernel;
+  const size_t smem = sizeof(jb::attn::Smem) + 1024;
+  if (!g_dev[dev].attn_attr) {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn_tc)");
+    g_dev[dev].attn_attr = true;
+  }
+  const int q_tiles = (S + jb::attn::BQ - 1) / jb::attn::BQ;
+  const int64_t work = (int64_t)q_tiles * B * Hq;
+  const int grid = (int)(work < device_sms(dev) ? work : device_sms(dev));
+  const float scale_log2 = scale * 1.4426950408889634f;
+  kern<<<grid, jb::attn::kThreads, smem, st>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(O), lse, B,
+                                               Hq, Hkv, S, scale_log2, causal);
+  return check_launch("attn_fwd_tc_kernel launch");
+}
+
+}  // namespace
+
+// ===========================================================================
+// Exported C ABI
+// ===========================================================================
+extern "C" {
+
+int jules_version(void) { return (0 << 16) | 1; }
+
+const char* jules_last_error_string(void) { return g_errbuf; }
+
+const char* jules_status_string(int s) {
+  switch (s) {
+    case JULES_OK: return "ok";
+    case JULES_ERR_SHAPE: return "bad shape";
+    case JULES_ERR_ALIGN: return "bad alignment";
+    case JULES_ERR_DTYPE: return "unsupported dtype";
+    case JULES_ERR_CUDA: return "cuda error";
+    case JULES_ERR_TIMEOUT: return "device wait timed out";
+    case JULES_ERR_ARG: return "bad argument";
+    case JULES_ERR_UNSUPPORTED: return "not implemented";
+    case JULES_ERR_WORKSPACE: return "workspace too small";
+    default: return "unknown status";
+  }
+}
+
+int jules_device_error(uint32_t* word, int clear) {
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  uint32_t w = 0;
+  e = cudaMemcpyFromSymbol(&w, jb::g_dev_error, sizeof(w));
+  if (e != cudaSuccess) return cuda_fail(e, "read device error word");
+  if (clear && w) {
+    const uint32_t z = 0;
+    e = cudaMemcpyToSymbol(jb::g_dev_error, &z, sizeof(z));
+    if (e != cudaSuccess) return cuda_fail(e, "clear device error word");
+  }
+  if (word) *word = w;
+  if (w & jb::kDevErrTimeout)
+    return fail(JULES_ERR_TIMEOUT, "device wait timed out (site %u)", (w >> 8) & 0xffu);
+  if (w) return fail(JULES_ERR_SHAPE, "device reported error word 0x%x", w);
+  return ok();
+}
+
+int jules_gemm_bias_act(const void* A, const void* W, const float* bias, const void* residual,
+                        void* C, int64_t M, int64_t N, int64_t K, int act, int in_dtype,
+                        int out_dtype, void* stream) {
+  if (!A || !W || !C) return fail(JULES_ERR_ARG, "gemm: NULL A, W or C");
+  if (M < 0 || N <= 0 || K <= 0) return fail(JULES_ERR_SHAPE, "gemm: M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail(JULES_ERR_SHAPE, "gemm: dimension exceeds 2^31-1");
+  if (act < JULES_ACT_NONE || act > JULES_ACT_GELU) return fail(JULES_ERR_ARG, "gemm: act=%d", act);
+  if (M == 0) return ok();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool in_bf = in_dtype == JULES_DTYPE_BF16, out_bf = out_dtype == JULES_DTYPE_BF16;
+  if ((in_dtype != JULES_DTYPE_F32 && !in_bf) || (out_dtype != JULES_DTYPE_F32 && !out_bf))
+    return fail(JULES_ERR_DTYPE, "gemm: dtypes %d/%d", in_dtype, out_dtype);
+  if (in_bf && out_bf && N % 8 == 0 && K % 8 == 0 && aligned16(A) && aligned16(W) &&
+      aligned16(C) && (!bias || aligned16(bias)) && (!residual || aligned16(residual)))
+    return gemm_tc(static_cast<const __nv_bfloat16*>(A), static_cast<const __nv_bfloat16*>(W), bias,
+                   static_cast<const __nv_bfloat16*>(residual), static_cast<__nv_bfloat16*>(C), M, N,
+                   K, act, st);
+  if (in_bf && out_bf) return gemm_simt<__nv_bfloat16, __nv_bfloat16>(A, W, bias, residual, C, M, N, K, act, 0, st);
+  if (in_bf) return gemm_simt<__nv_bfloat16, float>(A, W, bias, residual, C, M, N, K, act, 1, st);
+  if (out_bf) return gemm_simt<float, __nv_bfloat16>(A, W, bias, residual, C, M, N, K, act, 0, st);
+  return gemm_simt<float, float>(A, W, bias, residual, C, M, N, K, act, 1, st);
+}
+
+int jules_sgemm(int transA, int transB, int64_t M, int64_t N, int64_t K, float alpha,
+                const float* A, int64_t lda, const float* B, int64_t ldb, float beta, float* C,
+                int64_t ldc, void* stream) {
+  if (!A || !B || !C) return fail(JULES_ERR_ARG, "sgemm: NULL pointer");
+  if (M < 0 || N < 0 || K < 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+    return fail(JULES_ERR_SHAPE, "sgemm: M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+  if (ldc < N || lda < (transA ? M : K) || ldb < (transB ? K : N))
+    return fail(JULES_ERR_SHAPE, "sgemm: leading dimension too small");
+  if (M == 0 || N == 0) return ok();
+  dim3 grid((unsigned)((N + jb::simt::GBN - 1) / jb::simt::GBN),
+            (unsigned)((M + jb::simt::GBM - 1) / jb::simt::GBM));
+  if (grid.y > 65535u) return fail(JULES_ERR_SHAPE, "sgemm: M too large");
+  jb::simt::sgemm_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      transA ? 1 : 0, transB ? 1 : 0, (int)M, (int)N, (int)K, alpha, A, (int)lda, B, (int)ldb,
+      beta, C, (int)ldc);
+  return check_launch("sgemm_kernel launch");
+}
+
+int jules_flash_attention_fwd(const void* Q, const void* K, const void* V, void* O, float* lse,
+                              int B, int Hq, int Hkv, int S, int D, float scale, int causal,
+                              int dtype, void* stream) {
+  if (!Q || !K || !V || !O) return fail(JULES_ERR_ARG, "attention: NULL Q, K, V or O");
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || S < 0 || D <= 0 || Hq % Hkv != 0)
+    return fail(JULES_ERR_SHAPE, "attention: B=%d Hq=%d Hkv=%d S=%d D=%d", B, Hq, Hkv, S, D);
+  if (D > 256) return fail(JULES_ERR_SHAPE, "attention: head_dim %d > 256", D);
+  if ((int64_t)B * Hq > 65535 * 1024LL) return fail(JULES_ERR_SHAPE, "attention: too many heads");
+  if (B == 0 || S == 0) return ok();
+  if (!(scale > 0.0f)) scale = 1.0f / sqrtf((float)D);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == JULES_DTYPE_F32)
+    return attn_simt<float>(Q, K, V, O, lse, B, Hq, Hkv, S, D, scale, causal ? 1 : 0, st);
+  if (dtype != JULES_DTYPE_BF16) return fail(JULES_ERR_DTYPE, "attention: dtype %d", dtype);
+  if (D == jb::attn::HD && aligned16(Q) && aligned16(K) && aligned16(V) && aligned16(O))
+    return attn_tc(Q, K, V, O, lse, B, Hq, Hkv, S, D, scale, causal ? 1 : 0, st);
+  return attn_simt<__nv_bfloat16>(Q, K, V, O, lse, B, Hq, Hkv, S, D, scale, causal ? 1 : 0, st);
+}
+
+int jules_layernorm(const void* in, const float* gamma, const float* beta, void* out, int64_t M,
+                    int64_t N, float eps, int in_dtype, int out_dtype, float* mean_out,
+                    float* rstd_out, void* stream) {
+  if (!in || !gamma || !beta || !out) return fail(JULES_ERR_ARG, "layernorm: NULL pointer");
+  if (M < 0 || N <= 0 || M > INT32_MAX) return fail(JULES_ERR_SHAPE, "layernorm: M=%lld N=%lld", (long long)M, (long long)N);
+  if (M == 0) return ok();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool in_bf = in_dtype == JULES_DTYPE_BF16, out_bf = out_dtype == JULES_DTYPE_BF16;
+  if ((in_dtype != JULES_DTYPE_F32 && !in_bf) || (out_dtype != JULES_DTYPE_F32 && !out_bf))
+    return fail(JULES_ERR_DTYPE, "layernorm: dtypes %d/%d", in_dtype, out_dtype);
+  const unsigned grid = (unsigned)M;
+  if (in_bf && out_bf && N % 8 == 0 && N <= 8 * 256 * 4 && aligned16(in) && aligned16(out) &&
+      aligned16(gamma) && aligned16(beta)) {
+    jb::simt::layernorm_bf16_vec_kernel<4><<<grid, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(in), gamma, beta, static_cast<__nv_bfloat16*>(out),
+        mean_out, rstd_out, M, (int)N, eps);
+  } else if (in_bf && out_bf) {
+    jb::simt::layernorm_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(in), gamma, beta, static_cast<__nv_bfloat16*>(out),
+        mean_out, rstd_out, M, N, eps);
+  } else if (in_bf) {
+    jb::simt::layernorm_kernel<__nv_bfloat16, float><<<grid, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(in), gamma, beta, static_cast<float*>(out), mean_out,
+        rstd_out, M, N, eps);
+  } else if (out_bf) {
+    jb::simt::layernorm_kernel<float, __nv_bfloat16><<<grid, 256, 0, st>>>(
+        static_cast<const float*>(in), gamma, beta, static_cast<__nv_bfloat16*>(out), mean_out,
+        rstd_out, M, N, eps);
+  } else {
+    jb::simt::layernorm_kernel<float, float><<<grid, 256, 0, st>>>(
+        static_cast<const float*>(in), gamma, beta, static_cast<float*>(out), mean_out, rstd_out,
+        M, N, eps);
+  }
+  return check_launch("layernorm launch");
+}
+
+int jules_gelu(const void* in, void* out, int64_t n, int dtype, void* stream) {
+  if (!in || !out) return fail(JULES_ERR_ARG, "gelu: NULL pointer");
+  if (n < 0) return fail(JULES_ERR_SHAPE, "gelu: n=%lld", (long long)n);
+  if (n == 0) return ok();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int64_t blocks = (n + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (dtype == JULES_DTYPE_F32)
+    jb::simt::gelu_kernel<float><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const float*>(in), static_cast<float*>(out), n);
+  else if (dtype == JULES_DTYPE_BF16)
+    jb::simt::gelu_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(in), static_cast<__nv_bfloat16*>(out), n);
+  else
+    return fail(JULES_ERR_DTYPE, "gelu: dtype %d", dtype);
+  return check_launch("gelu launch");
+}
+
+size_t jules_mlp_block_workspace_bytes(int64_t T, int64_t d, int64_t dff) {
+  if (T <= 0 || d <= 0 || dff <= 0) return 0;
+  const size_t xn = ((size_t)T * d * 2 + 255) & ~size_t(255);
+  const size_t h = ((size_t)T * dff * 2 + 255) & ~size_t(255);
+  return xn + h;
+}
+
+int jules_mlp_block(const void* X, const float* gamma, const float* beta, const void* W1,
+                    const float* b1, const void* W2, const float* b2, void* out, int64_t T,
+                    int64_t d, int64_t dff, float eps, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+  if (!X || !gamma || !beta || !W1 || !W2 || !out) return fail(JULES_ERR_ARG, "mlp_block: NULL pointer");
+  if (T < 0 || d <= 0 || dff <= 0) return fail(JULES_ERR_SHAPE, "mlp_block: T=%lld d=%lld dff=%lld", (long long)T, (long long)d, (long long)dff);
+  if (T == 0) return ok();
+  const size_t need = jules_mlp_block_workspace_bytes(T, d, dff);
+  if (!workspace || workspace_bytes < need)
+    return fail(JULES_ERR_WORKSPACE, "mlp_block: workspace %zu < %zu bytes", workspace_bytes, need);
+  if (!aligned16(workspace)) return fail(JULES_ERR_ALIGN, "mlp_block: workspace not 16-byte aligned");
+  const size_t xn_bytes = ((size_t)T * d * 2 + 255) & ~size_t(255);
+  void* xn = workspace;
+  void* hid = static_cast<char*>(workspace) + xn_bytes;
+  if (int rc = jules_layernorm(X, gamma, beta, xn, T, d, eps, JULES_DTYPE_BF16, JULES_DTYPE_BF16,
+                               nullptr, nullptr, stream))
+    return rc;
+  if (int rc = jules_gemm_bias_act(xn, W1, b1, nullptr, hid, T, dff, d, JULES_ACT_GELU,
+                                   JULES_DTYPE_BF16, JULES_DTYPE_BF16, stream))
+    return rc;
+  return jules_gemm_bias_act(hid, W2, b2, X, out, T, d, dff, JULES_ACT_NONE, JULES_DTYPE_BF16,
+                             JULES_DTYPE_BF16, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,232 @@
+// Fused GEMM + bias + activation (+ residual) on tcgen05 tensor cores.
+//
+//   C[M,N] = act(A[M,K] . W[K,N] + bias[N]) (+ residual[M,N])
+//
+// A is row-major (K contiguous: the K-major UMMA operand); W is row-major
+// [K,N] (N contiguous: the MN-major UMMA operand), exactly the layouts of the
+// reference's tiledMatmulWithActivation / fusedMatmulBiasRelu
+// (include/jules/Kernel/FusedKernels.h:265-458), so no transposed weight copy
+// is needed.  bf16 operands, fp32 accumulation in TMEM, fp32 epilogue, one
+// round-to-nearest-even cast to bf16 on store (the mixed-precision rules of
+// lib/Passes/MixedPrecisionPass.cpp:350-459,490,632).
+//
+// Structure (one CTA per SM, persistent over 128 x BN output tiles):
+//   warp 0      TMA producer: A box 64x128, W boxes 64x64, 128B swizzle,
+//               STAGES-deep smem ring guarded by full/empty mbarriers.
+//   warp 1      allocates TMEM (2 x BN fp32 columns) and issues
+//               tcgen05.mma (M=128, N=BN, K=16) from one thread; commits free
+//               smem stages and signal finished accumulators.
+//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time, bias + activation
+//               + residual in fp32, bf16 pack, 16-byte stores.  The two
+//               accumulator buffers let the epilogue of tile i overlap the
+//               mainloop of tile i+1.
+#pragma once
+
+#include "sm100.cuh"
+
+namespace jb {
+
+enum Act : int { kActNone = 0, kActRelu = 1, kActSigmoid = 2, kActTanh = 3, kActGelu = 4 };
+
+// Fast activation for bf16-output epilogues (hardware tanh, ~2^-11 rel).
+__device__ __forceinline__ float act_fast(float v, int act) {
+  switch (act) {
+    case kActRelu: return fmaxf(v, 0.0f);
+    case kActSigmoid: return 0.5f + 0.5f * tanh_approx(0.5f * v);
+    case kActTanh: return tanh_approx(v);
+    case kActGelu: {
+      const float u = 0.7978845608f * (v + 0.044715f * v * v * v);
+      return 0.5f * v * (1.0f + tanh_approx(u));
+    }
+    default: return v;
+  }
+}
+
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // one 128-byte swizzle row of bf16
+constexpr int kThreads = 192;
+
+template <int BN, int STAGES>
+struct Smem {
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BK * BN * 2;
+  alignas(1024) uint8_t a[STAGES][kABytes];
+  alignas(1024) uint8_t b[STAGES][kBBytes];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmW, const float* __restrict__ bias,
+                        const __nv_bfloat16* __restrict__ residual, __nv_bfloat16* __restrict__ C,
+                        int M, int N, int K, int act) {
+  static_assert(BN % 64 == 0 && BN <= 256, "BN must be a multiple of 64, at most 256");
+  using S = Smem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  S& s = *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (M + BM - 1) / BM;
+  const int num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_k = (K + BK - 1) / BK;
+  constexpr uint32_t kTmemCols = 2 * BN <= 32 ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.tfull[i], 1);
+      mbar_init(&s.tempty[i], 128);
+    }
+    s.abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmW);
+  }
+  if (warp == 1) {
+    tmem_alloc(&s.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = s.tmem_base;
+  volatile int* abort_flag = &s.abort_flag;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const int m0 = (t % num_m) * BM;
+        const int n0 = (t / num_m) * BN;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&s.empty[stage], phase ^ 1u, 1, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&s.full[stage], S::kABytes + S::kBBytes);
+          tma_load_2d(s.a[stage], &tmA, &s.full[stage], kb * BK, m0);
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j)
+            tma_load_2d(s.b[stage] + j * (BK * 64 * 2), &tmW, &s.full[stage], n0 + j * 64, kb * BK);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, false, true);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&s.tempty[acc], acc_phase ^ 1u, 2, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&s.full[stage], phase, 3, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(s.a[stage]);
+          const uint32_t b_base = smem_u32(s.b[stage]);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            // K-major A: advance 16 elements = 32 bytes inside the swizzle row.
+            const uint64_t ad = sdesc_sw128(a_base + kk * 32, 16, 1024);
+            // MN-major W: advance 16 K-rows = 2048 bytes; 64-col chunks 8 KB apart.
+            const uint64_t bd = sdesc_sw128(b_base + kk * 2048, BK * 64 * 2, 1024);
+            umma_f16_ss(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&s.empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        umma_commit(&s.tfull[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      const int m0 = (t % num_m) * BM;
+      const int n0 = (t / num_m) * BN;
+      if (!mbar_wait(&s.tfull[acc], acc_phase, 4, abort_flag)) break;
+      tc_fence_after();
+      const int row = m0 + row_in_tile;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(t_row + c * 32, r);
+        tmem_ld_wait(r);
+        const int col0 = n0 + c * 32;
+        if (row < M && col0 < N) {
+          __nv_bfloat16* crow = C + (size_t)row * N;
+          const __nv_bfloat16* rrow = residual ? residual + (size_t)row * N : nullptr;
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int col = col0 + g * 8;
+            if (col < N) {  // N is a multiple of 8 on this path
+              float v[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[g * 8 + j]);
+              if (bias) {
+                const float4 b0 = *reinterpret_cast<const float4*>(bias + col);
+                const float4 b1 = *reinterpret_cast<const float4*>(bias + col + 4);
+                v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
+                v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
+              }
+#pragma unroll
+              for (int j = 0; j < 8; ++j) v[j] = act_fast(v[j], act);
+              if (rrow) {
+                const uint4 rv = *reinterpret_cast<const uint4*>(rrow + col);
+                const __nv_bfloat162* rp = reinterpret_cast<const __nv_bfloat162*>(&rv);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const float2 f = __bfloat1622float2(rp[j]);
+                  v[2 * j] += f.x;
+                  v[2 * j + 1] += f.y;
+                }
+              }
+              uint4 o;
+              o.x = pack_bf16x2(v[0], v[1]);
+              o.y = pack_bf16x2(v[2], v[3]);
+              o.z = pack_bf16x2(v[4], v[5]);
+              o.w = pack_bf16x2(v[6], v[7]);
+              *reinterpret_cast<uint4*>(crow + col) = o;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&s.tempty[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+}
+
+}  // namespace gemm
+}  // namespace jb

@@ -1,0 +1,334 @@
+// Host side of the drop-in boundary:
+//  - the reference's C++ kernel API (namespace jules::kernel, host float*
+//    arguments, same signatures as AVmakeralt/jules
+//    include/jules/Kernel/{FusedKernels,FlashAttention}.h), implemented by
+//    staging to the current GPU and calling the C ABI;
+//  - the extern_kernel name registry (jules_kernel_by_name & co.).
+//
+// Staging uses a per-thread, grow-only device buffer and the legacy default
+// stream, so each call is synchronous like the reference's.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+
+#include "jules/Kernel/ExecutionArena.h"
+#include "jules/Kernel/FlashAttention.h"
+#include "jules/Kernel/FusedKernels.h"
+#include "jules/Kernel/TilePlanner.h"
+#include "jules_kernels.h"
+
+namespace {
+
+void check(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+void check_status(int rc, const char* what) {
+  if (rc != JULES_OK)
+    throw std::runtime_error(std::string(what) + ": " + jules_status_string(rc) + " (" +
+                             jules_last_error_string() + ")");
+}
+
+// Grow-only device staging area for one host thread and device.
+class Staging {
+ public:
+  ~Staging() {
+    if (ptr_) cudaFree(ptr_);
+  }
+  // Returns device pointers for `n` buffers of the given byte sizes.
+  void reserve(const size_t* bytes, int n, char** out) {
+    size_t total = 0;
+    size_t off[8];
+    for (int i = 0; i < n; ++i) {
+      off[i] = total;
+      total += (bytes[i] + 255) & ~size_t(255);
+    }
+    int dev = 0;
+    check(cudaGetDevice(&dev), "cudaGetDevice");
+    if (total > cap_ || dev != dev_) {
+      if (ptr_) cudaFree(ptr_);
+      ptr_ = nullptr;
+      cap_ = 0;
+      check(cudaMalloc(&ptr_, total ? total : 256), "cudaMalloc(staging)");
+      cap_ = total;
+      dev_ = dev;
+    }
+    for (int i = 0; i < n; ++i) out[i] = static_cast<char*>(ptr_) + off[i];
+  }
+
+ private:
+  void* ptr_ = nullptr;
+  size_t cap_ = 0;
+  int dev_ = -1;
+};
+
+Staging& staging() {
+  thread_local Staging s;
+  return s;
+}
+
+void h2d(void* d, const void* h, size_t n) {
+  if (n) check(cudaMemcpy(d, h, n, cudaMemcpyHostToDevice), "cudaMemcpy H2D");
+}
+void d2h(void* h, const void* d, size_t n) {
+  if (n) check(cudaMemcpy(h, d, n, cudaMemcpyDeviceToHost), "cudaMemcpy D2H");
+}
+
+// act(X.W + bias), host pointers, fp32.
+void gemm_host(const float* X, const float* W, const float* bias, float* out, int M, int K, int N,
+               int act) {
+  if (M <= 0 || N <= 0 || K <= 0) return;
+  const size_t bx = (size_t)M * K * 4, bw = (size_t)K * N * 4, bb = bias ? (size_t)N * 4 : 0,
+               bo = (size_t)M * N * 4;
+  const size_t sizes[4] = {bx, bw, bb ? bb : 4, bo};
+  char* d[4];
+  staging().reserve(sizes, 4, d);
+  h2d(d[0], X, bx);
+  h2d(d[1], W, bw);
+  if (bias) h2d(d[2], bias, bb);
+  check_status(jules_gemm_bias_act(d[0], d[1], bias ? reinterpret_cast<float*>(d[2]) : nullptr,
+                                   nullptr, d[3], M, N, K, act, JULES_DTYPE_F32, JULES_DTYPE_F32,
+                                   nullptr),
+               "jules_gemm_bias_act");
+  d2h(out, d[3], bo);
+}
+
+void attention_host(float* out, const float* Q, const float* K, const float* V, int B, int H,
+                    int S, int D) {
+  if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return;
+  const size_t n = (size_t)B * H * S * D * 4;
+  const size_t sizes[4] = {n, n, n, n};
+  char* d[4];
+  staging().reserve(sizes, 4, d);
+  h2d(d[0], Q, n);
+  h2d(d[1], K, n);
+  h2d(d[2], V, n);
+  check_status(jules_flash_attention_fwd(d[0], d[1], d[2], d[3], nullptr, B, H, H, S, D, 0.0f, 0,
+                                         JULES_DTYPE_F32, nullptr),
+               "jules_flash_attention_fwd");
+  d2h(out, d[3], n);
+}
+
+}  // namespace
+
+namespace jules {
+namespace kernel {
+
+CacheInfo CacheInfo::detect() {
+  CacheInfo c{};
+  int dev = 0, smem = 0, l2 = 0, sms = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) {
+    cudaDeviceGetAttribute(&smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  c.l1d_bytes = smem > 0 ? (size_t)smem : 228 * 1024;
+  c.l2_bytes = l2 > 0 ? (size_t)l2 : 126u * 1024 * 1024;
+  c.l3_bytes = c.l2_bytes;
+  c.line_bytes = 128;
+  c.num_cores = sms > 0 ? sms : 148;
+  return c;
+}
+
+ExecutionArena::ExecutionArena(size_t maxSize)
+    : buffer_(nullptr), maxSize_(maxSize), offset_(0), highWaterMark_(0) {
+  void* p = nullptr;
+  if (cudaMalloc(&p, maxSize_ ? maxSize_ : 256) != cudaSuccess) throw std::bad_alloc();
+  buffer_ = static_cast<char*>(p);
+}
+
+ExecutionArena::~ExecutionArena() {
+  if (buffer_) cudaFree(buffer_);
+}
+
+void* ExecutionArena::allocateBytes(size_t bytes) {
+  const size_t aligned = (offset_ + 63) & ~size_t(63);
+  if (aligned + bytes > maxSize_) throw std::bad_alloc();
+  offset_ = aligned + bytes;
+  if (offset_ > highWaterMark_) highWaterMark_ = offset_;
+  return buffer_ + aligned;
+}
+
+void ExecutionArena::resetAndZero() {
+  if (offset_) check(cudaMemset(buffer_, 0, offset_), "cudaMemset(arena)");
+  offset_ = 0;
+}
+
+void tiledMatmulWithActivation(const float* A, const float* B, float* C, int M, int N, int K,
+                               const TileConfig& cfg, ActivationType act) {
+  (void)cfg;  // the GPU kernel's tile is fixed
+  gemm_host(A, B, nullptr, C, M, K, N, static_cast<int>(act));
+}
+
+void fusedMatmulRelu(const float* X, const float* W, float* output, int M, int K, int N) {
+  gemm_host(X, W, nullptr, output, M, K, N, JULES_ACT_RELU);
+}
+
+void fusedMatmulBiasRelu(const float* X, const float* W, const float* bias, float* output, int M,
+                         int K, int N) {
+  gemm_host(X, W, bias, output, M, K, N, JULES_ACT_RELU);
+}
+
+void fusedMatmulBiasGelu(const float* X, const float* W, const float* bias, float* output, int M,
+                         int K, int N) {
+  gemm_host(X, W, bias, output, M, K, N, JULES_ACT_GELU);
+}
+
+void fusedLayerNorm(float* output, const float* input, const float* gamma, const float* beta, int M,
+                    int N, float epsilon) {
+  if (M <= 0 || N <= 0) return;
+  const size_t bx = (size_t)M * N * 4, bg = (size_t)N * 4;
+  const size_t sizes[4] = {bx, bg, bg, bx};
+  char* d[4];
+  staging().reserve(sizes, 4, d);
+  h2d(d[0], input, bx);
+  h2d(d[1], gamma, bg);
+  h2d(d[2], beta, bg);
+  check_status(jules_layernorm(d[0], reinterpret_cast<float*>(d[1]), reinterpret_cast<float*>(d[2]),
+                               d[3], M, N, epsilon, JULES_DTYPE_F32, JULES_DTYPE_F32, nullptr,
+                               nullptr, nullptr),
+               "jules_layernorm");
+  d2h(output, d[3], bx);
+}
+
+void fusedGelu(float* output, const float* input, int N) {
+  if (N <= 0) return;
+  const size_t b = (size_t)N * 4;
+  const size_t sizes[2] = {b, b};
+  char* d[2];
+  staging().reserve(sizes, 2, d);
+  h2d(d[0], input, b);
+  check_status(jules_gelu(d[0], d[1], N, JULES_DTYPE_F32, nullptr), "jules_gelu");
+  d2h(output, d[1], b);
+}
+
+void blasMatmul(const float* A, const float* B, float* C, int M, int N, int K, float alpha,
+                float beta, bool transA, bool transB) {
+  if (M <= 0 || N <= 0) return;
+  const size_t ba = (size_t)M * K * 4, bb = (size_t)K * N * 4, bc = (size_t)M * N * 4;
+  const size_t sizes[3] = {ba ? ba : 4, bb ? bb : 4, bc};
+  char* d[3];
+  staging().reserve(sizes, 3, d);
+  h2d(d[0], A, ba);
+  h2d(d[1], B, bb);
+  if (beta != 0.0f) h2d(d[2], C, bc);
+  check_status(jules_sgemm(transA, transB, M, N, K, alpha, reinterpret_cast<float*>(d[0]),
+                           transA ? M : K, reinterpret_cast<float*>(d[1]), transB ? K : N, beta,
+                           reinterpret_cast<float*>(d[2]), N, nullptr),
+               "jules_sgemm");
+  d2h(C, d[2], bc);
+}
+
+void fusedMLPForward(float* output, const float* X, const MLPParams& p, ExecutionArena& arena,
+                     TilePlanner& planner) {
+  (void)planner;
+  const int M = p.batch_size, K1 = p.in_features, N1 = p.hidden_features, N2 = p.out_features;
+  if (M <= 0 || K1 <= 0 || N1 <= 0 || N2 <= 0) return;
+  // Operands live in the caller's device arena (the reference's arena holds
+  // the hidden activation, FusedKernels.h:669-700).
+  float* dX = arena.allocate<float>((size_t)M * K1);
+  float* dW1 = arena.allocate<float>((size_t)K1 * N1);
+  float* db1 = arena.allocate<float>(N1);
+  float* dW2 = arena.allocate<float>((size_t)N1 * N2);
+  float* db2 = arena.allocate<float>(N2);
+  float* dH = arena.allocate<float>((size_t)M * N1);
+  float* dO = arena.allocate<float>((size_t)M * N2);
+  h2d(dX, X, (size_t)M * K1 * 4);
+  h2d(dW1, p.W1, (size_t)K1 * N1 * 4);
+  h2d(db1, p.b1, (size_t)N1 * 4);
+  h2d(dW2, p.W2, (size_t)N1 * N2 * 4);
+  h2d(db2, p.b2, (size_t)N2 * 4);
+  check_status(jules_gemm_bias_act(dX, dW1, db1, nullptr, dH, M, N1, K1, JULES_ACT_RELU,
+                                   JULES_DTYPE_F32, JULES_DTYPE_F32, nullptr),
+               "mlp gemm1");
+  check_status(jules_gemm_bias_act(dH, dW2, db2, nullptr, dO, M, N2, N1, JULES_ACT_NONE,
+                                   JULES_DTYPE_F32, JULES_DTYPE_F32, nullptr),
+               "mlp gemm2");
+  d2h(output, dO, (size_t)M * N2 * 4);
+  arena.reset();
+}
+
+bool shouldUseFlashAttention(int seq_len, int head_dim, size_t l3_bytes) {
+  const size_t attn_matrix_bytes = (size_t)seq_len * seq_len * sizeof(float);
+  if (attn_matrix_bytes > l3_bytes) return true;
+  return seq_len >= 64 && head_dim <= 256;
+}
+
+void flashAttention(float* output, const float* Q, const float* K, const float* V, int batch,
+                    int heads, int seq, int head_dim, ExecutionArena& arena, TilePlanner& planner) {
+  (void)arena;
+  (void)planner;
+  attention_host(output, Q, K, V, batch, heads, seq, head_dim);
+}
+
+void standardAttention(float* output, const float* Q, const float* K, const float* V, int batch,
+                       int heads, int seq, int head_dim, ExecutionArena& arena) {
+  // On the GPU the tiled kernel is the standard path too; the result is the
+  // same softmax(QK^T/sqrt(D))V.
+  attention_host(output, Q, K, V, batch, heads, seq, head_dim);
+  arena.reset();
+}
+
+void attention(float* output, const float* Q, const float* K, const float* V, int batch, int heads,
+               int seq, int head_dim, ExecutionArena& arena, TilePlanner& planner) {
+  flashAttention(output, Q, K, V, batch, heads, seq, head_dim, arena, planner);
+}
+
+int flashAttentionBf16(uint16_t* output, float* lse, const uint16_t* Q, const uint16_t* K,
+                       const uint16_t* V, int batch, int q_heads, int kv_heads, int seq,
+                       int head_dim, bool causal, void* stream) {
+  return jules_flash_attention_fwd(Q, K, V, output, lse, batch, q_heads, kv_heads, seq, head_dim,
+                                   0.0f, causal ? 1 : 0, JULES_DTYPE_BF16, stream);
+}
+
+}  // namespace kernel
+}  // namespace jules
+
+// ---------------------------------------------------------------------------
+// extern_kernel name registry
+// ---------------------------------------------------------------------------
+namespace {
+
+struct KernelEntry {
+  const char* name;
+  int implemented;
+};
+
+// Names emitted by KernelRoutingPass (lib/Passes/KernelRoutingPass.cpp:
+// 134-419) and documented in include/jules/Passes/KernelRoutingPass.h:13-23,
+// plus the GELU forms the routing pass has no name for.
+const KernelEntry kKernels[] = {
+    {"fusedMatmulRelu", 1},        {"fusedMatmulSigmoid", 1},   {"fusedMatmulTanh", 1},
+    {"fusedMatmulGelu", 1},        {"fusedMatmulBiasRelu", 1},  {"fusedMatmulBiasSigmoid", 1},
+    {"fusedMatmulBiasTanh", 1},    {"fusedMatmulBiasGelu", 1},  {"fusedLayerNorm", 1},
+    {"fusedGelu", 1},              {"fusedMLPForward", 1},      {"flashAttention", 1},
+    {"blasMatmul", 1},             {"fusedSoftmax", 0},         {"fusedCrossEntropyLoss", 0},
+    {"matmulInt8", 0},
+};
+constexpr int kNumKernels = sizeof(kKernels) / sizeof(kKernels[0]);
+
+}  // namespace
+
+extern "C" {
+
+int jules_kernel_by_name(const char* name) {
+  if (!name) return -1;
+  for (int i = 0; i < kNumKernels; ++i)
+    if (std::strcmp(kKernels[i].name, name) == 0) return i;
+  return -1;
+}
+
+const char* jules_kernel_name(int id) {
+  return (id >= 0 && id < kNumKernels) ? kKernels[id].name : nullptr;
+}
+
+int jules_kernel_count(void) { return kNumKernels; }
+
+int jules_kernel_implemented(int id) {
+  return (id >= 0 && id < kNumKernels) ? kKernels[id].implemented : 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,415 @@
+// CUDA-core kernels: the fp32-exact paths behind the reference's float*
+// API, and the general-shape paths (any M/N/K, any alignment, head_dim other
+// than 128) that the tensor-core kernels do not take.
+//
+// All are GPU kernels; none falls back to the host.
+#pragma once
+
+#include "sm100.cuh"
+
+namespace jb {
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+// Accurate activations (fp32 outputs): the scalar forms of
+// include/jules/Kernel/FusedKernels.h:425-428, 616.
+__device__ __forceinline__ float act_exact(float v, int act) {
+  switch (act) {
+    case 1: return fmaxf(v, 0.0f);
+    case 2: return 1.0f / (1.0f + expf(-v));
+    case 3: return tanhf(v);
+    case 4: return 0.5f * v * (1.0f + tanhf(0.7978845608f * (v + 0.044715f * v * v * v)));
+    default: return v;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// GEMM: C = act(A.W + bias) (+ residual).  128x128 block tile, 8x8 per
+// thread, K step 8, smem staged.  fp32 accumulation in k order.
+// ---------------------------------------------------------------------------
+namespace simt {
+
+constexpr int GBM = 128, GBN = 128, GBK = 8;
+
+template <typename TIn, typename TOut>
+__global__ void __launch_bounds__(256)
+    gemm_kernel(const TIn* __restrict__ A, const TIn* __restrict__ W,
+                const float* __restrict__ bias, const TOut* __restrict__ residual,
+                TOut* __restrict__ C, int M, int N, int K, int act, int exact) {
+  __shared__ float As[GBK][GBM + 4];
+  __shared__ float Ws[GBK][GBN + 4];
+  const int tid = threadIdx.x;
+  const int tx = tid % 16, ty = tid / 16;
+  const int m0 = blockIdx.y * GBM, n0 = blockIdx.x * GBN;
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+
+  for (int k0 = 0; k0 < K; k0 += GBK) {
+    // A tile: 128 rows x 8 k -> 1024 elements, 4 per thread.
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = tid + i * 256;
+      const int r = e / GBK, kk = e % GBK;
+      const int gm = m0 + r, gk = k0 + kk;
+      As[kk][r] = (gm < M && gk < K) ? to_f32(A[(size_t)gm * K + gk]) : 0.0f;
+    }
+    // W tile: 8 k x 128 cols.
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = tid + i * 256;
+      const int kk = e / GBN, c = e % GBN;
+      const int gk = k0 + kk, gn = n0 + c;
+      Ws[kk][c] = (gk < K && gn < N) ? to_f32(W[(size_t)gk * N + gn]) : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < GBK; ++kk) {
+      float a[8], b[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a[i] = As[kk][ty * 8 + i];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) b[j] = Ws[kk][tx * 8 + j];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int gm = m0 + ty * 8 + i;
+    if (gm >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int gn = n0 + tx * 8 + j;
+      if (gn >= N) continue;
+      float v = acc[i][j];
+      if (bias) v += bias[gn];
+      v = exact ? act_exact(v, act) : act_fast(v, act);
+      if (residual) v += to_f32(residual[(size_t)gm * N + gn]);
+      C[(size_t)gm * N + gn] = from_f32<TOut>(v);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Row-major SGEMM with transposes, C = alpha op(A) op(B) + beta C (the
+// cblas_sgemm contract the reference calls, FusedKernels.h:633-644).
+// Same 128x128x8 tiling as gemm_kernel.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+    sgemm_kernel(int ta, int tb, int M, int N, int K, float alpha, const float* __restrict__ A,
+                 int lda, const float* __restrict__ Bm, int ldb, float beta,
+                 float* __restrict__ C, int ldc) {
+  __shared__ float As[GBK][GBM + 4];
+  __shared__ float Ws[GBK][GBN + 4];
+  const int tid = threadIdx.x;
+  const int tx = tid % 16, ty = tid / 16;
+  const int m0 = blockIdx.y * GBM, n0 = blockIdx.x * GBN;
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+  for (int k0 = 0; k0 < K; k0 += GBK) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = tid + i * 256;
+      const int r = e / GBK, kk = e % GBK;
+      const int gm = m0 + r, gk = k0 + kk;
+      As[kk][r] = (gm < M && gk < K) ? (ta ? A[(size_t)gk * lda + gm] : A[(size_t)gm * lda + gk]) : 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = tid + i * 256;
+      const int kk = e / GBN, c = e % GBN;
+      const int gk = k0 + kk, gn = n0 + c;
+      Ws[kk][c] = (gk < K && gn < N) ? (tb ? Bm[(size_t)gn * ldb + gk] : Bm[(size_t)gk * ldb + gn]) : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < GBK; ++kk) {
+      float a[8], b[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a[i] = As[kk][ty * 8 + i];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) b[j] = Ws[kk][tx * 8 + j];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int gm = m0 + ty * 8 + i;
+    if (gm >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int gn = n0 + tx * 8 + j;
+      if (gn >= N) continue;
+      float* c = C + (size_t)gm * ldc + gn;
+      *c = alpha * acc[i][j] + (beta == 0.0f ? 0.0f : beta * *c);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Attention forward (any head_dim <= 256), online softmax in fp32.
+// Block = 4 warps over BQ=16 query rows of one (b, h); key tiles of 32
+// (lane <-> key for scores, lane <-> head-dim slice for P.V).
+// Causal: key j > query i excluded; tiles past the block's last row skipped.
+// Grouped-query: kv head = h / (Hq / Hkv).  lse = max + log(sum).
+// ---------------------------------------------------------------------------
+constexpr int ABQ = 16, ABK = 32;
+
+template <typename TIn, typename TOut, int DPL>
+__global__ void __launch_bounds__(128)
+    attn_kernel(const TIn* __restrict__ Q, const TIn* __restrict__ Kp,
+                const TIn* __restrict__ Vp, TOut* __restrict__ O, float* __restrict__ lse,
+                int Hq, int Hkv, int S, int D, float scale, int causal) {
+  constexpr int DMAX = DPL * 32;
+  extern __shared__ float sm[];
+  float* Qs = sm;                     // [ABQ][DMAX]
+  float* Ks = Qs + ABQ * DMAX;        // [ABK][DMAX+1]
+  float* Vs = Ks + ABK * (DMAX + 1);  // [ABK][DMAX]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y;
+  const int b = bh / Hq, h = bh % Hq;
+  const int hk = h / (Hq / Hkv);
+  const int q0 = blockIdx.x * ABQ;
+  const TIn* qb = Q + (size_t)bh * S * D;
+  const TIn* kb = Kp + ((size_t)b * Hkv + hk) * S * D;
+  const TIn* vb = Vp + ((size_t)b * Hkv + hk) * S * D;
+
+  for (int e = threadIdx.x; e < ABQ * DMAX; e += blockDim.x) {
+    const int r = e / DMAX, d = e % DMAX;
+    Qs[e] = (q0 + r < S && d < D) ? to_f32(qb[(size_t)(q0 + r) * D + d]) : 0.0f;
+  }
+
+  float m[4], l[4], acc[4][DPL];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) acc[r][i] = 0.0f;
+  }
+
+  const int kv_end = causal ? min(S, q0 + ABQ) : S;
+  for (int k0 = 0; k0 < kv_end; k0 += ABK) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < ABK * DMAX; e += blockDim.x) {
+      const int j = e / DMAX, d = e % DMAX;
+      const bool in = (k0 + j < S) && d < D;
+      Ks[j * (DMAX + 1) + d] = in ? to_f32(kb[(size_t)(k0 + j) * D + d]) : 0.0f;
+      Vs[j * DMAX + d] = in ? to_f32(vb[(size_t)(k0 + j) * D + d]) : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int qr = warp * 4 + r;
+      const int qi = q0 + qr;
+      if (qi >= S) continue;  // warp-uniform
+      const int kj = k0 + lane;
+      float sdot = 0.0f;
+      const float* qrow = Qs + qr * DMAX;
+      const float* krow = Ks + lane * (DMAX + 1);
+      for (int d = 0; d < D; ++d) sdot = fmaf(qrow[d], krow[d], sdot);
+      float sc = scale * sdot;
+      const bool valid = (kj < S) && !(causal && kj > qi);
+      if (!valid) sc = -INFINITY;
+      float tmax = sc;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+      const float mnew = fmaxf(m[r], tmax);
+      if (mnew == -INFINITY) continue;  // nothing visible yet (warp-uniform)
+      const float p = valid ? expf(sc - mnew) : 0.0f;
+      const float alpha = (m[r] == -INFINITY) ? 0.0f : expf(m[r] - mnew);
+      float psum = p;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
+      l[r] = l[r] * alpha + psum;
+      m[r] = mnew;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) acc[r][i] *= alpha;
+      for (int j = 0; j < ABK; ++j) {
+        const float pj = __shfl_sync(0xffffffffu, p, j);
+        const float* vrow = Vs + j * DMAX;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) acc[r][i] = fmaf(pj, vrow[lane + 32 * i], acc[r][i]);
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int qi = q0 + warp * 4 + r;
+    if (qi >= S) continue;
+    const float inv = 1.0f / l[r];
+    TOut* orow = O + ((size_t)bh * S + qi) * D;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+      const int d = lane + 32 * i;
+      if (d < D) orow[d] = from_f32<TOut>(acc[r][i] * inv);
+    }
+    if (lse && lane == 0) lse[(size_t)bh * S + qi] = m[r] + logf(l[r]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// LayerNorm over rows (include/jules/Kernel/FusedKernels.h:532-600): mean,
+// biased variance (second pass over (x-mean)^2), inv_std = 1/sqrt(var+eps),
+// y = (x-mean)*inv_std*gamma + beta.  One 256-thread block per row; fp32
+// statistics.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float block_sum_256(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.0f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) t += red[w];
+  return t;
+}
+
+template <typename TIn, typename TOut>
+__global__ void __launch_bounds__(256)
+    layernorm_kernel(const TIn* __restrict__ in, const float* __restrict__ gamma,
+                     const float* __restrict__ beta, TOut* __restrict__ out,
+                     float* __restrict__ mean_out, float* __restrict__ rstd_out, int64_t M,
+                     int64_t N, float eps) {
+  __shared__ float red[8];
+  const int64_t row = blockIdx.x;
+  if (row >= M) return;
+  const TIn* x = in + row * N;
+  float s = 0.0f;
+  for (int64_t j = threadIdx.x; j < N; j += 256) s += to_f32(x[j]);
+  const float mean = block_sum_256(s, red) / (float)N;
+  float v = 0.0f;
+  for (int64_t j = threadIdx.x; j < N; j += 256) {
+    const float d = to_f32(x[j]) - mean;
+    v = fmaf(d, d, v);
+  }
+  const float var = block_sum_256(v, red) / (float)N;
+  const float inv_std = 1.0f / sqrtf(var + eps);
+  TOut* y = out + row * N;
+  for (int64_t j = threadIdx.x; j < N; j += 256)
+    y[j] = from_f32<TOut>((to_f32(x[j]) - mean) * inv_std * gamma[j] + beta[j]);
+  if (threadIdx.x == 0) {
+    if (mean_out) mean_out[row] = mean;
+    if (rstd_out) rstd_out[row] = inv_std;
+  }
+}
+
+// Vectorised bf16 LayerNorm for N % 8 == 0 and N <= 8 * 256 * LNV: the row
+// stays in registers between the three passes (one HBM read).
+template <int LNV>
+__global__ void __launch_bounds__(256)
+    layernorm_bf16_vec_kernel(const __nv_bfloat16* __restrict__ in,
+                              const float* __restrict__ gamma, const float* __restrict__ beta,
+                              __nv_bfloat16* __restrict__ out, float* __restrict__ mean_out,
+                              float* __restrict__ rstd_out, int64_t M, int N, float eps) {
+  __shared__ float red[8];
+  const int64_t row = blockIdx.x;
+  if (row >= M) return;
+  const uint4* x = reinterpret_cast<const uint4*>(in + row * N);
+  const int nv = N / 8;
+  float xv[LNV][8];
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < LNV; ++i) {
+    const int c = threadIdx.x + i * 256;
+    if (c < nv) {
+      const uint4 u = x[c];
+      const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(p[j]);
+        xv[i][2 * j] = f.x;
+        xv[i][2 * j + 1] = f.y;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += xv[i][j];
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xv[i][j] = 0.0f;
+    }
+  }
+  const float mean = block_sum_256(s, red) / (float)N;
+  float v = 0.0f;
+#pragma unroll
+  for (int i = 0; i < LNV; ++i) {
+    const int c = threadIdx.x + i * 256;
+    if (c < nv) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = xv[i][j] - mean;
+        v = fmaf(d, d, v);
+      }
+    }
+  }
+  const float var = block_sum_256(v, red) / (float)N;
+  const float inv_std = 1.0f / sqrtf(var + eps);
+  uint4* y = reinterpret_cast<uint4*>(out + row * N);
+#pragma unroll
+  for (int i = 0; i < LNV; ++i) {
+    const int c = threadIdx.x + i * 256;
+    if (c < nv) {
+      const float4 g0 = reinterpret_cast<const float4*>(gamma)[2 * c];
+      const float4 g1 = reinterpret_cast<const float4*>(gamma)[2 * c + 1];
+      const float4 b0 = reinterpret_cast<const float4*>(beta)[2 * c];
+      const float4 b1 = reinterpret_cast<const float4*>(beta)[2 * c + 1];
+      const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+      const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = (xv[i][j] - mean) * inv_std * g[j] + bb[j];
+      uint4 u;
+      u.x = pack_bf16x2(o[0], o[1]);
+      u.y = pack_bf16x2(o[2], o[3]);
+      u.z = pack_bf16x2(o[4], o[5]);
+      u.w = pack_bf16x2(o[6], o[7]);
+      y[c] = u;
+    }
+  }
+  if (threadIdx.x == 0) {
+    if (mean_out) mean_out[row] = mean;
+    if (rstd_out) rstd_out[row] = inv_std;
+  }
+}
+
+// GELU-tanh elementwise (FusedKernels.h:606-627).
+template <typename T>
+__global__ void gelu_kernel(const T* __restrict__ in, T* __restrict__ out, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = from_f32<T>(act_exact(to_f32(in[i]), 4));
+}
+
+}  // namespace simt
+}  // namespace jb

@@ -1,0 +1,119 @@
+"""Fused GEMM + bias + activation (+ residual): CUDA kernels vs the oracle.
+
+bf16 tensor-core path (tcgen05) against the C restatement of
+tiledMatmulWithActivation / fusedMatmulBiasRelu on the same bf16 values;
+fp32 CUDA-core path against the reference's own kernels (oracle/_ref)."""
+import numpy as np
+import pytest
+
+from conftest import BF16_MAX_ABS, BF16_REL_L2, F32_REL_L2, max_abs, rel_l2
+from helpers import bf16_np, gemm_inputs, to_dev, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+def _run_bf16(jb, A, W, b, act, residual=None):
+    import torch
+    r = to_dev(residual) if residual is not None else None
+    bias = torch.from_numpy(b).cuda() if b is not None else None
+    C = jb.gemm_bias_act(to_dev(A), to_dev(W), bias, r, act=act)
+    torch.cuda.synchronize()
+    assert jb.device_error() == 0
+    return to_np(C)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 256), (129, 264, 72), (1, 8, 8),
+                                   (300, 520, 136), (640, 1024, 1024)])
+@pytest.mark.parametrize("act", ["none", "gelu"])
+def test_gemm_tc_shapes(jb, orc, M, N, K, act):
+    A, W, b = gemm_inputs(M, N, K, seed=M + N + K)
+    got = _run_bf16(jb, A, W, b, act)
+    want = orc.gemm_bias_act(A, W, b, None, act)
+    assert max_abs(got, want) <= BF16_MAX_ABS
+    assert rel_l2(got, want) <= BF16_REL_L2
+
+
+@pytest.mark.parametrize("act", ["relu", "sigmoid", "tanh"])
+def test_gemm_tc_activations(jb, orc, act):
+    A, W, b = gemm_inputs(256, 512, 320, seed=7)
+    got = _run_bf16(jb, A, W, b, act)
+    want = orc.gemm_bias_act(A, W, b, None, act)
+    assert max_abs(got, want) <= BF16_MAX_ABS
+    assert rel_l2(got, want) <= BF16_REL_L2
+
+
+def test_gemm_tc_no_bias_residual(jb, orc):
+    A, W, _ = gemm_inputs(384, 768, 512, seed=3, bias=False)
+    R = bf16_np(np.random.default_rng(4).standard_normal((384, 768)).astype(np.float32))
+    got = _run_bf16(jb, A, W, None, "none", residual=R)
+    want = orc.gemm_bias_act(A, W, None, R, "none")
+    assert max_abs(got, want) <= BF16_MAX_ABS
+    assert rel_l2(got, want) <= BF16_REL_L2
+
+
+def test_gemm_tc_config_c2_sampled(jb, orc):
+    """Config C2 at full size (4096^3, bias + GELU); 256 rows checked
+    against the oracle, all rows through a size-independent property."""
+    import torch
+    M = N = K = 4096
+    A, W, b = gemm_inputs(M, N, K, seed=20260)
+    dA, dW = to_dev(A), to_dev(W)
+    bias = torch.from_numpy(b).cuda()
+    C = jb.gemm_bias_act(dA, dW, bias, act="gelu")
+    torch.cuda.synchronize()
+    assert jb.device_error() == 0
+    rows = np.linspace(0, M - 1, 256).astype(np.int64)
+    got = to_np(C[torch.from_numpy(rows).cuda()])
+    want = orc.gemm_bias_act(np.ascontiguousarray(A[rows]), W, b, None, "gelu")
+    assert max_abs(got, want) <= BF16_MAX_ABS
+    assert rel_l2(got, want) <= BF16_REL_L2
+    # Scaling A by 2 is exact in bf16 and fp32: the no-activation product must
+    # double bit-exactly in every row.
+    C1 = jb.gemm_bias_act(dA, dW, act="none")
+    C2 = jb.gemm_bias_act(dA * 2, dW, act="none")
+    torch.cuda.synchronize()
+    assert torch.equal(C2, C1 * 2)
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 96, 80), (33, 17, 129), (256, 256, 256)])
+@pytest.mark.parametrize("act", ["none", "relu", "gelu"])
+def test_gemm_fp32_vs_reference(jb, ref, M, N, K, act):
+    """fp32 CUDA-core path vs the reference's own tiled kernel."""
+    import torch
+    g = np.random.default_rng(M * 7 + K)
+    A = g.uniform(-1, 1, (M, K)).astype(np.float32)
+    W = g.uniform(-1, 1, (K, N)).astype(np.float32)
+    want = ref.tiled_matmul_act(A, W, act)
+    got = jb.gemm_bias_act(torch.from_numpy(A).cuda(), torch.from_numpy(W).cuda(), act=act)
+    assert rel_l2(to_np(got), want) <= F32_REL_L2
+
+
+def test_gemm_fp32_bias_relu_vs_reference(jb, ref):
+    import torch
+    g = np.random.default_rng(11)
+    X = g.uniform(-1, 1, (96, 200)).astype(np.float32)
+    W = g.uniform(-1, 1, (200, 144)).astype(np.float32)
+    b = g.uniform(-1, 1, 144).astype(np.float32)
+    want = ref.fused_matmul_bias_relu(X, W, b)
+    got = jb.gemm_bias_act(torch.from_numpy(X).cuda(), torch.from_numpy(W).cuda(),
+                           torch.from_numpy(b).cuda(), act="relu")
+    assert rel_l2(to_np(got), want) <= F32_REL_L2
+
+
+@pytest.mark.parametrize("ta,tb", [(False, False), (True, False), (False, True), (True, True)])
+def test_sgemm_vs_reference_blas(jb, ref, ta, tb):
+    import torch
+    g = np.random.default_rng(5)
+    M, N, K = 70, 50, 90
+    A = g.uniform(-1, 1, (K, M) if ta else (M, K)).astype(np.float32)
+    B = g.uniform(-1, 1, (N, K) if tb else (K, N)).astype(np.float32)
+    C0 = g.uniform(-1, 1, (M, N)).astype(np.float32)
+    want = (A.T if ta else A).astype(np.float64) @ (B.T if tb else B) * 0.5 + 2.0 * C0
+    dC = torch.from_numpy(C0.copy()).cuda()
+    got = jb.sgemm(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda(), dC, alpha=0.5, beta=2.0,
+                   transA=ta, transB=tb)
+    assert rel_l2(to_np(got), want) <= F32_REL_L2
+    if not ta and not tb:
+        r = ref.blas_matmul(A, B)
+        got2 = jb.sgemm(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda())
+        assert rel_l2(to_np(got2), r) <= F32_REL_L2

@@ -1,0 +1,110 @@
+"""LayerNorm, GELU and the MLP block: CUDA kernels vs the oracle."""
+import numpy as np
+import pytest
+
+from conftest import BF16_MAX_ABS, BF16_REL_L2, F32_REL_L2, max_abs, rel_l2
+from helpers import bf16_np, to_dev, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("M,N", [(64, 256), (2048, 256), (7, 1000), (3, 4096)])
+def test_layernorm_fp32_vs_reference(jb, ref, M, N):
+    import torch
+    g = np.random.default_rng(M + N)
+    x = g.uniform(-1, 1, (M, N)).astype(np.float32)
+    gam = (1 + 0.02 * g.standard_normal(N)).astype(np.float32)
+    bet = (0.02 * g.standard_normal(N)).astype(np.float32)
+    want = ref.layernorm(x, gam, bet)
+    got = jb.layernorm(torch.from_numpy(x).cuda(), torch.from_numpy(gam).cuda(),
+                       torch.from_numpy(bet).cuda())
+    assert rel_l2(to_np(got), want) <= F32_REL_L2
+
+
+@pytest.mark.parametrize("M,N", [(512, 4096), (33, 4104), (5, 200), (4, 9000)])
+def test_layernorm_bf16(jb, orc, M, N):
+    import torch
+    g = np.random.default_rng(N)
+    x = bf16_np(g.standard_normal((M, N)).astype(np.float32))
+    gam = (1 + 0.02 * g.standard_normal(N)).astype(np.float32)
+    bet = (0.02 * g.standard_normal(N)).astype(np.float32)
+    want, mean, rstd = orc.layernorm(x, gam, bet, stats=True)
+    got, gm, gr = jb.layernorm(to_dev(x), torch.from_numpy(gam).cuda(),
+                               torch.from_numpy(bet).cuda(), stats=True)
+    assert max_abs(to_np(got), want) <= BF16_MAX_ABS
+    assert rel_l2(to_np(got), want) <= BF16_REL_L2
+    assert max_abs(gm.cpu().numpy(), mean) <= 1e-5
+    assert rel_l2(gr.cpu().numpy(), rstd) <= 1e-5
+
+
+@pytest.mark.parametrize("n", [1, 15, 16, 1000, 1 << 20])
+def test_gelu_fp32_vs_reference(jb, ref, n):
+    import torch
+    x = np.random.default_rng(n).uniform(-6, 6, n).astype(np.float32)
+    want = ref.gelu(x)
+    got = jb.gelu(torch.from_numpy(x).cuda())
+    assert rel_l2(to_np(got), want) <= F32_REL_L2
+
+
+def test_gelu_bf16(jb, orc):
+    x = bf16_np(np.random.default_rng(9).uniform(-6, 6, 4096).astype(np.float32))
+    want = orc.gelu(x)
+    got = jb.gelu(to_dev(x))
+    assert max_abs(to_np(got), want) <= BF16_MAX_ABS
+
+
+def _mlp_inputs(T, d, dff, seed):
+    """Config C4 distributions: X ~ N(0,1); gamma = 1 + N(0,0.02),
+    beta ~ N(0,0.02); W ~ N(0,0.02) bf16; biases ~ N(0,0.02)."""
+    g = np.random.default_rng(seed)
+    X = bf16_np(g.standard_normal((T, d)).astype(np.float32))
+    gam = (1 + 0.02 * g.standard_normal(d)).astype(np.float32)
+    bet = (0.02 * g.standard_normal(d)).astype(np.float32)
+    W1 = bf16_np((0.02 * g.standard_normal((d, dff))).astype(np.float32))
+    b1 = (0.02 * g.standard_normal(dff)).astype(np.float32)
+    W2 = bf16_np((0.02 * g.standard_normal((dff, d))).astype(np.float32))
+    b2 = (0.02 * g.standard_normal(d)).astype(np.float32)
+    return X, gam, bet, W1, b1, W2, b2
+
+
+def _mlp_gpu(jb, X, gam, bet, W1, b1, W2, b2):
+    import torch
+    f = lambda a: torch.from_numpy(a).cuda()
+    out = jb.mlp_block(to_dev(X), f(gam), f(bet), to_dev(W1), f(b1), to_dev(W2), f(b2))
+    torch.cuda.synchronize()
+    assert jb.device_error() == 0
+    return out
+
+
+@pytest.mark.parametrize("T,d,dff", [(256, 512, 2048), (200, 256, 1024)])
+def test_mlp_block(jb, orc, T, d, dff):
+    ins = _mlp_inputs(T, d, dff, seed=T + d)
+    want = orc.mlp_block(*ins)
+    got = to_np(_mlp_gpu(jb, *ins))
+    assert max_abs(got, want) <= BF16_MAX_ABS
+    assert rel_l2(got, want) <= BF16_REL_L2
+
+
+@pytest.mark.slow
+def test_mlp_block_config_c4_sampled(jb, orc):
+    """Config C4 at full size: T=16384, d=4096, dff=16384; 48 rows vs oracle."""
+    import torch
+    T, d, dff = 16384, 4096, 16384
+    g = torch.Generator(device="cuda").manual_seed(4)
+    X = torch.randn((T, d), generator=g, device="cuda").to(torch.bfloat16)
+    gam = 1 + 0.02 * torch.randn(d, generator=g, device="cuda")
+    bet = 0.02 * torch.randn(d, generator=g, device="cuda")
+    W1 = (0.02 * torch.randn((d, dff), generator=g, device="cuda")).to(torch.bfloat16)
+    b1 = 0.02 * torch.randn(dff, generator=g, device="cuda")
+    W2 = (0.02 * torch.randn((dff, d), generator=g, device="cuda")).to(torch.bfloat16)
+    b2 = 0.02 * torch.randn(d, generator=g, device="cuda")
+    out = jb.mlp_block(X, gam, bet, W1, b1, W2, b2)
+    torch.cuda.synchronize()
+    assert jb.device_error() == 0
+    rows = np.linspace(0, T - 1, 48).astype(np.int64)
+    want = orc.mlp_block(to_np(X), gam.cpu().numpy(), bet.cpu().numpy(), to_np(W1),
+                         b1.cpu().numpy(), to_np(W2), b2.cpu().numpy(), rows=rows)
+    got = to_np(out[torch.from_numpy(rows).cuda()])
+    assert max_abs(got, want) <= BF16_MAX_ABS
+    assert rel_l2(got, want) <= BF16_REL_L2
+    assert bool(torch.isfinite(out.float()).all())
