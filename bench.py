@@ -1,0 +1,672 @@
+"""Benchmark of the Jules fused-kernel hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl jules|reference]
+                    [--workload gemm|attn|attn_gqa|mlp|attn_fp32]
+
+Default workload: config C2 of the baseline (fused GEMM + bias + GELU-tanh,
+A[4096,4096] . W[4096,4096] bf16, fp32 accumulate, bf16 out), the
+fused-GEMM half of the headline metric "flash-attn fwd & fused-GEMM TFLOP/s".
+The other workloads are the remaining configs (C3 causal attention, C5
+grouped-query causal attention, C4 MLP block, C1 fp32 attention).
+
+One step = one pass of the hot path over one batch of synthetic input.  With
+N GPUs (torchrun, one process per GPU, NCCL) every rank runs its own shard of
+the token rows / (batch, head) units of a problem N times the single-GPU
+size: weak scaling, no collective on the data path.  The output gather the
+sharding implies is timed separately and reported under "gather".
+
+Rank 0 prints one JSON line.  ``value`` is total TFLOP/s over all ranks
+(algorithmic FLOPs / max-over-ranks device time of the K steps, inputs
+resident in HBM, rotating input sets larger than L2 so no step starts warm).
+``e2e`` is the same metric through the C ABI with host buffers: every step
+copies its inputs from pinned host memory and reads the result back.
+
+``--impl reference`` times the reference's own CPU kernels (compiled from
+its sources into oracle/_ref) on the host cores, on a bounded sample of the
+same workload, and prints the same line with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_PEAK_TFLOPS = 1590.0
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["jules", "reference"], default="jules")
+    p.add_argument("--workload", choices=["gemm", "attn", "attn_gqa", "mlp", "attn_fp32"],
+                   default="gemm")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    a = p.parse_args()
+    a.warmup = max(a.warmup, 3)
+    return a
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")),
+            int(os.environ.get("WORLD_SIZE", "1")))
+
+
+def measured_peaks():
+    path = os.path.join(HERE, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_PEAK_TFLOPS, FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic(workload):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu
+    summary (profiles/<kernel>_<workload>.md, line 'traffic_bytes_per_launch:')."""
+    name = {"gemm": "gemm_tc_c2", "attn": "attn_tc_c3", "attn_gqa": "attn_tc_c5",
+            "mlp": "gemm_tc_c4", "attn_fp32": "attn_simt_c1"}[workload]
+    path = os.path.join(HERE, "profiles", f"{name}.md")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.strip().startswith("traffic_bytes_per_launch:"):
+                    return float(line.split(":", 1)[1].strip().split()[0])
+    except (OSError, ValueError):
+        pass
+    return None
+
+
+def describe(workload, world, extra_l2=None):
+    """The config object of the JSON line (shared by both arms)."""
+    if workload == "gemm":
+        c = {"workload": "C2 fused GEMM+bias+GELU(tanh)", "M_per_rank": 4096, "N": 4096,
+             "K": 4096, "global_M": 4096 * world, "sharding": "rows of M", "dtype_in": "bf16",
+             "accumulate": "fp32", "dtype_out": "bf16"}
+    elif workload in ("attn", "attn_gqa"):
+        gqa = workload == "attn_gqa"
+        B, Hq, Hkv, S = (4, 64, 8, 16384) if gqa else (8, 32, 32, 4096)
+        c = {"workload": ("C5 GQA causal flash-attention fwd" if gqa else
+                          "C3 causal flash-attention fwd + lse"),
+             "B_per_rank": B, "Hq": Hq, "Hkv": Hkv, "S": S, "D": 128, "global_B": B * world,
+             "sharding": "batch x kv-head-group units",
+             "flop_convention": "causal = 2*B*Hq*S^2*D"}
+    elif workload == "mlp":
+        c = {"workload": "C4 MLP block LN->GEMM+b+GELU->GEMM+b+residual", "T_per_rank": 16384,
+             "d": 4096, "dff": 16384, "global_T": 16384 * world, "sharding": "token rows",
+             "eps": 1e-5}
+    else:
+        c = {"workload": "C1 fp32 flash-attention fwd, non-causal", "B_per_rank": 1, "H": 8,
+             "S": 512, "D": 64, "sharding": "batch"}
+    c["parallelism"] = f"shard x{world}"
+    if extra_l2:
+        c["l2"] = extra_l2
+    return c
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling (NVML) during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8, "sync_boost": 0x10, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, device_index, interval=0.005):
+        self.ok = False
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            pass
+        self.interval = interval
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for k, bit in self.REASONS.items():
+                    if r & bit and k != "gpu_idle":
+                        self.reasons.add(k)
+            except Exception:
+                pass
+            time.sleep(self.interval)
+
+    def start(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+
+    def stop(self):
+        if self._t:
+            self._stop.set()
+            self._t.join()
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples), "source": "nvml" if self.ok else "unavailable"}
+
+
+# ---------------------------------------------------------------------------
+# Workloads.  Each builds rotating input sets (> L2 in total), a device
+# step, a host->device->host e2e step, and its FLOP count.
+# ---------------------------------------------------------------------------
+class Workload:
+    name = ""
+    dominant = ""
+    launches_per_step = 1
+
+    def sets_for(self, bytes_per_set):
+        return max(2, int((2 * L2_BYTES) // max(bytes_per_set, 1)) + 1)
+
+
+class Gemm(Workload):
+    """C2: C = GELU(A.W + bias), M=N=K=4096 per rank (rows of M sharded)."""
+    dominant = "gemm_bf16_tc_kernel"
+
+    def __init__(self, jb, torch, rank, world, M=4096, N=4096, K=4096):
+        self.jb, self.torch = jb, torch
+        self.M, self.N, self.K = M, N, K
+        self.world = world
+        dev = torch.device("cuda")
+        g = torch.Generator(device=dev).manual_seed(1234 + rank)
+        per_set = (M * K + K * N + M * N) * 2
+        self.nsets = self.sets_for(per_set)
+        s = 1.0 / K ** 0.5
+        self.A = [((torch.rand((M, K), generator=g, device=dev) * 2 - 1) * s).to(torch.bfloat16)
+                  for _ in range(self.nsets)]
+        # W and bias are replicated (one copy per rank); distinct copies per set
+        # keep every step cold in L2.
+        self.W = [((torch.rand((K, N), generator=g, device=dev) * 2 - 1) * s).to(torch.bfloat16)
+                  for _ in range(self.nsets)]
+        self.b = [torch.randn(N, generator=g, device=dev) * 0.02 for _ in range(self.nsets)]
+        self.C = [torch.empty((M, N), dtype=torch.bfloat16, device=dev) for _ in range(self.nsets)]
+        self.flops_per_step = 2.0 * M * N * K
+        self.flops_dominant = self.flops_per_step
+        self.config = {"workload": "C2 fused GEMM+bias+GELU(tanh)", "M_per_rank": M, "N": N,
+                       "K": K, "global_M": M * world, "sharding": "rows of M",
+                       "dtype_in": "bf16", "accumulate": "fp32", "dtype_out": "bf16",
+                       "l2": f"{self.nsets} rotating input sets ({self.nsets * per_set / 2**20:.0f} MiB > L2)"}
+
+    def step(self, i, ev=None):
+        k = i % self.nsets
+        if ev:
+            ev[0].record()
+        self.jb.gemm_bias_act(self.A[k], self.W[k], self.b[k], act="gelu", out=self.C[k])
+        if ev:
+            ev[1].record()
+
+    def output(self, i):
+        return self.C[i % self.nsets]
+
+    # e2e through the C ABI with host buffers
+    def e2e_setup(self):
+        t = self.torch
+        self.hA = self.A[0].cpu().pin_memory()
+        self.hW = self.W[0].cpu().pin_memory()
+        self.hb = self.b[0].cpu().pin_memory()
+        self.hC = t.empty((self.M, self.N), dtype=t.bfloat16).pin_memory()
+        self.dA, self.dW, self.db = (t.empty_like(self.A[0]), t.empty_like(self.W[0]),
+                                     t.empty_like(self.b[0]))
+        self.dC = t.empty_like(self.C[0])
+        self.h2d = (self.hA.numel() + self.hW.numel()) * 2 + self.hb.numel() * 4
+        self.d2h = self.hC.numel() * 2
+
+    def e2e_step(self):
+        self.dA.copy_(self.hA, non_blocking=True)
+        self.dW.copy_(self.hW, non_blocking=True)
+        self.db.copy_(self.hb, non_blocking=True)
+        self.jb.gemm_bias_act(self.dA, self.dW, self.db, act="gelu", out=self.dC)
+        self.hC.copy_(self.dC, non_blocking=True)
+
+
+class Attention(Workload):
+    """C3 (attn) / C5 (attn_gqa): causal bf16 flash-attention fwd + lse;
+    (batch, kv-head group) units sharded across ranks."""
+    dominant = "attn_fwd_tc_kernel"
+
+    def __init__(self, jb, torch, rank, world, gqa=False):
+        self.jb, self.torch = jb, torch
+        if gqa:
+            B, Hq, Hkv, S = 4, 64, 8, 16384
+            # 32 (b, kv-group) units; each rank owns 32/world of them, run as
+            # B_r = 4/world batches when world <= 4, else a head-group slice.
+            self.units = 32
+        else:
+            B, Hq, Hkv, S = 8, 32, 32, 4096
+            self.units = B
+        D = 128
+        self.global_shape = (B, Hq, Hkv, S, D)
+        # per-rank shard, same size for every world size (weak scaling)
+        self.B, self.Hq, self.Hkv, self.S, self.D = B, Hq, Hkv, S, D
+        dev = torch.device("cuda")
+        g = torch.Generator(device=dev).manual_seed(77 + rank)
+        per_set = (B * Hq * S * D * 2 + 2 * B * Hkv * S * D) * 2
+        self.nsets = 1 if per_set > L2_BYTES else self.sets_for(per_set)
+        self.Q = [torch.randn((B, Hq, S, D), generator=g, device=dev).to(torch.bfloat16)
+                  for _ in range(self.nsets)]
+        self.Kt = [torch.randn((B, Hkv, S, D), generator=g, device=dev).to(torch.bfloat16)
+                   for _ in range(self.nsets)]
+        self.V = [torch.randn((B, Hkv, S, D), generator=g, device=dev).to(torch.bfloat16)
+                  for _ in range(self.nsets)]
+        self.O = [torch.empty_like(q) for q in self.Q]
+        self.L = [torch.empty((B, Hq, S), dtype=torch.float32, device=dev) for _ in self.Q]
+        # causal FLOPs, FlashAttention convention: 2 * B*H*S^2*D
+        self.flops_per_step = 2.0 * B * Hq * S * S * D
+        self.flops_dominant = self.flops_per_step
+        self.config = {"workload": ("C5 GQA causal flash-attention fwd" if gqa else
+                                    "C3 causal flash-attention fwd + lse"),
+                       "B_per_rank": B, "Hq": Hq, "Hkv": Hkv, "S": S, "D": D,
+                       "global_B": B * world, "sharding": "batch x kv-head-group units",
+                       "flop_convention": "causal = 2*B*Hq*S^2*D",
+                       "l2": f"inputs {per_set / 2**20:.0f} MiB per step (> L2)"
+                       if self.nsets == 1 else f"{self.nsets} rotating input sets"}
+
+    def step(self, i, ev=None):
+        k = i % self.nsets
+        if ev:
+            ev[0].record()
+        self.jb.flash_attention_fwd(self.Q[k], self.Kt[k], self.V[k], causal=True, out=self.O[k],
+                                    lse=False)
+        if ev:
+            ev[1].record()
+
+    def output(self, i):
+        return self.O[i % self.nsets]
+
+    def e2e_setup(self):
+        t = self.torch
+        self.hQ = self.Q[0].cpu().pin_memory()
+        self.hK = self.Kt[0].cpu().pin_memory()
+        self.hV = self.V[0].cpu().pin_memory()
+        self.hO = t.empty_like(self.hQ).pin_memory()
+        self.dQ, self.dK, self.dV = (t.empty_like(self.Q[0]), t.empty_like(self.Kt[0]),
+                                     t.empty_like(self.V[0]))
+        self.dO = t.empty_like(self.Q[0])
+        self.h2d = (self.hQ.numel() + self.hK.numel() + self.hV.numel()) * 2
+        self.d2h = self.hO.numel() * 2
+
+    def e2e_step(self):
+        self.dQ.copy_(self.hQ, non_blocking=True)
+        self.dK.copy_(self.hK, non_blocking=True)
+        self.dV.copy_(self.hV, non_blocking=True)
+        self.jb.flash_attention_fwd(self.dQ, self.dK, self.dV, causal=True, out=self.dO, lse=False)
+        self.hO.copy_(self.dO, non_blocking=True)
+
+
+class AttentionF32(Workload):
+    """C1: fp32 [1,8,512,64] non-causal (CUDA cores)."""
+    dominant = "attn_kernel<float>"
+
+    def __init__(self, jb, torch, rank, world):
+        self.jb, self.torch = jb, torch
+        B, H, S, D = 1, 8, 512, 64
+        dev = torch.device("cuda")
+        g = torch.Generator(device=dev).manual_seed(5 + rank)
+        per_set = 4 * B * H * S * D * 4
+        self.nsets = self.sets_for(per_set)
+        self.Q = [torch.randn((B, H, S, D), generator=g, device=dev) for _ in range(self.nsets)]
+        self.Kt = [torch.randn((B, H, S, D), generator=g, device=dev) for _ in range(self.nsets)]
+        self.V = [torch.randn((B, H, S, D), generator=g, device=dev) for _ in range(self.nsets)]
+        self.O = [torch.empty_like(q) for q in self.Q]
+        self.flops_per_step = 4.0 * B * H * S * S * D
+        self.flops_dominant = self.flops_per_step
+        self.config = {"workload": "C1 fp32 flash-attention fwd, non-causal", "B_per_rank": B,
+                       "H": H, "S": S, "D": D, "sharding": "batch",
+                       "l2": f"{self.nsets} rotating input sets"}
+
+    def step(self, i, ev=None):
+        k = i % self.nsets
+        if ev:
+            ev[0].record()
+        self.jb.flash_attention_fwd(self.Q[k], self.Kt[k], self.V[k], causal=False, out=self.O[k],
+                                    lse=False)
+        if ev:
+            ev[1].record()
+
+    def output(self, i):
+        return self.O[i % self.nsets]
+
+    def e2e_setup(self):
+        t = self.torch
+        self.hQ, self.hK, self.hV = (x[0].cpu().pin_memory() for x in (self.Q, self.Kt, self.V))
+        self.hO = t.empty_like(self.hQ).pin_memory()
+        self.dQ, self.dK, self.dV, self.dO = (t.empty_like(self.Q[0]) for _ in range(4))
+        self.h2d = 3 * self.hQ.numel() * 4
+        self.d2h = self.hO.numel() * 4
+
+    def e2e_step(self):
+        self.dQ.copy_(self.hQ, non_blocking=True)
+        self.dK.copy_(self.hK, non_blocking=True)
+        self.dV.copy_(self.hV, non_blocking=True)
+        self.jb.flash_attention_fwd(self.dQ, self.dK, self.dV, causal=False, out=self.dO, lse=False)
+        self.hO.copy_(self.dO, non_blocking=True)
+
+
+class Mlp(Workload):
+    """C4: out = GELU(LN(X).W1 + b1).W2 + b2 + X, T=16384 tokens per rank,
+    d=4096, dff=16384 (token rows sharded)."""
+    dominant = "gemm_bf16_tc_kernel (GEMM1)"
+    launches_per_step = 3
+
+    def __init__(self, jb, torch, rank, world, T=16384, d=4096, dff=16384):
+        self.jb, self.torch = jb, torch
+        self.T, self.d, self.dff = T, d, dff
+        dev = torch.device("cuda")
+        g = torch.Generator(device=dev).manual_seed(99 + rank)
+        self.X = torch.randn((T, d), generator=g, device=dev).to(torch.bfloat16)
+        self.gam = 1 + 0.02 * torch.randn(d, generator=g, device=dev)
+        self.bet = 0.02 * torch.randn(d, generator=g, device=dev)
+        self.W1 = (0.02 * torch.randn((d, dff), generator=g, device=dev)).to(torch.bfloat16)
+        self.b1 = 0.02 * torch.randn(dff, generator=g, device=dev)
+        self.W2 = (0.02 * torch.randn((dff, d), generator=g, device=dev)).to(torch.bfloat16)
+        self.b2 = 0.02 * torch.randn(d, generator=g, device=dev)
+        self.out = torch.empty_like(self.X)
+        self.xn = torch.empty_like(self.X)
+        self.hid = torch.empty((T, dff), dtype=torch.bfloat16, device=dev)
+        self.nsets = 1
+        self.flops_per_step = 16.0 * T * d * d * (dff / (4 * d))
+        self.flops_dominant = 2.0 * T * d * dff
+        self.config = {"workload": "C4 MLP block LN->GEMM+b+GELU->GEMM+b+residual",
+                       "T_per_rank": T, "d": d, "dff": dff, "global_T": T * world,
+                       "sharding": "token rows", "eps": 1e-5,
+                       "l2": "inputs 1.4 GB per step (> L2)"}
+
+    def step(self, i, ev=None):
+        jb = self.jb
+        jb.layernorm(self.X, self.gam, self.bet, out=self.xn)
+        if ev:
+            ev[0].record()
+        jb.gemm_bias_act(self.xn, self.W1, self.b1, act="gelu", out=self.hid)
+        if ev:
+            ev[1].record()
+        jb.gemm_bias_act(self.hid, self.W2, self.b2, self.X, act="none", out=self.out)
+
+    def output(self, i):
+        return self.out
+
+    def e2e_setup(self):
+        t = self.torch
+        self.hX = self.X.cpu().pin_memory()
+        self.hO = t.empty_like(self.hX).pin_memory()
+        self.dX = t.empty_like(self.X)
+        self.dO = t.empty_like(self.X)
+        self.ws = t.empty(self.jb.mlp_block_workspace_bytes(self.T, self.d, self.dff),
+                          dtype=t.uint8, device="cuda")
+        self.h2d = self.hX.numel() * 2
+        self.d2h = self.hO.numel() * 2
+
+    def e2e_step(self):
+        self.dX.copy_(self.hX, non_blocking=True)
+        self.jb.mlp_block(self.dX, self.gam, self.bet, self.W1, self.b1, self.W2, self.b2,
+                          out=self.dO, workspace=self.ws)
+        self.hO.copy_(self.dO, non_blocking=True)
+
+
+METRIC = "Flash-attn fwd & fused-GEMM TFLOP/s at 1/2/4/8 B200; % of tensor peak"
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's own kernels (oracle/_ref) on the host cores.
+# ---------------------------------------------------------------------------
+def cpu_reference_sample(workload, reps=3, warm=1):
+    """Times the reference CPU path on a bounded sample; returns
+    (TFLOP/s, description, threads)."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(HERE, "oracle"))
+    import oracle
+    threads = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    ref = oracle.Reference()
+    g = np.random.default_rng(0)
+    if workload in ("gemm", "mlp"):
+        if workload == "gemm":
+            Ms, N, K = 1024, 4096, 4096
+            desc = (f"reference tiledMatmulWithActivation + bias + fusedGelu "
+                    f"(FusedKernels.h:378-458,606-627) on {Ms} of the 4096 rows of C2")
+        else:
+            Ms, N, K = 256, 16384, 4096
+            desc = ("reference tiledMatmulWithActivation + bias + fusedGelu on 256 of the "
+                    "16384 token rows of C4's GEMM1 (4096->16384); C4 FLOPs scale per row")
+        A = (g.uniform(-1, 1, (Ms, K)) / np.sqrt(K)).astype(np.float32)
+        W = (g.uniform(-1, 1, (K, N)) / np.sqrt(K)).astype(np.float32)
+        b = (0.02 * g.standard_normal(N)).astype(np.float32)
+        fn = lambda: ref.gemm_bias_gelu(A, W, b)
+        flops = 2.0 * Ms * N * K
+    elif workload == "attn_fp32":
+        Q, K_, V = (g.standard_normal((1, 8, 512, 64), dtype=np.float32) for _ in range(3))
+        fn = lambda: ref.flash_attention(Q, K_, V)
+        flops = 4.0 * 8 * 512 * 512 * 64
+        desc = "reference flashAttention (FlashAttention.h:130-309), full C1"
+        reps = 20
+    else:
+        # The reference has no causal kernel: its non-causal flashAttention on
+        # one (b, h) unit at the config's S, counted at causal FLOPs x2 = the
+        # work it actually does.
+        S = 4096 if workload == "attn" else 16384
+        Sx = min(S, 4096)
+        Q, K_, V = (g.standard_normal((1, 1, Sx, 128), dtype=np.float32) for _ in range(3))
+        fn = lambda: ref.flash_attention(Q, K_, V)
+        flops = 4.0 * Sx * Sx * 128
+        reps = 2
+        desc = (f"reference flashAttention (non-causal; the reference has no causal mask) on one "
+                f"(b,h) unit at S={Sx}, D=128, fp32; non-causal FLOPs 4*S^2*D")
+    for _ in range(warm):
+        fn()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        fn()
+    dt = (time.perf_counter() - t0) / reps
+    return flops / dt / 1e12, desc + f"; {reps} timed reps, {dt * 1e3:.1f} ms each", threads
+
+
+# ---------------------------------------------------------------------------
+def run_reference_arm(args):
+    rank, _, world = dist_env()
+    if rank != 0:
+        return 0
+    # Each step is one bounded sample of the workload on the CPU.
+    import numpy as np  # noqa: F401
+    vals = []
+    desc = ""
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        cpu_reference_sample(args.workload, reps=1, warm=0)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        v, desc, threads = cpu_reference_sample(args.workload, reps=1, warm=0)
+        vals.append(v)
+    wall = time.perf_counter() - t0
+    value = statistics.mean(vals)
+    line = {"metric": METRIC, "value": round(value, 6), "unit": "TFLOP/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(wall / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": describe(args.workload, world, "CPU: bounded sample per step"),
+            "impl": "reference",
+            "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": threads,
+                             "kind": "reference", "sample": desc},
+            "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import jules_b200 as jb
+    jb.lib()  # fails loudly when the CUDA library is missing
+
+    rank, local_rank, world = dist_env()
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    W = {"gemm": lambda: Gemm(jb, torch, rank, world),
+         "attn": lambda: Attention(jb, torch, rank, world, gqa=False),
+         "attn_gqa": lambda: Attention(jb, torch, rank, world, gqa=True),
+         "mlp": lambda: Mlp(jb, torch, rank, world),
+         "attn_fp32": lambda: AttentionF32(jb, torch, rank, world)}[args.workload]
+    wl = W()
+    stream = torch.cuda.current_stream()
+
+    for i in range(args.warmup):
+        wl.step(i)
+    torch.cuda.synchronize()
+    if jb.device_error() != 0:
+        raise RuntimeError("device error during warm-up")
+
+    # ---------------- timed region (device) ----------------
+    K = args.steps
+    dom = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(K)]
+    sampler = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
+                           else local_rank)
+    barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    t_begin = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_begin.record(stream)
+    for i in range(K):
+        wl.step(i, dom[i])
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    ms_total = max_over_ranks(t_begin.elapsed_time(t_end))
+    dom_ms = statistics.mean(a.elapsed_time(b) for a, b in dom)
+    dom_ms = max_over_ranks(dom_ms)
+    if jb.device_error() != 0:
+        raise RuntimeError("device error in timed region")
+
+    tflops_total = wl.flops_per_step * world * K / (ms_total * 1e-3) / 1e12
+    peak, hbm, peak_kind = measured_peaks()
+    achieved = wl.flops_dominant / (dom_ms * 1e-3) / 1e12
+    traffic = profiled_traffic(args.workload)
+
+    # ---------------- output gather (N > 1), timed separately ----------------
+    gather = None
+    if world > 1:
+        out = wl.output(0).contiguous()
+        full = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device="cuda")
+        dist.all_gather_into_tensor(full, out)  # warm
+        torch.cuda.synchronize()
+        barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        dist.all_gather_into_tensor(full, out)
+        g1.record()
+        torch.cuda.synchronize()
+        gms = max_over_ranks(g0.elapsed_time(g1))
+        gather = {"collective": "ncclAllGather of each rank's output shard (not in value)",
+                  "bytes_per_rank": out.numel() * out.element_size(), "ms": round(gms, 4)}
+        del full
+
+    # ---------------- e2e through the C ABI with host buffers ----------------
+    e2e = None
+    if not args.no_e2e:
+        wl.e2e_setup()
+        for _ in range(2):
+            wl.e2e_step()
+        torch.cuda.synchronize()
+        Ke = max(3, min(K, 10))
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(Ke):
+            wl.e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ems = max_over_ranks(e0.elapsed_time(e1))
+        e2e = {"value": round(wl.flops_per_step * world * Ke / (ems * 1e-3) / 1e12, 3),
+               "unit": "TFLOP/s", "h2d_bytes_per_step": int(wl.h2d), "d2h_bytes_per_step": int(wl.d2h),
+               "steps": Ke, "path": "pinned host -> cudaMemcpyAsync -> C ABI -> cudaMemcpyAsync -> host"}
+
+    # ---------------- CPU baseline (rank 0, N == 1) ----------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            v, desc, threads = cpu_reference_sample(args.workload)
+            cpu = {"value": round(v, 6), "unit": "TFLOP/s", "cores": threads, "kind": "reference",
+                   "sample": desc}
+        except Exception as ex:  # the GPU number stands without it
+            cpu = {"value": None, "unit": "TFLOP/s", "cores": None, "kind": "reference",
+                   "sample": f"unavailable: {ex}"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(tflops_total, 3), "unit": "TFLOP/s",
+            "n_gpus": world, "steps": K, "warmup": args.warmup,
+            "ms_per_step": round(ms_total / K, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16" if args.workload != "attn_fp32" else "f32",
+            "data": "synthetic (seeded; config shapes and distributions)",
+            "config": describe(args.workload, world, wl.config.get("l2")),
+            "pct_of_dense_bf16_peak_2250": round(100 * tflops_total / world / 2250.0, 2),
+            "roofline": {"bound": "tensor", "kernel": wl.dominant, "achieved": round(achieved, 2),
+                         "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                         "peak_kind": f"{peak_kind} cuBLAS bf16 burst",
+                         "traffic": traffic,
+                         "traffic_unit": "DRAM bytes per launch (ncu, profiles/)"},
+            "clocks": clocks,
+            "e2e": e2e,
+            "gpu_launches": K * wl.launches_per_step,
+            "cpu_baseline": cpu,
+        }
+        if gather:
+            line["gather"] = gather
+        print(json.dumps(line), flush=True)
+
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -71,11 +71,11 @@ int jules_device_error(uint32_t* word, int clear);
 /*
  * C = act(A . W + bias) (+ residual)
  *   A [M,K], W [K,N], C and residual [M,N], bias [N] (fp32, nullable),
- *   residual nullable (same dtype as C).
- *   in_dtype: dtype of A and W; out_dtype: dtype of C.
- * bf16 in / bf16 out with N % 8 == 0, K % 8 == 0 and 16-byte aligned
- * pointers runs on tcgen05 tensor cores (fp32 accumulate); everything else
- * on CUDA cores in fp32.
+ *   residual nullable (same dtype as A and W).
+ *   in_dtype: dtype of A, W and residual; out_dtype: dtype of C.
+ * bf16 in (bf16 or fp32 out) with N % 8 == 0, K % 8 == 0 and 16-byte
+ * aligned pointers runs on tcgen05 tensor cores (fp32 accumulate, fp32
+ * epilogue, one cast at the store); everything else on CUDA cores in fp32.
  * Replaces tiledMatmulWithActivation (FusedKernels.h:378-458),
  * fusedMatmulRelu (:203-259), fusedMatmulBiasRelu (:265-372) and
  * blasMatmul with alpha=1, beta=0, no transposes (:633-644).
@@ -131,15 +131,17 @@ int jules_gelu(const void* in, void* out, int64_t n, int dtype, void* stream);
  *   out = GELU(LN(X) . W1 + b1) . W2 + b2 + X
  *   X, out [T,d]; W1 [d,dff]; W2 [dff,d]; gamma, beta, b2 [d] and b1 [dff]
  *   fp32.  LN statistics, bias, GELU and residual in fp32; LN(X) and the
- *   hidden activation are stored as bf16 (matmul operands).
+ *   hidden activation are stored as bf16 (matmul operands).  out_dtype
+ *   BF16 or F32 (the cast back to the caller's type happens once, at the
+ *   final store).
  * workspace: device buffer of at least jules_mlp_block_workspace_bytes().
  * Generalises fusedMLPForward (FusedKernels.h:650-760).
  */
 size_t jules_mlp_block_workspace_bytes(int64_t T, int64_t d, int64_t dff);
 int jules_mlp_block(const void* X, const float* gamma, const float* beta, const void* W1,
-                    const float* b1, const void* W2, const float* b2, void* out, int64_t T,
-                    int64_t d, int64_t dff, float eps, void* workspace, size_t workspace_bytes,
-                    void* stream);
+                    const float* b1, const void* W2, const float* b2, void* out, int out_dtype,
+                    int64_t T, int64_t d, int64_t dff, float eps, void* workspace,
+                    size_t workspace_bytes, void* stream);
 
 /*
  * Kernel registry keyed by the jules.extern_kernel names that

@@ -45,8 +45,8 @@ _SIGNATURES = {
                          _c_vp, _c_vp], _c_int),
     "jules_gelu": ([_c_vp, _c_vp, _c_i64, _c_int, _c_vp], _c_int),
     "jules_mlp_block_workspace_bytes": ([_c_i64, _c_i64, _c_i64], ctypes.c_size_t),
-    "jules_mlp_block": ([_c_vp] * 8 + [_c_i64, _c_i64, _c_i64, _c_f, _c_vp, ctypes.c_size_t,
-                                       _c_vp], _c_int),
+    "jules_mlp_block": ([_c_vp] * 8 + [_c_int, _c_i64, _c_i64, _c_i64, _c_f, _c_vp,
+                                       ctypes.c_size_t, _c_vp], _c_int),
     "jules_kernel_by_name": ([ctypes.c_char_p], _c_int),
     "jules_kernel_name": ([_c_int], ctypes.c_char_p),
     "jules_kernel_count": ([], _c_int),
@@ -201,18 +201,21 @@ def mlp_block_workspace_bytes(T, d, dff) -> int:
     return int(lib().jules_mlp_block_workspace_bytes(T, d, dff))
 
 
-def mlp_block(X, gamma, beta, W1, b1, W2, b2, eps=1e-5, out=None, workspace=None, stream=None):
-    """out = GELU(LN(X) @ W1 + b1) @ W2 + b2 + X  (bf16)."""
+def mlp_block(X, gamma, beta, W1, b1, W2, b2, eps=1e-5, out=None, workspace=None, stream=None,
+              out_dtype=None):
+    """out = GELU(LN(X) @ W1 + b1) @ W2 + b2 + X  (bf16 operands; bf16 or
+    fp32 output)."""
     import torch
     T, d = X.shape
     dff = W1.shape[1]
     if out is None:
-        out = torch.empty_like(X)
+        out = torch.empty((T, d), dtype=out_dtype or X.dtype, device=X.device)
     need = mlp_block_workspace_bytes(T, d, dff)
     if workspace is None:
         workspace = torch.empty(need, dtype=torch.uint8, device=X.device)
     rc = lib().jules_mlp_block(_ptr(X), _ptr(gamma), _ptr(beta), _ptr(W1), _ptr(b1), _ptr(W2),
-                               _ptr(b2), _ptr(out), T, d, dff, float(eps), _ptr(workspace),
+                               _ptr(b2), _ptr(out), _dtype_code(out), T, d, dff, float(eps),
+                               _ptr(workspace),
                                workspace.numel() * workspace.element_size(), _stream(stream))
     _check(rc, "jules_mlp_block")
     return out

@@ -46,6 +46,7 @@ constexpr int kMaxDevices = 64;
 struct DeviceInfo {
   int sms = 0;
   bool gemm_attr = false;
+  bool gemm_attr_f32 = false;
   bool attn_attr = false;
 };
 DeviceInfo g_dev[kMaxDevices];
@@ -117,8 +118,9 @@ int check_launch(const char* what) {
 constexpr int kGemmBN = 256;
 constexpr int kGemmStages = 4;
 
+template <typename TOut>
 int gemm_tc(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
-            const __nv_bfloat16* res, __nv_bfloat16* C, int64_t M, int64_t N, int64_t K, int act,
+            const __nv_bfloat16* res, TOut* C, int64_t M, int64_t N, int64_t K, int act,
             cudaStream_t st) {
   int dev;
   if (int rc = current_device(&dev)) return rc;
@@ -135,13 +137,14 @@ int gemm_tc(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
     const uint32_t box[2] = {64, 64};
     if (int rc = make_tmap_bf16(&tw, W, 2, dims, strides, box)) return rc;
   }
-  auto kern = jb::gemm::gemm_bf16_tc_kernel<kGemmBN, kGemmStages>;
+  auto kern = jb::gemm::gemm_bf16_tc_kernel<kGemmBN, kGemmStages, TOut>;
   const size_t smem = sizeof(jb::gemm::Smem<kGemmBN, kGemmStages>) + 1024;
-  if (!g_dev[dev].gemm_attr) {
+  bool& attr_set = std::is_same<TOut, float>::value ? g_dev[dev].gemm_attr_f32 : g_dev[dev].gemm_attr;
+  if (!attr_set) {
     std::lock_guard<std::mutex> lk(g_dev_mu);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm)");
-    g_dev[dev].gemm_attr = true;
+    attr_set = true;
   }
   const int64_t tiles = ((M + 127) / 128) * ((N + kGemmBN - 1) / kGemmBN);
   const int grid = (int)(tiles < device_sms(dev) ? tiles : device_sms(dev));
@@ -157,7 +160,7 @@ int gemm_simt(const void* A, const void* W, const float* bias, const void* res, 
   if (grid.y > 65535u) return fail(JULES_ERR_SHAPE, "M=%lld too large for the CUDA-core GEMM", (long long)M);
   jb::simt::gemm_kernel<TIn, TOut><<<grid, 256, 0, st>>>(
       static_cast<const TIn*>(A), static_cast<const TIn*>(W), bias,
-      static_cast<const TOut*>(res), static_cast<TOut*>(C), (int)M, (int)N, (int)K, act, exact);
+      static_cast<const TIn*>(res), static_cast<TOut*>(C), (int)M, (int)N, (int)K, act, exact);
   return check_launch("gemm_kernel launch");
 }
 
@@ -282,11 +285,14 @@ int jules_gemm_bias_act(const void* A, const void* W, const float* bias, const v
   const bool in_bf = in_dtype == JULES_DTYPE_BF16, out_bf = out_dtype == JULES_DTYPE_BF16;
   if ((in_dtype != JULES_DTYPE_F32 && !in_bf) || (out_dtype != JULES_DTYPE_F32 && !out_bf))
     return fail(JULES_ERR_DTYPE, "gemm: dtypes %d/%d", in_dtype, out_dtype);
-  if (in_bf && out_bf && N % 8 == 0 && K % 8 == 0 && aligned16(A) && aligned16(W) &&
-      aligned16(C) && (!bias || aligned16(bias)) && (!residual || aligned16(residual)))
-    return gemm_tc(static_cast<const __nv_bfloat16*>(A), static_cast<const __nv_bfloat16*>(W), bias,
-                   static_cast<const __nv_bfloat16*>(residual), static_cast<__nv_bfloat16*>(C), M, N,
-                   K, act, st);
+  if (in_bf && N % 8 == 0 && K % 8 == 0 && aligned16(A) && aligned16(W) && aligned16(C) &&
+      (!bias || aligned16(bias)) && (!residual || aligned16(residual))) {
+    const auto* a = static_cast<const __nv_bfloat16*>(A);
+    const auto* w = static_cast<const __nv_bfloat16*>(W);
+    const auto* r = static_cast<const __nv_bfloat16*>(residual);
+    if (out_bf) return gemm_tc(a, w, bias, r, static_cast<__nv_bfloat16*>(C), M, N, K, act, st);
+    return gemm_tc(a, w, bias, r, static_cast<float*>(C), M, N, K, act, st);
+  }
   if (in_bf && out_bf) return gemm_simt<__nv_bfloat16, __nv_bfloat16>(A, W, bias, residual, C, M, N, K, act, 0, st);
   if (in_bf) return gemm_simt<__nv_bfloat16, float>(A, W, bias, residual, C, M, N, K, act, 1, st);
   if (out_bf) return gemm_simt<float, __nv_bfloat16>(A, W, bias, residual, C, M, N, K, act, 0, st);
@@ -391,10 +397,12 @@ size_t jules_mlp_block_workspace_bytes(int64_t T, int64_t d, int64_t dff) {
 }
 
 int jules_mlp_block(const void* X, const float* gamma, const float* beta, const void* W1,
-                    const float* b1, const void* W2, const float* b2, void* out, int64_t T,
-                    int64_t d, int64_t dff, float eps, void* workspace, size_t workspace_bytes,
-                    void* stream) {
+                    const float* b1, const void* W2, const float* b2, void* out, int out_dtype,
+                    int64_t T, int64_t d, int64_t dff, float eps, void* workspace,
+                    size_t workspace_bytes, void* stream) {
   if (!X || !gamma || !beta || !W1 || !W2 || !out) return fail(JULES_ERR_ARG, "mlp_block: NULL pointer");
+  if (out_dtype != JULES_DTYPE_BF16 && out_dtype != JULES_DTYPE_F32)
+    return fail(JULES_ERR_DTYPE, "mlp_block: out dtype %d", out_dtype);
   if (T < 0 || d <= 0 || dff <= 0) return fail(JULES_ERR_SHAPE, "mlp_block: T=%lld d=%lld dff=%lld", (long long)T, (long long)d, (long long)dff);
   if (T == 0) return ok();
   const size_t need = jules_mlp_block_workspace_bytes(T, d, dff);
@@ -411,7 +419,7 @@ int jules_mlp_block(const void* X, const float* gamma, const float* beta, const 
                                    JULES_DTYPE_BF16, JULES_DTYPE_BF16, stream))
     return rc;
   return jules_gemm_bias_act(hid, W2, b2, X, out, T, d, dff, JULES_ACT_NONE, JULES_DTYPE_BF16,
-                             JULES_DTYPE_BF16, stream);
+                             out_dtype, stream);
 }
 
 }  // extern "C"

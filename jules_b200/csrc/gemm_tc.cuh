@@ -62,11 +62,28 @@ struct Smem {
   int abort_flag;
 };
 
-template <int BN, int STAGES>
+// Stores 8 consecutive fp32 results as bf16 (one 16-byte store) or as fp32
+// (two 16-byte stores).
+__device__ __forceinline__ void store8(__nv_bfloat16* dst, const float (&v)[8]) {
+  uint4 o;
+  o.x = pack_bf16x2(v[0], v[1]);
+  o.y = pack_bf16x2(v[2], v[3]);
+  o.z = pack_bf16x2(v[4], v[5]);
+  o.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(dst) = o;
+}
+__device__ __forceinline__ void store8(float* dst, const float (&v)[8]) {
+  reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// TOut: __nv_bfloat16 (one RNE cast at the store) or float.  The residual
+// has the operands' dtype (bf16).
+template <int BN, int STAGES, typename TOut>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmW, const float* __restrict__ bias,
-                        const __nv_bfloat16* __restrict__ residual, __nv_bfloat16* __restrict__ C,
+                        const __nv_bfloat16* __restrict__ residual, TOut* __restrict__ C,
                         int M, int N, int K, int act) {
   static_assert(BN % 64 == 0 && BN <= 256, "BN must be a multiple of 64, at most 256");
   using S = Smem<BN, STAGES>;
@@ -178,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_wait(r);
         const int col0 = n0 + c * 32;
         if (row < M && col0 < N) {
-          __nv_bfloat16* crow = C + (size_t)row * N;
+          TOut* crow = C + (size_t)row * N;
           const __nv_bfloat16* rrow = residual ? residual + (size_t)row * N : nullptr;
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
@@ -205,12 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   v[2 * j + 1] += f.y;
                 }
               }
-              uint4 o;
-              o.x = pack_bf16x2(v[0], v[1]);
-              o.y = pack_bf16x2(v[2], v[3]);
-              o.z = pack_bf16x2(v[4], v[5]);
-              o.w = pack_bf16x2(v[6], v[7]);
-              *reinterpret_cast<uint4*>(crow + col) = o;
+              store8(crow + col, v);
             }
           }
         }

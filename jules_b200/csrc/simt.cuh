@@ -50,7 +50,7 @@ constexpr int GBM = 128, GBN = 128, GBK = 8;
 template <typename TIn, typename TOut>
 __global__ void __launch_bounds__(256)
     gemm_kernel(const TIn* __restrict__ A, const TIn* __restrict__ W,
-                const float* __restrict__ bias, const TOut* __restrict__ residual,
+                const float* __restrict__ bias, const TIn* __restrict__ residual,
                 TOut* __restrict__ C, int M, int N, int K, int act, int exact) {
   __shared__ float As[GBK][GBM + 4];
   __shared__ float Ws[GBK][GBN + 4];

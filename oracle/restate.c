@@ -315,10 +315,11 @@ void orc_flash_attention(float* out, float* lse, const float* Q,
 /* lib/Passes/MixedPrecisionPass.cpp: matmul operands cast to bf16      */
 /* (:350-459), fp32 accumulation, reductions (LayerNorm stats) in fp32  */
 /* (:288-340), activation and elementwise ops after a matmul stay fp32  */
-/* (:490, :632); the result is cast back to bf16 once at the end.       */
+/* (:490, :632).  The GPU casts the result to bf16 once at the end; the  */
+/* oracle returns the fp32 result it is compared against.               */
 /*   Xn  = bf16(LayerNorm(X))                  FusedKernels.h:532-600    */
 /*   Hd  = bf16(GELU(Xn.W1 + b1))              :378-458, :606-627        */
-/*   out = bf16(Hd.W2 + b2 + X)                residual: extension       */
+/*   out = Hd.W2 + b2 + X   (fp32)             residual: extension       */
 /* X holds bf16 values (as float).  rows selects which token rows are    */
 /* computed (NULL = all T); out is [n_rows, d].                          */
 /* ------------------------------------------------------------------ */
@@ -340,7 +341,6 @@ void orc_mlp_block(float* out, const float* X, const float* gamma,
   orc_gemm_bias_act(xn, W1, b1, NULL, hd, n_rows, dff, d, ORC_ACT_GELU);
   orc_round_bf16(hd, n_rows * dff);
   orc_gemm_bias_act(hd, W2, b2, xs, out, n_rows, d, dff, ORC_ACT_NONE);
-  orc_round_bf16(out, n_rows * d);
   free(xs);
   free(xn);
   free(hd);

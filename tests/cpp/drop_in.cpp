@@ -1,0 +1,68 @@
+// A caller written against the reference's jules::kernel API
+// (benchmarks/bench_kernel.cpp style), compiled against this repository's
+// headers and linked to libjules_b200.so.  Reads inputs from <dir>/in_*.bin,
+// writes results to <dir>/out_*.bin.
+#include <cstdio>
+#include <cstdlib>
+#include <string>
+#include <vector>
+
+#include "jules/Kernel/ExecutionArena.h"
+#include "jules/Kernel/FlashAttention.h"
+#include "jules/Kernel/FusedKernels.h"
+#include "jules/Kernel/TilePlanner.h"
+
+using namespace jules::kernel;
+
+static std::vector<float> load(const std::string& p, size_t n) {
+  std::vector<float> v(n);
+  FILE* f = std::fopen(p.c_str(), "rb");
+  if (!f || std::fread(v.data(), 4, n, f) != n) { std::fprintf(stderr, "read %s\n", p.c_str()); std::exit(2); }
+  std::fclose(f);
+  return v;
+}
+static void save(const std::string& p, const std::vector<float>& v) {
+  FILE* f = std::fopen(p.c_str(), "wb");
+  std::fwrite(v.data(), 4, v.size(), f);
+  std::fclose(f);
+}
+
+int main(int argc, char** argv) {
+  const std::string d = argc > 1 ? argv[1] : ".";
+  // attention [1,8,512,64]
+  const int B = 1, H = 8, S = 512, D = 64, n = B * H * S * D;
+  auto Q = load(d + "/in_q.bin", n), K = load(d + "/in_k.bin", n), V = load(d + "/in_v.bin", n);
+  std::vector<float> O(n);
+  ExecutionArena arena(64UL << 20);
+  TilePlanner planner;
+  flashAttention(O.data(), Q.data(), K.data(), V.data(), B, H, S, D, arena, planner);
+  save(d + "/out_flash.bin", O);
+  attention(O.data(), Q.data(), K.data(), V.data(), B, H, S, D, arena, planner);
+  save(d + "/out_attention.bin", O);
+  // tiled matmul + GELU [96,200]x[200,136]
+  const int M = 96, Kd = 200, N = 136;
+  auto A = load(d + "/in_a.bin", M * Kd), W = load(d + "/in_w.bin", Kd * N);
+  auto bias = load(d + "/in_bias.bin", N);
+  std::vector<float> C(M * N);
+  TileConfig cfg = planner.getTileConfig(M, N, Kd);
+  tiledMatmulWithActivation(A.data(), W.data(), C.data(), M, N, Kd, cfg, ActivationType::Gelu);
+  save(d + "/out_tiled_gelu.bin", C);
+  fusedMatmulBiasRelu(A.data(), W.data(), bias.data(), C.data(), M, Kd, N);
+  save(d + "/out_bias_relu.bin", C);
+  blasMatmul(A.data(), W.data(), C.data(), M, N, Kd);
+  save(d + "/out_blas.bin", C);
+  // layernorm [96,200] and gelu
+  std::vector<float> g(Kd, 1.0f), be(Kd, 0.0f), L(M * Kd);
+  fusedLayerNorm(L.data(), A.data(), g.data(), be.data(), M, Kd);
+  save(d + "/out_layernorm.bin", L);
+  fusedGelu(L.data(), A.data(), M * Kd);
+  save(d + "/out_gelu.bin", L);
+  // MLP forward [96,200] -> 136 -> 24
+  auto W2 = load(d + "/in_w2.bin", N * 24), b2 = load(d + "/in_b2.bin", 24);
+  MLPParams p{W.data(), bias.data(), W2.data(), b2.data(), M, Kd, N, 24};
+  std::vector<float> out(M * 24);
+  fusedMLPForward(out.data(), A.data(), p, arena, planner);
+  save(d + "/out_mlp.bin", out);
+  std::printf("drop-in ok\n");
+  return 0;
+}

@@ -1,0 +1,49 @@
+"""The reference's C++ API as a drop-in: a program written against
+jules::kernel (tests/cpp/drop_in.cpp) compiles against include/ and links
+libjules_b200.so; its results match the reference's own kernels."""
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+from conftest import F32_REL_L2, ROOT, rel_l2
+
+def _compile(tmp, jb):
+    exe = os.path.join(tmp, "drop_in")
+    libdir = os.path.dirname(jb.LIB_PATH)
+    cmd = ["g++", "-O2", "-std=c++17", "-I", os.path.join(ROOT, "include"),
+           os.path.join(ROOT, "tests", "cpp", "drop_in.cpp"), "-o", exe, "-L", libdir,
+           "-ljules_b200", f"-Wl,-rpath,{libdir}"]
+    subprocess.run(cmd, check=True)
+    return exe
+
+
+def test_compiles_without_gpu(tmp_path, jb):
+    _compile(str(tmp_path), jb)
+
+
+@pytest.mark.gpu
+def test_drop_in_matches_reference(tmp_path, jb, ref):
+    d = str(tmp_path)
+    exe = _compile(d, jb)
+    g = np.random.default_rng(42)
+    Q, K, V = (g.standard_normal((1, 8, 512, 64), dtype=np.float32) for _ in range(3))
+    A = g.uniform(-1, 1, (96, 200)).astype(np.float32)
+    W = g.uniform(-1, 1, (200, 136)).astype(np.float32)
+    bias = g.uniform(-1, 1, 136).astype(np.float32)
+    W2 = g.uniform(-1, 1, (136, 24)).astype(np.float32)
+    b2 = g.uniform(-1, 1, 24).astype(np.float32)
+    for name, arr in dict(q=Q, k=K, v=V, a=A, w=W, bias=bias, w2=W2, b2=b2).items():
+        arr.tofile(os.path.join(d, f"in_{name}.bin"))
+    subprocess.run([exe, d], check=True)
+    out = lambda n, shape: np.fromfile(os.path.join(d, f"out_{n}.bin"), np.float32).reshape(shape)
+    assert rel_l2(out("flash", Q.shape), ref.flash_attention(Q, K, V)) <= F32_REL_L2
+    assert rel_l2(out("attention", Q.shape), ref.attention(Q, K, V)) <= F32_REL_L2
+    assert rel_l2(out("tiled_gelu", (96, 136)), ref.tiled_matmul_act(A, W, "gelu")) <= F32_REL_L2
+    assert rel_l2(out("bias_relu", (96, 136)), ref.fused_matmul_bias_relu(A, W, bias)) <= F32_REL_L2
+    assert rel_l2(out("blas", (96, 136)), ref.blas_matmul(A, W)) <= F32_REL_L2
+    ln = ref.layernorm(A, np.ones(200, np.float32), np.zeros(200, np.float32))
+    assert rel_l2(out("layernorm", (96, 200)), ln) <= F32_REL_L2
+    assert rel_l2(out("gelu", (96, 200)), ref.gelu(A)) <= F32_REL_L2
+    assert rel_l2(out("mlp", (96, 24)), ref.mlp_forward(A, W, bias, W2, b2)) <= F32_REL_L2

@@ -42,6 +42,23 @@ def test_gemm_tc_activations(jb, orc, act):
     assert rel_l2(got, want) <= BF16_REL_L2
 
 
+@pytest.mark.parametrize("act", ["none", "gelu"])
+def test_gemm_tc_fp32_output(jb, orc, act):
+    """bf16 operands, fp32 result (the cast back to an fp32 caller's type)."""
+    import torch
+    A, W, b = gemm_inputs(320, 640, 448, seed=13)
+    R = bf16_np(np.random.default_rng(14).standard_normal((320, 640)).astype(np.float32))
+    got = jb.gemm_bias_act(to_dev(A), to_dev(W), torch.from_numpy(b).cuda(), to_dev(R), act=act,
+                           out_dtype=torch.float32)
+    got16 = jb.gemm_bias_act(to_dev(A), to_dev(W), torch.from_numpy(b).cuda(), to_dev(R), act=act)
+    torch.cuda.synchronize()
+    assert got.dtype == torch.float32
+    want = orc.gemm_bias_act(A, W, b, R, act)
+    assert max_abs(to_np(got), want) <= 2e-3
+    assert rel_l2(to_np(got), want) <= 1e-3
+    assert torch.equal(got16, got.to(torch.bfloat16))
+
+
 def test_gemm_tc_no_bias_residual(jb, orc):
     A, W, _ = gemm_inputs(384, 768, 512, seed=3, bias=False)
     R = bf16_np(np.random.default_rng(4).standard_normal((384, 768)).astype(np.float32))
