@@ -46,7 +46,7 @@ FALLBACK_HBM_GBS = 6650.0
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["jules", "reference"], default="jules")
     p.add_argument("--workload", choices=["gemm", "attn", "attn_gqa", "mlp", "attn_fp32"],
@@ -126,7 +126,7 @@ class ClockSampler:
         "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
     }
 
-    def __init__(self, device_index, interval=0.005):
+    def __init__(self, device_index, interval=0.001):
         self.ok = False
         self.samples = []
         self.reasons = set()

@@ -130,10 +130,12 @@ def gemm_bias_act(A, W, bias=None, residual=None, act="none", out=None, out_dtyp
         out = torch.empty((M, N), dtype=out_dtype or A.dtype, device=A.device)
     if bias is not None:
         _dense(bias, "bias")
-        assert bias.dtype == torch.float32 and bias.numel() == N
+        if bias.dtype != torch.float32 or bias.numel() != N:
+            raise ValueError("bias must be fp32 with N elements")
     if residual is not None:
         _dense(residual, "residual")
-        assert residual.dtype == out.dtype and residual.shape == out.shape
+        if residual.dtype != A.dtype or residual.shape != out.shape:
+            raise ValueError("residual must have A's dtype and C's shape")
     rc = lib().jules_gemm_bias_act(_ptr(A), _ptr(W), _ptr(bias), _ptr(residual), _ptr(out), M, N,
                                    K, ACT[act] if isinstance(act, str) else int(act),
                                    _dtype_code(A), _dtype_code(out), _stream(stream))
