@@ -10,20 +10,27 @@
 // skipped while the running max grows by less than 2^8 (the final division
 // uses the same stale max for O and the sum, so the result is unchanged).
 //
-// CTA = one 128-row query tile at a time (persistent over (tile, b, h) work
-// items, longest causal tiles first), 6 warps:
-//   warp 0     TMA producer: Q tile once per item; K and V tiles (128 keys x
-//              128 dims, two 64-dim 128B-swizzled boxes each) in 2-deep rings.
-//   warp 1     TMEM owner and MMA issuer: S_j = Q K_j^T into one of two TMEM
-//              S buffers, then O += P_{j-1} V_{j-1}; the S MMA of tile j+1 is
-//              issued before the PV MMA of tile j so the tensor core works
-//              while the softmax warps process S_j.
-//   warps 2-5  softmax, one query row per thread (TMEM lane = row): reads
-//              S_j, masks, row max, exp2, row sum, writes P_j as bf16 into a
-//              128B-swizzled smem tile (the K-major A operand of PV),
-//              rescales O in TMEM when needed, and finally normalises O and
-//              writes O and lse.
-// TMEM columns: S0 [0,128), S1 [128,256), O [256,384) (512 allocated).
+// Work item = two 128-row query tiles (256 rows) of one (b, h); persistent
+// CTAs take items longest-causal-first.  12 warps (3 warpgroups):
+//   warp 8     TMA producer: both Q tiles once per item; K and V tiles
+//              (128 keys x 128 dims as two 64-dim 128B-swizzled boxes) in
+//              2-deep rings shared by the two query tiles.
+//   warp 9     TMEM owner and MMA issuer.  Per key tile j the order is
+//              PV(0,j-1), S(0,j), PV(1,j-1), S(1,j): while softmax group 0
+//              works on S(0,j) the tensor core runs S(1,j) and PV(1,j-1), and
+//              the other way round (ping-pong).  Warps 10-11 only hold the
+//              warpgroup's registers low.
+//   warps 0-3  softmax group 0 (query tile 0), one row per thread (TMEM lane
+//   warps 4-7  = row); group 1 (query tile 1).  Each reads S from TMEM, masks,
+//              takes the row max and the exponentials (3/4 on the MUFU ex2
+//              unit, 1/4 as a polynomial on the FMA pipe), writes P as bf16
+//              back over S in TMEM, rescales O when needed, and at the end
+//              normalises O and writes O and lse.
+// PV runs with P as the TMEM A operand (no shared-memory round trip).
+// TMEM columns: S/P tile 0 [0,128), S/P tile 1 [128,256), O tile 0 [256,384),
+// O tile 1 [384,512).  S(t,j+1) reuses the columns of P(t,j): the tensor core
+// executes one thread's MMAs in issue order, and the softmax only writes P(t,j+1)
+// after the commit of S(t,j+1), which follows PV(t,j).
 #pragma once
 
 #include "sm100.cuh"
@@ -33,33 +40,97 @@ namespace attn {
 
 constexpr int HD = 128;   // head dim handled here
 constexpr int BQ = 128;   // query rows per tile (MMA M)
+constexpr int NQT = 2;    // query tiles per work item
 constexpr int BKV = 128;  // keys per tile (MMA N of S, K of PV)
 constexpr int KVS = 2;    // K and V ring depth
-constexpr int kThreads = 192;
+constexpr int kThreads = 384;  // 3 warpgroups
+// Register split (setmaxnreg): launched at 168 per thread (65536 / 384, in
+// steps of 8); the producer/MMA warpgroup drops to kRegsCtl and the two
+// softmax warpgroups rise to kRegsSoftmax.  Per SM sub-partition (one warp of
+// each warpgroup): 2*200 + 104 = 504 <= 512; per block 8*32*200 + 4*32*104 =
+// 64512 = 384*168.  (Both regions compile without spills at this split.)
+constexpr int kRegsLaunch = 168;
+constexpr int kRegsSoftmax = 200;
+constexpr int kRegsCtl = 104;
+static_assert(2 * kRegsSoftmax + kRegsCtl <= 512, "sub-partition register file");
+static_assert(8 * kRegsSoftmax + 4 * kRegsCtl <= 12 * kRegsLaunch, "block register budget");
+constexpr int kWarpProducer = 8;
+constexpr int kWarpMma = 9;
 constexpr int kChunk = 128 * 64 * 2;  // one 64-dim (128 B) swizzled box of 128 rows
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 struct Smem {
-  alignas(1024) uint8_t q[2][kChunk];
+  alignas(1024) uint8_t q[NQT][2][kChunk];
   alignas(1024) uint8_t k[KVS][2][kChunk];
   alignas(1024) uint8_t v[KVS][2][kChunk];
-  alignas(1024) uint8_t p[2][kChunk];
   uint64_t q_full, q_empty;
   uint64_t k_full[KVS], k_empty[KVS];
   uint64_t v_full[KVS], v_empty[KVS];
-  uint64_t s_full[2], s_empty[2];
-  uint64_t p_full, p_empty;
-  uint64_t o_full, o_empty;
+  uint64_t s_full[NQT], p_full[NQT], o_full[NQT], o_empty[NQT];
   uint32_t tmem_base;
   int abort_flag;
 };
 
-// Work item w -> (q tile, b*Hq + h); longest causal tiles first.
-__device__ __forceinline__ void decode_item(int w, int n_qt, int BH, int causal, int& qt,
+// Work item w -> (query-tile pair, b*Hq + h); longest causal pairs first.
+__device__ __forceinline__ void decode_item(int w, int n_pairs, int BH, int causal, int& pair,
                                             int& bh) {
   const int r = w / BH;
   bh = w % BH;
-  qt = causal ? (n_qt - 1 - r) : r;
+  pair = causal ? (n_pairs - 1 - r) : r;
+}
+
+__device__ __forceinline__ int kv_tiles(int pair, int n_kv_full, int causal) {
+  if (!causal) return n_kv_full;
+  const int n = 2 * pair + 2;
+  return n < n_kv_full ? n : n_kv_full;
+}
+
+// Packed fp32 pairs (sm_100 f32x2 instructions: one issue slot, two lanes).
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void upk2(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair, on the FMA pipe.  Inputs are clamped to >= -125, so keys
+// that the mask removed get 2^-125 (~2e-38) instead of 0 on this path.
+// Cody-Waite split x = n + f, n = rint(x) via the 1.5*2^23 shifter, 2^f from a
+// degree-3 polynomial fitted on [-0.5, 0.5] (max relative error 7.5e-5; see
+// fit_exp2.py), 2^n added into the exponent field.
+__device__ __forceinline__ void exp2_fma_pair(uint64_t x2, float& e0, float& e1) {
+  float x0, x1;
+  upk2(x2, x0, x1);
+  x2 = pk2(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
+  const uint64_t t2 = add2(x2, pk2(12582912.0f, 12582912.0f));
+  const uint64_t n2 = add2(t2, pk2(-12582912.0f, -12582912.0f));
+  const uint64_t f2 = fma2(n2, pk2(-1.0f, -1.0f), x2);
+  uint64_t p2 = fma2(pk2(0.05517137795686722f, 0.05517137795686722f), f2,
+                     pk2(0.24261121451854706f, 0.24261121451854706f));
+  p2 = fma2(p2, f2, pk2(0.6932610273361206f, 0.6932610273361206f));
+  p2 = fma2(p2, f2, pk2(0.9999280571937561f, 0.9999280571937561f));
+  float p0, p1, t0, t1;
+  upk2(p2, p0, p1);
+  upk2(t2, t0, t1);
+  e0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  e1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
 #define JB_W128(r)                                                                     \
@@ -92,9 +163,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int BH = B * Hq;
-  const int n_qt = (S + BQ - 1) / BQ;
+  const int n_pairs = (S + NQT * BQ - 1) / (NQT * BQ);
   const int n_kv_full = (S + BKV - 1) / BKV;
-  const int total = n_qt * BH;
+  const int total = n_pairs * BH;
   const int group = Hq / Hkv;
 
   if (threadIdx.x == 0) {
@@ -106,21 +177,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.v_full[i], 1);
       mbar_init(&s.v_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s.s_full[i], 1);
-      mbar_init(&s.s_empty[i], 128);
+    for (int t = 0; t < NQT; ++t) {
+      mbar_init(&s.s_full[t], 1);
+      mbar_init(&s.p_full[t], 128);
+      mbar_init(&s.o_full[t], 1);
+      mbar_init(&s.o_empty[t], 128);
     }
-    mbar_init(&s.p_full, 128);
-    mbar_init(&s.p_empty, 1);
-    mbar_init(&s.o_full, 1);
-    mbar_init(&s.o_empty, 128);
     s.abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmQ);
     prefetch_tmap(&tmK);
     prefetch_tmap(&tmV);
   }
-  if (warp == 1) {
+  if (warp == kWarpMma) {
     tmem_alloc(&s.tmem_base, 512);
     tmem_relinquish();
   }
@@ -130,21 +199,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tbase = s.tmem_base;
   volatile int* abort_flag = &s.abort_flag;
 
-  if (warp == 0) {
+  if (warp >= 8) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsCtl));
+  if (warp == kWarpProducer) {
     // ------------------------------ producer ------------------------------
     if (lane == 0) {
       uint32_t kvi = 0, wi = 0;
       bool ok = true;
       for (int w = blockIdx.x; w < total && ok; w += gridDim.x, ++wi) {
-        int qt, bh;
-        decode_item(w, n_qt, BH, causal, qt, bh);
+        int pair, bh;
+        decode_item(w, n_pairs, BH, causal, pair, bh);
         const int b = bh / Hq, h = bh % Hq;
         const int zkv = b * Hkv + h / group;
-        const int n_kv = causal ? (qt + 1 < n_kv_full ? qt + 1 : n_kv_full) : n_kv_full;
+        const int n_kv = kv_tiles(pair, n_kv_full, causal);
+        const int q0 = pair * NQT * BQ;
         if (!mbar_wait(&s.q_empty, (wi & 1u) ^ 1u, 10, abort_flag)) break;
-        mbar_arrive_expect_tx(&s.q_full, 2 * kChunk);
-        tma_load_3d(s.q[0], &tmQ, &s.q_full, 0, qt * BQ, bh);
-        tma_load_3d(s.q[1], &tmQ, &s.q_full, 64, qt * BQ, bh);
+        mbar_arrive_expect_tx(&s.q_full, NQT * 2 * kChunk);
+#pragma unroll
+        for (int t = 0; t < NQT; ++t) {
+          tma_load_3d(s.q[t][0], &tmQ, &s.q_full, 0, q0 + t * BQ, bh);
+          tma_load_3d(s.q[t][1], &tmQ, &s.q_full, 64, q0 + t * BQ, bh);
+        }
         for (int j = 0; j < n_kv; ++j, ++kvi) {
           const uint32_t st = kvi % KVS, ph = (kvi / KVS) & 1u;
           if (!mbar_wait(&s.k_empty[st], ph ^ 1u, 11, abort_flag)) { ok = false; break; }
@@ -158,134 +233,167 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == kWarpMma) {
     // ------------------------------ MMA issuer ------------------------------
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16_f32(BQ, BKV, false, false);
       constexpr uint32_t idPV = idesc_bf16_f32(BQ, HD, false, true);
-      const uint32_t tO = tbase + 256;
-      uint32_t kvi = 0, sc = 0, pc = 0, wi = 0;
+      uint32_t kvi = 0, pvc = 0, wi = 0;
       bool ok = true;
-      const uint32_t q0a = smem_u32(s.q[0]), q1a = smem_u32(s.q[1]);
-      const uint32_t p0a = smem_u32(s.p[0]), p1a = smem_u32(s.p[1]);
-      for (int w = blockIdx.x; w < total && ok; w += gridDim.x, ++wi) {
-        int qt, bh;
-        decode_item(w, n_qt, BH, causal, qt, bh);
-        const int n_kv = causal ? (qt + 1 < n_kv_full ? qt + 1 : n_kv_full) : n_kv_full;
-        if (!mbar_wait(&s.q_full, wi & 1u, 20, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t kv0 = kvi;
-        auto issue_pv = [&](int jj) -> bool {
-          const uint32_t st = (kv0 + jj) % KVS, ph = ((kv0 + jj) / KVS) & 1u;
-          if (!mbar_wait(&s.p_full, pc & 1u, 21, abort_flag)) return false;
-          if (jj == 0 && !mbar_wait(&s.o_empty, (wi & 1u) ^ 1u, 22, abort_flag)) return false;
-          if (!mbar_wait(&s.v_full[st], ph, 23, abort_flag)) return false;
-          tc_fence_after();
-          const uint32_t va = smem_u32(s.v[st][0]);
+      auto issue_s = [&](int t, uint32_t st) {
+        const uint32_t qa0 = smem_u32(s.q[t][0]), qa1 = smem_u32(s.q[t][1]);
+        const uint32_t ka0 = smem_u32(s.k[st][0]), ka1 = smem_u32(s.k[st][1]);
 #pragma unroll
-          for (int kk = 0; kk < BKV / 16; ++kk) {
-            const uint64_t ad = sdesc_sw128((kk < 4 ? p0a : p1a) + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = sdesc_sw128(va + kk * 2048, kChunk, 1024);
-            umma_f16_ss(tO, ad, bd, idPV, (jj > 0 || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(&s.v_empty[st]);
-          umma_commit(&s.p_empty);
-          ++pc;
-          return true;
-        };
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint64_t ad = sdesc_sw128((kk < 4 ? qa0 : qa1) + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128((kk < 4 ? ka0 : ka1) + (kk & 3) * 32, 16, 1024);
+          umma_f16_ss(tbase + t * BKV, ad, bd, idS, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s.s_full[t]);
+      };
+      auto issue_pv = [&](int t, uint32_t st, bool accumulate) {
+        const uint32_t va = smem_u32(s.v[st][0]);
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk) {
+          const uint64_t bd = sdesc_sw128(va + kk * 2048, kChunk, 1024);
+          umma_f16_ts(tbase + 256 + t * HD, tbase + t * BKV + kk * 8, bd, idPV,
+                      (accumulate || kk > 0) ? 1u : 0u);
+        }
+      };
+      for (int w = blockIdx.x; w < total && ok; w += gridDim.x, ++wi) {
+        int pair, bh;
+        decode_item(w, n_pairs, BH, causal, pair, bh);
+        const int n_kv = kv_tiles(pair, n_kv_full, causal);
+        if (!mbar_wait(&s.q_full, wi & 1u, 20, abort_flag)) break;
+        const uint32_t kv0 = kvi;
+        {
+          const uint32_t st = kv0 % KVS, ph = (kv0 / KVS) & 1u;
+          if (!mbar_wait(&s.k_full[st], ph, 21, abort_flag)) break;
+          tc_fence_after();
+          issue_s(0, st);
+          issue_s(1, st);
+          umma_commit(&s.k_empty[st]);
+          if (n_kv == 1) umma_commit(&s.q_empty);
+        }
         for (int j = 0; j < n_kv && ok; ++j) {
           const uint32_t st = (kv0 + j) % KVS, ph = ((kv0 + j) / KVS) & 1u;
-          const uint32_t sb = sc & 1u, sph = (sc >> 1) & 1u;
-          if (!mbar_wait(&s.k_full[st], ph, 24, abort_flag)) { ok = false; break; }
-          if (!mbar_wait(&s.s_empty[sb], sph ^ 1u, 25, abort_flag)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t k0a = smem_u32(s.k[st][0]), k1a = smem_u32(s.k[st][1]);
+          const uint32_t g = pvc + j;
+          const bool more = j + 1 < n_kv;
+          const uint32_t st1 = (kv0 + j + 1) % KVS, ph1 = ((kv0 + j + 1) / KVS) & 1u;
 #pragma unroll
-          for (int kk = 0; kk < HD / 16; ++kk) {
-            const uint64_t ad = sdesc_sw128((kk < 4 ? q0a : q1a) + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = sdesc_sw128((kk < 4 ? k0a : k1a) + (kk & 3) * 32, 16, 1024);
-            umma_f16_ss(tbase + sb * BKV, ad, bd, idS, kk > 0 ? 1u : 0u);
+          for (int t = 0; t < NQT; ++t) {
+            if (!mbar_wait(&s.p_full[t], g & 1u, 22, abort_flag)) { ok = false; break; }
+            if (j == 0 && !mbar_wait(&s.o_empty[t], (wi & 1u) ^ 1u, 23, abort_flag)) { ok = false; break; }
+            if (t == 0 && !mbar_wait(&s.v_full[st], ph, 24, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            issue_pv(t, st, j > 0);
+            if (t == NQT - 1) umma_commit(&s.v_empty[st]);
+            if (!more) umma_commit(&s.o_full[t]);
+            if (more) {
+              if (t == 0) {
+                if (!mbar_wait(&s.k_full[st1], ph1, 25, abort_flag)) { ok = false; break; }
+                tc_fence_after();
+              }
+              issue_s(t, st1);
+              if (t == NQT - 1) {
+                umma_commit(&s.k_empty[st1]);
+                if (j + 1 == n_kv - 1) umma_commit(&s.q_empty);
+              }
+            }
           }
-          umma_commit(&s.k_empty[st]);
-          umma_commit(&s.s_full[sb]);
-          ++sc;
-          if (j == n_kv - 1) umma_commit(&s.q_empty);
-          if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
         }
         if (!ok) break;
-        if (!issue_pv(n_kv - 1)) break;
-        umma_commit(&s.o_full);
+        pvc += n_kv;
         kvi = kv0 + n_kv;
       }
     }
+  }
   } else {
-    // ------------------------------ softmax ------------------------------
-    const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;  // row within the query tile
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
+    // ------------------------------ softmax groups ------------------------------
+    const int t = warp >> 2;          // query tile of this group (warpgroup 0 or 1)
+    const int quarter = warp & 3;     // TMEM lane quarter this warp may access
+    const int r = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const uint32_t tO = tbase + 256 + lane_off;
-    uint32_t sc = 0, pw = 0, wi = 0;
-    // swizzled row base inside a P chunk
-    const uint32_t prow = (uint32_t)r * 128u;
-    const uint32_t pswz = (uint32_t)(r & 7);
+    const uint32_t tS = tbase + t * BKV + lane_off;
+    const uint32_t tO = tbase + 256 + t * HD + lane_off;
+    uint32_t pvc = 0, wi = 0;
     for (int w = blockIdx.x; w < total; w += gridDim.x, ++wi) {
-      int qt, bh;
-      decode_item(w, n_qt, BH, causal, qt, bh);
-      const int n_kv = causal ? (qt + 1 < n_kv_full ? qt + 1 : n_kv_full) : n_kv_full;
-      const int q = qt * BQ + r;
+      int pair, bh;
+      decode_item(w, n_pairs, BH, causal, pair, bh);
+      const int n_kv = kv_tiles(pair, n_kv_full, causal);
+      const int qt0 = pair * NQT * BQ + t * BQ;  // first row of this tile
+      const int q = qt0 + r;
       float m_run = -INFINITY, l_run = 0.0f;
       bool ok = true;
       for (int j = 0; j < n_kv; ++j) {
-        const uint32_t sb = sc & 1u, sph = (sc >> 1) & 1u;
-        if (!mbar_wait(&s.s_full[sb], sph, 30, abort_flag)) { ok = false; break; }
+        const uint32_t g = pvc + j;
+        if (!mbar_wait(&s.s_full[t], g & 1u, 30, abort_flag)) { ok = false; break; }
         tc_fence_after();
         uint32_t sr[128];
-        const uint32_t ts = tbase + lane_off + sb * BKV;
-        tmem_ld32_at(ts + 0, sr + 0);
-        tmem_ld32_at(ts + 32, sr + 32);
-        tmem_ld32_at(ts + 64, sr + 64);
-        tmem_ld32_at(ts + 96, sr + 96);
+        tmem_ld32_at(tS + 0, sr + 0);
+        tmem_ld32_at(tS + 32, sr + 32);
+        tmem_ld32_at(tS + 64, sr + 64);
+        tmem_ld32_at(tS + 96, sr + 96);
         tmem_ld_wait128(sr);
-        tc_fence_before();
-        mbar_arrive(&s.s_empty[sb]);
-        ++sc;
-
-        float x[128];
-#pragma unroll
-        for (int c = 0; c < 128; ++c) x[c] = __uint_as_float(sr[c]) * scale_log2;
-        if (j == n_kv - 1) {  // only the last tile can hold masked keys
-          const int kbase = j * BKV;
-          int lim = S - kbase;                         // keys >= S are padding
-          if (causal && q - kbase + 1 < lim) lim = q - kbase + 1;  // keys > q
+        const int kbase = j * BKV;
+        if (kbase + BKV > S || (causal && kbase + BKV - 1 > qt0)) {
+          int lim = S - kbase;                                      // keys >= S are padding
+          if (causal && q - kbase + 1 < lim) lim = q - kbase + 1;   // keys > q
 #pragma unroll
           for (int c = 0; c < 128; ++c)
-            if (c >= lim) x[c] = -INFINITY;
+            if (c >= lim) sr[c] = __float_as_uint(-INFINITY);
         }
-        float mt = x[0];
+        // Row max of the raw scores (scale > 0 commutes with max).
+        float mx[4];
 #pragma unroll
-        for (int c = 1; c < 128; ++c) mt = fmaxf(mt, x[c]);
+        for (int i = 0; i < 4; ++i) mx[i] = __uint_as_float(sr[i]);
+#pragma unroll
+        for (int c = 4; c < 128; c += 8) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            mx[i] = max3(mx[i], __uint_as_float(sr[c + 2 * i]), __uint_as_float(sr[c + 2 * i + 1]));
+        }
+        const float mt = max3(mx[0], mx[1], fmaxf(mx[2], mx[3])) * scale_log2;
         // Lazy rescale: keep the old max unless the new one exceeds it by
         // more than the threshold.
         const bool need = mt > m_run + kRescaleThreshold;
         const float m_new = need ? mt : m_run;
         const float alpha = need ? ex2_approx(m_run - m_new) : 1.0f;
         const float neg_m = (m_new == -INFINITY) ? 0.0f : -m_new;
-        float rowsum = 0.0f;
-        uint32_t pk[64];
+        const uint64_t scale2 = pk2(scale_log2, scale_log2);
+        const uint64_t negm2 = pk2(neg_m, neg_m);
+        uint64_t sum2[2] = {pk2(0.0f, 0.0f), pk2(0.0f, 0.0f)};
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const float e0 = ex2_approx(x[2 * c] + neg_m);
-          const float e1 = ex2_approx(x[2 * c + 1] + neg_m);
-          rowsum += e0 + e1;
-          pk[c] = pack_bf16x2(e0, e1);
+        for (int half = 0; half < 2; ++half) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const int e = half * 64 + 2 * c;
+            // x = s * scale*log2(e) - m, two lanes per instruction
+            const uint64_t x2 =
+                fma2(pk2(__uint_as_float(sr[e]), __uint_as_float(sr[e + 1])), scale2, negm2);
+            float e0, e1;
+            if ((c & 3) == 3) {
+              exp2_fma_pair(x2, e0, e1);
+            } else {
+              float x0, x1;
+              upk2(x2, x0, x1);
+              e0 = ex2_approx(x0);
+              e1 = ex2_approx(x1);
+            }
+            sum2[c & 1] = add2(sum2[c & 1], pk2(e0, e1));
+            pk[c] = pack_bf16x2(e0, e1);
+          }
+          // P (bf16 pairs) over the first 64 columns of this tile's S.
+          tmem_st32(tS + half * 32, pk);
         }
-        l_run = l_run * alpha + rowsum;
-        m_run = m_new;
-
-        // P buffer is free once the previous PV MMA has completed.
-        if (pw > 0 && !mbar_wait(&s.p_empty, (pw - 1) & 1u, 31, abort_flag)) { ok = false; break; }
-        tc_fence_after();
+        float sa, sb, sc2, sd;
+        upk2(sum2[0], sa, sb);
+        upk2(sum2[1], sc2, sd);
+        const float rowsum = (sa + sb) + (sc2 + sd);
         if (j > 0 && __any_sync(0xffffffffu, need)) {
+          // PV(t, j-1) has completed: its commit precedes S(t, j)'s.
 #pragma unroll 1
           for (int c = 0; c < HD; c += 32) {
             uint32_t o[32];
@@ -295,30 +403,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
             tmem_st32(tO + c, o);
           }
-          tmem_st_wait();
         }
-        // P row -> two 128B-swizzled chunks (keys 0-63, 64-127).
-#pragma unroll
-        for (int ch = 0; ch < 2; ++ch) {
-          uint8_t* base = s.p[ch] + prow;
-#pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            uint4 v;
-            v.x = pk[ch * 32 + g * 4 + 0];
-            v.y = pk[ch * 32 + g * 4 + 1];
-            v.z = pk[ch * 32 + g * 4 + 2];
-            v.w = pk[ch * 32 + g * 4 + 3];
-            *reinterpret_cast<uint4*>(base + (((uint32_t)g ^ pswz) << 4)) = v;
-          }
-        }
-        fence_proxy_async_smem();
+        tmem_st_wait();
+        l_run = l_run * alpha + rowsum;
+        m_run = m_new;
         tc_fence_before();
-        mbar_arrive(&s.p_full);
-        ++pw;
+        mbar_arrive(&s.p_full[t]);
       }
       if (!ok) break;
       // ----- epilogue: O / l -> bf16, lse -----
-      if (!mbar_wait(&s.o_full, wi & 1u, 32, abort_flag)) break;
+      if (!mbar_wait(&s.o_full[t], wi & 1u, 32, abort_flag)) break;
       tc_fence_after();
       const float inv_l = 1.0f / l_run;
       const bool row_ok = q < S;
@@ -331,19 +425,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (row_ok) {
           uint4* dst = reinterpret_cast<uint4*>(orow + c);
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
+          for (int g8 = 0; g8 < 4; ++g8) {
             uint4 v;
-            v.x = pack_bf16x2(__uint_as_float(o[8 * g + 0]) * inv_l, __uint_as_float(o[8 * g + 1]) * inv_l);
-            v.y = pack_bf16x2(__uint_as_float(o[8 * g + 2]) * inv_l, __uint_as_float(o[8 * g + 3]) * inv_l);
-            v.z = pack_bf16x2(__uint_as_float(o[8 * g + 4]) * inv_l, __uint_as_float(o[8 * g + 5]) * inv_l);
-            v.w = pack_bf16x2(__uint_as_float(o[8 * g + 6]) * inv_l, __uint_as_float(o[8 * g + 7]) * inv_l);
-            dst[g] = v;
+            v.x = pack_bf16x2(__uint_as_float(o[8 * g8 + 0]) * inv_l, __uint_as_float(o[8 * g8 + 1]) * inv_l);
+            v.y = pack_bf16x2(__uint_as_float(o[8 * g8 + 2]) * inv_l, __uint_as_float(o[8 * g8 + 3]) * inv_l);
+            v.z = pack_bf16x2(__uint_as_float(o[8 * g8 + 4]) * inv_l, __uint_as_float(o[8 * g8 + 5]) * inv_l);
+            v.w = pack_bf16x2(__uint_as_float(o[8 * g8 + 6]) * inv_l, __uint_as_float(o[8 * g8 + 7]) * inv_l);
+            dst[g8] = v;
           }
         }
       }
       if (lse && row_ok) lse[(size_t)bh * S + q] = (m_run + log2f(l_run)) * 0.69314718055994531f;
       tc_fence_before();
-      mbar_arrive(&s.o_empty);
+      mbar_arrive(&s.o_empty[t]);
+      pvc += n_kv;
     }
   }
 
@@ -351,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tbase, 512);
+  if (warp == kWarpMma) tmem_dealloc(tbase, 512);
 }
 
 }  // namespace attn

@@ -220,8 +220,9 @@ int attn_tc(const void* Q, const void* K, const void* V, void* O, float* lse, in
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn_tc)");
     g_dev[dev].attn_attr = true;
   }
-  const int q_tiles = (S + jb::attn::BQ - 1) / jb::attn::BQ;
-  const int64_t work = (int64_t)q_tiles * B * Hq;
+  constexpr int kRowsPerItem = jb::attn::NQT * jb::attn::BQ;
+  const int n_pairs = (S + kRowsPerItem - 1) / kRowsPerItem;
+  const int64_t work = (int64_t)n_pairs * B * Hq;
   const int grid = (int)(work < device_sms(dev) ? work : device_sms(dev));
   const float scale_log2 = scale * 1.4426950408889634f;
   kern<<<grid, jb::attn::kThreads, smem, st>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(O), lse, B,
