@@ -240,25 +240,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idPV = idesc_bf16_f32(BQ, HD, false, true);
       uint32_t kvi = 0, pvc = 0, wi = 0;
       bool ok = true;
+      // Descriptors for every operand slot, built once.  A K step moves the
+      // start-address field (bytes >> 4): +2 per 32 bytes inside a 128-byte
+      // swizzle row (K-major), +128 per 16 rows of 128 bytes (MN-major V).
+      // Q/K: two 64-dim chunks kChunk bytes apart, so chunk 1 = chunk 0 +
+      // kChunk >> 4 in the same field.
+      const uint64_t dq0 = sdesc_sw128(smem_u32(s.q[0][0]), 16, 1024);
+      const uint64_t dk0 = sdesc_sw128(smem_u32(s.k[0][0]), 16, 1024);
+      const uint64_t dv0 = sdesc_sw128(smem_u32(s.v[0][0]), kChunk, 1024);
+      constexpr uint64_t kChunkStep = kChunk >> 4;           // next 64-dim chunk
+      constexpr uint64_t kStageStep = (2 * kChunk) >> 4;     // next Q tile / ring slot
       auto issue_s = [&](int t, uint32_t st) {
-        const uint32_t qa0 = smem_u32(s.q[t][0]), qa1 = smem_u32(s.q[t][1]);
-        const uint32_t ka0 = smem_u32(s.k[st][0]), ka1 = smem_u32(s.k[st][1]);
+        uint64_t a[8], b[8];
+        const uint64_t qa = dq0 + t * kStageStep, kb = dk0 + st * kStageStep;
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint64_t ad = sdesc_sw128((kk < 4 ? qa0 : qa1) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128((kk < 4 ? ka0 : ka1) + (kk & 3) * 32, 16, 1024);
-          umma_f16_ss(tbase + t * BKV, ad, bd, idS, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk) {
+          a[kk] = qa + (kk >> 2) * kChunkStep + (kk & 3) * 2;
+          b[kk] = kb + (kk >> 2) * kChunkStep + (kk & 3) * 2;
         }
+        umma8_ss(tbase + t * BKV, a, b, 0u, idS);
         umma_commit(&s.s_full[t]);
       };
       auto issue_pv = [&](int t, uint32_t st, bool accumulate) {
-        const uint32_t va = smem_u32(s.v[st][0]);
+        uint32_t pa[8];
+        uint64_t b[8];
+        const uint64_t vb = dv0 + st * kStageStep;
 #pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk) {
-          const uint64_t bd = sdesc_sw128(va + kk * 2048, kChunk, 1024);
-          umma_f16_ts(tbase + 256 + t * HD, tbase + t * BKV + kk * 8, bd, idPV,
-                      (accumulate || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk) {
+          pa[kk] = tbase + t * BKV + kk * 8;
+          b[kk] = vb + kk * 128;
         }
+        umma8_ts(tbase + 256 + t * HD, pa, b, accumulate ? 1u : 0u, idPV);
       };
       for (int w = blockIdx.x; w < total && ok; w += gridDim.x, ++wi) {
         int pair, bh;
@@ -345,14 +357,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (c >= lim) sr[c] = __float_as_uint(-INFINITY);
         }
         // Row max of the raw scores (scale > 0 commutes with max).
+        // Four independent chains; chain k takes columns 8m + 2k and 8m + 2k + 1
+        // (m = 0..15).
         float mx[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) mx[i] = __uint_as_float(sr[i]);
+        for (int k = 0; k < 4; ++k)
+          mx[k] = fmaxf(__uint_as_float(sr[2 * k]), __uint_as_float(sr[2 * k + 1]));
 #pragma unroll
-        for (int c = 4; c < 128; c += 8) {
+        for (int m = 1; m < 16; ++m) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            mx[i] = max3(mx[i], __uint_as_float(sr[c + 2 * i]), __uint_as_float(sr[c + 2 * i + 1]));
+          for (int k = 0; k < 4; ++k)
+            mx[k] = max3(mx[k], __uint_as_float(sr[8 * m + 2 * k]),
+                         __uint_as_float(sr[8 * m + 2 * k + 1]));
         }
         const float mt = max3(mx[0], mx[1], fmaxf(mx[2], mx[3])) * scale_log2;
         // Lazy rescale: keep the old max unless the new one exceeds it by

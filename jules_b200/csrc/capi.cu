@@ -47,6 +47,8 @@ struct DeviceInfo {
   int sms = 0;
   bool gemm_attr = false;
   bool gemm_attr_f32 = false;
+  int gemm2_pairs = 0;      // resident CTA pairs of the pair GEMM (bf16 out)
+  int gemm2_pairs_f32 = 0;  // same, fp32 out
   bool attn_attr = false;
 };
 DeviceInfo g_dev[kMaxDevices];
@@ -150,6 +152,60 @@ int gemm_tc(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
   const int grid = (int)(tiles < device_sms(dev) ? tiles : device_sms(dev));
   kern<<<grid, jb::gemm::kThreads, smem, st>>>(ta, tw, bias, res, C, (int)M, (int)N, (int)K, act);
   return check_launch("gemm_bf16_tc_kernel launch");
+}
+
+constexpr int kGemm2Stages = 6;
+
+// CTA-pair tcgen05 GEMM (256 x 256 tiles, cluster of 2).
+template <typename TOut>
+int gemm_tc2(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
+             const __nv_bfloat16* res, TOut* C, int64_t M, int64_t N, int64_t K, int act,
+             cudaStream_t st) {
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  CUtensorMap ta, tw;
+  {
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)K * 2};
+    const uint32_t box[2] = {64, 128};
+    if (int rc = make_tmap_bf16(&ta, A, 2, dims, strides, box)) return rc;
+  }
+  {
+    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
+    const uint64_t strides[1] = {(uint64_t)N * 2};
+    const uint32_t box[2] = {64, 64};
+    if (int rc = make_tmap_bf16(&tw, W, 2, dims, strides, box)) return rc;
+  }
+  auto kern = jb::gemm::gemm_bf16_tc2_kernel<kGemm2Stages, TOut>;
+  const size_t smem = sizeof(jb::gemm::Smem2<kGemm2Stages>) + 1024;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(jb::gemm::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int& max_pairs = std::is_same<TOut, float>::value ? g_dev[dev].gemm2_pairs_f32 : g_dev[dev].gemm2_pairs;
+  if (max_pairs == 0) {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm2)");
+    cfg.gridDim = dim3(2 * (device_sms(dev) / 2));
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+    if (e != cudaSuccess || clusters <= 0) clusters = device_sms(dev) / 2;
+    max_pairs = clusters;
+  }
+  const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  const int pairs = (int)(tiles < max_pairs ? tiles : max_pairs);
+  cfg.gridDim = dim3(2 * pairs);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tw, bias, res, C, (int)M, (int)N, (int)K, act);
+  if (e != cudaSuccess) return cuda_fail(e, "gemm_bf16_tc2_kernel launch");
+  return check_launch("gemm_bf16_tc2_kernel launch");
 }
 
 template <typename TIn, typename TOut>
@@ -291,8 +347,16 @@ int jules_gemm_bias_act(const void* A, const void* W, const float* bias, const v
     const auto* a = static_cast<const __nv_bfloat16*>(A);
     const auto* w = static_cast<const __nv_bfloat16*>(W);
     const auto* r = static_cast<const __nv_bfloat16*>(residual);
-    if (out_bf) return gemm_tc(a, w, bias, r, static_cast<__nv_bfloat16*>(C), M, N, K, act, st);
-    return gemm_tc(a, w, bias, r, static_cast<float*>(C), M, N, K, act, st);
+    // 256 x 256 pair tiles once both dimensions fill them; 128 x 256 tiles otherwise.
+    const bool pair = M >= 256 && N >= 256;
+    if (out_bf) {
+      auto* c = static_cast<__nv_bfloat16*>(C);
+      return pair ? gemm_tc2(a, w, bias, r, c, M, N, K, act, st)
+                  : gemm_tc(a, w, bias, r, c, M, N, K, act, st);
+    }
+    auto* c = static_cast<float*>(C);
+    return pair ? gemm_tc2(a, w, bias, r, c, M, N, K, act, st)
+                : gemm_tc(a, w, bias, r, c, M, N, K, act, st);
   }
   if (in_bf && out_bf) return gemm_simt<__nv_bfloat16, __nv_bfloat16>(A, W, bias, residual, C, M, N, K, act, 0, st);
   if (in_bf) return gemm_simt<__nv_bfloat16, float>(A, W, bias, residual, C, M, N, K, act, 1, st);

@@ -136,6 +136,46 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// ---------------------------------------------------------------------------
+// CTA pairs (cluster of 2) for cta_group::2 MMAs.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+// Address of the same shared-memory variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+// Arrive on an mbarrier given by its shared::cluster address (own or peer).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+// Tile load of one CTA of a pair; the transaction bytes complete on the
+// barrier at the same offset in the even (leader) CTA of the pair: address
+// bit 24 selects the CTA of the pair.
+constexpr uint32_t kPairLeaderMask = 0xFEFFFFFFu;
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                                 int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar) & kPairLeaderMask), "r"(x), "r"(y)
+      : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -187,6 +227,86 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Back-to-back K=16 steps from one thread.  A single asm block sets the
+// accumulate predicates once (first step: acc_first, then 1) so the issuing
+// thread spends no dependent arithmetic between MMAs; descriptors are passed
+// precomputed.
+#define JB_L8(a) "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7])
+#define JB_U8(a) "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(a[4]), "r"(a[5]), "r"(a[6]), "r"(a[7])
+#define JB_MMA_SS(ai, bi, pr) \
+  "tcgen05.mma.cta_group::1.kind::f16 [%0], %" #ai ", %" #bi ", %18, " pr ";\n\t"
+
+// D (+)= sum over 8 K-steps of A[smem] * B[smem].
+__device__ __forceinline__ void umma8_ss(uint32_t d_tmem, const uint64_t (&a)[8],
+                                         const uint64_t (&b)[8], uint32_t acc_first,
+                                         uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %17, 0;\n\t"
+      "setp.eq.b32 q, %17, %17;\n\t"
+      JB_MMA_SS(1, 9, "p") JB_MMA_SS(2, 10, "q") JB_MMA_SS(3, 11, "q") JB_MMA_SS(4, 12, "q")
+      JB_MMA_SS(5, 13, "q") JB_MMA_SS(6, 14, "q") JB_MMA_SS(7, 15, "q") JB_MMA_SS(8, 16, "q")
+      "}" ::"r"(d_tmem), JB_L8(a), JB_L8(b), "r"(acc_first), "r"(idesc)
+      : "memory");
+}
+
+#define JB_MMA_TS(ai, bi, pr) \
+  "tcgen05.mma.cta_group::1.kind::f16 [%0], [%" #ai "], %" #bi ", %18, " pr ";\n\t"
+
+// D (+)= sum over 8 K-steps of A[tmem] * B[smem].
+__device__ __forceinline__ void umma8_ts(uint32_t d_tmem, const uint32_t (&a)[8],
+                                         const uint64_t (&b)[8], uint32_t acc_first,
+                                         uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %17, 0;\n\t"
+      "setp.eq.b32 q, %17, %17;\n\t"
+      JB_MMA_TS(1, 9, "p") JB_MMA_TS(2, 10, "q") JB_MMA_TS(3, 11, "q") JB_MMA_TS(4, 12, "q")
+      JB_MMA_TS(5, 13, "q") JB_MMA_TS(6, 14, "q") JB_MMA_TS(7, 15, "q") JB_MMA_TS(8, 16, "q")
+      "}" ::"r"(d_tmem), JB_U8(a), JB_L8(b), "r"(acc_first), "r"(idesc)
+      : "memory");
+}
+
+// Pair versions (issued by the leader CTA of a cluster of 2).
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+#define JB_MMA2_SS(ai, bi, pr) \
+  "tcgen05.mma.cta_group::2.kind::f16 [%0], %" #ai ", %" #bi ", %10, " pr ";\n\t"
+// Four K=16 steps of the pair MMA: D (+)= A[smem] * B[smem].
+__device__ __forceinline__ void umma4_pair_ss(uint32_t d_tmem, const uint64_t (&a)[4],
+                                              const uint64_t (&b)[4], uint32_t acc_first,
+                                              uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %9, 0;\n\t"
+      "setp.eq.b32 q, %9, %9;\n\t"
+      JB_MMA2_SS(1, 5, "p") JB_MMA2_SS(2, 6, "q") JB_MMA2_SS(3, 7, "q") JB_MMA2_SS(4, 8, "q")
+      "}" ::"r"(d_tmem), "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(b[0]), "l"(b[1]),
+      "l"(b[2]), "l"(b[3]), "r"(acc_first), "r"(idesc)
+      : "memory");
+}
+
+// Arrive on the barrier at a shared::cluster address (own CTA or its pair
+// peer) when the pair MMAs issued so far by this thread have completed.
+__device__ __forceinline__ void umma_commit_pair(uint32_t cluster_addr) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          cluster_addr)
       : "memory");
 }
 
