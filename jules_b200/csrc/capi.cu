@@ -8,6 +8,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 
 #include "../../include/jules_kernels.h"
@@ -47,8 +48,7 @@ struct DeviceInfo {
   int sms = 0;
   bool gemm_attr = false;
   bool gemm_attr_f32 = false;
-  int gemm2_pairs = 0;      // resident CTA pairs of the pair GEMM (bf16 out)
-  int gemm2_pairs_f32 = 0;  // same, fp32 out
+  int gemm2_pairs[2][2] = {{0, 0}, {0, 0}};  // resident CTA pairs, [fp32 out][TN == 256]
   bool attn_attr = false;
 };
 DeviceInfo g_dev[kMaxDevices];
@@ -154,13 +154,45 @@ int gemm_tc(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
   return check_launch("gemm_bf16_tc_kernel launch");
 }
 
-constexpr int kGemm2Stages = 6;
+// Scratch of the split tail: per (device, stream) so launches on different
+// streams never share it; grown on demand, counters zeroed once (the kernel
+// leaves them at zero).  Layout: a fixed counter area (kSplitMaxRegions x
+// u32, the same for every request so counters never move), then per region
+// two halves of 128 x tn fp32.
+constexpr int kSplitMaxRegions = 1024;  // regions = 2 x tail tiles <= resident pairs
+struct SplitScratch {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+std::map<std::pair<int, cudaStream_t>, SplitScratch> g_split_scratch;
+
+int split_scratch(int dev, cudaStream_t st, int regions, int tn, float** partial,
+                  unsigned** counters) {
+  if (regions > kSplitMaxRegions) return fail(JULES_ERR_SHAPE, "split tail: %d regions", regions);
+  const size_t cbytes = (size_t)kSplitMaxRegions * 4;
+  const size_t need = cbytes + (size_t)regions * 2 * 128 * tn * 4;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  SplitScratch& sc = g_split_scratch[{dev, st}];
+  if (sc.bytes < need) {
+    if (sc.ptr) cudaFree(sc.ptr);
+    sc.ptr = nullptr;
+    sc.bytes = 0;
+    cudaError_t e = cudaMalloc(&sc.ptr, need);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(split scratch)");
+    e = cudaMemset(sc.ptr, 0, need);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(split scratch)");
+    sc.bytes = need;
+  }
+  *counters = static_cast<unsigned*>(sc.ptr);
+  *partial = reinterpret_cast<float*>(static_cast<char*>(sc.ptr) + cbytes);
+  return JULES_OK;
+}
 
 // CTA-pair tcgen05 GEMM (256 x 256 tiles, cluster of 2).
-template <typename TOut>
+template <int TN, typename TOut>
 int gemm_tc2(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
              const __nv_bfloat16* res, TOut* C, int64_t M, int64_t N, int64_t K, int act,
-             cudaStream_t st) {
+             cudaStream_t st, bool allow_split) {
   int dev;
   if (int rc = current_device(&dev)) return rc;
   CUtensorMap ta, tw;
@@ -176,8 +208,9 @@ int gemm_tc2(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
     const uint32_t box[2] = {64, 64};
     if (int rc = make_tmap_bf16(&tw, W, 2, dims, strides, box)) return rc;
   }
-  auto kern = jb::gemm::gemm_bf16_tc2_kernel<kGemm2Stages, TOut>;
-  const size_t smem = sizeof(jb::gemm::Smem2<kGemm2Stages>) + 1024;
+  constexpr int kStages = TN == 256 ? 6 : 8;
+  auto kern = jb::gemm::gemm_bf16_tc2_kernel<kStages, TN, TOut>;
+  const size_t smem = sizeof(jb::gemm::Smem2<kStages, TN>) + 1024;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -189,7 +222,7 @@ int gemm_tc2(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  int& max_pairs = std::is_same<TOut, float>::value ? g_dev[dev].gemm2_pairs_f32 : g_dev[dev].gemm2_pairs;
+  int& max_pairs = g_dev[dev].gemm2_pairs[std::is_same<TOut, float>::value ? 1 : 0][TN == 256 ? 1 : 0];
   if (max_pairs == 0) {
     std::lock_guard<std::mutex> lk(g_dev_mu);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -200,12 +233,39 @@ int gemm_tc2(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
     if (e != cudaSuccess || clusters <= 0) clusters = device_sms(dev) / 2;
     max_pairs = clusters;
   }
-  const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
-  const int pairs = (int)(tiles < max_pairs ? tiles : max_pairs);
+  const int64_t tiles = ((M + 255) / 256) * ((N + TN - 1) / TN);
+  const int num_k = (int)((K + 63) / 64);
+  int whole = (int)tiles, units = (int)tiles;
+  float* partial = nullptr;
+  unsigned* counters = nullptr;
+  const int64_t tail = tiles % max_pairs;
+  // Split the tail tiles along K (see gemm_bf16_tc2_kernel) only when the
+  // last round would be nearly empty.  For larger tails the split measured
+  // slower (4096^3: 34 tail tiles on 74 pairs, 1118 vs 1190 TFLOP/s): the
+  // half-empty last round runs at higher clocks under the power cap.
+  if (allow_split && tiles > max_pairs && tail > 0 && 4 * tail <= max_pairs && num_k >= 2) {
+    whole = (int)(tiles - tail);
+    units = whole + 2 * (int)tail;
+    if (int rc = split_scratch(dev, st, 2 * (int)tail, TN, &partial, &counters)) return rc;
+  }
+  const int pairs = units < max_pairs ? units : max_pairs;
   cfg.gridDim = dim3(2 * pairs);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tw, bias, res, C, (int)M, (int)N, (int)K, act);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tw, bias, res, C, (int)M, (int)N, (int)K, act,
+                                     whole, units, partial, counters);
   if (e != cudaSuccess) return cuda_fail(e, "gemm_bf16_tc2_kernel launch");
   return check_launch("gemm_bf16_tc2_kernel launch");
+}
+
+// Tile choice for the tensor-core GEMM: 256 x 256 CTA-pair tiles once M and
+// N fill them, 128 x 256 single-CTA tiles below that.  (256 x 128 pair tiles
+// measured slower: their N=128 MMAs leave the tensor pipe idle between
+// instructions.)
+template <typename TOut>
+int gemm_tc_dispatch(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
+                     const __nv_bfloat16* res, TOut* C, int64_t M, int64_t N, int64_t K, int act,
+                     cudaStream_t st, bool allow_split = true) {
+  if (M < 256 || N < 256) return gemm_tc(A, W, bias, res, C, M, N, K, act, st);
+  return gemm_tc2<256>(A, W, bias, res, C, M, N, K, act, st, allow_split);
 }
 
 template <typename TIn, typename TOut>
@@ -347,16 +407,9 @@ int jules_gemm_bias_act(const void* A, const void* W, const float* bias, const v
     const auto* a = static_cast<const __nv_bfloat16*>(A);
     const auto* w = static_cast<const __nv_bfloat16*>(W);
     const auto* r = static_cast<const __nv_bfloat16*>(residual);
-    // 256 x 256 pair tiles once both dimensions fill them; 128 x 256 tiles otherwise.
-    const bool pair = M >= 256 && N >= 256;
-    if (out_bf) {
-      auto* c = static_cast<__nv_bfloat16*>(C);
-      return pair ? gemm_tc2(a, w, bias, r, c, M, N, K, act, st)
-                  : gemm_tc(a, w, bias, r, c, M, N, K, act, st);
-    }
-    auto* c = static_cast<float*>(C);
-    return pair ? gemm_tc2(a, w, bias, r, c, M, N, K, act, st)
-                : gemm_tc(a, w, bias, r, c, M, N, K, act, st);
+    if (out_bf)
+      return gemm_tc_dispatch(a, w, bias, r, static_cast<__nv_bfloat16*>(C), M, N, K, act, st);
+    return gemm_tc_dispatch(a, w, bias, r, static_cast<float*>(C), M, N, K, act, st);
   }
   if (in_bf && out_bf) return gemm_simt<__nv_bfloat16, __nv_bfloat16>(A, W, bias, residual, C, M, N, K, act, 0, st);
   if (in_bf) return gemm_simt<__nv_bfloat16, float>(A, W, bias, residual, C, M, N, K, act, 1, st);

@@ -254,11 +254,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 //                       mark the accumulator ready in both CTAs.
 //   warps 2-5 (both)    epilogue of the CTA's 128 rows; they release the
 //                       accumulator on the leader's barrier (256 arrivals).
+//
+// Tail split.  With T tiles on P resident pairs, the last round holds only
+// T mod P tiles.  When that is at most P/2, those tiles are split in two
+// halves along K ("units"), so the last round takes half as long.  Each half
+// writes its fp32 partial tile to the scratch buffer and bumps a per-tile
+// counter; the half that arrives second adds the other half's partial to its
+// own accumulator and runs the epilogue.  Nothing waits on another CTA.
 // ---------------------------------------------------------------------------
-template <int STAGES>
+template <int STAGES, int TN>
 struct Smem2 {
-  static constexpr int kABytes = 128 * BK * 2;  // this CTA's 128 rows of A
-  static constexpr int kBBytes = BK * 128 * 2;  // this CTA's 128 columns of W
+  static constexpr int kABytes = 128 * BK * 2;     // this CTA's 128 rows of A
+  static constexpr int kBBytes = BK * (TN / 2) * 2;  // this CTA's TN/2 columns of W
   alignas(1024) uint8_t a[STAGES][kABytes];
   alignas(1024) uint8_t b[STAGES][kBBytes];
   uint64_t full[STAGES];
@@ -267,16 +274,73 @@ struct Smem2 {
   uint64_t tempty[2];
   uint32_t tmem_base;
   int abort_flag;
+  int split_last;
 };
 
-template <int STAGES, typename TOut>
+// Work unit u of the tail-split schedule: whole tiles first, then the two
+// K-halves of each tail tile.
+struct PairUnit {
+  int tile, k0, k1, split, half;
+};
+__device__ __forceinline__ PairUnit pair_unit(int u, int whole_units, int num_k) {
+  PairUnit r;
+  if (u < whole_units) {
+    r.tile = u;
+    r.k0 = 0;
+    r.k1 = num_k;
+    r.split = 0;
+    r.half = 0;
+  } else {
+    const int v = u - whole_units;
+    r.tile = whole_units + (v >> 1);
+    r.half = v & 1;
+    r.k0 = r.half ? num_k / 2 : 0;
+    r.k1 = r.half ? num_k : num_k / 2;
+    r.split = 1;
+  }
+  return r;
+}
+
+// Named barrier over the four epilogue warps (128 threads).
+__device__ __forceinline__ void epilogue_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Epilogue math for 8 consecutive columns: bias, activation, residual, store.
+template <typename TOut>
+__device__ __forceinline__ void epilogue8(float (&v)[8], const float* bias,
+                                          const __nv_bfloat16* rrow, TOut* crow, int col,
+                                          int act) {
+  if (bias) {
+    const float4 b0 = *reinterpret_cast<const float4*>(bias + col);
+    const float4 b1 = *reinterpret_cast<const float4*>(bias + col + 4);
+    v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
+    v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = act_fast(v[j], act);
+  if (rrow) {
+    const uint4 rv = *reinterpret_cast<const uint4*>(rrow + col);
+    const __nv_bfloat162* rp = reinterpret_cast<const __nv_bfloat162*>(&rv);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(rp[j]);
+      v[2 * j] += f.x;
+      v[2 * j + 1] += f.y;
+    }
+  }
+  store8(crow + col, v);
+}
+
+template <int STAGES, int TN, typename TOut>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc2_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmW, const float* __restrict__ bias,
                          const __nv_bfloat16* __restrict__ residual, TOut* __restrict__ C, int M,
-                         int N, int K, int act) {
-  constexpr int TM = 256, TN = 256;
-  using S = Smem2<STAGES>;
+                         int N, int K, int act, int whole_units, int num_units,
+                         float* __restrict__ partial, unsigned* __restrict__ counters) {
+  static_assert(TN == 128 || TN == 256, "pair tile N is 128 or 256");
+  constexpr int TM = 256;
+  constexpr uint32_t kTmemCols = 2 * TN;  // two accumulators
+  using S = Smem2<STAGES, TN>;
   extern __shared__ uint8_t smem_raw[];
   S& s = *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -306,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tmW);
   }
   if (warp == 1) {
-    tmem_alloc_pair(&s.tmem_base, 512);
+    tmem_alloc_pair(&s.tmem_base, kTmemCols);
     tmem_relinquish_pair();
   }
   tc_fence_before();
@@ -321,15 +385,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = pair_id; t < num_tiles && ok; t += num_pairs) {
-        const int m0 = (t % num_m) * TM + (int)rank * 128;
-        const int n0 = (t / num_m) * TN + (int)rank * 128;
-        for (int kb = 0; kb < num_k; ++kb) {
+      for (int u = pair_id; u < num_units && ok; u += num_pairs) {
+        const PairUnit pu = pair_unit(u, whole_units, num_k);
+        const int m0 = (pu.tile % num_m) * TM + (int)rank * 128;
+        const int n0 = (pu.tile / num_m) * TN + (int)rank * (TN / 2);
+        for (int kb = pu.k0; kb < pu.k1; ++kb) {
           if (!mbar_wait(&s.empty[stage], phase ^ 1u, 41, abort_flag)) { ok = false; break; }
           if (leader) mbar_arrive_expect_tx(&s.full[stage], 2 * (S::kABytes + S::kBBytes));
           tma_load_2d_pair(s.a[stage], &tmA, &s.full[stage], kb * BK, m0);
-          tma_load_2d_pair(s.b[stage], &tmW, &s.full[stage], n0, kb * BK);
-          tma_load_2d_pair(s.b[stage] + BK * 64 * 2, &tmW, &s.full[stage], n0 + 64, kb * BK);
+#pragma unroll
+          for (int j = 0; j < TN / 128; ++j)
+            tma_load_2d_pair(s.b[stage] + j * (BK * 64 * 2), &tmW, &s.full[stage], n0 + j * 64, kb * BK);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
       }
@@ -347,11 +413,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = pair_id; t < num_tiles && ok; t += num_pairs) {
+      for (int u = pair_id; u < num_units && ok; u += num_pairs) {
+        const PairUnit pu = pair_unit(u, whole_units, num_k);
         if (!mbar_wait(&s.tempty[acc], acc_phase ^ 1u, 42, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * TN;
-        for (int kb = 0; kb < num_k; ++kb) {
+        for (int kb = pu.k0; kb < pu.k1; ++kb) {
           if (!mbar_wait(&s.full[stage], phase, 43, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint64_t a0 = sdesc_sw128(smem_u32(s.a[stage]), 16, 1024);
@@ -362,7 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ad[kk] = a0 + kk * 2;    // +32 bytes inside the swizzle row
             bd[kk] = b0 + kk * 128;  // +16 K rows of 128 bytes
           }
-          umma4_pair_ss(d_tmem, ad, bd, kb > 0 ? 1u : 0u, idesc);
+          umma4_pair_ss(d_tmem, ad, bd, kb > pu.k0 ? 1u : 0u, idesc);
           umma_commit_pair(empty0 + stage * 8);
           umma_commit_pair(empty0_peer + stage * 8);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -380,48 +447,74 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tempty0_leader = mapa_shared(smem_u32(&s.tempty[0]), 0);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = pair_id; t < num_tiles; t += num_pairs) {
-      const int m0 = (t % num_m) * TM + (int)rank * 128;
-      const int n0 = (t / num_m) * TN;
+    for (int u = pair_id; u < num_units; u += num_pairs) {
+      const PairUnit pu = pair_unit(u, whole_units, num_k);
+      const int m0 = (pu.tile % num_m) * TM + (int)rank * 128;
+      const int n0 = (pu.tile / num_m) * TN;
       if (!mbar_wait(&s.tfull[acc], acc_phase, 44, abort_flag)) break;
       tc_fence_after();
       const int row = m0 + row_in_tile;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * TN;
+      TOut* crow = C + (size_t)(row < M ? row : 0) * N;
+      const __nv_bfloat16* rrow = residual ? residual + (size_t)(row < M ? row : 0) * N : nullptr;
+      const float* other = nullptr;  // the other K-half's partial row (split units)
+      bool finish = true;
+      if (pu.split) {
+        // This CTA's slice of the tile, one region per (tail tile, rank),
+        // two halves per region, 128 rows x TN fp32 per half.
+        const int region = (pu.tile - whole_units) * 2 + (int)rank;
+        float* mine = partial + ((size_t)(region * 2 + pu.half) * 128 + row_in_tile) * TN;
 #pragma unroll 1
-      for (int c = 0; c < TN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(t_row + c * 32, r);
-        tmem_ld_wait(r);
-        const int col0 = n0 + c * 32;
-        if (row < M && col0 < N) {
-          TOut* crow = C + (size_t)row * N;
-          const __nv_bfloat16* rrow = residual ? residual + (size_t)row * N : nullptr;
+        for (int c = 0; c < TN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(t_row + c * 32, r);
+          tmem_ld_wait(r);
+          float4* dst = reinterpret_cast<float4*>(mine + c * 32);
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const int col = col0 + g * 8;
-            if (col < N) {
-              float v[8];
+          for (int q = 0; q < 8; ++q)
+            dst[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                 __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+        }
+        __threadfence();
+        epilogue_bar();
+        if (threadIdx.x == 64) {  // first epilogue thread
+          const unsigned prev = atomicAdd(&counters[region], 1u);
+          s.split_last = prev == 1u;
+          if (prev == 1u) counters[region] = 0u;  // ready for the next launch
+        }
+        epilogue_bar();
+        finish = s.split_last != 0;
+        __threadfence();
+        other = partial + ((size_t)(region * 2 + (pu.half ^ 1)) * 128 + row_in_tile) * TN;
+      }
+      if (finish) {
+#pragma unroll 1
+        for (int c = 0; c < TN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(t_row + c * 32, r);
+          tmem_ld_wait(r);
+          if (other) {
+            const float4* src = reinterpret_cast<const float4*>(other + c * 32);
 #pragma unroll
-              for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[g * 8 + j]);
-              if (bias) {
-                const float4 b0 = *reinterpret_cast<const float4*>(bias + col);
-                const float4 b1 = *reinterpret_cast<const float4*>(bias + col + 4);
-                v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
-                v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
+            for (int q = 0; q < 8; ++q) {
+              const float4 o = __ldcg(src + q);
+              r[4 * q] = __float_as_uint(__uint_as_float(r[4 * q]) + o.x);
+              r[4 * q + 1] = __float_as_uint(__uint_as_float(r[4 * q + 1]) + o.y);
+              r[4 * q + 2] = __float_as_uint(__uint_as_float(r[4 * q + 2]) + o.z);
+              r[4 * q + 3] = __float_as_uint(__uint_as_float(r[4 * q + 3]) + o.w);
+            }
+          }
+          const int col0 = n0 + c * 32;
+          if (row < M && col0 < N) {
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              const int col = col0 + g * 8;
+              if (col < N) {
+                float v[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[g * 8 + j]);
+                epilogue8(v, bias, rrow, crow, col, act);
               }
-#pragma unroll
-              for (int j = 0; j < 8; ++j) v[j] = act_fast(v[j], act);
-              if (rrow) {
-                const uint4 rv = *reinterpret_cast<const uint4*>(rrow + col);
-                const __nv_bfloat162* rp = reinterpret_cast<const __nv_bfloat162*>(&rv);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  const float2 f = __bfloat1622float2(rp[j]);
-                  v[2 * j] += f.x;
-                  v[2 * j + 1] += f.y;
-                }
-              }
-              store8(crow + col, v);
             }
           }
         }
@@ -436,7 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   cluster_sync();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc_pair(tmem_base, 512);
+  if (warp == 1) tmem_dealloc_pair(tmem_base, kTmemCols);
 }
 
 }  // namespace gemm

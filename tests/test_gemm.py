@@ -59,6 +59,28 @@ def test_gemm_tc_fp32_output(jb, orc, act):
     assert torch.equal(got16, got.to(torch.bfloat16))
 
 
+@pytest.mark.parametrize("M,N,K", [(2560, 2048, 520), (2560, 2048, 136), (4096, 4096, 1024)])
+@pytest.mark.parametrize("out", ["bf16", "f32"])
+def test_gemm_tc_split_tail(jb, orc, M, N, K, out):
+    """Shapes whose last round of 256x256 tiles is split in two along K
+    (80 tiles on 74 CTA pairs; 256 tiles); odd and even k-block counts."""
+    import torch
+    A, W, b = gemm_inputs(M, N, K, seed=M + K)
+    R = bf16_np(np.random.default_rng(K).standard_normal((M, N)).astype(np.float32))
+    od = torch.float32 if out == "f32" else torch.bfloat16
+    for _ in range(2):  # second call reuses the scratch counters
+        got = jb.gemm_bias_act(to_dev(A), to_dev(W), torch.from_numpy(b).cuda(), to_dev(R),
+                               act="gelu", out_dtype=od)
+    torch.cuda.synchronize()
+    assert jb.device_error() == 0
+    rows = np.concatenate([np.arange(0, M, 97), [M - 1]])
+    want = orc.gemm_bias_act(np.ascontiguousarray(A[rows]), W, b, np.ascontiguousarray(R[rows]),
+                             "gelu")
+    g = to_np(got[torch.from_numpy(rows).cuda()])
+    assert max_abs(g, want) <= BF16_MAX_ABS
+    assert rel_l2(g, want) <= BF16_REL_L2
+
+
 def test_gemm_tc_no_bias_residual(jb, orc):
     A, W, _ = gemm_inputs(384, 768, 512, seed=3, bias=False)
     R = bf16_np(np.random.default_rng(4).standard_normal((384, 768)).astype(np.float32))
