@@ -144,6 +144,27 @@ int jules_mlp_block(const void* X, const float* gamma, const float* beta, const 
                     size_t workspace_bytes, void* stream);
 
 /*
+ * The MLP block of jules_mlp_block without any allocation: no counterpart in
+ * the reference.  For callers that cannot allocate device memory, such as a
+ * runtime's custom-call handler (the jules.extern_kernel ->
+ * stablehlo.custom_call route), which receives only its operand and result
+ * buffers while the device memory belongs to the runtime's allocator.
+ * The workspace is an array compiled into the library, of
+ * jules_mlp_block_noalloc_max_workspace_bytes() (32 MiB) on every device
+ * that loads it; a call whose jules_mlp_block_workspace_bytes(T, d, dff)
+ * exceeds that fails with JULES_ERR_WORKSPACE (e.g. d = 4096, dff = 16384
+ * allows T <= 819).  All calls on a device share the array: calls that
+ * overlap on the GPU race.  The first call on a device looks up the array's
+ * device address (set-up); make that first call before any stream capture.
+ * It calls no cudaMalloc / cudaFree and no allocating routine.
+ */
+size_t jules_mlp_block_noalloc_max_workspace_bytes(void);
+int jules_mlp_block_noalloc(const void* X, const float* gamma, const float* beta, const void* W1,
+                            const float* b1, const void* W2, const float* b2, void* out,
+                            int out_dtype, int64_t T, int64_t d, int64_t dff, float eps,
+                            void* stream);
+
+/*
  * Kernel registry keyed by the jules.extern_kernel names that
  * KernelRoutingPass emits (lib/Passes/KernelRoutingPass.cpp:134-419) plus
  * the documented fusedMLPForward / flashAttention and the GELU variants the

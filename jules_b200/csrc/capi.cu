@@ -541,3 +541,107 @@ int jules_mlp_block(const void* X, const float* gamma, const float* beta, const 
 }
 
 }  // extern "C"
+
+// ===========================================================================
+// MLP block without allocation (jules_mlp_block_noalloc).
+//
+// Some callers cannot allocate device memory: a runtime's custom-call handler
+// (the route jules.extern_kernel -> stablehlo.custom_call takes) receives only
+// its operand and result buffers, and the device memory belongs to that
+// runtime's allocator, so the handler may neither cudaMalloc nor keep a
+// workspace of its own.  This entry point takes its workspace from a
+// fixed-size array compiled into the library instead.
+// ===========================================================================
+
+// Workspace of jules_mlp_block_noalloc: LN(X) and the hidden activation, bf16.
+// Every device that loads the library holds these 32 MiB until the process
+// exits.  All calls on a device share it: calls whose kernels overlap on the
+// GPU (different streams, no ordering between them) race on it.  Nothing in
+// it needs to start at zero (each call writes both parts before reading
+// them), so stale contents from the previous call are harmless.
+constexpr size_t kNoAllocScratchBytes = 32ull << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+// Device address of g_noalloc_scratch per device.  In host code the array's
+// name is only a host-side stand-in, so the address is looked up once per
+// device, with that device current.
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+int noalloc_scratch(void** out) {
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(noalloc scratch)");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return JULES_OK;
+}
+
+// bf16 GEMM for the no-allocation path: the same kernels as
+// jules_gemm_bias_act, but never the K-split tail (whose scratch is
+// allocated on demand).
+int gemm_noalloc(const void* A, const void* W, const float* bias, const void* residual, void* C,
+                 int64_t M, int64_t N, int64_t K, int act, int out_dtype, cudaStream_t st) {
+  const bool out_bf = out_dtype == JULES_DTYPE_BF16;
+  if (N % 8 == 0 && K % 8 == 0 && aligned16(A) && aligned16(W) && aligned16(C) &&
+      (!bias || aligned16(bias)) && (!residual || aligned16(residual))) {
+    const auto* a = static_cast<const __nv_bfloat16*>(A);
+    const auto* w = static_cast<const __nv_bfloat16*>(W);
+    const auto* r = static_cast<const __nv_bfloat16*>(residual);
+    if (out_bf)
+      return gemm_tc_dispatch(a, w, bias, r, static_cast<__nv_bfloat16*>(C), M, N, K, act, st,
+                              /*allow_split=*/false);
+    return gemm_tc_dispatch(a, w, bias, r, static_cast<float*>(C), M, N, K, act, st,
+                            /*allow_split=*/false);
+  }
+  if (out_bf)
+    return gemm_simt<__nv_bfloat16, __nv_bfloat16>(A, W, bias, residual, C, M, N, K, act, 0, st);
+  return gemm_simt<__nv_bfloat16, float>(A, W, bias, residual, C, M, N, K, act, 1, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t jules_mlp_block_noalloc_max_workspace_bytes(void) { return kNoAllocScratchBytes; }
+
+int jules_mlp_block_noalloc(const void* X, const float* gamma, const float* beta, const void* W1,
+                            const float* b1, const void* W2, const float* b2, void* out,
+                            int out_dtype, int64_t T, int64_t d, int64_t dff, float eps,
+                            void* stream) {
+  if (!X || !gamma || !beta || !W1 || !W2 || !out)
+    return fail(JULES_ERR_ARG, "mlp_block_noalloc: NULL pointer");
+  if (T < 0 || d <= 0 || dff <= 0 || T > INT32_MAX || d > INT32_MAX || dff > INT32_MAX)
+    return fail(JULES_ERR_SHAPE, "mlp_block_noalloc: T=%lld d=%lld dff=%lld", (long long)T,
+                (long long)d, (long long)dff);
+  if (out_dtype != JULES_DTYPE_BF16 && out_dtype != JULES_DTYPE_F32)
+    return fail(JULES_ERR_DTYPE, "mlp_block_noalloc: out dtype %d", out_dtype);
+  const size_t need = jules_mlp_block_workspace_bytes(T, d, dff);
+  if (need > kNoAllocScratchBytes)
+    return fail(JULES_ERR_WORKSPACE,
+                "mlp_block_noalloc: T=%lld d=%lld dff=%lld needs %zu bytes of workspace; the "
+                "built-in array holds %zu (use jules_mlp_block with a caller workspace)",
+                (long long)T, (long long)d, (long long)dff, need, kNoAllocScratchBytes);
+  if (T == 0) return ok();
+  void* ws = nullptr;
+  if (int rc = noalloc_scratch(&ws)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t xn_bytes = ((size_t)T * d * 2 + 255) & ~size_t(255);
+  void* xn = ws;
+  void* hid = static_cast<char*>(ws) + xn_bytes;
+  if (int rc = jules_layernorm(X, gamma, beta, xn, T, d, eps, JULES_DTYPE_BF16, JULES_DTYPE_BF16,
+                               nullptr, nullptr, stream))
+    return rc;
+  if (int rc = gemm_noalloc(xn, W1, b1, nullptr, hid, T, dff, d, JULES_ACT_GELU, JULES_DTYPE_BF16,
+                            st))
+    return rc;
+  return gemm_noalloc(hid, W2, b2, X, out, T, d, dff, JULES_ACT_NONE, out_dtype, st);
+}
+
+}  // extern "C"
