@@ -186,7 +186,7 @@ class Workload:
 
 class Gemm(Workload):
     """C2: C = GELU(A.W + bias), M=N=K=4096 per rank (rows of M sharded)."""
-    dominant = "gemm_bf16_tc_kernel"
+    dominant = "gemm_bf16_tc2_kernel (CTA pair)"
 
     def __init__(self, jb, torch, rank, world, M=4096, N=4096, K=4096):
         self.jb, self.torch = jb, torch
@@ -370,7 +370,7 @@ class AttentionF32(Workload):
 class Mlp(Workload):
     """C4: out = GELU(LN(X).W1 + b1).W2 + b2 + X, T=16384 tokens per rank,
     d=4096, dff=16384 (token rows sharded)."""
-    dominant = "gemm_bf16_tc_kernel (GEMM1)"
+    dominant = "gemm_bf16_tc2_kernel (GEMM1, CTA pair)"
     launches_per_step = 3
 
     def __init__(self, jb, torch, rank, world, T=16384, d=4096, dff=16384):
@@ -428,6 +428,11 @@ class Mlp(Workload):
 
 
 METRIC = "Flash-attn fwd & fused-GEMM TFLOP/s at 1/2/4/8 B200; % of tensor peak"
+JSON_OUT = sys.stdout
+
+
+def emit(line):
+    print(json.dumps(line), file=JSON_OUT, flush=True)
 
 
 # ---------------------------------------------------------------------------
@@ -440,8 +445,8 @@ def cpu_reference_sample(workload, reps=3, warm=1):
     sys.path.insert(0, os.path.join(HERE, "oracle"))
     import oracle
     threads = os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
     ref = oracle.Reference()
+    ref.set_threads(threads)  # all host threads, whatever OMP_NUM_THREADS says
     g = np.random.default_rng(0)
     if workload in ("gemm", "mlp"):
         if workload == "gemm":
@@ -512,7 +517,7 @@ def run_reference_arm(args):
                              "kind": "reference", "sample": desc},
             "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
@@ -660,7 +665,7 @@ def main():
         }
         if gather:
             line["gather"] = gather
-        print(json.dumps(line), flush=True)
+        emit(line)
 
     if world > 1:
         barrier()
@@ -669,4 +674,10 @@ def main():
 
 
 if __name__ == "__main__":
+    # The JSON line is the only thing on stdout: keep a private handle on the
+    # real stdout and send everything else written to fd 1 (library banners
+    # such as NCCL's version line) to stderr.
+    JSON_OUT = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
     sys.exit(main())

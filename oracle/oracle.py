@@ -199,6 +199,7 @@ class Reference:
         lib.ref_fused_mlp_forward.argtypes = [_f32p] * 6 + [ctypes.c_int] * 4
         lib.ref_cache_info.argtypes = [ctypes.POINTER(ctypes.c_size_t)]
         lib.oracle_set_sgemm64.argtypes = [ctypes.c_void_p]
+        lib.ref_set_threads.argtypes = [ctypes.c_int]
         self.lib = lib
         self.openblas = False
         if use_openblas:
@@ -206,6 +207,9 @@ class Reference:
             if fn:
                 lib.oracle_set_sgemm64(fn)
                 self.openblas = True
+
+    def set_threads(self, n: int) -> None:
+        self.lib.ref_set_threads(int(n))
 
     def cache_info(self):
         out = (ctypes.c_size_t * 4)()

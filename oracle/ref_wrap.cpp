@@ -8,6 +8,9 @@
 #include "jules/Kernel/FlashAttention.h"  // pulls FusedKernels.h, TilePlanner.h, ExecutionArena.h
 
 #include <cstdlib>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
 
 using namespace jules::kernel;
 
@@ -35,6 +38,14 @@ TilePlanner& planner() {
 }  // namespace
 
 extern "C" {
+
+// OpenMP threads for the reference kernels (launchers such as torchrun set
+// OMP_NUM_THREADS=1).
+void ref_set_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#endif
+}
 
 int ref_has_avx512(void) {
 #if defined(__AVX512F__)
