@@ -71,11 +71,23 @@ struct Smem {
   int abort_flag;
 };
 
-// Work item w -> (query-tile pair, b*Hq + h); longest causal pairs first.
-__device__ __forceinline__ void decode_item(int w, int n_pairs, int BH, int causal, int& pair,
-                                            int& bh) {
-  const int r = w / BH;
-  bh = w % BH;
+// Work item w -> (query-tile pair, b*Hq + h).  Items come in groups of G
+// consecutive (b, h) (whole grouped-query sets, at least 8 heads); inside a
+// group the pairs run longest-causal-first and, for each pair, the heads of
+// the group run back to back.  The ~148 items resident at one time therefore
+// read the K/V of a few heads, which stay in L2, and the end of the grid
+// holds the shortest items.
+__device__ __forceinline__ int head_group(int group) {
+  return group >= 8 ? group : group * (8 / group);
+}
+__device__ __forceinline__ void decode_item(int w, int n_pairs, int BH, int G, int causal,
+                                            int& pair, int& bh) {
+  const int per_group = G * n_pairs;
+  const int g = w / per_group;
+  const int idx = w - g * per_group;
+  const int gh = min(G, BH - g * G);
+  const int r = idx / gh;
+  bh = g * G + idx % gh;
   pair = causal ? (n_pairs - 1 - r) : r;
 }
 
@@ -167,6 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_kv_full = (S + BKV - 1) / BKV;
   const int total = n_pairs * BH;
   const int group = Hq / Hkv;
+  const int hgroup = head_group(group);
 
   if (threadIdx.x == 0) {
     mbar_init(&s.q_full, 1);
@@ -208,7 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int w = blockIdx.x; w < total && ok; w += gridDim.x, ++wi) {
         int pair, bh;
-        decode_item(w, n_pairs, BH, causal, pair, bh);
+        decode_item(w, n_pairs, BH, hgroup, causal, pair, bh);
         const int b = bh / Hq, h = bh % Hq;
         const int zkv = b * Hkv + h / group;
         const int n_kv = kv_tiles(pair, n_kv_full, causal);
@@ -274,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       for (int w = blockIdx.x; w < total && ok; w += gridDim.x, ++wi) {
         int pair, bh;
-        decode_item(w, n_pairs, BH, causal, pair, bh);
+        decode_item(w, n_pairs, BH, hgroup, causal, pair, bh);
         const int n_kv = kv_tiles(pair, n_kv_full, causal);
         if (!mbar_wait(&s.q_full, wi & 1u, 20, abort_flag)) break;
         const uint32_t kv0 = kvi;
@@ -332,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t pvc = 0, wi = 0;
     for (int w = blockIdx.x; w < total; w += gridDim.x, ++wi) {
       int pair, bh;
-      decode_item(w, n_pairs, BH, causal, pair, bh);
+      decode_item(w, n_pairs, BH, hgroup, causal, pair, bh);
       const int n_kv = kv_tiles(pair, n_kv_full, causal);
       const int qt0 = pair * NQT * BQ + t * BQ;  // first row of this tile
       const int q = qt0 + r;

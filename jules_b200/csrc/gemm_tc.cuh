@@ -48,6 +48,21 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // one 128-byte swizzle row of bf16
 constexpr int kThreads = 192;
 
+// Tile order shared by both GEMM kernels: groups of kGroupM tile rows; inside
+// a group m runs fastest and n advances once per group height, so the tiles
+// resident at one time (one per SM or SM pair) cover a compact block of A row
+// panels and W column panels that stays in L2 instead of sweeping all of one
+// operand per tile row.
+constexpr int kGroupM = 16;
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mi, int& ni) {
+  const int per_group = kGroupM * num_n;
+  const int g = t / per_group;
+  const int idx = t - g * per_group;
+  const int gm = min(kGroupM, num_m - g * kGroupM);
+  mi = g * kGroupM + idx % gm;
+  ni = idx / gm;
+}
+
 template <int BN, int STAGES>
 struct Smem {
   static constexpr int kABytes = BM * BK * 2;
@@ -129,8 +144,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const int m0 = (t % num_m) * BM;
-        const int n0 = (t / num_m) * BN;
+        int mi, ni;
+        tile_coords(t, num_m, num_n, mi, ni);
+        const int m0 = mi * BM;
+        const int n0 = ni * BN;
         for (int kb = 0; kb < num_k; ++kb) {
           if (!mbar_wait(&s.empty[stage], phase ^ 1u, 1, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&s.full[stage], S::kABytes + S::kBBytes);
@@ -182,8 +199,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-      const int m0 = (t % num_m) * BM;
-      const int n0 = (t / num_m) * BN;
+      int mi, ni;
+      tile_coords(t, num_m, num_n, mi, ni);
+      const int m0 = mi * BM;
+      const int n0 = ni * BN;
       if (!mbar_wait(&s.tfull[acc], acc_phase, 4, abort_flag)) break;
       tc_fence_after();
       const int row = m0 + row_in_tile;
@@ -387,8 +406,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int u = pair_id; u < num_units && ok; u += num_pairs) {
         const PairUnit pu = pair_unit(u, whole_units, num_k);
-        const int m0 = (pu.tile % num_m) * TM + (int)rank * 128;
-        const int n0 = (pu.tile / num_m) * TN + (int)rank * (TN / 2);
+        int mi, ni;
+        tile_coords(pu.tile, num_m, num_n, mi, ni);
+        const int m0 = mi * TM + (int)rank * 128;
+        const int n0 = ni * TN + (int)rank * (TN / 2);
         for (int kb = pu.k0; kb < pu.k1; ++kb) {
           if (!mbar_wait(&s.empty[stage], phase ^ 1u, 41, abort_flag)) { ok = false; break; }
           if (leader) mbar_arrive_expect_tx(&s.full[stage], 2 * (S::kABytes + S::kBBytes));
@@ -449,8 +470,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     for (int u = pair_id; u < num_units; u += num_pairs) {
       const PairUnit pu = pair_unit(u, whole_units, num_k);
-      const int m0 = (pu.tile % num_m) * TM + (int)rank * 128;
-      const int n0 = (pu.tile / num_m) * TN;
+      int mi, ni;
+      tile_coords(pu.tile, num_m, num_n, mi, ni);
+      const int m0 = mi * TM + (int)rank * 128;
+      const int n0 = ni * TN;
       if (!mbar_wait(&s.tfull[acc], acc_phase, 44, abort_flag)) break;
       tc_fence_after();
       const int row = m0 + row_in_tile;
