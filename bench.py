@@ -73,6 +73,25 @@ def measured_peaks():
         return FALLBACK_PEAK_TFLOPS, FALLBACK_HBM_GBS, "fallback"
 
 
+# fp32 CUDA-core peak for the C1 kernel (no measured fp32 figure exists):
+# 148 SMs x 128 FP32 lanes x 2 FLOP (FMA) x 1965 MHz.
+NOMINAL_FP32_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
+
+
+def roofline(wl, achieved, peak, peak_kind, traffic):
+    """Roofline object of the dominant kernel: bf16 tensor kernels against the
+    measured cuBLAS bf16 burst peak, the fp32 CUDA-core kernel (C1) against the
+    nominal fp32 FMA peak."""
+    fp32 = isinstance(wl, AttentionF32)
+    p = NOMINAL_FP32_TFLOPS if fp32 else peak
+    return {"bound": "fp32_cuda_cores" if fp32 else "tensor", "kernel": wl.dominant,
+            "achieved": round(achieved, 2), "peak": round(p, 1), "unit": "TFLOP/s",
+            "frac": round(achieved / p, 4),
+            "peak_kind": ("nominal fp32 FMA, 148 SM x 128 lanes x 2 x 1965 MHz" if fp32
+                          else f"{peak_kind} cuBLAS bf16 burst"),
+            "traffic": traffic, "traffic_unit": "DRAM bytes per launch (ncu, profiles/)"}
+
+
 def profiled_traffic(workload):
     """Per-launch DRAM bytes of the dominant kernel from the committed ncu
     summary (profiles/<kernel>_<workload>.md, line 'traffic_bytes_per_launch:')."""
@@ -653,11 +672,7 @@ def main():
             "data": "synthetic (seeded; config shapes and distributions)",
             "config": describe(args.workload, world, wl.config.get("l2")),
             "pct_of_dense_bf16_peak_2250": round(100 * tflops_total / world / 2250.0, 2),
-            "roofline": {"bound": "tensor", "kernel": wl.dominant, "achieved": round(achieved, 2),
-                         "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
-                         "peak_kind": f"{peak_kind} cuBLAS bf16 burst",
-                         "traffic": traffic,
-                         "traffic_unit": "DRAM bytes per launch (ncu, profiles/)"},
+            "roofline": roofline(wl, achieved, peak, peak_kind, traffic),
             "clocks": clocks,
             "e2e": e2e,
             "gpu_launches": K * wl.launches_per_step,
