@@ -307,15 +307,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t st1 = (kv0 + j + 1) % KVS, ph1 = ((kv0 + j + 1) / KVS) & 1u;
 #pragma unroll
           for (int t = 0; t < NQT; ++t) {
-            if (!mbar_wait(&s.p_full[t], g & 1u, 22, abort_flag)) { ok = false; break; }
-            if (j == 0 && !mbar_wait(&s.o_empty[t], (wi & 1u) ^ 1u, 23, abort_flag)) { ok = false; break; }
-            if (t == 0 && !mbar_wait(&s.v_full[st], ph, 24, abort_flag)) { ok = false; break; }
+            bool kready = false;
+            {
+              // Poll every barrier this group needs at once; the slow path
+              // (rare) waits on them one by one.
+              const uint32_t r0 = mbar_try_wait(&s.p_full[t], g & 1u) ? 1u : 0u;
+              const uint32_t r1 = (j != 0) ? 1u : (mbar_try_wait(&s.o_empty[t], (wi & 1u) ^ 1u) ? 1u : 0u);
+              const uint32_t r2 = (t != 0) ? 1u : (mbar_try_wait(&s.v_full[st], ph) ? 1u : 0u);
+              const uint32_t r3 = (t == 0 && more) ? (mbar_try_wait(&s.k_full[st1], ph1) ? 1u : 0u) : 0u;
+              kready = r3 != 0u;
+              if ((r0 & r1 & r2) == 0u) {
+                if (!mbar_wait(&s.p_full[t], g & 1u, 22, abort_flag)) { ok = false; break; }
+                if (j == 0 && !mbar_wait(&s.o_empty[t], (wi & 1u) ^ 1u, 23, abort_flag)) { ok = false; break; }
+                if (t == 0 && !mbar_wait(&s.v_full[st], ph, 24, abort_flag)) { ok = false; break; }
+              }
+            }
             tc_fence_after();
             issue_pv(t, st, j > 0);
             if (t == NQT - 1) umma_commit(&s.v_empty[st]);
             if (!more) umma_commit(&s.o_full[t]);
             if (more) {
-              if (t == 0) {
+              if (t == 0 && !kready) {
                 if (!mbar_wait(&s.k_full[st1], ph1, 25, abort_flag)) { ok = false; break; }
                 tc_fence_after();
               }

@@ -371,7 +371,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_pairs = gridDim.x >> 1;
   const int num_m = (M + TM - 1) / TM;
   const int num_n = (N + TN - 1) / TN;
-  const int num_tiles = num_m * num_n;
   const int num_k = (K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
