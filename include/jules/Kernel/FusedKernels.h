@@ -56,6 +56,15 @@ void fusedLayerNorm(float* output, const float* input, const float* gamma, const
 // FusedKernels.h:606-627
 void fusedGelu(float* output, const float* input, int N);
 
+// Row softmax over [M, N].  FusedKernels.h:464-526.
+void fusedSoftmax(float* output, const float* input, int M, int N);
+
+// Softmax + cross-entropy: writes grad = (softmax - onehot(targets)) / M and
+// returns the mean of -log(p[target] + 1e-10).  FusedKernels.h:766-854.
+// A target outside [0, N) throws std::runtime_error (undefined in the
+// reference).
+float fusedCrossEntropyLoss(const float* logits, const int32_t* targets, float* grad, int M, int N);
+
 // Row-major SGEMM, C = alpha op(A) op(B) + beta C.  FusedKernels.h:633-644.
 void blasMatmul(const float* A, const float* B, float* C, int M, int N, int K, float alpha = 1.0f,
                 float beta = 0.0f, bool transA = false, bool transB = false);

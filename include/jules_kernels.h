@@ -127,6 +127,30 @@ int jules_layernorm(const void* in, const float* gamma, const float* beta, void*
 int jules_gelu(const void* in, void* out, int64_t n, int dtype, void* stream);
 
 /*
+ * Row softmax: out[i,:] = exp(x[i,:] - max_i) / sum_j exp(x[i,j] - max_i),
+ * in/out [M,N] row-major, fp32 arithmetic.  in_dtype and out_dtype each F32
+ * or BF16.
+ * Replaces fusedSoftmax (FusedKernels.h:464-526).
+ */
+int jules_softmax(const void* in, void* out, int64_t M, int64_t N, int in_dtype, int out_dtype,
+                  void* stream);
+
+/*
+ * Fused softmax + cross-entropy over logits [M,N] and int32 targets [M]:
+ *   p = softmax(logits[i,:]),  loss = mean_i -log(p[i, targets[i]] + 1e-10),
+ *   grad[i,:] = (p - onehot(targets[i])) / M.
+ * loss points to ONE device float, overwritten with the mean loss (row losses
+ * are added atomically, so the last bits may vary between runs).  grad may be
+ * NULL (loss only); otherwise it has the logits' dtype (F32 or BF16).  A
+ * target outside [0, N) adds nothing to the loss and sets the device error
+ * word (jules_device_error reports JULES_ERR_SHAPE).
+ * Replaces fusedCrossEntropyLoss (FusedKernels.h:766-854), which returns the
+ * loss on the host and always writes grad.
+ */
+int jules_cross_entropy_loss(const void* logits, const int32_t* targets, void* grad, float* loss,
+                             int64_t M, int64_t N, int dtype, void* stream);
+
+/*
  * Transformer MLP block, bf16:
  *   out = GELU(LN(X) . W1 + b1) . W2 + b2 + X
  *   X, out [T,d]; W1 [d,dff]; W2 [dff,d]; gamma, beta, b2 [d] and b1 [dff]

@@ -44,6 +44,9 @@ _SIGNATURES = {
     "jules_layernorm": ([_c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_f, _c_int, _c_int, _c_vp,
                          _c_vp, _c_vp], _c_int),
     "jules_gelu": ([_c_vp, _c_vp, _c_i64, _c_int, _c_vp], _c_int),
+    "jules_softmax": ([_c_vp, _c_vp, _c_i64, _c_i64, _c_int, _c_int, _c_vp], _c_int),
+    "jules_cross_entropy_loss": ([_c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_int, _c_vp],
+                                 _c_int),
     "jules_mlp_block_workspace_bytes": ([_c_i64, _c_i64, _c_i64], ctypes.c_size_t),
     "jules_mlp_block": ([_c_vp] * 8 + [_c_int, _c_i64, _c_i64, _c_i64, _c_f, _c_vp,
                                        ctypes.c_size_t, _c_vp], _c_int),
@@ -197,6 +200,39 @@ def gelu(x, out=None, stream=None):
     rc = lib().jules_gelu(_ptr(x), _ptr(out), x.numel(), _dtype_code(x), _stream(stream))
     _check(rc, "jules_gelu")
     return out
+
+
+def softmax(x, out=None, out_dtype=None, stream=None):
+    """Row softmax of a 2-D tensor (fp32 or bf16; fp32 arithmetic)."""
+    import torch
+    _dense(x, "x")
+    if x.dim() != 2:
+        raise ValueError("softmax: x must be 2-D [M, N]")
+    if out is None:
+        out = torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
+    M, N = x.shape
+    rc = lib().jules_softmax(_ptr(x), _ptr(out), M, N, _dtype_code(x), _dtype_code(out),
+                             _stream(stream))
+    _check(rc, "jules_softmax")
+    return out
+
+
+def cross_entropy_loss(logits, targets, grad=True, stream=None):
+    """Fused softmax + cross-entropy.  Returns (loss as a 0-d fp32 device
+    tensor, grad [M, N] in the logits' dtype or None)."""
+    import torch
+    _dense(logits, "logits")
+    if logits.dim() != 2:
+        raise ValueError("cross_entropy_loss: logits must be 2-D [M, N]")
+    if targets.dtype != torch.int32 or not targets.is_contiguous():
+        raise ValueError("cross_entropy_loss: targets must be contiguous int32")
+    M, N = logits.shape
+    g = torch.empty_like(logits) if grad else None
+    loss = torch.empty((), dtype=torch.float32, device=logits.device)
+    rc = lib().jules_cross_entropy_loss(_ptr(logits), _ptr(targets), _ptr(g) if g is not None else None,
+                                        _ptr(loss), M, N, _dtype_code(logits), _stream(stream))
+    _check(rc, "jules_cross_entropy_loss")
+    return loss, g
 
 
 def mlp_block_workspace_bytes(T, d, dff) -> int:

@@ -16,6 +16,7 @@
 #include "gemm_tc.cuh"
 #include "sm100.cuh"
 #include "simt.cuh"
+#include "rowwise.cuh"
 
 namespace {
 
@@ -351,6 +352,37 @@ int attn_tc(const void* Q, const void* K, const void* V, void* O, float* lse, in
 // ===========================================================================
 // Exported C ABI
 // ===========================================================================
+namespace {
+
+// Row softmax / fused cross-entropy launcher: one warp per row up to
+// kWarpRowMax columns, one CTA per row beyond.  Grids are capped at a few
+// waves of resident blocks; the kernels stride over rows.
+template <typename TIn, typename TOut, bool XENT>
+int rows_launch(const void* in, void* out, const int32_t* targets, float* loss, int64_t M,
+                int64_t N, cudaStream_t st) {
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  const float inv_M = 1.0f / (float)M;
+  const auto* x = static_cast<const TIn*>(in);
+  auto* y = static_cast<TOut*>(out);
+  if (N <= jb::rows::kWarpRowMax) {
+    int64_t blocks = (M + 7) / 8;
+    const int64_t cap = (int64_t)device_sms(dev) * 8;
+    if (blocks > cap) blocks = cap;
+    jb::rows::softmax_warp_kernel<TIn, TOut, XENT>
+        <<<(unsigned)blocks, 256, 0, st>>>(x, y, targets, loss, M, (int)N, inv_M);
+  } else {
+    int64_t blocks = M;
+    const int64_t cap = (int64_t)device_sms(dev) * 8;
+    if (blocks > cap) blocks = cap;
+    jb::rows::softmax_cta_kernel<TIn, TOut, XENT>
+        <<<(unsigned)blocks, jb::rows::kCtaThreads, 0, st>>>(x, y, targets, loss, M, (int)N, inv_M);
+  }
+  return check_launch(XENT ? "cross_entropy launch" : "softmax launch");
+}
+
+}  // namespace
+
 extern "C" {
 
 int jules_version(void) { return (0 << 16) | 1; }
@@ -505,6 +537,34 @@ int jules_gelu(const void* in, void* out, int64_t n, int dtype, void* stream) {
   else
     return fail(JULES_ERR_DTYPE, "gelu: dtype %d", dtype);
   return check_launch("gelu launch");
+}
+
+int jules_softmax(const void* in, void* out, int64_t M, int64_t N, int in_dtype, int out_dtype,
+                  void* stream) {
+  if (!in || !out) return fail(JULES_ERR_ARG, "softmax: NULL pointer");
+  if (M < 0 || N < 0 || N > INT32_MAX) return fail(JULES_ERR_SHAPE, "softmax: M=%lld N=%lld", (long long)M, (long long)N);
+  if (M == 0 || N == 0) return ok();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool fi = in_dtype == JULES_DTYPE_F32, bi = in_dtype == JULES_DTYPE_BF16;
+  const bool fo = out_dtype == JULES_DTYPE_F32, bo = out_dtype == JULES_DTYPE_BF16;
+  if (fi && fo) return rows_launch<float, float, false>(in, out, nullptr, nullptr, M, N, st);
+  if (fi && bo) return rows_launch<float, __nv_bfloat16, false>(in, out, nullptr, nullptr, M, N, st);
+  if (bi && fo) return rows_launch<__nv_bfloat16, float, false>(in, out, nullptr, nullptr, M, N, st);
+  if (bi && bo) return rows_launch<__nv_bfloat16, __nv_bfloat16, false>(in, out, nullptr, nullptr, M, N, st);
+  return fail(JULES_ERR_DTYPE, "softmax: dtypes %d -> %d", in_dtype, out_dtype);
+}
+
+int jules_cross_entropy_loss(const void* logits, const int32_t* targets, void* grad, float* loss,
+                             int64_t M, int64_t N, int dtype, void* stream) {
+  if (!logits || !targets || !loss) return fail(JULES_ERR_ARG, "cross_entropy: NULL pointer");
+  if (M <= 0 || N <= 0 || N > INT32_MAX) return fail(JULES_ERR_SHAPE, "cross_entropy: M=%lld N=%lld", (long long)M, (long long)N);
+  if (dtype != JULES_DTYPE_F32 && dtype != JULES_DTYPE_BF16) return fail(JULES_ERR_DTYPE, "cross_entropy: dtype %d", dtype);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(loss, 0, sizeof(float), st);
+  if (e != cudaSuccess) return cuda_fail(e, "cross_entropy: clear loss");
+  if (dtype == JULES_DTYPE_F32)
+    return rows_launch<float, float, true>(logits, grad, targets, loss, M, N, st);
+  return rows_launch<__nv_bfloat16, __nv_bfloat16, true>(logits, grad, targets, loss, M, N, st);
 }
 
 size_t jules_mlp_block_workspace_bytes(int64_t T, int64_t d, int64_t dff) {

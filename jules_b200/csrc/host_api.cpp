@@ -205,6 +205,38 @@ void fusedGelu(float* output, const float* input, int N) {
   d2h(output, d[1], b);
 }
 
+void fusedSoftmax(float* output, const float* input, int M, int N) {
+  if (M <= 0 || N <= 0) return;
+  const size_t b = (size_t)M * N * 4;
+  const size_t sizes[2] = {b, b};
+  char* d[2];
+  staging().reserve(sizes, 2, d);
+  h2d(d[0], input, b);
+  check_status(jules_softmax(d[0], d[1], M, N, JULES_DTYPE_F32, JULES_DTYPE_F32, nullptr),
+               "jules_softmax");
+  d2h(output, d[1], b);
+}
+
+float fusedCrossEntropyLoss(const float* logits, const int32_t* targets, float* grad, int M,
+                            int N) {
+  if (M <= 0 || N <= 0) return 0.0f;
+  const size_t bl = (size_t)M * N * 4, bt = (size_t)M * 4;
+  const size_t sizes[4] = {bl, bt, bl, 256};
+  char* d[4];
+  staging().reserve(sizes, 4, d);
+  h2d(d[0], logits, bl);
+  h2d(d[1], targets, bt);
+  check_status(jules_cross_entropy_loss(d[0], reinterpret_cast<const int32_t*>(d[1]), d[2],
+                                        reinterpret_cast<float*>(d[3]), M, N, JULES_DTYPE_F32,
+                                        nullptr),
+               "jules_cross_entropy_loss");
+  d2h(grad, d[2], bl);
+  float loss = 0.0f;
+  d2h(&loss, d[3], sizeof(float));
+  check_status(jules_device_error(nullptr, 1), "fusedCrossEntropyLoss (target outside [0, N))");
+  return loss;
+}
+
 void blasMatmul(const float* A, const float* B, float* C, int M, int N, int K, float alpha,
                 float beta, bool transA, bool transB) {
   if (M <= 0 || N <= 0) return;
@@ -305,7 +337,7 @@ const KernelEntry kKernels[] = {
     {"fusedMatmulGelu", 1},        {"fusedMatmulBiasRelu", 1},  {"fusedMatmulBiasSigmoid", 1},
     {"fusedMatmulBiasTanh", 1},    {"fusedMatmulBiasGelu", 1},  {"fusedLayerNorm", 1},
     {"fusedGelu", 1},              {"fusedMLPForward", 1},      {"flashAttention", 1},
-    {"blasMatmul", 1},             {"fusedSoftmax", 0},         {"fusedCrossEntropyLoss", 0},
+    {"blasMatmul", 1},             {"fusedSoftmax", 1},         {"fusedCrossEntropyLoss", 1},
     {"matmulInt8", 0},
 };
 constexpr int kNumKernels = sizeof(kKernels) / sizeof(kKernels[0]);

@@ -48,6 +48,11 @@ def _fp(a: np.ndarray | None):
     return a.ctypes.data_as(_f32p)
 
 
+def _ip(a: np.ndarray):
+    assert a.dtype == np.int32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_i32p)
+
+
 def _cpu_has_avx512() -> bool:
     try:
         with open("/proc/cpuinfo") as f:
@@ -96,6 +101,9 @@ class Restated:
             ctypes.c_int, ctypes.c_int]
         lib.orc_mlp_block.argtypes = [_f32p] * 8 + [ctypes.c_int64] * 3 + [ctypes.c_float, _i64p,
                                                                           ctypes.c_int64]
+        lib.orc_softmax.argtypes = [_f32p, _f32p, ctypes.c_int64, ctypes.c_int64]
+        lib.orc_cross_entropy.argtypes = [_f32p, _i32p, _f32p, ctypes.c_int64, ctypes.c_int64]
+        lib.orc_cross_entropy.restype = ctypes.c_float
         lib.orc_num_threads.restype = ctypes.c_int
         self.lib = lib
 
@@ -122,6 +130,22 @@ class Restated:
         out = np.empty_like(x)
         self.lib.orc_gelu(_fp(out), _fp(x), x.size)
         return out
+
+    def softmax(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        M, N = x.shape
+        out = np.empty_like(x)
+        self.lib.orc_softmax(_fp(out), _fp(x), M, N)
+        return out
+
+    def cross_entropy(self, logits, targets):
+        """Returns (mean loss, grad)."""
+        logits = np.ascontiguousarray(logits, np.float32)
+        targets = np.ascontiguousarray(targets, np.int32)
+        M, N = logits.shape
+        grad = np.empty_like(logits)
+        loss = self.lib.orc_cross_entropy(_fp(logits), _ip(targets), _fp(grad), M, N)
+        return float(loss), grad
 
     def flash_attention(self, Q, K, V, causal=False, scale=None, units=None, q_begin=0, q_end=0,
                         tile_q=32, tile_k=64, want_lse=True):
@@ -194,6 +218,8 @@ class Reference:
         lib.ref_fused_layernorm.argtypes = [_f32p] * 4 + [ctypes.c_int] * 2 + [ctypes.c_float]
         lib.ref_fused_gelu.argtypes = [_f32p, _f32p, ctypes.c_int]
         lib.ref_fused_softmax.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int]
+        lib.ref_fused_cross_entropy.argtypes = [_f32p, _i32p, _f32p, ctypes.c_int, ctypes.c_int]
+        lib.ref_fused_cross_entropy.restype = ctypes.c_float
         lib.ref_blas_matmul.argtypes = [_f32p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_float] * 2 + [
             ctypes.c_int] * 2
         lib.ref_fused_mlp_forward.argtypes = [_f32p] * 6 + [ctypes.c_int] * 4
@@ -277,10 +303,20 @@ class Reference:
         return out
 
     def softmax(self, x):
+        x = np.ascontiguousarray(x, np.float32)
         M, N = x.shape
         out = np.empty_like(x)
         self.lib.ref_fused_softmax(_fp(out), _fp(x), M, N)
         return out
+
+    def cross_entropy(self, logits, targets):
+        """Returns (mean loss, grad) from the reference's fusedCrossEntropyLoss."""
+        logits = np.ascontiguousarray(logits, np.float32)
+        targets = np.ascontiguousarray(targets, np.int32)
+        M, N = logits.shape
+        grad = np.empty_like(logits)
+        loss = self.lib.ref_fused_cross_entropy(_fp(logits), _ip(targets), _fp(grad), M, N)
+        return float(loss), grad
 
     def blas_matmul(self, A, B, alpha=1.0, beta=0.0):
         M, K = A.shape

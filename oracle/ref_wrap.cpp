@@ -130,6 +130,12 @@ void ref_fused_softmax(float* out, const float* in, int M, int N) {
   fusedSoftmax(out, in, M, N);
 }
 
+// FusedKernels.h:766-854
+float ref_fused_cross_entropy(const float* logits, const int32_t* targets, float* grad, int M,
+                              int N) {
+  return fusedCrossEntropyLoss(logits, targets, grad, M, N);
+}
+
 // FusedKernels.h:633-644
 void ref_blas_matmul(const float* A, const float* B, float* C, int M, int N,
                      int K, float alpha, float beta, int transA, int transB) {

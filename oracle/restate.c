@@ -153,6 +153,47 @@ void orc_gemm_bias_act(const float* A, const float* B, const float* bias,
 /* 16-lane AVX-512 accumulation (:545-566).                             */
 /* Optional outputs: per-row mean and inv_std.                          */
 /* ------------------------------------------------------------------ */
+/*
+ * Row softmax.  FusedKernels.h:464-526 (the scalar branch :507-525): max over
+ * the row (from -FLT_MAX), e = exp(x - max) stored and summed in column
+ * order, then each e divided by the sum.
+ */
+void orc_softmax(float* out, const float* in, int64_t M, int64_t N) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < M; i++) {
+    const float* x = in + i * N;
+    float* y = out + i * N;
+    float mx = -FLT_MAX;
+    for (int64_t j = 0; j < N; j++) mx = fmaxf(mx, x[j]);
+    float sum = 0.0f;
+    for (int64_t j = 0; j < N; j++) {
+      y[j] = expf(x[j] - mx);
+      sum += y[j];
+    }
+    for (int64_t j = 0; j < N; j++) y[j] /= sum;
+  }
+}
+
+/*
+ * Softmax + cross-entropy.  FusedKernels.h:766-854 (scalar branch :827-850):
+ * grad = softmax(row); row loss = -log(grad[target] + 1e-10); grad[target]
+ * -= 1; grad /= M; returns the sum of row losses / M.  The row losses are
+ * summed in row order here (the reference sums them in an OpenMP reduction).
+ */
+float orc_cross_entropy(const float* logits, const int32_t* targets, float* grad, int64_t M,
+                        int64_t N) {
+  orc_softmax(grad, logits, M, N);
+  double total = 0.0;
+  for (int64_t i = 0; i < M; i++) {
+    float* g = grad + i * N;
+    const int32_t t = targets[i];
+    total += -logf(g[t] + 1e-10f);
+    g[t] -= 1.0f;
+    for (int64_t j = 0; j < N; j++) g[j] /= (float)M;
+  }
+  return (float)(total / (double)M);
+}
+
 void orc_layernorm(float* out, const float* in, const float* gamma,
                    const float* beta, int64_t M, int64_t N, float eps,
                    float* mean_out, float* rstd_out) {

@@ -63,6 +63,15 @@ int main(int argc, char** argv) {
   std::vector<float> out(M * 24);
   fusedMLPForward(out.data(), A.data(), p, arena, planner);
   save(d + "/out_mlp.bin", out);
+  // softmax and cross-entropy over the [96,136] GEMM output, targets i % 136
+  std::vector<float> sm(M * N), grad(M * N);
+  fusedSoftmax(sm.data(), C.data(), M, N);
+  save(d + "/out_softmax.bin", sm);
+  std::vector<int32_t> tgt(M);
+  for (int i = 0; i < M; ++i) tgt[i] = (i * 7) % N;
+  std::vector<float> loss(1, fusedCrossEntropyLoss(C.data(), tgt.data(), grad.data(), M, N));
+  save(d + "/out_xent_grad.bin", grad);
+  save(d + "/out_xent_loss.bin", loss);
   std::printf("drop-in ok\n");
   return 0;
 }

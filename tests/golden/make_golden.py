@@ -54,6 +54,12 @@ def golden_cases():
     cases["mlp_forward"] = dict(kind="mlp", M=64, K1=784, N1=256, N2=10, seed=600)
     # Config C2's composition (GEMM -> bias -> GELU) on bf16-valued inputs.
     cases["gemm_bias_gelu"] = dict(kind="gemm_bias_gelu", M=32, N=384, K=512, seed=700)
+    # bench_kernel.cpp:396-400 softmax shapes, plus a ragged row length
+    cases["softmax_mlp"] = dict(kind="softmax", M=64, N=256, seed=800)
+    cases["softmax_cls"] = dict(kind="softmax", M=64, N=10, seed=801)
+    cases["softmax_ragged"] = dict(kind="softmax", M=7, N=1000, seed=802)
+    cases["xent"] = dict(kind="xent", M=64, N=1000, seed=900)
+    cases["xent_ragged"] = dict(kind="xent", M=13, N=37, seed=901)
     return cases
 
 
@@ -89,6 +95,11 @@ def make_inputs(c):
         return [oracle.bf16_round(g.uniform(-1, 1, (c["M"], c["K"])).astype(np.float32) * s),
                 oracle.bf16_round(g.uniform(-1, 1, (c["K"], c["N"])).astype(np.float32) * s),
                 (0.02 * g.standard_normal(c["N"])).astype(np.float32)]
+    if k == "softmax":
+        return [(3 * g.standard_normal((c["M"], c["N"]))).astype(np.float32)]
+    if k == "xent":
+        return [(3 * g.standard_normal((c["M"], c["N"]))).astype(np.float32),
+                g.integers(0, c["N"], c["M"]).astype(np.int32)]
     raise ValueError(k)
 
 
@@ -108,6 +119,11 @@ def run_reference(ref, c, ins):
         return {"out": ref.mlp_forward(*ins)}
     if k == "gemm_bias_gelu":
         return {"out": ref.gemm_bias_gelu(*ins)}
+    if k == "softmax":
+        return {"out": ref.softmax(ins[0])}
+    if k == "xent":
+        loss, grad = ref.cross_entropy(ins[0], ins[1])
+        return {"grad": grad, "loss": np.array([loss], np.float32)}
     raise ValueError(k)
 
 

@@ -24,7 +24,7 @@ def _cxx_decls():
     for f in ("FusedKernels.h", "FlashAttention.h"):
         src = open(os.path.join(INC, "jules", "Kernel", f)).read()
         src = re.sub(r"//.*", "", src)
-        for m in re.finditer(r"^\s*(?:void|int|bool)\s+([A-Za-z0-9_]+)\s*\(", src, flags=re.M):
+        for m in re.finditer(r"^\s*(?:void|int|bool|float)\s+([A-Za-z0-9_]+)\s*\(", src, flags=re.M):
             names.add(m.group(1))
     return sorted(names)
 

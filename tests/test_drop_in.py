@@ -47,3 +47,10 @@ def test_drop_in_matches_reference(tmp_path, jb, ref):
     assert rel_l2(out("layernorm", (96, 200)), ln) <= F32_REL_L2
     assert rel_l2(out("gelu", (96, 200)), ref.gelu(A)) <= F32_REL_L2
     assert rel_l2(out("mlp", (96, 24)), ref.mlp_forward(A, W, bias, W2, b2)) <= F32_REL_L2
+    # softmax / cross-entropy of C = blasMatmul(A, W) (the last value written to C)
+    C = out("blas", (96, 136))
+    assert rel_l2(out("softmax", (96, 136)), ref.softmax(C)) <= F32_REL_L2
+    tgt = ((np.arange(96) * 7) % 136).astype(np.int32)
+    loss, grad = ref.cross_entropy(C, tgt)
+    assert rel_l2(out("xent_grad", (96, 136)), grad) <= F32_REL_L2
+    assert abs(float(out("xent_loss", (1,))[0]) - loss) <= 1e-5 * max(1.0, abs(loss))

@@ -48,6 +48,11 @@ def _restated(orc, c, ins):
         return {"out": orc.gemm_bias_act(h, W2, b2, None, "none")}
     if k == "gemm_bias_gelu":
         return {"out": orc.gemm_bias_act(ins[0], ins[1], ins[2], None, "gelu")}
+    if k == "softmax":
+        return {"out": orc.softmax(ins[0])}
+    if k == "xent":
+        loss, grad = orc.cross_entropy(ins[0], ins[1])
+        return {"grad": grad, "loss": np.array([loss], np.float32)}
     raise ValueError(k)
 
 
