@@ -49,7 +49,8 @@ def parse():
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["jules", "reference"], default="jules")
-    p.add_argument("--workload", choices=["gemm", "attn", "attn_gqa", "mlp", "attn_fp32"],
+    p.add_argument("--workload", choices=["gemm", "attn", "attn_gqa", "mlp", "attn_fp32",
+                                          "softmax", "xent"],
                    default="gemm")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
@@ -82,6 +83,12 @@ def roofline(wl, achieved, peak, peak_kind, traffic):
     """Roofline object of the dominant kernel: bf16 tensor kernels against the
     measured cuBLAS bf16 burst peak, the fp32 CUDA-core kernel (C1) against the
     nominal fp32 FMA peak."""
+    if wl.unit == "GB/s":
+        hbm = measured_peaks()[1]
+        return {"bound": "hbm", "kernel": wl.dominant, "achieved": round(achieved, 1),
+                "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                "peak_kind": "measured HBM copy (MEASURED_PEAKS.json hbm_gbs)",
+                "traffic": traffic, "traffic_unit": "DRAM bytes per launch (ncu, profiles/)"}
     fp32 = isinstance(wl, AttentionF32)
     p = NOMINAL_FP32_TFLOPS if fp32 else peak
     return {"bound": "fp32_cuda_cores" if fp32 else "tensor", "kernel": wl.dominant,
@@ -96,7 +103,8 @@ def profiled_traffic(workload):
     """Per-launch DRAM bytes of the dominant kernel from the committed ncu
     summary (profiles/<kernel>_<workload>.md, line 'traffic_bytes_per_launch:')."""
     name = {"gemm": "gemm_tc_c2", "attn": "attn_tc_c3", "attn_gqa": "attn_tc_c5",
-            "mlp": "gemm_tc_c4", "attn_fp32": "attn_simt_c1"}[workload]
+            "mlp": "gemm_tc_c4", "attn_fp32": "attn_simt_c1", "softmax": "rows_softmax",
+            "xent": "rows_xent"}[workload]
     path = os.path.join(HERE, "profiles", f"{name}.md")
     try:
         with open(path) as f:
@@ -126,6 +134,14 @@ def describe(workload, world, extra_l2=None):
         c = {"workload": "C4 MLP block LN->GEMM+b+GELU->GEMM+b+residual", "T_per_rank": 16384,
              "d": 4096, "dff": 16384, "global_T": 16384 * world, "sharding": "token rows",
              "eps": 1e-5}
+    elif workload == "softmax":
+        c = {"workload": "row softmax (fusedSoftmax), fp32", "M_per_rank": 16384, "N": 4096,
+             "global_M": 16384 * world, "sharding": "rows",
+             "bytes_convention": "M*N*4 read + M*N*4 written"}
+    elif workload == "xent":
+        c = {"workload": "fused softmax + cross-entropy (fusedCrossEntropyLoss), fp32 logits",
+             "M_per_rank": 4096, "N": 32768, "global_M": 4096 * world, "sharding": "rows",
+             "bytes_convention": "logits read + grad written + targets read"}
     else:
         c = {"workload": "C1 fp32 flash-attention fwd, non-causal", "B_per_rank": 1, "H": 8,
              "S": 512, "D": 64, "sharding": "batch"}
@@ -198,6 +214,11 @@ class Workload:
     name = ""
     dominant = ""
     launches_per_step = 1
+    # Work accounting: flops_per_step / flops_dominant count FLOPs for the
+    # tensor-core workloads and HBM bytes for the row-wise ones (unit GB/s).
+    unit = "TFLOP/s"
+    unit_scale = 1e12
+    dtype = "bf16"
 
     def sets_for(self, bytes_per_set):
         return max(2, int((2 * L2_BYTES) // max(bytes_per_set, 1)) + 1)
@@ -446,7 +467,73 @@ class Mlp(Workload):
         self.hO.copy_(self.dO, non_blocking=True)
 
 
+class RowWise(Workload):
+    """Row softmax (softmax) or fused softmax + cross-entropy (xent), fp32,
+    rows sharded across ranks.  HBM-bound: work is counted in bytes."""
+    unit = "GB/s"
+    unit_scale = 1e9
+    dtype = "f32"
+
+    def __init__(self, jb, torch, rank, world, xent=False):
+        self.jb, self.torch, self.xent = jb, torch, xent
+        M, N = (4096, 32768) if xent else (16384, 4096)
+        self.M, self.N = M, N
+        dev = torch.device("cuda")
+        g = torch.Generator(device=dev).manual_seed(31 + rank)
+        per_set = 2 * M * N * 4
+        self.nsets = 1 if per_set > L2_BYTES else self.sets_for(per_set)
+        self.X = [3 * torch.randn((M, N), generator=g, device=dev) for _ in range(self.nsets)]
+        self.Y = [torch.empty_like(x) for x in self.X]
+        self.T = [torch.randint(0, N, (M,), generator=g, device=dev, dtype=torch.int32)
+                  for _ in range(self.nsets)]
+        self.loss = torch.empty((), dtype=torch.float32, device=dev)
+        self.flops_per_step = 2.0 * M * N * 4 + (M * 4 if xent else 0)  # bytes
+        self.flops_dominant = self.flops_per_step
+        self.dominant = ("softmax_cta_kernel<float,float,true> (cross-entropy)" if xent
+                         else "softmax_cta_kernel<float,float,false>")
+        self.config = {"l2": f"inputs {per_set / 2**20:.0f} MiB per step (> L2)"
+                       if self.nsets == 1 else f"{self.nsets} rotating input sets"}
+
+    def _run(self, x, y, t):
+        if self.xent:
+            rc = self.jb.lib().jules_cross_entropy_loss(
+                self.jb._ptr(x), self.jb._ptr(t), self.jb._ptr(y), self.jb._ptr(self.loss),
+                self.M, self.N, self.jb.DT_F32, None)
+            self.jb._check(rc, "jules_cross_entropy_loss")
+        else:
+            self.jb.softmax(x, out=y)
+
+    def step(self, i, ev=None):
+        k = i % self.nsets
+        if ev:
+            ev[0].record()
+        self._run(self.X[k], self.Y[k], self.T[k])
+        if ev:
+            ev[1].record()
+
+    def output(self, i):
+        return self.Y[i % self.nsets]
+
+    def e2e_setup(self):
+        t = self.torch
+        self.hX = self.X[0].cpu().pin_memory()
+        self.hT = self.T[0].cpu().pin_memory()
+        self.hY = t.empty_like(self.hX).pin_memory()
+        self.dX, self.dY, self.dT = t.empty_like(self.X[0]), t.empty_like(self.X[0]), t.empty_like(self.T[0])
+        self.h2d = self.hX.numel() * 4 + (self.hT.numel() * 4 if self.xent else 0)
+        self.d2h = self.hY.numel() * 4
+
+    def e2e_step(self):
+        self.dX.copy_(self.hX, non_blocking=True)
+        if self.xent:
+            self.dT.copy_(self.hT, non_blocking=True)
+        self._run(self.dX, self.dY, self.dT)
+        self.hY.copy_(self.dY, non_blocking=True)
+
+
 METRIC = "Flash-attn fwd & fused-GEMM TFLOP/s at 1/2/4/8 B200; % of tensor peak"
+# Extra (non-headline) workloads of the row-wise kernels report HBM bytes per second.
+ROWS_METRIC = "Row softmax / fused cross-entropy GB/s (HBM bytes moved) per B200"
 JSON_OUT = sys.stdout
 
 
@@ -481,6 +568,27 @@ def cpu_reference_sample(workload, reps=3, warm=1):
         b = (0.02 * g.standard_normal(N)).astype(np.float32)
         fn = lambda: ref.gemm_bias_gelu(A, W, b)
         flops = 2.0 * Ms * N * K
+    elif workload in ("softmax", "xent"):
+        if workload == "softmax":
+            Ms, N = 2048, 4096
+            X = (3 * g.standard_normal((Ms, N))).astype(np.float32)
+            fn = lambda: ref.softmax(X)
+            desc = f"reference fusedSoftmax (FusedKernels.h:464-526) on {Ms} of the 16384 rows"
+        else:
+            Ms, N = 512, 32768
+            X = (3 * g.standard_normal((Ms, N))).astype(np.float32)
+            T = g.integers(0, N, Ms).astype(np.int32)
+            fn = lambda: ref.cross_entropy(X, T)
+            desc = f"reference fusedCrossEntropyLoss (FusedKernels.h:766-854) on {Ms} of the 4096 rows"
+        flops = 2.0 * Ms * N * 4  # bytes, reported in GB/s below
+        reps = 5
+        for _ in range(warm):
+            fn()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        dt = (time.perf_counter() - t0) / reps
+        return flops / dt / 1e9, desc + f"; {reps} timed reps, {dt * 1e3:.1f} ms each", threads
     elif workload == "attn_fp32":
         Q, K_, V = (g.standard_normal((1, 8, 512, 64), dtype=np.float32) for _ in range(3))
         fn = lambda: ref.flash_attention(Q, K_, V)
@@ -526,15 +634,17 @@ def run_reference_arm(args):
         vals.append(v)
     wall = time.perf_counter() - t0
     value = statistics.mean(vals)
-    line = {"metric": METRIC, "value": round(value, 6), "unit": "TFLOP/s",
+    rowwise = args.workload in ("softmax", "xent")
+    unit = "GB/s" if rowwise else "TFLOP/s"
+    line = {"metric": ROWS_METRIC if rowwise else METRIC, "value": round(value, 6), "unit": unit,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(wall / args.steps * 1e3, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": describe(args.workload, world, "CPU: bounded sample per step"),
             "impl": "reference",
-            "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": threads,
+            "cpu_baseline": {"value": round(value, 6), "unit": unit, "cores": threads,
                              "kind": "reference", "sample": desc},
-            "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+            "e2e": {"value": round(value, 6), "unit": unit, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     emit(line)
     return 0
@@ -573,7 +683,9 @@ def main():
          "attn": lambda: Attention(jb, torch, rank, world, gqa=False),
          "attn_gqa": lambda: Attention(jb, torch, rank, world, gqa=True),
          "mlp": lambda: Mlp(jb, torch, rank, world),
-         "attn_fp32": lambda: AttentionF32(jb, torch, rank, world)}[args.workload]
+         "attn_fp32": lambda: AttentionF32(jb, torch, rank, world),
+         "softmax": lambda: RowWise(jb, torch, rank, world, xent=False),
+         "xent": lambda: RowWise(jb, torch, rank, world, xent=True)}[args.workload]
     wl = W()
     stream = torch.cuda.current_stream()
 
@@ -607,9 +719,9 @@ def main():
     if jb.device_error() != 0:
         raise RuntimeError("device error in timed region")
 
-    tflops_total = wl.flops_per_step * world * K / (ms_total * 1e-3) / 1e12
+    tflops_total = wl.flops_per_step * world * K / (ms_total * 1e-3) / wl.unit_scale
     peak, hbm, peak_kind = measured_peaks()
-    achieved = wl.flops_dominant / (dom_ms * 1e-3) / 1e12
+    achieved = wl.flops_dominant / (dom_ms * 1e-3) / wl.unit_scale
     traffic = profiled_traffic(args.workload)
 
     # ---------------- output gather (N > 1), timed separately ----------------
@@ -648,8 +760,8 @@ def main():
         torch.cuda.synchronize()
         barrier()
         ems = max_over_ranks(e0.elapsed_time(e1))
-        e2e = {"value": round(wl.flops_per_step * world * Ke / (ems * 1e-3) / 1e12, 3),
-               "unit": "TFLOP/s", "h2d_bytes_per_step": int(wl.h2d), "d2h_bytes_per_step": int(wl.d2h),
+        e2e = {"value": round(wl.flops_per_step * world * Ke / (ems * 1e-3) / wl.unit_scale, 3),
+               "unit": wl.unit, "h2d_bytes_per_step": int(wl.h2d), "d2h_bytes_per_step": int(wl.d2h),
                "steps": Ke, "path": "pinned host -> cudaMemcpyAsync -> C ABI -> cudaMemcpyAsync -> host"}
 
     # ---------------- CPU baseline (rank 0, N == 1) ----------------
@@ -657,22 +769,24 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             v, desc, threads = cpu_reference_sample(args.workload)
-            cpu = {"value": round(v, 6), "unit": "TFLOP/s", "cores": threads, "kind": "reference",
+            cpu = {"value": round(v, 6), "unit": wl.unit, "cores": threads, "kind": "reference",
                    "sample": desc}
         except Exception as ex:  # the GPU number stands without it
-            cpu = {"value": None, "unit": "TFLOP/s", "cores": None, "kind": "reference",
+            cpu = {"value": None, "unit": wl.unit, "cores": None, "kind": "reference",
                    "sample": f"unavailable: {ex}"}
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": round(tflops_total, 3), "unit": "TFLOP/s",
+            "metric": METRIC if wl.unit == "TFLOP/s" else ROWS_METRIC,
+            "value": round(tflops_total, 3), "unit": wl.unit,
             "n_gpus": world, "steps": K, "warmup": args.warmup,
             "ms_per_step": round(ms_total / K, 5), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16" if args.workload != "attn_fp32" else "f32",
+            "vs_baseline": None, "dtype": "f32" if args.workload == "attn_fp32" else wl.dtype,
             "data": "synthetic (seeded; config shapes and distributions)",
             "config": describe(args.workload, world, wl.config.get("l2")),
-            "pct_of_dense_bf16_peak_2250": round(100 * tflops_total / world / 2250.0, 2),
             "roofline": roofline(wl, achieved, peak, peak_kind, traffic),
+            **({"pct_of_dense_bf16_peak_2250": round(100 * tflops_total / world / 2250.0, 2)}
+               if wl.unit == "TFLOP/s" else {}),
             "clocks": clocks,
             "e2e": e2e,
             "gpu_launches": K * wl.launches_per_step,

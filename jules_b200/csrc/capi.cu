@@ -10,6 +10,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <type_traits>
 
 #include "../../include/jules_kernels.h"
 #include "attn_tc.cuh"
@@ -354,6 +355,37 @@ int attn_tc(const void* Q, const void* K, const void* V, void* O, float* lse, in
 // ===========================================================================
 namespace {
 
+// Register-resident CTA-per-row softmax when the types match, rows are
+// 16-byte aligned and a row fits THREADS x NV vectors; returns false when it
+// does not apply.
+template <int THREADS, int NV, typename T, bool XENT>
+void rows_reg_go(const T* x, T* y, const int32_t* targets, float* loss, int64_t M, int64_t N,
+                 float inv_M, int sms, cudaStream_t st) {
+  int64_t blocks = M;
+  const int64_t cap = (int64_t)sms * (2048 / THREADS);
+  if (blocks > cap) blocks = cap;
+  jb::rows::softmax_reg_kernel<THREADS, NV, T, XENT>
+      <<<(unsigned)blocks, THREADS, 0, st>>>(x, y, targets, loss, M, (int)N, inv_M);
+}
+
+template <typename TIn, typename TOut, bool XENT>
+bool rows_reg_launch(const TIn* x, TOut* y, const int32_t* targets, float* loss, int64_t M,
+                     int64_t N, float inv_M, int sms, cudaStream_t st) {
+  if constexpr (!std::is_same<TIn, TOut>::value) {
+    return false;
+  } else {
+    constexpr int E = jb::rows::Vec16<TIn>::kN;
+    if (N % E || !aligned16(x) || (y && !aligned16(y)) || (N * sizeof(TIn)) % 16) return false;
+    if (N <= 256 * 4 * E) rows_reg_go<256, 4, TIn, XENT>(x, y, targets, loss, M, N, inv_M, sms, st);
+    else if (N <= 512 * 4 * E) rows_reg_go<512, 4, TIn, XENT>(x, y, targets, loss, M, N, inv_M, sms, st);
+    else if (N <= 1024 * 4 * E) rows_reg_go<1024, 4, TIn, XENT>(x, y, targets, loss, M, N, inv_M, sms, st);
+    else if (E == 4 && N <= 1024 * 8 * E)  // 8 vectors of bf16 would spill at 1024 threads
+      rows_reg_go<1024, (E == 4 ? 8 : 4), TIn, XENT>(x, y, targets, loss, M, N, inv_M, sms, st);
+    else return false;
+    return true;
+  }
+}
+
 // Row softmax / fused cross-entropy launcher: one warp per row up to
 // kWarpRowMax columns, one CTA per row beyond.  Grids are capped at a few
 // waves of resident blocks; the kernels stride over rows.
@@ -371,7 +403,7 @@ int rows_launch(const void* in, void* out, const int32_t* targets, float* loss, 
     if (blocks > cap) blocks = cap;
     jb::rows::softmax_warp_kernel<TIn, TOut, XENT>
         <<<(unsigned)blocks, 256, 0, st>>>(x, y, targets, loss, M, (int)N, inv_M);
-  } else {
+  } else if (!rows_reg_launch<TIn, TOut, XENT>(x, y, targets, loss, M, N, inv_M, device_sms(dev), st)) {
     int64_t blocks = M;
     const int64_t cap = (int64_t)device_sms(dev) * 8;
     if (blocks > cap) blocks = cap;

@@ -8,9 +8,11 @@
 // mean of the row losses.  Arithmetic is fp32 whatever the storage type.
 //
 // Rows of up to kWarpRowMax elements are held in one warp's registers (one
-// read, one write).  Longer rows take one CTA each: an online pass keeps a
-// running (max, sum) per thread and merges them, a second pass (served mostly
-// by L2, the row was just read) writes the output.
+// read, one write).  Longer rows take one CTA each: with 16-byte aligned rows
+// of up to 32K fp32 / 64K bf16 elements the row stays in the CTA's registers
+// (softmax_reg_kernel: one vectorised read, one write); otherwise an online
+// pass keeps a running (max, sum) per thread and merges them, and a second
+// pass (served mostly by L2, the row was just read) writes the output.
 #pragma once
 
 #include <cstdint>
@@ -169,6 +171,137 @@ __global__ void __launch_bounds__(kCtaThreads) softmax_cta_kernel(const TIn* __r
     }
     if (XENT && threadIdx.x == 0 && tv) {
       const float p = expf(to_f32(x[t]) - m) * inv;
+      loss_acc += -logf(p + 1e-10f) * inv_M;
+    }
+  }
+  if (XENT && threadIdx.x == 0 && loss_acc != 0.0f) atomicAdd(loss, loss_acc);
+}
+
+// 16-byte vectors: 4 floats or 8 bf16.
+template <typename T>
+struct Vec16;
+template <>
+struct Vec16<float> {
+  static constexpr int kN = 4;
+  __device__ __forceinline__ static void load(const float* p, float (&f)[4]) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(p));
+    f[0] = v.x; f[1] = v.y; f[2] = v.z; f[3] = v.w;
+  }
+  __device__ __forceinline__ static void store(float* p, const float (&f)[4]) {
+    *reinterpret_cast<float4*>(p) = make_float4(f[0], f[1], f[2], f[3]);
+  }
+};
+template <>
+struct Vec16<__nv_bfloat16> {
+  static constexpr int kN = 8;
+  __device__ __forceinline__ static void load(const __nv_bfloat16* p, float (&f)[8]) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+  __device__ __forceinline__ static void store(__nv_bfloat16* p, const float (&f)[8]) {
+    uint4 v;
+    v.x = pack_bf16x2(f[0], f[1]);
+    v.y = pack_bf16x2(f[2], f[3]);
+    v.z = pack_bf16x2(f[4], f[5]);
+    v.w = pack_bf16x2(f[6], f[7]);
+    *reinterpret_cast<uint4*>(p) = v;
+  }
+};
+
+// Block-wide max / sum over THREADS threads (smem scratch of THREADS/32).
+template <int THREADS>
+__device__ __forceinline__ float block_max(float v, float* red) {
+  v = warp_max(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = red[0];
+#pragma unroll
+  for (int w = 1; w < THREADS / 32; ++w) t = fmaxf(t, red[w]);
+  return t;
+}
+template <int THREADS>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = red[0];
+#pragma unroll
+  for (int w = 1; w < THREADS / 32; ++w) t += red[w];
+  return t;
+}
+
+// One CTA per row with the row held in registers: NV 16-byte vectors per
+// thread, so rows of up to THREADS * NV * Vec16<T>::kN elements take one
+// vectorised read and one vectorised write.  Needs N to be a multiple of the
+// vector width and 16-byte aligned rows; input and output share the type.
+template <int THREADS, int NV, typename T, bool XENT>
+__global__ void __launch_bounds__(THREADS) softmax_reg_kernel(const T* __restrict__ in,
+                                                              T* __restrict__ out,
+                                                              const int32_t* __restrict__ targets,
+                                                              float* __restrict__ loss, int64_t M,
+                                                              int N, float inv_M) {
+  constexpr int E = Vec16<T>::kN;
+  __shared__ float red[THREADS / 32];
+  float loss_acc = 0.0f;
+  const int nvec = N / E;
+  for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
+    const T* x = in + row * N;
+    float f[NV][E];
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int vi = threadIdx.x + k * THREADS;
+      if (vi < nvec) {
+        Vec16<T>::load(x + (size_t)vi * E, f[k]);
+#pragma unroll
+        for (int e = 0; e < E; ++e) m = fmaxf(m, f[k][e]);
+      }
+    }
+    m = block_max<THREADS>(m, red);
+    float sum = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int vi = threadIdx.x + k * THREADS;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        f[k][e] = (vi < nvec) ? __expf(f[k][e] - m) : 0.0f;
+        sum += f[k][e];
+      }
+    }
+    sum = block_sum<THREADS>(sum, red);
+    const float inv = 1.0f / sum;
+    int t = -1;
+    bool tv = false;
+    if (XENT) {
+      t = targets[row];
+      tv = t >= 0 && t < N;
+      if (threadIdx.x == 0 && !target_ok(t, N)) tv = false;
+    }
+    if (!XENT || out) {
+      T* y = out + row * N;
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        const int vi = threadIdx.x + k * THREADS;
+        if (vi < nvec) {
+          float o[E];
+#pragma unroll
+          for (int e = 0; e < E; ++e) {
+            const float p = f[k][e] * inv;
+            o[e] = XENT ? (p - (vi * E + e == t ? 1.0f : 0.0f)) * inv_M : p;
+          }
+          Vec16<T>::store(y + (size_t)vi * E, o);
+        }
+      }
+    }
+    if (XENT && threadIdx.x == 0 && tv) {
+      const float p = __expf(to_f32(x[t]) - m) * inv;
       loss_acc += -logf(p + 1e-10f) * inv_M;
     }
   }

@@ -154,9 +154,10 @@ void orc_gemm_bias_act(const float* A, const float* B, const float* bias,
 /* Optional outputs: per-row mean and inv_std.                          */
 /* ------------------------------------------------------------------ */
 /*
- * Row softmax.  FusedKernels.h:464-526 (the scalar branch :507-525): max over
- * the row (from -FLT_MAX), e = exp(x - max) stored and summed in column
- * order, then each e divided by the sum.
+ * Row softmax.  FusedKernels.h:464-526, in the summation order of its
+ * AVX-512 branch (:466-505): max over the row (from -FLT_MAX); e = exp(x -
+ * max) stored and summed in 16 lanes over 16-wide chunks, the lanes reduced,
+ * then the scalar tail added; each e multiplied by 1/sum (the tail divided).
  */
 void orc_softmax(float* out, const float* in, int64_t M, int64_t N) {
 #pragma omp parallel for schedule(static)
@@ -165,12 +166,25 @@ void orc_softmax(float* out, const float* in, int64_t M, int64_t N) {
     float* y = out + i * N;
     float mx = -FLT_MAX;
     for (int64_t j = 0; j < N; j++) mx = fmaxf(mx, x[j]);
-    float sum = 0.0f;
-    for (int64_t j = 0; j < N; j++) {
+    float lane[16] = {0};
+    int64_t j = 0;
+    for (; j + 15 < N; j += 16)
+      for (int l = 0; l < 16; l++) {
+        y[j + l] = expf(x[j + l] - mx);
+        lane[l] += y[j + l];
+      }
+    /* lane reduction as a halving tree */
+    for (int w = 8; w > 0; w >>= 1)
+      for (int l = 0; l < w; l++) lane[l] += lane[l + w];
+    float sum = lane[0];
+    const int64_t vec_end = j;
+    for (; j < N; j++) {
       y[j] = expf(x[j] - mx);
       sum += y[j];
     }
-    for (int64_t j = 0; j < N; j++) y[j] /= sum;
+    const float inv = 1.0f / sum;
+    for (j = 0; j < vec_end; j++) y[j] *= inv;
+    for (; j < N; j++) y[j] /= sum;
   }
 }
 

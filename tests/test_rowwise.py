@@ -9,9 +9,11 @@ from helpers import to_dev, to_np
 
 pytestmark = pytest.mark.gpu
 
-# warp-per-row path (N <= 1024), its edge, and the CTA-per-row path
+# warp-per-row path (N <= 1024), the register-resident CTA path at each of its
+# sizes (N a multiple of the vector width), and the two-pass CTA path
+# (ragged N, or N beyond 32K fp32)
 SHAPES = [(64, 256), (64, 10), (2048, 2048), (7, 1000), (5, 1024), (5, 1025), (3, 5000),
-          (2, 70000), (1, 1), (300, 1)]
+          (4, 8192), (4, 16384), (4, 32768), (2, 70000), (1, 1), (300, 1)]
 
 
 def _logits(M, N, seed, scale=3.0):
@@ -31,7 +33,7 @@ def test_softmax_fp32_vs_reference(jb, ref, M, N):
     assert np.allclose(to_np(got).sum(axis=1), 1.0, atol=1e-5)
 
 
-@pytest.mark.parametrize("M,N", [(64, 256), (7, 1000), (3, 5000)])
+@pytest.mark.parametrize("M,N", [(64, 256), (7, 1000), (3, 5000), (4, 32768), (2, 40000)])
 def test_softmax_bf16(jb, orc, M, N):
     import torch
     x = to_dev(_logits(M, N, seed=N), "bf16")
@@ -44,11 +46,13 @@ def test_softmax_bf16(jb, orc, M, N):
     assert rel_l2(to_np(got32), want) <= F32_REL_L2  # bf16 in, fp32 arithmetic and out
     assert max_abs(to_np(got16), want) <= BF16_MAX_ABS
     assert rel_l2(to_np(got16), want) <= BF16_REL_L2
-    assert torch.equal(got16, got32.to(torch.bfloat16))
+    # the bf16 output is the fp32 result rounded once (the two outputs may come
+    # from different kernels, so allow the rounding of a 1-ulp fp32 difference)
+    assert bool(((got16.float() - got32).abs() <= got32.abs() * 2.0 ** -8).all())
 
 
 @pytest.mark.parametrize("M,N", [(64, 10), (64, 1000), (13, 37), (5, 3000), (2, 50257),
-                                 (300, 1024)])
+                                 (300, 1024), (8, 32768), (3, 40000)])
 def test_cross_entropy_fp32_vs_reference(jb, ref, M, N):
     import torch
     x = _logits(M, N, seed=M + 7 * N)
