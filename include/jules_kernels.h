@@ -113,7 +113,8 @@ int jules_flash_attention_fwd(const void* Q, const void* K, const void* V, void*
 /*
  * Row LayerNorm: out = (x - mean) * inv_std * gamma + beta, biased variance,
  * inv_std = 1/sqrt(var + eps).  in [M,N], gamma/beta [N] fp32, optional
- * mean_out / rstd_out [M] fp32.
+ * mean_out / rstd_out [M] fp32.  gamma and beta may both be NULL (no affine
+ * transform, the form KernelRoutingPass routes).
  * Replaces fusedLayerNorm (FusedKernels.h:532-600).
  */
 int jules_layernorm(const void* in, const float* gamma, const float* beta, void* out, int64_t M,
@@ -187,6 +188,41 @@ int jules_mlp_block_noalloc(const void* X, const float* gamma, const float* beta
                             const float* b1, const void* W2, const float* b2, void* out,
                             int out_dtype, int64_t T, int64_t d, int64_t dff, float eps,
                             void* stream);
+
+/*
+ * Custom-call entry: runs the kernel registered under `name` on the buffers a
+ * runtime's custom-call handler receives (the jules.extern_kernel ->
+ * stablehlo.custom_call call_target_name route, StableHLOLowering.cpp:
+ * 1175-1214), inputs first, then outputs.  Shapes and scalars travel in the
+ * opaque bytes as one jules_call_desc (opaque_len == sizeof).  Allocates
+ * nothing (the MLP block runs as jules_mlp_block_noalloc).  Buffers per name:
+ *   fusedMatmul{Relu,Sigmoid,Tanh,Gelu}   A, W, C          dims {M, N, K}
+ *   fusedMatmulBias{Relu,Sigmoid,Tanh,Gelu} A, W, bias(f32), C   dims {M, N, K}
+ *       dtype F32 or BF16 (operands); flags bit 0: C is fp32 for bf16 operands
+ *   blasMatmul      A, B, C (f32)   dims {M, N, K}, fparams {alpha, beta},
+ *                   flags bit 0 transA, bit 1 transB (dense row-major)
+ *   fusedLayerNorm  x, out  or  x, gamma, beta, out   dims {M, N}, fparams[0]
+ *                   eps (0 means 1e-5)
+ *   fusedGelu       x, out          dims {n}
+ *   fusedSoftmax    x, out          dims {M, N}
+ *   fusedCrossEntropyLoss  logits, targets(int32), [grad,] loss(f32 scalar)
+ *                   dims {M, N}
+ *   flashAttention  Q, K, V, O [, lse]   dims {B, Hq, Hkv, S, D},
+ *                   fparams[0] scale (0 means 1/sqrt(D)), flags bit 0 causal
+ *   fusedMLPForward X, gamma, beta, W1, b1, W2, b2, out   dims {T, d, dff},
+ *                   fparams[0] eps (0 means 1e-5), flags bit 0: out is fp32
+ * A registered name without an implementation returns JULES_ERR_UNSUPPORTED;
+ * an unknown name, a wrong buffer count or opaque size JULES_ERR_ARG.
+ */
+typedef struct jules_call_desc {
+  int64_t dims[6];
+  float fparams[2];
+  int32_t dtype; /* JULES_DTYPE_* of the floating-point operands */
+  int32_t flags;
+} jules_call_desc;
+
+int jules_custom_call(const char* name, void* stream, void** buffers, int n_buffers,
+                      const void* opaque, size_t opaque_len);
 
 /*
  * Kernel registry keyed by the jules.extern_kernel names that

@@ -50,11 +50,20 @@ _SIGNATURES = {
     "jules_mlp_block_workspace_bytes": ([_c_i64, _c_i64, _c_i64], ctypes.c_size_t),
     "jules_mlp_block": ([_c_vp] * 8 + [_c_int, _c_i64, _c_i64, _c_i64, _c_f, _c_vp,
                                        ctypes.c_size_t, _c_vp], _c_int),
+    "jules_custom_call": ([ctypes.c_char_p, _c_vp, ctypes.POINTER(_c_vp), _c_int, _c_vp,
+                           ctypes.c_size_t], _c_int),
     "jules_kernel_by_name": ([ctypes.c_char_p], _c_int),
     "jules_kernel_name": ([_c_int], ctypes.c_char_p),
     "jules_kernel_count": ([], _c_int),
     "jules_kernel_implemented": ([_c_int], _c_int),
 }
+
+
+class CallDesc(ctypes.Structure):
+    """jules_call_desc (include/jules_kernels.h): shapes and scalars of a
+    custom call, passed as the opaque bytes."""
+    _fields_ = [("dims", ctypes.c_int64 * 6), ("fparams", ctypes.c_float * 2),
+                ("dtype", ctypes.c_int32), ("flags", ctypes.c_int32)]
 
 
 class JulesError(RuntimeError):
@@ -233,6 +242,25 @@ def cross_entropy_loss(logits, targets, grad=True, stream=None):
                                         _ptr(loss), M, N, _dtype_code(logits), _stream(stream))
     _check(rc, "jules_cross_entropy_loss")
     return loss, g
+
+
+def custom_call(name, buffers, dims=(), fparams=(), dtype=DT_BF16, flags=0, stream=None, check=True):
+    """Run a registered kernel the way a runtime's custom-call handler does:
+    a name, device buffers (tensors or raw addresses, inputs then outputs) and
+    one CallDesc as the opaque bytes.  Returns the status code."""
+    d = CallDesc()
+    for i, v in enumerate(dims):
+        d.dims[i] = int(v)
+    for i, v in enumerate(fparams):
+        d.fparams[i] = float(v)
+    d.dtype, d.flags = int(dtype), int(flags)
+    arr = (_c_vp * max(1, len(buffers)))(
+        *[b if isinstance(b, int) or b is None else b.data_ptr() for b in buffers])
+    rc = lib().jules_custom_call(name.encode(), _stream(stream), arr, len(buffers),
+                                 ctypes.cast(ctypes.pointer(d), _c_vp), ctypes.sizeof(d))
+    if check:
+        _check(rc, f"jules_custom_call({name})")
+    return rc
 
 
 def mlp_block_workspace_bytes(T, d, dff) -> int:

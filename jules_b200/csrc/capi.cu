@@ -10,6 +10,8 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <string>
+#include <utility>
 #include <type_traits>
 
 #include "../../include/jules_kernels.h"
@@ -521,7 +523,7 @@ int jules_flash_attention_fwd(const void* Q, const void* K, const void* V, void*
 int jules_layernorm(const void* in, const float* gamma, const float* beta, void* out, int64_t M,
                     int64_t N, float eps, int in_dtype, int out_dtype, float* mean_out,
                     float* rstd_out, void* stream) {
-  if (!in || !gamma || !beta || !out) return fail(JULES_ERR_ARG, "layernorm: NULL pointer");
+  if (!in || !out || (!gamma != !beta)) return fail(JULES_ERR_ARG, "layernorm: NULL pointer");
   if (M < 0 || N <= 0 || M > INT32_MAX) return fail(JULES_ERR_SHAPE, "layernorm: M=%lld N=%lld", (long long)M, (long long)N);
   if (M == 0) return ok();
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -529,8 +531,8 @@ int jules_layernorm(const void* in, const float* gamma, const float* beta, void*
   if ((in_dtype != JULES_DTYPE_F32 && !in_bf) || (out_dtype != JULES_DTYPE_F32 && !out_bf))
     return fail(JULES_ERR_DTYPE, "layernorm: dtypes %d/%d", in_dtype, out_dtype);
   const unsigned grid = (unsigned)M;
-  if (in_bf && out_bf && N % 8 == 0 && N <= 8 * 256 * 4 && aligned16(in) && aligned16(out) &&
-      aligned16(gamma) && aligned16(beta)) {
+  if (in_bf && out_bf && gamma && N % 8 == 0 && N <= 8 * 256 * 4 && aligned16(in) &&
+      aligned16(out) && aligned16(gamma) && aligned16(beta)) {
     jb::simt::layernorm_bf16_vec_kernel<4><<<grid, 256, 0, st>>>(
         static_cast<const __nv_bfloat16*>(in), gamma, beta, static_cast<__nv_bfloat16*>(out),
         mean_out, rstd_out, M, (int)N, eps);
@@ -597,6 +599,85 @@ int jules_cross_entropy_loss(const void* logits, const int32_t* targets, void* g
   if (dtype == JULES_DTYPE_F32)
     return rows_launch<float, float, true>(logits, grad, targets, loss, M, N, st);
   return rows_launch<__nv_bfloat16, __nv_bfloat16, true>(logits, grad, targets, loss, M, N, st);
+}
+
+int jules_custom_call(const char* name, void* stream, void** buffers, int n_buffers,
+                      const void* opaque, size_t opaque_len) {
+  const int id = jules_kernel_by_name(name);
+  if (id < 0) return fail(JULES_ERR_ARG, "custom_call: unknown kernel name");
+  if (!jules_kernel_implemented(id)) return fail(JULES_ERR_UNSUPPORTED, "custom_call: kernel not implemented");
+  if (!opaque || opaque_len != sizeof(jules_call_desc))
+    return fail(JULES_ERR_ARG, "custom_call: opaque must be one jules_call_desc");
+  if (!buffers || n_buffers <= 0) return fail(JULES_ERR_ARG, "custom_call: no buffers");
+  jules_call_desc d;
+  std::memcpy(&d, opaque, sizeof(d));
+  const std::string n(name);
+  auto need = [&](int a, int b = -1) { return n_buffers == a || n_buffers == b; };
+  void** B = buffers;
+  // fusedMatmul<Act> / fusedMatmulBias<Act>
+  static const std::pair<const char*, int> kActs[] = {
+      {"Relu", JULES_ACT_RELU}, {"Sigmoid", JULES_ACT_SIGMOID}, {"Tanh", JULES_ACT_TANH},
+      {"Gelu", JULES_ACT_GELU}};
+  for (const auto& a : kActs) {
+    const bool plain = n == std::string("fusedMatmul") + a.first;
+    const bool bias = n == std::string("fusedMatmulBias") + a.first;
+    if (!plain && !bias) continue;
+    if (!need(bias ? 4 : 3)) return fail(JULES_ERR_ARG, "custom_call: matmul buffer count");
+    const int out_dt = (d.dtype == JULES_DTYPE_BF16 && (d.flags & 1)) ? JULES_DTYPE_F32 : d.dtype;
+    return jules_gemm_bias_act(B[0], B[1], bias ? static_cast<const float*>(B[2]) : nullptr,
+                               nullptr, B[bias ? 3 : 2], d.dims[0], d.dims[1], d.dims[2], a.second,
+                               d.dtype, out_dt, stream);
+  }
+  if (n == "blasMatmul") {
+    if (!need(3)) return fail(JULES_ERR_ARG, "custom_call: blasMatmul buffer count");
+    const int64_t M = d.dims[0], N = d.dims[1], K = d.dims[2];
+    const int ta = d.flags & 1, tb = (d.flags >> 1) & 1;
+    return jules_sgemm(ta, tb, M, N, K, d.fparams[0], static_cast<const float*>(B[0]), ta ? M : K,
+                       static_cast<const float*>(B[1]), tb ? K : N, d.fparams[1],
+                       static_cast<float*>(B[2]), N, stream);
+  }
+  if (n == "fusedLayerNorm") {
+    if (!need(2, 4)) return fail(JULES_ERR_ARG, "custom_call: fusedLayerNorm buffer count");
+    const bool affine = n_buffers == 4;
+    const float eps = d.fparams[0] > 0.0f ? d.fparams[0] : 1e-5f;
+    return jules_layernorm(B[0], affine ? static_cast<const float*>(B[1]) : nullptr,
+                           affine ? static_cast<const float*>(B[2]) : nullptr, B[affine ? 3 : 1],
+                           d.dims[0], d.dims[1], eps, d.dtype, d.dtype, nullptr, nullptr, stream);
+  }
+  if (n == "fusedGelu") {
+    if (!need(2)) return fail(JULES_ERR_ARG, "custom_call: fusedGelu buffer count");
+    return jules_gelu(B[0], B[1], d.dims[0], d.dtype, stream);
+  }
+  if (n == "fusedSoftmax") {
+    if (!need(2)) return fail(JULES_ERR_ARG, "custom_call: fusedSoftmax buffer count");
+    return jules_softmax(B[0], B[1], d.dims[0], d.dims[1], d.dtype, d.dtype, stream);
+  }
+  if (n == "fusedCrossEntropyLoss") {
+    if (!need(3, 4)) return fail(JULES_ERR_ARG, "custom_call: fusedCrossEntropyLoss buffer count");
+    const bool grad = n_buffers == 4;
+    return jules_cross_entropy_loss(B[0], static_cast<const int32_t*>(B[1]), grad ? B[2] : nullptr,
+                                    static_cast<float*>(B[grad ? 3 : 2]), d.dims[0], d.dims[1],
+                                    d.dtype, stream);
+  }
+  if (n == "flashAttention") {
+    if (!need(4, 5)) return fail(JULES_ERR_ARG, "custom_call: flashAttention buffer count");
+    return jules_flash_attention_fwd(B[0], B[1], B[2], B[3],
+                                     n_buffers == 5 ? static_cast<float*>(B[4]) : nullptr,
+                                     (int)d.dims[0], (int)d.dims[1], (int)d.dims[2],
+                                     (int)d.dims[3], (int)d.dims[4], d.fparams[0], d.flags & 1,
+                                     d.dtype, stream);
+  }
+  if (n == "fusedMLPForward") {
+    if (!need(8)) return fail(JULES_ERR_ARG, "custom_call: fusedMLPForward buffer count");
+    const float eps = d.fparams[0] > 0.0f ? d.fparams[0] : 1e-5f;
+    return jules_mlp_block_noalloc(B[0], static_cast<const float*>(B[1]),
+                                   static_cast<const float*>(B[2]), B[3],
+                                   static_cast<const float*>(B[4]), B[5],
+                                   static_cast<const float*>(B[6]), B[7],
+                                   (d.flags & 1) ? JULES_DTYPE_F32 : JULES_DTYPE_BF16, d.dims[0],
+                                   d.dims[1], d.dims[2], eps, stream);
+  }
+  return fail(JULES_ERR_UNSUPPORTED, "custom_call: no dispatch for this name");
 }
 
 size_t jules_mlp_block_workspace_bytes(int64_t T, int64_t d, int64_t dff) {

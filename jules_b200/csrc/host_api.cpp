@@ -363,4 +363,5 @@ int jules_kernel_implemented(int id) {
   return (id >= 0 && id < kNumKernels) ? kKernels[id].implemented : 0;
 }
 
+
 }  // extern "C"

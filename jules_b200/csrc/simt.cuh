@@ -318,8 +318,10 @@ __global__ void __launch_bounds__(256)
   const float var = block_sum_256(v, red) / (float)N;
   const float inv_std = 1.0f / sqrtf(var + eps);
   TOut* y = out + row * N;
+  // gamma == beta == NULL: no affine transform (the routed fusedLayerNorm form)
   for (int64_t j = threadIdx.x; j < N; j += 256)
-    y[j] = from_f32<TOut>((to_f32(x[j]) - mean) * inv_std * gamma[j] + beta[j]);
+    y[j] = from_f32<TOut>((to_f32(x[j]) - mean) * inv_std * (gamma ? gamma[j] : 1.0f) +
+                          (beta ? beta[j] : 0.0f));
   if (threadIdx.x == 0) {
     if (mean_out) mean_out[row] = mean;
     if (rstd_out) rstd_out[row] = inv_std;
