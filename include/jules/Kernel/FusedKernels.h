@@ -65,6 +65,14 @@ void fusedSoftmax(float* output, const float* input, int M, int N);
 // reference).
 float fusedCrossEntropyLoss(const float* logits, const int32_t* targets, float* grad, int M, int N);
 
+class ExecutionArena;
+
+// int8 GEMM with int32 accumulation: C = float(A . B) * scale_A * scale_B
+// (+ bias per column).  FusedKernels.h:867-1073 (the arena held the int32
+// accumulator there; here it is unused and may be null).
+void matmulInt8(const int8_t* A, const int8_t* B, float* C, int M, int N, int K, float scale_A,
+                float scale_B, const float* bias = nullptr, ExecutionArena* arena = nullptr);
+
 // Row-major SGEMM, C = alpha op(A) op(B) + beta C.  FusedKernels.h:633-644.
 void blasMatmul(const float* A, const float* B, float* C, int M, int N, int K, float alpha = 1.0f,
                 float beta = 0.0f, bool transA = false, bool transB = false);

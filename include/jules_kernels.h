@@ -128,6 +128,17 @@ int jules_layernorm(const void* in, const float* gamma, const float* beta, void*
 int jules_gelu(const void* in, void* out, int64_t n, int dtype, void* stream);
 
 /*
+ * int8 GEMM: C = float(A . B) * (scale_a * scale_b) (+ bias), int32
+ * accumulation.  A [M,K], B [K,N] int8 row-major; C [M,N] and bias [N]
+ * (nullable) fp32.  K and N multiples of 16 with 16-byte aligned pointers run
+ * on tcgen05 (kind::i8); other shapes on CUDA cores.
+ * Replaces matmulInt8 (FusedKernels.h:867-1073), whose int32 product is the
+ * one its scalar branch (:1046-1057) computes.
+ */
+int jules_matmul_int8(const int8_t* A, const int8_t* B, float* C, int64_t M, int64_t N,
+                      int64_t K, float scale_a, float scale_b, const float* bias, void* stream);
+
+/*
  * Row softmax: out[i,:] = exp(x[i,:] - max_i) / sum_j exp(x[i,j] - max_i),
  * in/out [M,N] row-major, fp32 arithmetic.  in_dtype and out_dtype each F32
  * or BF16.
@@ -211,6 +222,7 @@ int jules_mlp_block_noalloc(const void* X, const float* gamma, const float* beta
  *                   fparams[0] scale (0 means 1/sqrt(D)), flags bit 0 causal
  *   fusedMLPForward X, gamma, beta, W1, b1, W2, b2, out   dims {T, d, dff},
  *                   fparams[0] eps (0 means 1e-5), flags bit 0: out is fp32
+ *   matmulInt8      A, B [, bias], C   dims {M, N, K}, fparams {scale_a, scale_b}
  * A registered name without an implementation returns JULES_ERR_UNSUPPORTED;
  * an unknown name, a wrong buffer count or opaque size JULES_ERR_ARG.
  */

@@ -45,6 +45,8 @@ _SIGNATURES = {
                          _c_vp, _c_vp], _c_int),
     "jules_gelu": ([_c_vp, _c_vp, _c_i64, _c_int, _c_vp], _c_int),
     "jules_softmax": ([_c_vp, _c_vp, _c_i64, _c_i64, _c_int, _c_int, _c_vp], _c_int),
+    "jules_matmul_int8": ([_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_f, _c_f, _c_vp, _c_vp],
+                          _c_int),
     "jules_cross_entropy_loss": ([_c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_int, _c_vp],
                                  _c_int),
     "jules_mlp_block_workspace_bytes": ([_c_i64, _c_i64, _c_i64], ctypes.c_size_t),
@@ -208,6 +210,24 @@ def gelu(x, out=None, stream=None):
         out = torch.empty_like(x)
     rc = lib().jules_gelu(_ptr(x), _ptr(out), x.numel(), _dtype_code(x), _stream(stream))
     _check(rc, "jules_gelu")
+    return out
+
+
+def matmul_int8(A, B, scale_a=1.0, scale_b=1.0, bias=None, out=None, stream=None):
+    """C = float(A @ B) * scale_a * scale_b (+ bias); A [M,K], B [K,N] int8,
+    int32 accumulation, fp32 C."""
+    import torch
+    for t, n in ((A, "A"), (B, "B")):
+        _dense(t, n)
+        if t.dtype != torch.int8:
+            raise ValueError(f"matmul_int8: {n} must be int8")
+    M, K = A.shape
+    N = B.shape[1]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=A.device)
+    rc = lib().jules_matmul_int8(_ptr(A), _ptr(B), _ptr(out), M, N, K, scale_a, scale_b,
+                                 _ptr(bias), _stream(stream))
+    _check(rc, "jules_matmul_int8")
     return out
 
 

@@ -17,6 +17,7 @@
 #include "../../include/jules_kernels.h"
 #include "attn_tc.cuh"
 #include "gemm_tc.cuh"
+#include "gemm_i8.cuh"
 #include "sm100.cuh"
 #include "simt.cuh"
 #include "rowwise.cuh"
@@ -109,6 +110,23 @@ int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t*
                    bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(JULES_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return JULES_OK;
+}
+
+// 2-D int8 tensor map (row-major [rows, cols], cols contiguous), 128-byte
+// swizzle.
+int make_tmap_i8(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows,
+                 uint32_t box_cols, uint32_t box_rows) {
+  auto enc = tmap_encoder();
+  if (!enc) return fail(JULES_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t d[2] = {cols, rows};
+  cuuint64_t st[1] = {cols};
+  cuuint32_t bx[2] = {box_cols, box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), d, st, bx, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(JULES_ERR_CUDA, "cuTensorMapEncodeTiled (int8) failed (%d)", (int)r);
   return JULES_OK;
 }
 
@@ -357,6 +375,37 @@ int attn_tc(const void* Q, const void* K, const void* V, void* O, float* lse, in
 // ===========================================================================
 namespace {
 
+// int8 GEMM: tcgen05 kind::i8 when K and N are multiples of 16 and the
+// pointers 16-byte aligned, CUDA cores otherwise.
+int gemm_s8(const int8_t* A, const int8_t* B, const float* bias, float* C, int64_t M, int64_t N,
+            int64_t K, float scale, cudaStream_t st) {
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  if (K % 16 == 0 && N % 16 == 0 && aligned16(A) && aligned16(B) && aligned16(C) &&
+      (!bias || aligned16(bias))) {
+    constexpr int BN = 256, STAGES = 4;
+    CUtensorMap ta, tb;
+    if (int rc = make_tmap_i8(&ta, A, (uint64_t)K, (uint64_t)M, jb::gemm8::BK, jb::gemm8::BM)) return rc;
+    if (int rc = make_tmap_i8(&tb, B, (uint64_t)N, (uint64_t)K, 128, jb::gemm8::BK)) return rc;
+    auto kern = jb::gemm8::gemm_s8_tc_kernel<BN, STAGES>;
+    const size_t smem = sizeof(jb::gemm8::Smem8<BN, STAGES>) + 1024;
+    static bool attr_set[64] = {};
+    if (!attr_set[dev & 63]) {
+      std::lock_guard<std::mutex> lk(g_dev_mu);
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_s8)");
+      attr_set[dev & 63] = true;
+    }
+    const int64_t tiles = ((M + jb::gemm8::BM - 1) / jb::gemm8::BM) * ((N + BN - 1) / BN);
+    const int grid = (int)(tiles < device_sms(dev) ? tiles : device_sms(dev));
+    kern<<<grid, jb::gemm8::kThreads, smem, st>>>(ta, tb, bias, C, (int)M, (int)N, (int)K, scale);
+    return check_launch("gemm_s8_tc_kernel launch");
+  }
+  dim3 grid((unsigned)((N + 15) / 16), (unsigned)((M + 15) / 16));
+  jb::gemm8::gemm_s8_simt_kernel<<<grid, 256, 0, st>>>(A, B, bias, C, (int)M, (int)N, (int)K, scale);
+  return check_launch("gemm_s8_simt_kernel launch");
+}
+
 // Register-resident CTA-per-row softmax when the types match, rows are
 // 16-byte aligned and a row fits THREADS x NV vectors; returns false when it
 // does not apply.
@@ -573,6 +622,15 @@ int jules_gelu(const void* in, void* out, int64_t n, int dtype, void* stream) {
   return check_launch("gelu launch");
 }
 
+int jules_matmul_int8(const int8_t* A, const int8_t* B, float* C, int64_t M, int64_t N,
+                      int64_t K, float scale_a, float scale_b, const float* bias, void* stream) {
+  if (!A || !B || !C) return fail(JULES_ERR_ARG, "matmul_int8: NULL A, B or C");
+  if (M < 0 || N <= 0 || K <= 0) return fail(JULES_ERR_SHAPE, "matmul_int8: M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail(JULES_ERR_SHAPE, "matmul_int8: dimension exceeds 2^31-1");
+  if (M == 0) return ok();
+  return gemm_s8(A, B, bias, C, M, N, K, scale_a * scale_b, static_cast<cudaStream_t>(stream));
+}
+
 int jules_softmax(const void* in, void* out, int64_t M, int64_t N, int in_dtype, int out_dtype,
                   void* stream) {
   if (!in || !out) return fail(JULES_ERR_ARG, "softmax: NULL pointer");
@@ -635,6 +693,14 @@ int jules_custom_call(const char* name, void* stream, void** buffers, int n_buff
     return jules_sgemm(ta, tb, M, N, K, d.fparams[0], static_cast<const float*>(B[0]), ta ? M : K,
                        static_cast<const float*>(B[1]), tb ? K : N, d.fparams[1],
                        static_cast<float*>(B[2]), N, stream);
+  }
+  if (n == "matmulInt8") {
+    if (!need(3, 4)) return fail(JULES_ERR_ARG, "custom_call: matmulInt8 buffer count");
+    const bool bias = n_buffers == 4;
+    return jules_matmul_int8(static_cast<const int8_t*>(B[0]), static_cast<const int8_t*>(B[1]),
+                             static_cast<float*>(B[bias ? 3 : 2]),
+                             d.dims[0], d.dims[1], d.dims[2], d.fparams[0], d.fparams[1],
+                             bias ? static_cast<const float*>(B[2]) : nullptr, stream);
   }
   if (n == "fusedLayerNorm") {
     if (!need(2, 4)) return fail(JULES_ERR_ARG, "custom_call: fusedLayerNorm buffer count");

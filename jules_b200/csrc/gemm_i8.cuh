@@ -1,0 +1,243 @@
+// int8 GEMM with int32 accumulation on tcgen05 (kind::i8), fp32 epilogue:
+//   C[i,j] = float(sum_k A[i,k] * B[k,j]) * (scale_a * scale_b) (+ bias[j])
+// A [M,K] and B [K,N] row-major int8, C [M,N] fp32.  This is the contract of
+// the reference's matmulInt8 (FusedKernels.h:867-1073): int32 accumulation
+// (its scalar branch :1046-1057), then the scale and the bias per column
+// (:1060-1065).
+//
+// Structure as the bf16 1-CTA GEMM (gemm_tc.cuh): persistent CTAs over
+// 128x256 output tiles in grouped order, warp 0 TMA, warp 1 MMA issuer,
+// warps 2-5 epilogue from one of two TMEM accumulators (2 x 256 s32 columns)
+// while the other accumulates.  A k-block is 128 bytes of K (one 128-byte
+// swizzle row): A as K-major, B read as MN-major (its rows are K), 4 MMA
+// K-steps of 32 int8 each.
+#pragma once
+
+#include "gemm_tc.cuh"
+
+namespace jb {
+namespace gemm8 {
+
+constexpr int BM = 128;
+constexpr int BK = 128;  // int8 elements = bytes per k-block
+constexpr int kThreads = 192;
+
+// Instruction descriptor, kind::i8: s32 D (bits 4-5 = 2), s8 A and B (bits
+// 7-9 and 10-12 = 1), B MN-major (bit 16), N >> 3 at 17, M >> 4 at 24.
+__host__ __device__ constexpr uint32_t idesc_s8_s32(int M, int N, bool b_mn) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((b_mn ? 1u : 0u) << 16) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_i8_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+template <int BN, int STAGES>
+struct Smem8 {
+  static constexpr int kABytes = BM * BK;
+  static constexpr int kBBytes = BK * BN;
+  alignas(1024) uint8_t a[STAGES][kABytes];
+  alignas(1024) uint8_t b[STAGES][kBBytes];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_s8_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+                      const __grid_constant__ CUtensorMap tmB, const float* __restrict__ bias,
+                      float* __restrict__ C, int M, int N, int K, float scale) {
+  static_assert(BN % 128 == 0 && BN <= 256, "BN must be 128 or 256");
+  using S = Smem8<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  S& s = *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (M + BM - 1) / BM;
+  const int num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_k = (K + BK - 1) / BK;
+  constexpr uint32_t kTmemCols = 2 * BN <= 256 ? 256 : 512;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.tfull[i], 1);
+      mbar_init(&s.tempty[i], 128);
+    }
+    s.abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(&s.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = s.tmem_base;
+  volatile int* abort_flag = &s.abort_flag;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int mi, ni;
+        gemm::tile_coords(t, num_m, num_n, mi, ni);
+        const int m0 = mi * BM;
+        const int n0 = ni * BN;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&s.empty[stage], phase ^ 1u, 80, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&s.full[stage], S::kABytes + S::kBBytes);
+          tma_load_2d(s.a[stage], &tmA, &s.full[stage], kb * BK, m0);
+#pragma unroll
+          for (int j = 0; j < BN / 128; ++j)
+            tma_load_2d(s.b[stage] + j * (BK * 128), &tmB, &s.full[stage], n0 + j * 128, kb * BK);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_s8_s32(BM, BN, true);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&s.tempty[acc], acc_phase ^ 1u, 81, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&s.full[stage], phase, 82, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(s.a[stage]);
+          const uint32_t b_base = smem_u32(s.b[stage]);
+#pragma unroll
+          for (int kk = 0; kk < BK / 32; ++kk) {
+            // K-major A: 32 int8 = 32 bytes further along the swizzle row.
+            const uint64_t ad = sdesc_sw128(a_base + kk * 32, 16, 1024);
+            // MN-major B: 32 K-rows of 128 bytes further; 128-column chunks
+            // BK * 128 bytes apart.
+            const uint64_t bd = sdesc_sw128(b_base + kk * 32 * 128, BK * 128, 1024);
+            umma_i8_ss(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&s.empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        umma_commit(&s.tfull[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      int mi, ni;
+      gemm::tile_coords(t, num_m, num_n, mi, ni);
+      const int m0 = mi * BM;
+      const int n0 = ni * BN;
+      if (!mbar_wait(&s.tfull[acc], acc_phase, 83, abort_flag)) break;
+      tc_fence_after();
+      const int row = m0 + row_in_tile;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(t_row + c * 32, r);
+        tmem_ld_wait(r);
+        const int col0 = n0 + c * 32;
+        if (row < M && col0 < N) {
+          float* crow = C + (size_t)row * N;
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int col = col0 + g * 8;
+            if (col < N) {  // N is a multiple of 16 on this path
+              float v[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) v[j] = (float)(int32_t)r[g * 8 + j] * scale;
+              if (bias) {
+                const float4 b0 = *reinterpret_cast<const float4*>(bias + col);
+                const float4 b1 = *reinterpret_cast<const float4*>(bias + col + 4);
+                v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
+                v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
+              }
+              gemm::store8(crow + col, v);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&s.tempty[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+}
+
+// CUDA-core fallback for shapes the tensor-core path does not take (K or N
+// not a multiple of 16, unaligned pointers): 16x16 output tiles, K in
+// chunks of 64 staged through shared memory, exact int32 accumulation.
+__global__ void __launch_bounds__(256) gemm_s8_simt_kernel(const int8_t* __restrict__ A,
+                                                           const int8_t* __restrict__ B,
+                                                           const float* __restrict__ bias,
+                                                           float* __restrict__ C, int M, int N,
+                                                           int K, float scale) {
+  __shared__ int8_t sa[16][64];
+  __shared__ int8_t sb[64][16];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int row = blockIdx.y * 16 + ty, col = blockIdx.x * 16 + tx;
+  int32_t acc = 0;
+  for (int k0 = 0; k0 < K; k0 += 64) {
+    for (int i = threadIdx.x; i < 16 * 64; i += 256) {
+      const int r = i >> 6, kk = i & 63;
+      const int gr = blockIdx.y * 16 + r, gk = k0 + kk;
+      sa[r][kk] = (gr < M && gk < K) ? A[(size_t)gr * K + gk] : (int8_t)0;
+      const int br = i >> 4, bc = i & 15;
+      const int gbk = k0 + br, gbc = blockIdx.x * 16 + bc;
+      sb[br][bc] = (gbk < K && gbc < N) ? B[(size_t)gbk * N + gbc] : (int8_t)0;
+    }
+    __syncthreads();
+#pragma unroll 16
+    for (int kk = 0; kk < 64; ++kk) acc += (int32_t)sa[ty][kk] * (int32_t)sb[kk][tx];
+    __syncthreads();
+  }
+  if (row < M && col < N) {
+    float v = (float)acc * scale;
+    if (bias) v += bias[col];
+    C[(size_t)row * N + col] = v;
+  }
+}
+
+}  // namespace gemm8
+}  // namespace jb

@@ -237,6 +237,24 @@ float fusedCrossEntropyLoss(const float* logits, const int32_t* targets, float* 
   return loss;
 }
 
+void matmulInt8(const int8_t* A, const int8_t* B, float* C, int M, int N, int K, float scale_A,
+                float scale_B, const float* bias, ExecutionArena* /*arena*/) {
+  if (M <= 0 || N <= 0) return;
+  const size_t ba = (size_t)M * K, bb = (size_t)K * N, bc = (size_t)M * N * 4;
+  const size_t sizes[4] = {ba ? ba : 16, bb ? bb : 16, bc, (size_t)N * 4};
+  char* d[4];
+  staging().reserve(sizes, 4, d);
+  h2d(d[0], A, ba);
+  h2d(d[1], B, bb);
+  if (bias) h2d(d[3], bias, (size_t)N * 4);
+  check_status(jules_matmul_int8(reinterpret_cast<const int8_t*>(d[0]),
+                                 reinterpret_cast<const int8_t*>(d[1]),
+                                 reinterpret_cast<float*>(d[2]), M, N, K, scale_A, scale_B,
+                                 bias ? reinterpret_cast<const float*>(d[3]) : nullptr, nullptr),
+               "jules_matmul_int8");
+  d2h(C, d[2], bc);
+}
+
 void blasMatmul(const float* A, const float* B, float* C, int M, int N, int K, float alpha,
                 float beta, bool transA, bool transB) {
   if (M <= 0 || N <= 0) return;
@@ -338,7 +356,7 @@ const KernelEntry kKernels[] = {
     {"fusedMatmulBiasTanh", 1},    {"fusedMatmulBiasGelu", 1},  {"fusedLayerNorm", 1},
     {"fusedGelu", 1},              {"fusedMLPForward", 1},      {"flashAttention", 1},
     {"blasMatmul", 1},             {"fusedSoftmax", 1},         {"fusedCrossEntropyLoss", 1},
-    {"matmulInt8", 0},
+    {"matmulInt8", 1},
 };
 constexpr int kNumKernels = sizeof(kKernels) / sizeof(kKernels[0]);
 

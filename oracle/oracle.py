@@ -48,6 +48,11 @@ def _fp(a: np.ndarray | None):
     return a.ctypes.data_as(_f32p)
 
 
+def _i8(a: np.ndarray):
+    assert a.dtype == np.int8 and a.flags.c_contiguous
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
 def _ip(a: np.ndarray):
     assert a.dtype == np.int32 and a.flags.c_contiguous
     return a.ctypes.data_as(_i32p)
@@ -101,6 +106,9 @@ class Restated:
             ctypes.c_int, ctypes.c_int]
         lib.orc_mlp_block.argtypes = [_f32p] * 8 + [ctypes.c_int64] * 3 + [ctypes.c_float, _i64p,
                                                                           ctypes.c_int64]
+        lib.orc_matmul_int8.argtypes = [ctypes.c_void_p, ctypes.c_void_p, _f32p, ctypes.c_int64,
+                                        ctypes.c_int64, ctypes.c_int64, ctypes.c_float,
+                                        ctypes.c_float, _f32p]
         lib.orc_softmax.argtypes = [_f32p, _f32p, ctypes.c_int64, ctypes.c_int64]
         lib.orc_cross_entropy.argtypes = [_f32p, _i32p, _f32p, ctypes.c_int64, ctypes.c_int64]
         lib.orc_cross_entropy.restype = ctypes.c_float
@@ -137,6 +145,16 @@ class Restated:
         out = np.empty_like(x)
         self.lib.orc_softmax(_fp(out), _fp(x), M, N)
         return out
+
+    def matmul_int8(self, A, B, scale_a=1.0, scale_b=1.0, bias=None):
+        A = np.ascontiguousarray(A, np.int8)
+        B = np.ascontiguousarray(B, np.int8)
+        M, K = A.shape
+        N = B.shape[1]
+        C = np.empty((M, N), np.float32)
+        self.lib.orc_matmul_int8(_i8(A), _i8(B), _fp(C), M, N, K, scale_a, scale_b,
+                                 _fp(None if bias is None else np.ascontiguousarray(bias, np.float32)))
+        return C
 
     def cross_entropy(self, logits, targets):
         """Returns (mean loss, grad)."""
@@ -219,6 +237,8 @@ class Reference:
         lib.ref_fused_gelu.argtypes = [_f32p, _f32p, ctypes.c_int]
         lib.ref_fused_softmax.argtypes = [_f32p, _f32p, ctypes.c_int, ctypes.c_int]
         lib.ref_fused_cross_entropy.argtypes = [_f32p, _i32p, _f32p, ctypes.c_int, ctypes.c_int]
+        lib.ref_matmul_int8.argtypes = [ctypes.c_void_p, ctypes.c_void_p, _f32p] + [ctypes.c_int] * 3 + [
+            ctypes.c_float, ctypes.c_float, _f32p]
         lib.ref_fused_cross_entropy.restype = ctypes.c_float
         lib.ref_blas_matmul.argtypes = [_f32p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_float] * 2 + [
             ctypes.c_int] * 2
@@ -308,6 +328,18 @@ class Reference:
         out = np.empty_like(x)
         self.lib.ref_fused_softmax(_fp(out), _fp(x), M, N)
         return out
+
+    def matmul_int8(self, A, B, scale_a=1.0, scale_b=1.0, bias=None):
+        """The reference's matmulInt8.  Only the "avx2" variant (compiled
+        without AVX-512, so its scalar branch) computes the documented product."""
+        A = np.ascontiguousarray(A, np.int8)
+        B = np.ascontiguousarray(B, np.int8)
+        M, K = A.shape
+        N = B.shape[1]
+        C = np.empty((M, N), np.float32)
+        self.lib.ref_matmul_int8(_i8(A), _i8(B), _fp(C), M, N, K, scale_a, scale_b,
+                                 _fp(None if bias is None else np.ascontiguousarray(bias, np.float32)))
+        return C
 
     def cross_entropy(self, logits, targets):
         """Returns (mean loss, grad) from the reference's fusedCrossEntropyLoss."""

@@ -130,6 +130,13 @@ void ref_fused_softmax(float* out, const float* in, int M, int N) {
   fusedSoftmax(out, in, M, N);
 }
 
+// FusedKernels.h:867-1073.  Only the build without AVX-512 (the scalar
+// branch) computes the documented product; see orc_matmul_int8.
+void ref_matmul_int8(const int8_t* A, const int8_t* B, float* C, int M, int N, int K,
+                     float scale_a, float scale_b, const float* bias) {
+  matmulInt8(A, B, C, M, N, K, scale_a, scale_b, bias, nullptr);
+}
+
 // FusedKernels.h:766-854
 float ref_fused_cross_entropy(const float* logits, const int32_t* targets, float* grad, int M,
                               int N) {

@@ -154,6 +154,32 @@ void orc_gemm_bias_act(const float* A, const float* B, const float* bias,
 /* Optional outputs: per-row mean and inv_std.                          */
 /* ------------------------------------------------------------------ */
 /*
+ * int8 GEMM.  FusedKernels.h:867-1073: int32 accumulation as its scalar
+ * branch (:1046-1057), C = (float)acc * (scale_a * scale_b), plus bias[j]
+ * (:1060-1065).  (The reference's AVX-512 branches load 32 columns of B per
+ * 16-column step and sum adjacent columns pairwise; the scalar branch is the
+ * routine's stated contract.)
+ */
+void orc_matmul_int8(const int8_t* A, const int8_t* B, float* C, int64_t M, int64_t N, int64_t K,
+                     float scale_a, float scale_b, const float* bias) {
+  const float s = scale_a * scale_b;
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < M; i++) {
+    int32_t* acc = (int32_t*)calloc((size_t)N, sizeof(int32_t));
+    for (int64_t k = 0; k < K; k++) {
+      const int32_t a = A[i * K + k];
+      const int8_t* b = B + k * N;
+      for (int64_t j = 0; j < N; j++) acc[j] += a * (int32_t)b[j];
+    }
+    for (int64_t j = 0; j < N; j++) {
+      C[i * N + j] = (float)acc[j] * s;
+      if (bias) C[i * N + j] += bias[j];
+    }
+    free(acc);
+  }
+}
+
+/*
  * Row softmax.  FusedKernels.h:464-526, in the summation order of its
  * AVX-512 branch (:466-505): max over the row (from -FLT_MAX); e = exp(x -
  * max) stored and summed in 16 lanes over 16-wide chunks, the lanes reduced,

@@ -60,6 +60,9 @@ def golden_cases():
     cases["softmax_ragged"] = dict(kind="softmax", M=7, N=1000, seed=802)
     cases["xent"] = dict(kind="xent", M=64, N=1000, seed=900)
     cases["xent_ragged"] = dict(kind="xent", M=13, N=37, seed=901)
+    # matmulInt8 (FusedKernels.h:867-1073), from the reference build's scalar branch
+    cases["int8"] = dict(kind="int8", M=64, N=96, K=200, seed=1000)
+    cases["int8_bias"] = dict(kind="int8", M=33, N=40, K=77, seed=1001, bias=True)
     return cases
 
 
@@ -100,6 +103,12 @@ def make_inputs(c):
     if k == "xent":
         return [(3 * g.standard_normal((c["M"], c["N"]))).astype(np.float32),
                 g.integers(0, c["N"], c["M"]).astype(np.int32)]
+    if k == "int8":
+        ins = [g.integers(-128, 128, (c["M"], c["K"])).astype(np.int8),
+               g.integers(-128, 128, (c["K"], c["N"])).astype(np.int8)]
+        if c.get("bias"):
+            ins.append(g.standard_normal(c["N"]).astype(np.float32))
+        return ins
     raise ValueError(k)
 
 
@@ -124,6 +133,10 @@ def run_reference(ref, c, ins):
     if k == "xent":
         loss, grad = ref.cross_entropy(ins[0], ins[1])
         return {"grad": grad, "loss": np.array([loss], np.float32)}
+    if k == "int8":
+        scalar = ref if ref.variant == "avx2" else oracle.Reference(variant="avx2")
+        return {"out": scalar.matmul_int8(ins[0], ins[1], 0.02, 0.03,
+                                          ins[2] if len(ins) > 2 else None)}
     raise ValueError(k)
 
 

@@ -22,7 +22,7 @@ def _raw_call(jb, name, n_buffers=2, opaque_len=None):
 
 def test_custom_call_argument_errors(jb):
     assert _raw_call(jb, "noSuchKernel") == JULES_ERR_ARG
-    assert _raw_call(jb, "matmulInt8") == JULES_ERR_UNSUPPORTED
+    assert _raw_call(jb, "matmulInt8", n_buffers=2) == JULES_ERR_ARG
     assert _raw_call(jb, "fusedSoftmax", opaque_len=8) == JULES_ERR_ARG
     assert _raw_call(jb, "fusedSoftmax", n_buffers=3) == JULES_ERR_ARG
     assert _raw_call(jb, "fusedMatmulBiasGelu", n_buffers=3) == JULES_ERR_ARG
@@ -108,5 +108,11 @@ def test_custom_call_matches_direct_entry_points(jb):
     jb.custom_call("fusedMLPForward", [Xm, gm, bm, W1, b1, W2, b2, Om], dims=(Tn, d, dff),
                    fparams=(1e-5,), dtype=jb.DT_BF16, flags=1)
     assert torch.equal(Om, jb.mlp_block(Xm, gm, bm, W1, b1, W2, b2, out_dtype=f32))
+    # matmulInt8 with bias
+    Ai = torch.randint(-128, 128, (M, K), generator=g, device=dev, dtype=torch.int8)
+    Bi = torch.randint(-128, 128, (K, N), generator=g, device=dev, dtype=torch.int8)
+    Ci = torch.empty((M, N), dtype=f32, device=dev)
+    jb.custom_call("matmulInt8", [Ai, Bi, bias, Ci], dims=(M, N, K), fparams=(0.01, 0.02))
+    assert torch.equal(Ci, jb.matmul_int8(Ai, Bi, 0.01, 0.02, bias))
     torch.cuda.synchronize()
     assert jb.device_error() == 0
