@@ -50,7 +50,7 @@ def parse():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["jules", "reference"], default="jules")
     p.add_argument("--workload", choices=["gemm", "attn", "attn_gqa", "mlp", "attn_fp32",
-                                          "softmax", "xent"],
+                                          "softmax", "xent", "int8"],
                    default="gemm")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
@@ -83,6 +83,11 @@ def roofline(wl, achieved, peak, peak_kind, traffic):
     """Roofline object of the dominant kernel: bf16 tensor kernels against the
     measured cuBLAS bf16 burst peak, the fp32 CUDA-core kernel (C1) against the
     nominal fp32 FMA peak."""
+    if wl.unit == "TOPS":
+        return {"bound": "tensor", "kernel": wl.dominant, "achieved": round(achieved, 2),
+                "peak": NOMINAL_INT8_TOPS, "unit": "TOPS", "frac": round(achieved / NOMINAL_INT8_TOPS, 4),
+                "peak_kind": "nominal dense int8 (datasheet; no measured int8 figure)",
+                "traffic": traffic, "traffic_unit": "DRAM bytes per launch (ncu, profiles/)"}
     if wl.unit == "GB/s":
         hbm = measured_peaks()[1]
         return {"bound": "hbm", "kernel": wl.dominant, "achieved": round(achieved, 1),
@@ -104,7 +109,7 @@ def profiled_traffic(workload):
     summary (profiles/<kernel>_<workload>.md, line 'traffic_bytes_per_launch:')."""
     name = {"gemm": "gemm_tc_c2", "attn": "attn_tc_c3", "attn_gqa": "attn_tc_c5",
             "mlp": "gemm_tc_c4", "attn_fp32": "attn_simt_c1", "softmax": "rows_softmax",
-            "xent": "rows_xent"}[workload]
+            "xent": "rows_xent", "int8": "gemm_s8_int8"}[workload]
     path = os.path.join(HERE, "profiles", f"{name}.md")
     try:
         with open(path) as f:
@@ -134,6 +139,10 @@ def describe(workload, world, extra_l2=None):
         c = {"workload": "C4 MLP block LN->GEMM+b+GELU->GEMM+b+residual", "T_per_rank": 16384,
              "d": 4096, "dff": 16384, "global_T": 16384 * world, "sharding": "token rows",
              "eps": 1e-5}
+    elif workload == "int8":
+        c = {"workload": "int8 GEMM (matmulInt8): s8 x s8 -> s32 -> fp32 * scale + bias",
+             "M_per_rank": 8192, "N": 8192, "K": 8192, "global_M": 8192 * world,
+             "sharding": "rows of M", "op_convention": "2*M*N*K int8 ops"}
     elif workload == "softmax":
         c = {"workload": "row softmax (fusedSoftmax), fp32", "M_per_rank": 16384, "N": 4096,
              "global_M": 16384 * world, "sharding": "rows",
@@ -467,6 +476,56 @@ class Mlp(Workload):
         self.hO.copy_(self.dO, non_blocking=True)
 
 
+class Int8Gemm(Workload):
+    """int8 GEMM, M = N = K = 8192 per rank (rows of M sharded): tcgen05
+    kind::i8.  Counted in int8 ops (2*M*N*K), reported as TOPS."""
+    unit = "TOPS"
+    dtype = "s8"
+    dominant = "gemm_s8_tc_kernel<256, 4>"
+
+    def __init__(self, jb, torch, rank, world, M=8192, N=8192, K=8192):
+        self.jb, self.torch = jb, torch
+        self.M, self.N, self.K = M, N, K
+        dev = torch.device("cuda")
+        g = torch.Generator(device=dev).manual_seed(8 + rank)
+        per_set = M * K + K * N + M * N * 4
+        self.nsets = self.sets_for(per_set)
+        self.A = [torch.randint(-128, 128, (M, K), generator=g, device=dev, dtype=torch.int8)
+                  for _ in range(self.nsets)]
+        self.B = [torch.randint(-128, 128, (K, N), generator=g, device=dev, dtype=torch.int8)
+                  for _ in range(self.nsets)]
+        self.bias = torch.randn(N, generator=g, device=dev)
+        self.C = [torch.empty((M, N), dtype=torch.float32, device=dev) for _ in range(self.nsets)]
+        self.flops_per_step = 2.0 * M * N * K
+        self.flops_dominant = self.flops_per_step
+        self.config = {"l2": f"{self.nsets} rotating input sets ({self.nsets * per_set / 2**20:.0f} MiB > L2)"}
+
+    def step(self, i, ev=None):
+        k = i % self.nsets
+        if ev:
+            ev[0].record()
+        self.jb.matmul_int8(self.A[k], self.B[k], 0.01, 0.02, self.bias, out=self.C[k])
+        if ev:
+            ev[1].record()
+
+    def output(self, i):
+        return self.C[i % self.nsets]
+
+    def e2e_setup(self):
+        t = self.torch
+        self.hA, self.hB = self.A[0].cpu().pin_memory(), self.B[0].cpu().pin_memory()
+        self.hC = t.empty_like(self.C[0], device="cpu").pin_memory()
+        self.dA, self.dB, self.dC = t.empty_like(self.A[0]), t.empty_like(self.B[0]), t.empty_like(self.C[0])
+        self.h2d = self.hA.numel() + self.hB.numel()
+        self.d2h = self.hC.numel() * 4
+
+    def e2e_step(self):
+        self.dA.copy_(self.hA, non_blocking=True)
+        self.dB.copy_(self.hB, non_blocking=True)
+        self.jb.matmul_int8(self.dA, self.dB, 0.01, 0.02, self.bias, out=self.dC)
+        self.hC.copy_(self.dC, non_blocking=True)
+
+
 class RowWise(Workload):
     """Row softmax (softmax) or fused softmax + cross-entropy (xent), fp32,
     rows sharded across ranks.  HBM-bound: work is counted in bytes."""
@@ -534,6 +593,9 @@ class RowWise(Workload):
 METRIC = "Flash-attn fwd & fused-GEMM TFLOP/s at 1/2/4/8 B200; % of tensor peak"
 # Extra (non-headline) workloads of the row-wise kernels report HBM bytes per second.
 ROWS_METRIC = "Row softmax / fused cross-entropy GB/s (HBM bytes moved) per B200"
+INT8_METRIC = "int8 GEMM TOPS (matmulInt8) per B200"
+# B200 datasheet dense int8 tensor throughput (no measured figure on this pool).
+NOMINAL_INT8_TOPS = 4500.0
 JSON_OUT = sys.stdout
 
 
@@ -568,6 +630,19 @@ def cpu_reference_sample(workload, reps=3, warm=1):
         b = (0.02 * g.standard_normal(N)).astype(np.float32)
         fn = lambda: ref.gemm_bias_gelu(A, W, b)
         flops = 2.0 * Ms * N * K
+    elif workload == "int8":
+        Ms, N, K = 16, 8192, 8192
+        A = g.integers(-128, 128, (Ms, K)).astype(np.int8)
+        B = g.integers(-128, 128, (K, N)).astype(np.int8)
+        bias = g.standard_normal(N).astype(np.float32)
+        # the scalar build: the AVX-512 build's int8 branches compute a different product
+        ref8 = oracle.Reference(variant="avx2")
+        ref8.set_threads(threads)
+        fn = lambda: ref8.matmul_int8(A, B, 0.01, 0.02, bias)
+        flops = 2.0 * Ms * N * K
+        desc = (f"reference matmulInt8 (FusedKernels.h:867-1073, scalar branch) on {Ms} of the "
+                f"8192 rows; ops 2*M*N*K")
+        reps = 2
     elif workload in ("softmax", "xent"):
         if workload == "softmax":
             Ms, N = 2048, 4096
@@ -635,8 +710,9 @@ def run_reference_arm(args):
     wall = time.perf_counter() - t0
     value = statistics.mean(vals)
     rowwise = args.workload in ("softmax", "xent")
-    unit = "GB/s" if rowwise else "TFLOP/s"
-    line = {"metric": ROWS_METRIC if rowwise else METRIC, "value": round(value, 6), "unit": unit,
+    unit = "GB/s" if rowwise else ("TOPS" if args.workload == "int8" else "TFLOP/s")
+    metric = ROWS_METRIC if rowwise else (INT8_METRIC if args.workload == "int8" else METRIC)
+    line = {"metric": metric, "value": round(value, 6), "unit": unit,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(wall / args.steps * 1e3, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -685,7 +761,8 @@ def main():
          "mlp": lambda: Mlp(jb, torch, rank, world),
          "attn_fp32": lambda: AttentionF32(jb, torch, rank, world),
          "softmax": lambda: RowWise(jb, torch, rank, world, xent=False),
-         "xent": lambda: RowWise(jb, torch, rank, world, xent=True)}[args.workload]
+         "xent": lambda: RowWise(jb, torch, rank, world, xent=True),
+         "int8": lambda: Int8Gemm(jb, torch, rank, world)}[args.workload]
     wl = W()
     stream = torch.cuda.current_stream()
 
@@ -777,7 +854,7 @@ def main():
 
     if rank == 0:
         line = {
-            "metric": METRIC if wl.unit == "TFLOP/s" else ROWS_METRIC,
+            "metric": {"TFLOP/s": METRIC, "GB/s": ROWS_METRIC, "TOPS": INT8_METRIC}[wl.unit],
             "value": round(tflops_total, 3), "unit": wl.unit,
             "n_gpus": world, "steps": K, "warmup": args.warmup,
             "ms_per_step": round(ms_total / K, 5), "higher_is_better": True, "scaling": "weak",
