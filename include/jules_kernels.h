@@ -163,6 +163,25 @@ int jules_cross_entropy_loss(const void* logits, const int32_t* targets, void* g
                              int64_t M, int64_t N, int dtype, void* stream);
 
 /*
+ * 2-layer MLP training step, fp32 (the reference's
+ * interleavedMLPForwardBackward, InterleavedAutodiff.h:55-160, computed over
+ * the whole batch; its tiling only changes summation order):
+ *   a = relu(X . W1 + b1), output = a . W2 + b2,
+ *   *loss = mean_i -log(softmax(output_i)[targets_i] + 1e-10),
+ *   dout = (softmax(output) - onehot) / M, dW2 = a^T dout, db2 = colsum(dout),
+ *   dh = (dout . W2^T) * (a > 0), dW1 = X^T dh, db1 = colsum(dh),
+ *   dX = dh . W1^T (skipped when dX is NULL).
+ * X [M,K1], W1 [K1,N1], W2 [N1,N2], output [M,N2], targets [M] int32; loss is
+ * one device float.  workspace: at least jules_mlp_fwd_bwd_workspace_bytes().
+ */
+size_t jules_mlp_fwd_bwd_workspace_bytes(int64_t M, int64_t N1, int64_t N2);
+int jules_mlp_fwd_bwd(const float* X, const float* W1, const float* b1, const float* W2,
+                      const float* b2, const int32_t* targets, float* output, float* loss,
+                      float* dW1, float* db1, float* dW2, float* db2, float* dX, int64_t M,
+                      int64_t K1, int64_t N1, int64_t N2, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/*
  * Transformer MLP block, bf16:
  *   out = GELU(LN(X) . W1 + b1) . W2 + b2 + X
  *   X, out [T,d]; W1 [d,dff]; W2 [dff,d]; gamma, beta, b2 [d] and b1 [dff]

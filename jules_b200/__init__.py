@@ -45,6 +45,8 @@ _SIGNATURES = {
                          _c_vp, _c_vp], _c_int),
     "jules_gelu": ([_c_vp, _c_vp, _c_i64, _c_int, _c_vp], _c_int),
     "jules_softmax": ([_c_vp, _c_vp, _c_i64, _c_i64, _c_int, _c_int, _c_vp], _c_int),
+    "jules_mlp_fwd_bwd_workspace_bytes": ([_c_i64, _c_i64, _c_i64], ctypes.c_size_t),
+    "jules_mlp_fwd_bwd": ([_c_vp] * 13 + [_c_i64] * 4 + [_c_vp, ctypes.c_size_t, _c_vp], _c_int),
     "jules_matmul_int8": ([_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_f, _c_f, _c_vp, _c_vp],
                           _c_int),
     "jules_cross_entropy_loss": ([_c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_int, _c_vp],
@@ -211,6 +213,28 @@ def gelu(x, out=None, stream=None):
     rc = lib().jules_gelu(_ptr(x), _ptr(out), x.numel(), _dtype_code(x), _stream(stream))
     _check(rc, "jules_gelu")
     return out
+
+
+def mlp_fwd_bwd(X, W1, b1, W2, b2, targets, want_dx=True, workspace=None, stream=None):
+    """2-layer ReLU MLP training step in fp32 (the reference's
+    interleavedMLPForwardBackward): returns dict(loss (0-d device tensor),
+    out, dW1, db1, dW2, db2, dX)."""
+    import torch
+    M, K1 = X.shape
+    N1, N2 = W1.shape[1], W2.shape[1]
+    dev = X.device
+    e = lambda *s: torch.empty(s, dtype=torch.float32, device=dev)
+    r = dict(out=e(M, N2), loss=e(), dW1=e(K1, N1), db1=e(N1), dW2=e(N1, N2), db2=e(N2),
+             dX=e(M, K1) if want_dx else None)
+    need = int(lib().jules_mlp_fwd_bwd_workspace_bytes(M, N1, N2))
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+    rc = lib().jules_mlp_fwd_bwd(_ptr(X), _ptr(W1), _ptr(b1), _ptr(W2), _ptr(b2), _ptr(targets),
+                                 _ptr(r["out"]), _ptr(r["loss"]), _ptr(r["dW1"]), _ptr(r["db1"]),
+                                 _ptr(r["dW2"]), _ptr(r["db2"]), _ptr(r["dX"]), M, K1, N1, N2,
+                                 _ptr(workspace), workspace.numel(), _stream(stream))
+    _check(rc, "jules_mlp_fwd_bwd")
+    return r
 
 
 def matmul_int8(A, B, scale_a=1.0, scale_b=1.0, bias=None, out=None, stream=None):

@@ -5,6 +5,7 @@
 // (jb::g_dev_error) is one symbol without relocatable device code.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -21,6 +22,7 @@
 #include "sm100.cuh"
 #include "simt.cuh"
 #include "rowwise.cuh"
+#include "train.cuh"
 
 namespace {
 
@@ -744,6 +746,56 @@ int jules_custom_call(const char* name, void* stream, void** buffers, int n_buff
                                    d.dims[1], d.dims[2], eps, stream);
   }
   return fail(JULES_ERR_UNSUPPORTED, "custom_call: no dispatch for this name");
+}
+
+size_t jules_mlp_fwd_bwd_workspace_bytes(int64_t M, int64_t N1, int64_t N2) {
+  if (M <= 0 || N1 <= 0 || N2 <= 0) return 0;
+  const size_t a = ((size_t)M * N1 * 4 + 255) & ~size_t(255);
+  const size_t dout = ((size_t)M * N2 * 4 + 255) & ~size_t(255);
+  return 2 * a + dout;
+}
+
+int jules_mlp_fwd_bwd(const float* X, const float* W1, const float* b1, const float* W2,
+                      const float* b2, const int32_t* targets, float* output, float* loss,
+                      float* dW1, float* db1, float* dW2, float* db2, float* dX, int64_t M,
+                      int64_t K1, int64_t N1, int64_t N2, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  if (!X || !W1 || !b1 || !W2 || !b2 || !targets || !output || !loss || !dW1 || !db1 || !dW2 ||
+      !db2)
+    return fail(JULES_ERR_ARG, "mlp_fwd_bwd: NULL pointer");
+  if (M <= 0 || K1 <= 0 || N1 <= 0 || N2 <= 0 || M > INT32_MAX || K1 > INT32_MAX || N1 > INT32_MAX ||
+      N2 > INT32_MAX)
+    return fail(JULES_ERR_SHAPE, "mlp_fwd_bwd: M=%lld K1=%lld N1=%lld N2=%lld", (long long)M,
+                (long long)K1, (long long)N1, (long long)N2);
+  const size_t need = jules_mlp_fwd_bwd_workspace_bytes(M, N1, N2);
+  if (!workspace || workspace_bytes < need)
+    return fail(JULES_ERR_WORKSPACE, "mlp_fwd_bwd: workspace %zu < %zu bytes", workspace_bytes, need);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  const size_t a_bytes = ((size_t)M * N1 * 4 + 255) & ~size_t(255);
+  float* a = reinterpret_cast<float*>(ws);                  // relu(X W1 + b1)   [M, N1]
+  float* dh = reinterpret_cast<float*>(ws + a_bytes);       // dL/dh             [M, N1]
+  float* dout = reinterpret_cast<float*>(ws + 2 * a_bytes); // dL/dout           [M, N2]
+  auto blocks = [](int64_t n) { return (unsigned)std::min<int64_t>((n + 255) / 256, 148 * 16); };
+  // forward
+  if (int rc = jules_sgemm(0, 0, M, N1, K1, 1.0f, X, K1, W1, N1, 0.0f, a, N1, stream)) return rc;
+  jb::train::bias_relu_kernel<<<blocks(M * N1), 256, 0, st>>>(a, b1, M, N1);
+  if (int rc = jules_sgemm(0, 0, M, N2, N1, 1.0f, a, N1, W2, N2, 0.0f, output, N2, stream)) return rc;
+  jb::train::bias_add_kernel<<<blocks(M * N2), 256, 0, st>>>(output, b2, M, N2);
+  if (int rc = check_launch("mlp_fwd_bwd forward")) return rc;
+  // loss and dL/dout = (softmax - onehot) / M
+  if (int rc = jules_cross_entropy_loss(output, targets, dout, loss, M, N2, JULES_DTYPE_F32, stream))
+    return rc;
+  // backward
+  if (int rc = jules_sgemm(1, 0, N1, N2, M, 1.0f, a, N1, dout, N2, 0.0f, dW2, N2, stream)) return rc;
+  jb::train::colsum_kernel<<<(unsigned)((N2 + 31) / 32), 256, 0, st>>>(dout, db2, M, N2);
+  if (int rc = jules_sgemm(0, 1, M, N1, N2, 1.0f, dout, N2, W2, N2, 0.0f, dh, N1, stream)) return rc;
+  jb::train::relu_grad_kernel<<<blocks(M * N1), 256, 0, st>>>(dh, a, M * N1);
+  if (int rc = jules_sgemm(1, 0, K1, N1, M, 1.0f, X, K1, dh, N1, 0.0f, dW1, N1, stream)) return rc;
+  jb::train::colsum_kernel<<<(unsigned)((N1 + 31) / 32), 256, 0, st>>>(dh, db1, M, N1);
+  if (dX)
+    if (int rc = jules_sgemm(0, 1, M, K1, N1, 1.0f, dh, N1, W1, N1, 0.0f, dX, K1, stream)) return rc;
+  return check_launch("mlp_fwd_bwd backward");
 }
 
 size_t jules_mlp_block_workspace_bytes(int64_t T, int64_t d, int64_t dff) {

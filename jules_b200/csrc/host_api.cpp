@@ -17,6 +17,7 @@
 #include "jules/Kernel/ExecutionArena.h"
 #include "jules/Kernel/FlashAttention.h"
 #include "jules/Kernel/FusedKernels.h"
+#include "jules/Kernel/InterleavedAutodiff.h"
 #include "jules/Kernel/TilePlanner.h"
 #include "jules_kernels.h"
 
@@ -39,9 +40,11 @@ class Staging {
     if (ptr_) cudaFree(ptr_);
   }
   // Returns device pointers for `n` buffers of the given byte sizes.
+  static constexpr int kMaxBuffers = 16;
   void reserve(const size_t* bytes, int n, char** out) {
+    if (n < 0 || n > kMaxBuffers) throw std::runtime_error("jules: too many staging buffers");
     size_t total = 0;
-    size_t off[8];
+    size_t off[kMaxBuffers];
     for (int i = 0; i < n; ++i) {
       off[i] = total;
       total += (bytes[i] + 255) & ~size_t(255);
@@ -255,6 +258,45 @@ void matmulInt8(const int8_t* A, const int8_t* B, float* C, int M, int N, int K,
   d2h(C, d[2], bc);
 }
 
+InterleavedMLPResult interleavedMLPForwardBackward(const float* X, const float* W1,
+                                                   const float* b1, const float* W2,
+                                                   const float* b2, const int32_t* targets,
+                                                   float* output, float* dW1, float* db1,
+                                                   float* dW2, float* db2, float* dX, int M,
+                                                   int K1, int N1, int N2, ExecutionArena&,
+                                                   TilePlanner&) {
+  InterleavedMLPResult res{0.0f, MLPGradients{dW1, db1, dW2, db2, dX}};
+  if (M <= 0) return res;
+  const size_t bx = (size_t)M * K1 * 4, bw1 = (size_t)K1 * N1 * 4, bw2 = (size_t)N1 * N2 * 4;
+  const size_t bo = (size_t)M * N2 * 4, bt = (size_t)M * 4;
+  const size_t ws = jules_mlp_fwd_bwd_workspace_bytes(M, N1, N2);
+  // X W1 b1 W2 b2 t out loss dW1 db1 dW2 db2 dX ws
+  const size_t sizes[14] = {bx, bw1, (size_t)N1 * 4, bw2, (size_t)N2 * 4, bt, bo, 256,
+                            bw1, (size_t)N1 * 4, bw2, (size_t)N2 * 4, dX ? bx : 16, ws};
+  char* d[14];
+  staging().reserve(sizes, 14, d);
+  h2d(d[0], X, bx);
+  h2d(d[1], W1, bw1);
+  h2d(d[2], b1, (size_t)N1 * 4);
+  h2d(d[3], W2, bw2);
+  h2d(d[4], b2, (size_t)N2 * 4);
+  h2d(d[5], targets, bt);
+  auto f = [&](int i) { return reinterpret_cast<float*>(d[i]); };
+  check_status(jules_mlp_fwd_bwd(f(0), f(1), f(2), f(3), f(4), reinterpret_cast<const int32_t*>(d[5]),
+                                 f(6), f(7), f(8), f(9), f(10), f(11), dX ? f(12) : nullptr, M, K1,
+                                 N1, N2, d[13], ws, nullptr),
+               "jules_mlp_fwd_bwd");
+  d2h(output, d[6], bo);
+  d2h(&res.loss, d[7], 4);
+  d2h(dW1, d[8], bw1);
+  d2h(db1, d[9], (size_t)N1 * 4);
+  d2h(dW2, d[10], bw2);
+  d2h(db2, d[11], (size_t)N2 * 4);
+  if (dX) d2h(dX, d[12], bx);
+  check_status(jules_device_error(nullptr, 1), "interleavedMLPForwardBackward (target outside [0, N2))");
+  return res;
+}
+
 void blasMatmul(const float* A, const float* B, float* C, int M, int N, int K, float alpha,
                 float beta, bool transA, bool transB) {
   if (M <= 0 || N <= 0) return;
@@ -356,7 +398,7 @@ const KernelEntry kKernels[] = {
     {"fusedMatmulBiasTanh", 1},    {"fusedMatmulBiasGelu", 1},  {"fusedLayerNorm", 1},
     {"fusedGelu", 1},              {"fusedMLPForward", 1},      {"flashAttention", 1},
     {"blasMatmul", 1},             {"fusedSoftmax", 1},         {"fusedCrossEntropyLoss", 1},
-    {"matmulInt8", 1},
+    {"matmulInt8", 1},             {"interleavedMLPForwardBackward", 1},
 };
 constexpr int kNumKernels = sizeof(kKernels) / sizeof(kKernels[0]);
 

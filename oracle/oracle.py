@@ -88,6 +88,20 @@ def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
     return (b.astype(np.uint32) << 16).view(np.float32)
 
 
+def _mlp_fwd_bwd(fn, X, W1, b1, W2, b2, targets, want_dx):
+    X, W1, b1, W2, b2 = (np.ascontiguousarray(a, np.float32) for a in (X, W1, b1, W2, b2))
+    t = np.ascontiguousarray(targets, np.int32)
+    M, K1 = X.shape
+    N1, N2 = W1.shape[1], W2.shape[1]
+    r = dict(out=np.empty((M, N2), np.float32), dW1=np.empty((K1, N1), np.float32),
+             db1=np.empty(N1, np.float32), dW2=np.empty((N1, N2), np.float32),
+             db2=np.empty(N2, np.float32), dX=np.empty((M, K1), np.float32) if want_dx else None)
+    r["loss"] = float(fn(_fp(X), _fp(W1), _fp(b1), _fp(W2), _fp(b2), _ip(t), _fp(r["out"]),
+                         _fp(r["dW1"]), _fp(r["db1"]), _fp(r["dW2"]), _fp(r["db2"]), _fp(r["dX"]),
+                         M, K1, N1, N2))
+    return r
+
+
 class Restated:
     """oracle/restate.c via ctypes."""
 
@@ -109,6 +123,8 @@ class Restated:
         lib.orc_matmul_int8.argtypes = [ctypes.c_void_p, ctypes.c_void_p, _f32p, ctypes.c_int64,
                                         ctypes.c_int64, ctypes.c_int64, ctypes.c_float,
                                         ctypes.c_float, _f32p]
+        lib.orc_mlp_fwd_bwd.argtypes = [_f32p] * 5 + [_i32p] + [_f32p] * 6 + [ctypes.c_int64] * 4
+        lib.orc_mlp_fwd_bwd.restype = ctypes.c_float
         lib.orc_softmax.argtypes = [_f32p, _f32p, ctypes.c_int64, ctypes.c_int64]
         lib.orc_cross_entropy.argtypes = [_f32p, _i32p, _f32p, ctypes.c_int64, ctypes.c_int64]
         lib.orc_cross_entropy.restype = ctypes.c_float
@@ -145,6 +161,10 @@ class Restated:
         out = np.empty_like(x)
         self.lib.orc_softmax(_fp(out), _fp(x), M, N)
         return out
+
+    def mlp_fwd_bwd(self, X, W1, b1, W2, b2, targets, want_dx=True):
+        """Returns dict(loss, out, dW1, db1, dW2, db2, dX)."""
+        return _mlp_fwd_bwd(self.lib.orc_mlp_fwd_bwd, X, W1, b1, W2, b2, targets, want_dx)
 
     def matmul_int8(self, A, B, scale_a=1.0, scale_b=1.0, bias=None):
         A = np.ascontiguousarray(A, np.int8)
@@ -239,6 +259,8 @@ class Reference:
         lib.ref_fused_cross_entropy.argtypes = [_f32p, _i32p, _f32p, ctypes.c_int, ctypes.c_int]
         lib.ref_matmul_int8.argtypes = [ctypes.c_void_p, ctypes.c_void_p, _f32p] + [ctypes.c_int] * 3 + [
             ctypes.c_float, ctypes.c_float, _f32p]
+        lib.ref_interleaved_mlp.argtypes = [_f32p] * 5 + [_i32p] + [_f32p] * 6 + [ctypes.c_int] * 4
+        lib.ref_interleaved_mlp.restype = ctypes.c_float
         lib.ref_fused_cross_entropy.restype = ctypes.c_float
         lib.ref_blas_matmul.argtypes = [_f32p] * 3 + [ctypes.c_int] * 3 + [ctypes.c_float] * 2 + [
             ctypes.c_int] * 2
@@ -328,6 +350,11 @@ class Reference:
         out = np.empty_like(x)
         self.lib.ref_fused_softmax(_fp(out), _fp(x), M, N)
         return out
+
+    def mlp_fwd_bwd(self, X, W1, b1, W2, b2, targets, want_dx=True):
+        """The reference's interleavedMLPForwardBackward; dict(loss, out, dW1,
+        db1, dW2, db2, dX)."""
+        return _mlp_fwd_bwd(self.lib.ref_interleaved_mlp, X, W1, b1, W2, b2, targets, want_dx)
 
     def matmul_int8(self, A, B, scale_a=1.0, scale_b=1.0, bias=None):
         """The reference's matmulInt8.  Only the "avx2" variant (compiled

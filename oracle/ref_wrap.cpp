@@ -6,6 +6,7 @@
 // The reference headers define non-inline functions, so this must stay the
 // only translation unit that includes them (ODR, FusedKernels.h:203).
 #include "jules/Kernel/FlashAttention.h"  // pulls FusedKernels.h, TilePlanner.h, ExecutionArena.h
+#include "jules/Kernel/InterleavedAutodiff.h"
 
 #include <cstdlib>
 #ifdef _OPENMP
@@ -128,6 +129,17 @@ void ref_fused_gelu(float* out, const float* in, int N) {
 // FusedKernels.h:464-526
 void ref_fused_softmax(float* out, const float* in, int M, int N) {
   fusedSoftmax(out, in, M, N);
+}
+
+// InterleavedAutodiff.h:55-160: 2-layer ReLU MLP forward, softmax
+// cross-entropy, backward; returns the mean loss.
+float ref_interleaved_mlp(const float* X, const float* W1, const float* b1, const float* W2,
+                          const float* b2, const int32_t* targets, float* output, float* dW1,
+                          float* db1, float* dW2, float* db2, float* dX, int M, int K1, int N1,
+                          int N2) {
+  return interleavedMLPForwardBackward(X, W1, b1, W2, b2, targets, output, dW1, db1, dW2, db2, dX,
+                                       M, K1, N1, N2, arena(), planner())
+      .loss;
 }
 
 // FusedKernels.h:867-1073.  Only the build without AVX-512 (the scalar

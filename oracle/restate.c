@@ -154,6 +154,86 @@ void orc_gemm_bias_act(const float* A, const float* B, const float* bias,
 /* Optional outputs: per-row mean and inv_std.                          */
 /* ------------------------------------------------------------------ */
 /*
+ * 2-layer MLP training step.  InterleavedAutodiff.h:55-160 (per tile: :127-
+ * 160 forward, :162-185 loss and dL/do, :187-258 backward), over the whole
+ * batch at once (the tiling only changes summation order):
+ *   h = X W1 + b1, a = relu(h), out = a W2 + b2,
+ *   p = softmax(out row), loss = sum_i -log(p[i, t_i] + 1e-10) / M,
+ *   do = (p - onehot(t)) / M, dW2 = a^T do, db2 = colsum(do),
+ *   dh = (do W2^T) * (h > 0), dW1 = X^T dh, db1 = colsum(dh), dX = dh W1^T.
+ * Accumulation in double here (the fixtures pin it to the reference within
+ * the fp32 tolerance).  dX may be NULL.
+ */
+float orc_mlp_fwd_bwd(const float* X, const float* W1, const float* b1, const float* W2,
+                      const float* b2, const int32_t* t, float* out, float* dW1, float* db1,
+                      float* dW2, float* db2, float* dX, int64_t M, int64_t K1, int64_t N1,
+                      int64_t N2) {
+  float* a = (float*)malloc(sizeof(float) * (size_t)(M * N1));
+  float* dout = (float*)malloc(sizeof(float) * (size_t)(M * N2));
+  float* dh = (float*)malloc(sizeof(float) * (size_t)(M * N1));
+  double loss = 0.0;
+  for (int64_t i = 0; i < M; i++) {
+    for (int64_t j = 0; j < N1; j++) {
+      double s = b1[j];
+      for (int64_t k = 0; k < K1; k++) s += (double)X[i * K1 + k] * W1[k * N1 + j];
+      a[i * N1 + j] = s > 0.0 ? (float)s : 0.0f;
+    }
+    for (int64_t j = 0; j < N2; j++) {
+      double s = b2[j];
+      for (int64_t k = 0; k < N1; k++) s += (double)a[i * N1 + k] * W2[k * N2 + j];
+      out[i * N2 + j] = (float)s;
+    }
+    double mx = -DBL_MAX, sum = 0.0;
+    for (int64_t j = 0; j < N2; j++) mx = fmax(mx, out[i * N2 + j]);
+    for (int64_t j = 0; j < N2; j++) sum += exp(out[i * N2 + j] - mx);
+    for (int64_t j = 0; j < N2; j++) {
+      const double p = exp(out[i * N2 + j] - mx) / sum;
+      dout[i * N2 + j] = (float)((p - (j == t[i] ? 1.0 : 0.0)) / (double)M);
+      if (j == t[i]) loss += -log(p + 1e-10);
+    }
+  }
+  for (int64_t i = 0; i < M; i++)
+    for (int64_t j = 0; j < N1; j++) {
+      double s = 0.0;
+      for (int64_t k = 0; k < N2; k++) s += (double)dout[i * N2 + k] * W2[j * N2 + k];
+      dh[i * N1 + j] = a[i * N1 + j] > 0.0f ? (float)s : 0.0f;
+    }
+  for (int64_t r = 0; r < N1; r++)
+    for (int64_t c = 0; c < N2; c++) {
+      double s = 0.0;
+      for (int64_t i = 0; i < M; i++) s += (double)a[i * N1 + r] * dout[i * N2 + c];
+      dW2[r * N2 + c] = (float)s;
+    }
+  for (int64_t c = 0; c < N2; c++) {
+    double s = 0.0;
+    for (int64_t i = 0; i < M; i++) s += dout[i * N2 + c];
+    db2[c] = (float)s;
+  }
+  for (int64_t r = 0; r < K1; r++)
+    for (int64_t c = 0; c < N1; c++) {
+      double s = 0.0;
+      for (int64_t i = 0; i < M; i++) s += (double)X[i * K1 + r] * dh[i * N1 + c];
+      dW1[r * N1 + c] = (float)s;
+    }
+  for (int64_t c = 0; c < N1; c++) {
+    double s = 0.0;
+    for (int64_t i = 0; i < M; i++) s += dh[i * N1 + c];
+    db1[c] = (float)s;
+  }
+  if (dX)
+    for (int64_t i = 0; i < M; i++)
+      for (int64_t k = 0; k < K1; k++) {
+        double s = 0.0;
+        for (int64_t j = 0; j < N1; j++) s += (double)dh[i * N1 + j] * W1[k * N1 + j];
+        dX[i * K1 + k] = (float)s;
+      }
+  free(a);
+  free(dout);
+  free(dh);
+  return (float)(loss / (double)M);
+}
+
+/*
  * int8 GEMM.  FusedKernels.h:867-1073: int32 accumulation as its scalar
  * branch (:1046-1057), C = (float)acc * (scale_a * scale_b), plus bias[j]
  * (:1060-1065).  (The reference's AVX-512 branches load 32 columns of B per

@@ -10,6 +10,7 @@
 #include "jules/Kernel/ExecutionArena.h"
 #include "jules/Kernel/FlashAttention.h"
 #include "jules/Kernel/FusedKernels.h"
+#include "jules/Kernel/InterleavedAutodiff.h"
 #include "jules/Kernel/TilePlanner.h"
 
 using namespace jules::kernel;
@@ -72,6 +73,20 @@ int main(int argc, char** argv) {
   std::vector<float> loss(1, fusedCrossEntropyLoss(C.data(), tgt.data(), grad.data(), M, N));
   save(d + "/out_xent_grad.bin", grad);
   save(d + "/out_xent_loss.bin", loss);
+  // interleavedMLPForwardBackward [96,200] -> 136 -> 24 (ReLU), targets i % 24
+  {
+    std::vector<int32_t> t24(M);
+    for (int i = 0; i < M; ++i) t24[i] = i % 24;
+    std::vector<float> o(M * 24), gW1(Kd * N), gb1(N), gW2(N * 24), gb2(24), gX(M * Kd);
+    auto r = interleavedMLPForwardBackward(A.data(), W.data(), bias.data(), W2.data(), b2.data(),
+                                           t24.data(), o.data(), gW1.data(), gb1.data(),
+                                           gW2.data(), gb2.data(), gX.data(), M, Kd, N, 24, arena,
+                                           planner);
+    save(d + "/out_train_out.bin", o);
+    save(d + "/out_train_dW1.bin", gW1);
+    save(d + "/out_train_dX.bin", gX);
+    save(d + "/out_train_loss.bin", std::vector<float>(1, r.loss));
+  }
   std::printf("drop-in ok\n");
   return 0;
 }

@@ -63,6 +63,8 @@ def golden_cases():
     # matmulInt8 (FusedKernels.h:867-1073), from the reference build's scalar branch
     cases["int8"] = dict(kind="int8", M=64, N=96, K=200, seed=1000)
     cases["int8_bias"] = dict(kind="int8", M=33, N=40, K=77, seed=1001, bias=True)
+    # interleavedMLPForwardBackward (InterleavedAutodiff.h:55-160), bench_kernel.cpp-style shape
+    cases["mlp_train"] = dict(kind="mlp_train", M=64, K1=100, N1=48, N2=10, seed=1100)
     return cases
 
 
@@ -103,6 +105,14 @@ def make_inputs(c):
     if k == "xent":
         return [(3 * g.standard_normal((c["M"], c["N"]))).astype(np.float32),
                 g.integers(0, c["N"], c["M"]).astype(np.int32)]
+    if k == "mlp_train":
+        M, K1, N1, N2 = c["M"], c["K1"], c["N1"], c["N2"]
+        return [g.uniform(-1, 1, (M, K1)).astype(np.float32),
+                (g.uniform(-1, 1, (K1, N1)) / np.sqrt(K1)).astype(np.float32),
+                (0.1 * g.standard_normal(N1)).astype(np.float32),
+                (g.uniform(-1, 1, (N1, N2)) / np.sqrt(N1)).astype(np.float32),
+                (0.1 * g.standard_normal(N2)).astype(np.float32),
+                g.integers(0, N2, M).astype(np.int32)]
     if k == "int8":
         ins = [g.integers(-128, 128, (c["M"], c["K"])).astype(np.int8),
                g.integers(-128, 128, (c["K"], c["N"])).astype(np.int8)]
@@ -133,6 +143,10 @@ def run_reference(ref, c, ins):
     if k == "xent":
         loss, grad = ref.cross_entropy(ins[0], ins[1])
         return {"grad": grad, "loss": np.array([loss], np.float32)}
+    if k == "mlp_train":
+        r = ref.mlp_fwd_bwd(*ins)
+        r["loss"] = np.array([r["loss"]], np.float32)
+        return r
     if k == "int8":
         scalar = ref if ref.variant == "avx2" else oracle.Reference(variant="avx2")
         return {"out": scalar.matmul_int8(ins[0], ins[1], 0.02, 0.03,

@@ -21,10 +21,11 @@ def _c_decls():
 
 def _cxx_decls():
     names = set()
-    for f in ("FusedKernels.h", "FlashAttention.h"):
+    for f in ("FusedKernels.h", "FlashAttention.h", "InterleavedAutodiff.h"):
         src = open(os.path.join(INC, "jules", "Kernel", f)).read()
         src = re.sub(r"//.*", "", src)
-        for m in re.finditer(r"^\s*(?:void|int|bool|float)\s+([A-Za-z0-9_]+)\s*\(", src, flags=re.M):
+        for m in re.finditer(r"^\s*(?:void|int|bool|float|InterleavedMLPResult)\s+([A-Za-z0-9_]+)\s*\(",
+                             src, flags=re.M):
             names.add(m.group(1))
     return sorted(names)
 

@@ -54,3 +54,9 @@ def test_drop_in_matches_reference(tmp_path, jb, ref):
     loss, grad = ref.cross_entropy(C, tgt)
     assert rel_l2(out("xent_grad", (96, 136)), grad) <= F32_REL_L2
     assert abs(float(out("xent_loss", (1,))[0]) - loss) <= 1e-5 * max(1.0, abs(loss))
+    t24 = (np.arange(96) % 24).astype(np.int32)
+    tr = ref.mlp_fwd_bwd(A, W, bias, W2, b2, t24)
+    assert rel_l2(out("train_out", (96, 24)), tr["out"]) <= F32_REL_L2
+    assert rel_l2(out("train_dW1", (200, 136)), tr["dW1"]) <= F32_REL_L2
+    assert rel_l2(out("train_dX", (96, 200)), tr["dX"]) <= F32_REL_L2
+    assert abs(float(out("train_loss", (1,))[0]) - tr["loss"]) <= 1e-5 * max(1.0, abs(tr["loss"]))

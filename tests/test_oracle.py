@@ -53,6 +53,10 @@ def _restated(orc, c, ins):
     if k == "xent":
         loss, grad = orc.cross_entropy(ins[0], ins[1])
         return {"grad": grad, "loss": np.array([loss], np.float32)}
+    if k == "mlp_train":
+        r = orc.mlp_fwd_bwd(*ins)
+        r["loss"] = np.array([r["loss"]], np.float32)
+        return r
     if k == "int8":
         return {"out": orc.matmul_int8(ins[0], ins[1], 0.02, 0.03, ins[2] if len(ins) > 2 else None)}
     raise ValueError(k)
