@@ -481,7 +481,7 @@ class Int8Gemm(Workload):
     kind::i8.  Counted in int8 ops (2*M*N*K), reported as TOPS."""
     unit = "TOPS"
     dtype = "s8"
-    dominant = "gemm_s8_tc_kernel<256, 4>"
+    dominant = "gemm_s8_tc2_kernel<6>"
 
     def __init__(self, jb, torch, rank, world, M=8192, N=8192, K=8192):
         self.jb, self.torch = jb, torch

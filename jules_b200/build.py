@@ -19,7 +19,7 @@ LIB_DIR = os.path.join(HERE, "_lib")
 LIB = os.path.join(LIB_DIR, "libjules_b200.so")
 
 SOURCES = ["capi.cu", "host_api.cpp"]
-HEADERS = ["sm100.cuh", "gemm_tc.cuh", "attn_tc.cuh", "simt.cuh"]
+HEADERS = sorted(f for f in os.listdir(CSRC) if f.endswith(".cuh"))
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC,-O3",
                      "-I" + os.path.join(ROOT, "include")]

@@ -383,8 +383,46 @@ int gemm_s8(const int8_t* A, const int8_t* B, const float* bias, float* C, int64
             int64_t K, float scale, cudaStream_t st) {
   int dev;
   if (int rc = current_device(&dev)) return rc;
-  if (K % 16 == 0 && N % 16 == 0 && aligned16(A) && aligned16(B) && aligned16(C) &&
-      (!bias || aligned16(bias))) {
+  const bool tc_ok = K % 16 == 0 && N % 16 == 0 && aligned16(A) && aligned16(B) && aligned16(C) &&
+                     (!bias || aligned16(bias));
+  if (tc_ok && M >= 256 && N >= 256) {
+    // CTA pairs, 256 x 256 tiles
+    constexpr int STAGES = 6;
+    CUtensorMap ta, tb;
+    if (int rc = make_tmap_i8(&ta, A, (uint64_t)K, (uint64_t)M, jb::gemm8::BK, 128)) return rc;
+    if (int rc = make_tmap_i8(&tb, B, (uint64_t)N, (uint64_t)K, 128, jb::gemm8::BK)) return rc;
+    auto kern = jb::gemm8::gemm_s8_tc2_kernel<STAGES>;
+    const size_t smem = sizeof(jb::gemm8::Smem8p<STAGES>) + 1024;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(jb::gemm8::kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    static int max_pairs[64] = {};
+    int& mp = max_pairs[dev & 63];
+    if (mp == 0) {
+      std::lock_guard<std::mutex> lk(g_dev_mu);
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_s8 pair)");
+      cfg.gridDim = dim3(2 * (device_sms(dev) / 2));
+      int clusters = 0;
+      e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+      if (e != cudaSuccess || clusters <= 0) clusters = device_sms(dev) / 2;
+      mp = clusters;
+    }
+    const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
+    cfg.gridDim = dim3((unsigned)(2 * (tiles < mp ? tiles : mp)));
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, bias, C, (int)M, (int)N, (int)K, scale);
+    if (e != cudaSuccess) return cuda_fail(e, "gemm_s8_tc2_kernel launch");
+    return check_launch("gemm_s8_tc2_kernel launch");
+  }
+  if (tc_ok) {
     constexpr int BN = 256, STAGES = 4;
     CUtensorMap ta, tb;
     if (int rc = make_tmap_i8(&ta, A, (uint64_t)K, (uint64_t)M, jb::gemm8::BK, jb::gemm8::BM)) return rc;

@@ -205,6 +205,201 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
 }
 
+#define JB_MMA2_I8(ai, bi, pr) \
+  "tcgen05.mma.cta_group::2.kind::i8 [%0], %" #ai ", %" #bi ", %10, " pr ";\n\t"
+// Four K=32 steps of the pair MMA, int8: D (+)= A[smem] * B[smem].
+__device__ __forceinline__ void umma4_pair_i8(uint32_t d_tmem, const uint64_t (&a)[4],
+                                              const uint64_t (&b)[4], uint32_t acc_first,
+                                              uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %9, 0;\n\t"
+      "setp.eq.b32 q, %9, %9;\n\t"
+      JB_MMA2_I8(1, 5, "p") JB_MMA2_I8(2, 6, "q") JB_MMA2_I8(3, 7, "q") JB_MMA2_I8(4, 8, "q")
+      "}" ::"r"(d_tmem), "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(b[0]), "l"(b[1]),
+      "l"(b[2]), "l"(b[3]), "r"(acc_first), "r"(idesc)
+      : "memory");
+}
+
+template <int STAGES>
+struct Smem8p {
+  static constexpr int kABytes = 128 * BK;  // this CTA's 128 rows of A
+  static constexpr int kBBytes = BK * 128;  // this CTA's 128 columns of B
+  alignas(1024) uint8_t a[STAGES][kABytes];
+  alignas(1024) uint8_t b[STAGES][kBBytes];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+// CTA-pair form (cta_group::2, cluster of 2): 256 x 256 output tiles, each
+// CTA stages its 128 rows of A and its 128 columns of B, the leader issues
+// M=256, N=256 MMAs for both, and each CTA's epilogue handles its own 128
+// rows (TMEM holds a CTA's rows x all 256 columns).  Same barrier protocol as
+// gemm_bf16_tc2_kernel (gemm_tc.cuh).
+template <int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_s8_tc2_kernel(const __grid_constant__ CUtensorMap tmA,
+                       const __grid_constant__ CUtensorMap tmB, const float* __restrict__ bias,
+                       float* __restrict__ C, int M, int N, int K, float scale) {
+  constexpr int TM = 256, TN = 256;
+  constexpr uint32_t kTmemCols = 2 * TN;
+  using S = Smem8p<STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  S& s = *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair_id = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+  const int num_m = (M + TM - 1) / TM;
+  const int num_n = (N + TN - 1) / TN;
+  const int num_tiles = num_m * num_n;
+  const int num_k = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.tfull[i], 1);
+      mbar_init(&s.tempty[i], 2 * 128);
+    }
+    s.abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&s.tmem_base, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = s.tmem_base;
+  volatile int* abort_flag = &s.abort_flag;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair_id; t < num_tiles && ok; t += num_pairs) {
+        int mi, ni;
+        gemm::tile_coords(t, num_m, num_n, mi, ni);
+        const int m0 = mi * TM + (int)rank * 128;
+        const int n0 = ni * TN + (int)rank * 128;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&s.empty[stage], phase ^ 1u, 84, abort_flag)) { ok = false; break; }
+          if (leader) mbar_arrive_expect_tx(&s.full[stage], 2 * (S::kABytes + S::kBBytes));
+          tma_load_2d_pair(s.a[stage], &tmA, &s.full[stage], kb * BK, m0);
+          tma_load_2d_pair(s.b[stage], &tmB, &s.full[stage], n0, kb * BK);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader CTA) ----------------
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc_s8_s32(TM, TN, true);
+      const uint32_t empty0 = smem_u32(&s.empty[0]);
+      const uint32_t tfull0 = smem_u32(&s.tfull[0]);
+      const uint32_t empty0_peer = mapa_shared(empty0, 1);
+      const uint32_t tfull0_peer = mapa_shared(tfull0, 1);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = pair_id; t < num_tiles && ok; t += num_pairs) {
+        if (!mbar_wait(&s.tempty[acc], acc_phase ^ 1u, 85, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * TN;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&s.full[stage], phase, 86, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t a0 = sdesc_sw128(smem_u32(s.a[stage]), 16, 1024);
+          const uint64_t b0 = sdesc_sw128(smem_u32(s.b[stage]), BK * 128, 1024);
+          uint64_t ad[4], bd[4];
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            ad[kk] = a0 + kk * 2;    // +32 bytes (32 int8 of K) inside the swizzle row
+            bd[kk] = b0 + kk * 256;  // +32 K rows of 128 bytes
+          }
+          umma4_pair_i8(d_tmem, ad, bd, kb > 0 ? 1u : 0u, idesc);
+          umma_commit_pair(empty0 + stage * 8);
+          umma_commit_pair(empty0_peer + stage * 8);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit_pair(tfull0 + acc * 8);
+        umma_commit_pair(tfull0_peer + acc * 8);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5, both CTAs) ----------------
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    const uint32_t tempty0_leader = mapa_shared(smem_u32(&s.tempty[0]), 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = pair_id; t < num_tiles; t += num_pairs) {
+      int mi, ni;
+      gemm::tile_coords(t, num_m, num_n, mi, ni);
+      const int m0 = mi * TM + (int)rank * 128;
+      const int n0 = ni * TN;
+      if (!mbar_wait(&s.tfull[acc], acc_phase, 87, abort_flag)) break;
+      tc_fence_after();
+      const int row = m0 + row_in_tile;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * TN;
+#pragma unroll 1
+      for (int c = 0; c < TN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(t_row + c * 32, r);
+        tmem_ld_wait(r);
+        const int col0 = n0 + c * 32;
+        if (row < M && col0 < N) {
+          float* crow = C + (size_t)row * N;
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int col = col0 + g * 8;
+            if (col < N) {
+              float v[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) v[j] = (float)(int32_t)r[g * 8 + j] * scale;
+              if (bias) {
+                const float4 b0 = *reinterpret_cast<const float4*>(bias + col);
+                const float4 b1 = *reinterpret_cast<const float4*>(bias + col + 4);
+                v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
+                v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
+              }
+              gemm::store8(crow + col, v);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(tempty0_leader + acc * 8);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, kTmemCols);
+}
+
 // CUDA-core fallback for shapes the tensor-core path does not take (K or N
 // not a multiple of 16, unaligned pointers): 16x16 output tiles, K in
 // chunks of 64 staged through shared memory, exact int32 accumulation.

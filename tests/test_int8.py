@@ -16,8 +16,9 @@ def _exact(A, B, sa, sb, bias):
     return C + bias if bias is not None else C
 
 
+# M, N >= 256 take the CTA-pair kernel (256 x 256 tiles), the rest the 1-CTA one
 @pytest.mark.parametrize("M,N,K", [(256, 256, 128), (300, 512, 384), (1, 16, 16), (129, 272, 4096),
-                                   (640, 1024, 1024)])
+                                   (640, 1024, 1024), (1000, 784, 528), (2048, 2304, 2048)])
 @pytest.mark.parametrize("with_bias", [False, True])
 def test_matmul_int8_tensor_cores(jb, M, N, K, with_bias):
     import torch
