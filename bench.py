@@ -50,7 +50,7 @@ def parse():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["jules", "reference"], default="jules")
     p.add_argument("--workload", choices=["gemm", "attn", "attn_gqa", "mlp", "attn_fp32",
-                                          "softmax", "xent", "int8"],
+                                          "softmax", "xent", "int8", "fp8"],
                    default="gemm")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
@@ -94,6 +94,12 @@ def roofline(wl, achieved, peak, peak_kind, traffic):
                 "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                 "peak_kind": "measured HBM copy (MEASURED_PEAKS.json hbm_gbs)",
                 "traffic": traffic, "traffic_unit": "DRAM bytes per launch (ncu, profiles/)"}
+    if isinstance(wl, Fp8Gemm):
+        return {"bound": "tensor", "kernel": wl.dominant, "achieved": round(achieved, 2),
+                "peak": NOMINAL_FP8_TFLOPS, "unit": "TFLOP/s",
+                "frac": round(achieved / NOMINAL_FP8_TFLOPS, 4),
+                "peak_kind": "nominal dense fp8 (datasheet; no measured fp8 figure)",
+                "traffic": traffic, "traffic_unit": "DRAM bytes per launch (ncu, profiles/)"}
     fp32 = isinstance(wl, AttentionF32)
     p = NOMINAL_FP32_TFLOPS if fp32 else peak
     return {"bound": "fp32_cuda_cores" if fp32 else "tensor", "kernel": wl.dominant,
@@ -109,7 +115,7 @@ def profiled_traffic(workload):
     summary (profiles/<kernel>_<workload>.md, line 'traffic_bytes_per_launch:')."""
     name = {"gemm": "gemm_tc_c2", "attn": "attn_tc_c3", "attn_gqa": "attn_tc_c5",
             "mlp": "gemm_tc_c4", "attn_fp32": "attn_simt_c1", "softmax": "rows_softmax",
-            "xent": "rows_xent", "int8": "gemm_s8_int8"}[workload]
+            "xent": "rows_xent", "int8": "gemm_s8_int8", "fp8": "gemm_f8_fp8"}[workload]
     path = os.path.join(HERE, "profiles", f"{name}.md")
     try:
         with open(path) as f:
@@ -143,6 +149,10 @@ def describe(workload, world, extra_l2=None):
         c = {"workload": "int8 GEMM (matmulInt8): s8 x s8 -> s32 -> fp32 * scale + bias",
              "M_per_rank": 8192, "N": 8192, "K": 8192, "global_M": 8192 * world,
              "sharding": "rows of M", "op_convention": "2*M*N*K int8 ops"}
+    elif workload == "fp8":
+        c = {"workload": "fp8 GEMM + bias + GELU(tanh): e4m3 x e4m3 -> fp32 accumulate -> bf16",
+             "M_per_rank": 8192, "N": 8192, "K": 8192, "global_M": 8192 * world,
+             "sharding": "rows of M", "flop_convention": "2*M*N*K"}
     elif workload == "softmax":
         c = {"workload": "row softmax (fusedSoftmax), fp32", "M_per_rank": 16384, "N": 4096,
              "global_M": 16384 * world, "sharding": "rows",
@@ -526,6 +536,58 @@ class Int8Gemm(Workload):
         self.hC.copy_(self.dC, non_blocking=True)
 
 
+class Fp8Gemm(Workload):
+    """fp8 GEMM + bias + GELU, M = N = K = 8192 per rank (rows of M sharded):
+    E4M3 operands (the mixed-precision pass's fp8 target), fp32 accumulation
+    on tcgen05 kind::f8f6f4, bf16 output."""
+    dtype = "e4m3"
+    dominant = "gemm_f8_tc2_kernel<6, bf16>"
+
+    def __init__(self, jb, torch, rank, world, M=8192, N=8192, K=8192):
+        self.jb, self.torch = jb, torch
+        self.M, self.N, self.K = M, N, K
+        dev = torch.device("cuda")
+        g = torch.Generator(device=dev).manual_seed(9 + rank)
+        per_set = M * K + K * N + M * N * 2
+        self.nsets = self.sets_for(per_set)
+        f8 = torch.float8_e4m3fn
+        self.A = [torch.randn((M, K), generator=g, device=dev).to(f8) for _ in range(self.nsets)]
+        self.B = [(torch.randn((K, N), generator=g, device=dev) / 16).to(f8)
+                  for _ in range(self.nsets)]
+        self.bias = 0.02 * torch.randn(N, generator=g, device=dev)
+        self.C = [torch.empty((M, N), dtype=torch.bfloat16, device=dev) for _ in range(self.nsets)]
+        self.scale = 1.0 / 8.0
+        self.flops_per_step = 2.0 * M * N * K
+        self.flops_dominant = self.flops_per_step
+        self.config = {"l2": f"{self.nsets} rotating input sets ({self.nsets * per_set / 2**20:.0f} MiB > L2)"}
+
+    def step(self, i, ev=None):
+        k = i % self.nsets
+        if ev:
+            ev[0].record()
+        self.jb.gemm_fp8(self.A[k], self.B[k], self.bias, act="gelu", scale=self.scale,
+                         out=self.C[k])
+        if ev:
+            ev[1].record()
+
+    def output(self, i):
+        return self.C[i % self.nsets]
+
+    def e2e_setup(self):
+        t = self.torch
+        self.hA, self.hB = self.A[0].cpu().pin_memory(), self.B[0].cpu().pin_memory()
+        self.hC = t.empty_like(self.C[0], device="cpu").pin_memory()
+        self.dA, self.dB, self.dC = t.empty_like(self.A[0]), t.empty_like(self.B[0]), t.empty_like(self.C[0])
+        self.h2d = self.hA.numel() + self.hB.numel()
+        self.d2h = self.hC.numel() * 2
+
+    def e2e_step(self):
+        self.dA.copy_(self.hA, non_blocking=True)
+        self.dB.copy_(self.hB, non_blocking=True)
+        self.jb.gemm_fp8(self.dA, self.dB, self.bias, act="gelu", scale=self.scale, out=self.dC)
+        self.hC.copy_(self.dC, non_blocking=True)
+
+
 class RowWise(Workload):
     """Row softmax (softmax) or fused softmax + cross-entropy (xent), fp32,
     rows sharded across ranks.  HBM-bound: work is counted in bytes."""
@@ -594,8 +656,13 @@ METRIC = "Flash-attn fwd & fused-GEMM TFLOP/s at 1/2/4/8 B200; % of tensor peak"
 # Extra (non-headline) workloads of the row-wise kernels report HBM bytes per second.
 ROWS_METRIC = "Row softmax / fused cross-entropy GB/s (HBM bytes moved) per B200"
 INT8_METRIC = "int8 GEMM TOPS (matmulInt8) per B200"
-# B200 datasheet dense int8 tensor throughput (no measured figure on this pool).
+FP8_METRIC = "fp8 GEMM + bias + GELU TFLOP/s (mixed-precision matmul at fp8) per B200"
+# B200 datasheet dense int8 / fp8 tensor throughput (no measured figures on this pool).
 NOMINAL_INT8_TOPS = 4500.0
+NOMINAL_FP8_TFLOPS = 4500.0
+# The reference has no fp8 kernel (its mixed-precision pass only names the
+# types), so the fp8 CPU leg times the oracle's restatement ("port").
+CPU_KIND = {"fp8": "port"}
 JSON_OUT = sys.stdout
 
 
@@ -642,6 +709,17 @@ def cpu_reference_sample(workload, reps=3, warm=1):
         flops = 2.0 * Ms * N * K
         desc = (f"reference matmulInt8 (FusedKernels.h:867-1073, scalar branch) on {Ms} of the "
                 f"8192 rows; ops 2*M*N*K")
+        reps = 2
+    elif workload == "fp8":
+        Ms, N, K = 16, 8192, 8192
+        R = oracle.Restated()
+        A = R.fp8_encode(g.standard_normal((Ms, K)).astype(np.float32), "e4m3")
+        B = R.fp8_encode((g.standard_normal((K, N)) / 16).astype(np.float32), "e4m3")
+        bias = (0.02 * g.standard_normal(N)).astype(np.float32)
+        fn = lambda: R.gemm_fp8(A, B, "e4m3", "e4m3", bias, None, "gelu", 1.0 / 8.0)
+        flops = 2.0 * Ms * N * K
+        desc = (f"oracle restatement orc_gemm_fp8 (oracle/restate.c; the reference has no fp8 "
+                f"kernel) on {Ms} of the 8192 rows; FLOPs 2*M*N*K")
         reps = 2
     elif workload in ("softmax", "xent"):
         if workload == "softmax":
@@ -711,7 +789,7 @@ def run_reference_arm(args):
     value = statistics.mean(vals)
     rowwise = args.workload in ("softmax", "xent")
     unit = "GB/s" if rowwise else ("TOPS" if args.workload == "int8" else "TFLOP/s")
-    metric = ROWS_METRIC if rowwise else (INT8_METRIC if args.workload == "int8" else METRIC)
+    metric = ROWS_METRIC if rowwise else {"int8": INT8_METRIC, "fp8": FP8_METRIC}.get(args.workload, METRIC)
     line = {"metric": metric, "value": round(value, 6), "unit": unit,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(wall / args.steps * 1e3, 3), "higher_is_better": True,
@@ -719,7 +797,7 @@ def run_reference_arm(args):
             "config": describe(args.workload, world, "CPU: bounded sample per step"),
             "impl": "reference",
             "cpu_baseline": {"value": round(value, 6), "unit": unit, "cores": threads,
-                             "kind": "reference", "sample": desc},
+                             "kind": CPU_KIND.get(args.workload, "reference"), "sample": desc},
             "e2e": {"value": round(value, 6), "unit": unit, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     emit(line)
@@ -762,7 +840,8 @@ def main():
          "attn_fp32": lambda: AttentionF32(jb, torch, rank, world),
          "softmax": lambda: RowWise(jb, torch, rank, world, xent=False),
          "xent": lambda: RowWise(jb, torch, rank, world, xent=True),
-         "int8": lambda: Int8Gemm(jb, torch, rank, world)}[args.workload]
+         "int8": lambda: Int8Gemm(jb, torch, rank, world),
+         "fp8": lambda: Fp8Gemm(jb, torch, rank, world)}[args.workload]
     wl = W()
     stream = torch.cuda.current_stream()
 
@@ -846,15 +925,16 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
             v, desc, threads = cpu_reference_sample(args.workload)
-            cpu = {"value": round(v, 6), "unit": wl.unit, "cores": threads, "kind": "reference",
-                   "sample": desc}
+            cpu = {"value": round(v, 6), "unit": wl.unit, "cores": threads,
+                   "kind": CPU_KIND.get(args.workload, "reference"), "sample": desc}
         except Exception as ex:  # the GPU number stands without it
             cpu = {"value": None, "unit": wl.unit, "cores": None, "kind": "reference",
                    "sample": f"unavailable: {ex}"}
 
     if rank == 0:
         line = {
-            "metric": {"TFLOP/s": METRIC, "GB/s": ROWS_METRIC, "TOPS": INT8_METRIC}[wl.unit],
+            "metric": (FP8_METRIC if isinstance(wl, Fp8Gemm) else
+                       {"TFLOP/s": METRIC, "GB/s": ROWS_METRIC, "TOPS": INT8_METRIC}[wl.unit]),
             "value": round(tflops_total, 3), "unit": wl.unit,
             "n_gpus": world, "steps": K, "warmup": args.warmup,
             "ms_per_step": round(ms_total / K, 5), "higher_is_better": True, "scaling": "weak",
@@ -863,7 +943,7 @@ def main():
             "config": describe(args.workload, world, wl.config.get("l2")),
             "roofline": roofline(wl, achieved, peak, peak_kind, traffic),
             **({"pct_of_dense_bf16_peak_2250": round(100 * tflops_total / world / 2250.0, 2)}
-               if wl.unit == "TFLOP/s" else {}),
+               if wl.unit == "TFLOP/s" and not isinstance(wl, Fp8Gemm) else {}),
             "clocks": clocks,
             "e2e": e2e,
             "gpu_launches": K * wl.launches_per_step,

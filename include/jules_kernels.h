@@ -43,6 +43,11 @@ extern "C" {
 /* Element types. */
 #define JULES_DTYPE_F32 0
 #define JULES_DTYPE_BF16 1
+/* 8-bit floats (OCP FP8): E4M3 (finite only, max 448) and E5M2 (max 57344),
+ * the two fp8 types of the reference's mixed-precision pass
+ * (lib/Passes/MixedPrecisionPass.cpp:55-62, lib/Dialect/JulesDialect.cpp:41). */
+#define JULES_DTYPE_FP8E4M3 2
+#define JULES_DTYPE_FP8E5M2 3
 
 /* Activations: same order as jules::kernel::ActivationType
  * (include/jules/Kernel/FusedKernels.h:61-67). */
@@ -76,6 +81,8 @@ int jules_device_error(uint32_t* word, int clear);
  * bf16 in (bf16 or fp32 out) with N % 8 == 0, K % 8 == 0 and 16-byte
  * aligned pointers runs on tcgen05 tensor cores (fp32 accumulate, fp32
  * epilogue, one cast at the store); everything else on CUDA cores in fp32.
+ * in_dtype JULES_DTYPE_FP8E4M3 / FP8E5M2 runs jules_gemm_fp8 with scale 1
+ * (residual then bf16).
  * Replaces tiledMatmulWithActivation (FusedKernels.h:378-458),
  * fusedMatmulRelu (:203-259), fusedMatmulBiasRelu (:265-372) and
  * blasMatmul with alpha=1, beta=0, no transposes (:633-644).
@@ -137,6 +144,33 @@ int jules_gelu(const void* in, void* out, int64_t n, int dtype, void* stream);
  */
 int jules_matmul_int8(const int8_t* A, const int8_t* B, float* C, int64_t M, int64_t N,
                       int64_t K, float scale_a, float scale_b, const float* bias, void* stream);
+
+/*
+ * fp8 GEMM: C = act((A . W) * scale + bias) (+ residual), fp32 accumulation
+ * of products of 8-bit floats, fp32 epilogue, one cast at the store.
+ *   A [M,K] (a_dtype), W [K,N] (w_dtype), each JULES_DTYPE_FP8E4M3 or
+ *   JULES_DTYPE_FP8E5M2; bias [N] fp32 (nullable); residual [M,N] bf16
+ *   (nullable); C [M,N] fp32 or bf16 (out_dtype).  scale: the product of the
+ *   operands' dequantisation scales (1 for a plain cast).
+ * The matmul of the reference's mixed-precision pass at target "fp8"
+ * (lib/Passes/MixedPrecisionPass.cpp:1-28,125-140: inputs cast to fp8,
+ * accumulation in f32, result cast back), with the epilogue of
+ * tiledMatmulWithActivation (FusedKernels.h:378-458).  K and N multiples of
+ * 16 with 16-byte aligned pointers run on tcgen05 (kind::f8f6f4); other
+ * shapes on CUDA cores.
+ */
+int jules_gemm_fp8(const void* A, const void* W, const float* bias, const void* residual, void* C,
+                   int64_t M, int64_t N, int64_t K, float scale, int act, int a_dtype,
+                   int w_dtype, int out_dtype, void* stream);
+
+/*
+ * Element type conversion, n elements, any pair of JULES_DTYPE_* codes: the
+ * reference's jules.cast (include/jules/Dialect/JulesOps.td:369, inserted by
+ * lib/Passes/MixedPrecisionPass.cpp:176-184 createCastOp).  To bf16: round to nearest even.
+ * To fp8: round to nearest even, saturating to the largest finite value
+ * (E4M3 +-448, E5M2 +-57344); NaN stays NaN.  Widening casts are exact.
+ */
+int jules_cast(const void* src, void* dst, int64_t n, int src_dtype, int dst_dtype, void* stream);
 
 /*
  * Row softmax: out[i,:] = exp(x[i,:] - max_i) / sum_j exp(x[i,j] - max_i),

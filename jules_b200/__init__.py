@@ -17,13 +17,14 @@ import os
 __all__ = [
     "lib", "JulesError", "ACT", "gemm_bias_act", "flash_attention_fwd", "layernorm", "gelu",
     "mlp_block", "mlp_block_workspace_bytes", "sgemm", "device_error", "kernel_by_name",
-    "kernel_names", "LIB_PATH",
+    "kernel_names", "LIB_PATH", "gemm_fp8", "cast", "matmul_int8", "softmax",
+    "cross_entropy_loss", "custom_call", "mlp_fwd_bwd",
 ]
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libjules_b200.so")
 
 ACT = {"none": 0, "relu": 1, "sigmoid": 2, "tanh": 3, "gelu": 4}
-DT_F32, DT_BF16 = 0, 1
+DT_F32, DT_BF16, DT_FP8E4M3, DT_FP8E5M2 = 0, 1, 2, 3
 
 _c_vp = ctypes.c_void_p
 _c_i64 = ctypes.c_int64
@@ -49,6 +50,8 @@ _SIGNATURES = {
     "jules_mlp_fwd_bwd": ([_c_vp] * 13 + [_c_i64] * 4 + [_c_vp, ctypes.c_size_t, _c_vp], _c_int),
     "jules_matmul_int8": ([_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_f, _c_f, _c_vp, _c_vp],
                           _c_int),
+    "jules_gemm_fp8": ([_c_vp] * 5 + [_c_i64] * 3 + [_c_f] + [_c_int] * 4 + [_c_vp], _c_int),
+    "jules_cast": ([_c_vp, _c_vp, _c_i64, _c_int, _c_int, _c_vp], _c_int),
     "jules_cross_entropy_loss": ([_c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_int, _c_vp],
                                  _c_int),
     "jules_mlp_block_workspace_bytes": ([_c_i64, _c_i64, _c_i64], ctypes.c_size_t),
@@ -111,6 +114,10 @@ def _dtype_code(t) -> int:
         return DT_F32
     if t.dtype == torch.bfloat16:
         return DT_BF16
+    if t.dtype == torch.float8_e4m3fn:
+        return DT_FP8E4M3
+    if t.dtype == torch.float8_e5m2:
+        return DT_FP8E5M2
     raise TypeError(f"unsupported dtype {t.dtype}")
 
 
@@ -135,23 +142,26 @@ def device_error(clear: bool = True) -> int:
 
 def gemm_bias_act(A, W, bias=None, residual=None, act="none", out=None, out_dtype=None,
                   stream=None):
-    """C = act(A @ W + bias) (+ residual); A [M,K], W [K,N] (same dtype)."""
+    """C = act(A @ W + bias) (+ residual); A [M,K], W [K,N] (same dtype: fp32,
+    bf16, or an fp8 type with a bf16 residual and bf16 C by default)."""
     import torch
     _dense(A, "A"), _dense(W, "W")
     M, K = A.shape
     K2, N = W.shape
     if K2 != K or W.dtype != A.dtype:
         raise ValueError("A/W shape or dtype mismatch")
+    fp8 = A.dtype in (torch.float8_e4m3fn, torch.float8_e5m2)
     if out is None:
-        out = torch.empty((M, N), dtype=out_dtype or A.dtype, device=A.device)
+        out = torch.empty((M, N), dtype=out_dtype or (torch.bfloat16 if fp8 else A.dtype),
+                          device=A.device)
     if bias is not None:
         _dense(bias, "bias")
         if bias.dtype != torch.float32 or bias.numel() != N:
             raise ValueError("bias must be fp32 with N elements")
     if residual is not None:
         _dense(residual, "residual")
-        if residual.dtype != A.dtype or residual.shape != out.shape:
-            raise ValueError("residual must have A's dtype and C's shape")
+        if residual.dtype != (torch.bfloat16 if fp8 else A.dtype) or residual.shape != out.shape:
+            raise ValueError("residual must have A's dtype (bf16 for fp8 A) and C's shape")
     rc = lib().jules_gemm_bias_act(_ptr(A), _ptr(W), _ptr(bias), _ptr(residual), _ptr(out), M, N,
                                    K, ACT[act] if isinstance(act, str) else int(act),
                                    _dtype_code(A), _dtype_code(out), _stream(stream))
@@ -252,6 +262,50 @@ def matmul_int8(A, B, scale_a=1.0, scale_b=1.0, bias=None, out=None, stream=None
     rc = lib().jules_matmul_int8(_ptr(A), _ptr(B), _ptr(out), M, N, K, scale_a, scale_b,
                                  _ptr(bias), _stream(stream))
     _check(rc, "jules_matmul_int8")
+    return out
+
+
+def gemm_fp8(A, W, bias=None, residual=None, act="none", scale=1.0, out=None, out_dtype=None,
+             stream=None):
+    """C = act((A @ W) * scale + bias) (+ residual); A [M,K], W [K,N] in
+    torch.float8_e4m3fn / float8_e5m2 (each its own), fp32 accumulation;
+    residual bf16; C bf16 (default) or fp32."""
+    import torch
+    _dense(A, "A"), _dense(W, "W")
+    M, K = A.shape
+    K2, N = W.shape
+    if K2 != K:
+        raise ValueError("gemm_fp8: A/W shape mismatch")
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype or torch.bfloat16, device=A.device)
+    if bias is not None:
+        _dense(bias, "bias")
+        if bias.dtype != torch.float32 or bias.numel() != N:
+            raise ValueError("bias must be fp32 with N elements")
+    if residual is not None:
+        _dense(residual, "residual")
+        if residual.dtype != torch.bfloat16 or residual.shape != out.shape:
+            raise ValueError("residual must be bf16 with C's shape")
+    rc = lib().jules_gemm_fp8(_ptr(A), _ptr(W), _ptr(bias), _ptr(residual), _ptr(out), M, N, K,
+                              float(scale), ACT[act] if isinstance(act, str) else int(act),
+                              _dtype_code(A), _dtype_code(W), _dtype_code(out), _stream(stream))
+    _check(rc, "jules_gemm_fp8")
+    return out
+
+
+def cast(x, dtype, out=None, stream=None):
+    """Element type conversion among fp32, bf16, float8_e4m3fn and
+    float8_e5m2 (to fp8: round to nearest even, saturating to the largest
+    finite value)."""
+    import torch
+    _dense(x, "x")
+    if out is None:
+        out = torch.empty(x.shape, dtype=dtype, device=x.device)
+    elif out.numel() != x.numel():
+        raise ValueError("cast: out must have x's size")
+    rc = lib().jules_cast(_ptr(x), _ptr(out), x.numel(), _dtype_code(x), _dtype_code(out),
+                          _stream(stream))
+    _check(rc, "jules_cast")
     return out
 
 

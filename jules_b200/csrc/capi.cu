@@ -377,6 +377,76 @@ int attn_tc(const void* Q, const void* K, const void* V, void* O, float* lse, in
 // ===========================================================================
 namespace {
 
+// Launch an 8-bit CTA-pair kernel (cluster of 2) over the 256 x 256 tiles of
+// an M x N output: one pair per tile up to the number of co-resident pairs
+// (queried once per device and kernel, cached in max_pairs).
+template <typename... KArgs, typename... Args>
+int launch_pair8(void (*kern)(KArgs...), size_t smem, int dev, int64_t M, int64_t N,
+                 int (&max_pairs)[64], cudaStream_t st, const char* what, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(jb::gemm8::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int mp;
+  {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    mp = max_pairs[dev & 63];
+    if (mp == 0) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return cuda_fail(e, what);
+      cfg.gridDim = dim3(2 * (device_sms(dev) / 2));
+      int clusters = 0;
+      e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+      if (e != cudaSuccess || clusters <= 0) {
+        (void)cudaGetLastError();
+        clusters = device_sms(dev) / 2;
+      }
+      mp = max_pairs[dev & 63] = clusters;
+    }
+  }
+  const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  cfg.gridDim = dim3((unsigned)(2 * (tiles < mp ? tiles : mp)));
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return check_launch(what);
+}
+
+// fp8 GEMM (E4M3 / E5M2 operands, fp32 accumulation): tcgen05 kind::f8f6f4
+// on CTA pairs when K and N are multiples of 16 and the pointers 16-byte
+// aligned, CUDA cores otherwise.
+template <typename TOut>
+int gemm_f8(const uint8_t* A, const uint8_t* W, const float* bias, const __nv_bfloat16* res,
+            TOut* C, int64_t M, int64_t N, int64_t K, float scale, int a_fmt, int w_fmt, int act,
+            cudaStream_t st) {
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  if (K % 16 == 0 && N % 16 == 0 && aligned16(A) && aligned16(W) && aligned16(C) &&
+      (!bias || aligned16(bias)) && (!res || aligned16(res))) {
+    constexpr int STAGES = 6;
+    CUtensorMap ta, tb;
+    if (int rc = make_tmap_i8(&ta, A, (uint64_t)K, (uint64_t)M, jb::gemm8::BK, 128)) return rc;
+    if (int rc = make_tmap_i8(&tb, W, (uint64_t)N, (uint64_t)K, 128, jb::gemm8::BK)) return rc;
+    static int max_pairs[64] = {};
+    const uint32_t idesc = jb::gemm8::idesc_f8_f32(256, 256, a_fmt, w_fmt, true);
+    return launch_pair8(jb::gemm8::gemm_f8_tc2_kernel<STAGES, TOut>,
+                        sizeof(jb::gemm8::Smem8p<STAGES>) + 1024, dev, M, N, max_pairs, st,
+                        "gemm_f8_tc2_kernel", ta, tb, bias, res, C, (int)M, (int)N, (int)K, scale,
+                        idesc, act);
+  }
+  dim3 grid((unsigned)((N + 15) / 16), (unsigned)((M + 15) / 16));
+  if (grid.y > 65535u) return fail(JULES_ERR_SHAPE, "gemm_fp8: M too large for the CUDA-core path");
+  jb::gemm8::gemm_f8_simt_kernel<TOut><<<grid, 256, 0, st>>>(A, W, bias, res, C, (int)M, (int)N,
+                                                             (int)K, scale, a_fmt, w_fmt, act);
+  return check_launch("gemm_f8_simt_kernel launch");
+}
+
 // int8 GEMM: tcgen05 kind::i8 when K and N are multiples of 16 and the
 // pointers 16-byte aligned, CUDA cores otherwise.
 int gemm_s8(const int8_t* A, const int8_t* B, const float* bias, float* C, int64_t M, int64_t N,
@@ -391,36 +461,10 @@ int gemm_s8(const int8_t* A, const int8_t* B, const float* bias, float* C, int64
     CUtensorMap ta, tb;
     if (int rc = make_tmap_i8(&ta, A, (uint64_t)K, (uint64_t)M, jb::gemm8::BK, 128)) return rc;
     if (int rc = make_tmap_i8(&tb, B, (uint64_t)N, (uint64_t)K, 128, jb::gemm8::BK)) return rc;
-    auto kern = jb::gemm8::gemm_s8_tc2_kernel<STAGES>;
-    const size_t smem = sizeof(jb::gemm8::Smem8p<STAGES>) + 1024;
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.blockDim = dim3(jb::gemm8::kThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
     static int max_pairs[64] = {};
-    int& mp = max_pairs[dev & 63];
-    if (mp == 0) {
-      std::lock_guard<std::mutex> lk(g_dev_mu);
-      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm_s8 pair)");
-      cfg.gridDim = dim3(2 * (device_sms(dev) / 2));
-      int clusters = 0;
-      e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
-      if (e != cudaSuccess || clusters <= 0) clusters = device_sms(dev) / 2;
-      mp = clusters;
-    }
-    const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
-    cfg.gridDim = dim3((unsigned)(2 * (tiles < mp ? tiles : mp)));
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, bias, C, (int)M, (int)N, (int)K, scale);
-    if (e != cudaSuccess) return cuda_fail(e, "gemm_s8_tc2_kernel launch");
-    return check_launch("gemm_s8_tc2_kernel launch");
+    return launch_pair8(jb::gemm8::gemm_s8_tc2_kernel<STAGES>,
+                        sizeof(jb::gemm8::Smem8p<STAGES>) + 1024, dev, M, N, max_pairs, st,
+                        "gemm_s8_tc2_kernel", ta, tb, bias, C, (int)M, (int)N, (int)K, scale);
   }
   if (tc_ok) {
     constexpr int BN = 256, STAGES = 4;
@@ -553,6 +597,9 @@ int jules_gemm_bias_act(const void* A, const void* W, const float* bias, const v
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail(JULES_ERR_SHAPE, "gemm: dimension exceeds 2^31-1");
   if (act < JULES_ACT_NONE || act > JULES_ACT_GELU) return fail(JULES_ERR_ARG, "gemm: act=%d", act);
   if (M == 0) return ok();
+  if (in_dtype == JULES_DTYPE_FP8E4M3 || in_dtype == JULES_DTYPE_FP8E5M2)
+    return jules_gemm_fp8(A, W, bias, residual, C, M, N, K, 1.0f, act, in_dtype, in_dtype,
+                          out_dtype, stream);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool in_bf = in_dtype == JULES_DTYPE_BF16, out_bf = out_dtype == JULES_DTYPE_BF16;
   if ((in_dtype != JULES_DTYPE_F32 && !in_bf) || (out_dtype != JULES_DTYPE_F32 && !out_bf))
@@ -669,6 +716,58 @@ int jules_matmul_int8(const int8_t* A, const int8_t* B, float* C, int64_t M, int
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail(JULES_ERR_SHAPE, "matmul_int8: dimension exceeds 2^31-1");
   if (M == 0) return ok();
   return gemm_s8(A, B, bias, C, M, N, K, scale_a * scale_b, static_cast<cudaStream_t>(stream));
+}
+
+int jules_gemm_fp8(const void* A, const void* W, const float* bias, const void* residual, void* C,
+                   int64_t M, int64_t N, int64_t K, float scale, int act, int a_dtype,
+                   int w_dtype, int out_dtype, void* stream) {
+  if (!A || !W || !C) return fail(JULES_ERR_ARG, "gemm_fp8: NULL A, W or C");
+  if (M < 0 || N <= 0 || K <= 0) return fail(JULES_ERR_SHAPE, "gemm_fp8: M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail(JULES_ERR_SHAPE, "gemm_fp8: dimension exceeds 2^31-1");
+  if (act < JULES_ACT_NONE || act > JULES_ACT_GELU) return fail(JULES_ERR_ARG, "gemm_fp8: act=%d", act);
+  auto fmt = [](int dt) {
+    return dt == JULES_DTYPE_FP8E4M3 ? jb::gemm8::kFmtE4M3 : (dt == JULES_DTYPE_FP8E5M2 ? jb::gemm8::kFmtE5M2 : -1);
+  };
+  const int af = fmt(a_dtype), wf = fmt(w_dtype);
+  if (af < 0 || wf < 0 || (out_dtype != JULES_DTYPE_F32 && out_dtype != JULES_DTYPE_BF16))
+    return fail(JULES_ERR_DTYPE, "gemm_fp8: dtypes %d/%d/%d", a_dtype, w_dtype, out_dtype);
+  if (M == 0) return ok();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const auto* a = static_cast<const uint8_t*>(A);
+  const auto* w = static_cast<const uint8_t*>(W);
+  const auto* r = static_cast<const __nv_bfloat16*>(residual);
+  if (out_dtype == JULES_DTYPE_BF16)
+    return gemm_f8(a, w, bias, r, static_cast<__nv_bfloat16*>(C), M, N, K, scale, af, wf, act, st);
+  return gemm_f8(a, w, bias, r, static_cast<float*>(C), M, N, K, scale, af, wf, act, st);
+}
+
+int jules_cast(const void* src, void* dst, int64_t n, int src_dtype, int dst_dtype, void* stream) {
+  if (!src || !dst) return fail(JULES_ERR_ARG, "cast: NULL pointer");
+  if (n < 0) return fail(JULES_ERR_SHAPE, "cast: n=%lld", (long long)n);
+  auto valid = [](int d) { return d >= JULES_DTYPE_F32 && d <= JULES_DTYPE_FP8E5M2; };
+  if (!valid(src_dtype) || !valid(dst_dtype)) return fail(JULES_ERR_DTYPE, "cast: dtypes %d -> %d", src_dtype, dst_dtype);
+  if (n == 0) return ok();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  const int grid_cap = device_sms(dev) * 8;
+  const bool to_f8 = dst_dtype == JULES_DTYPE_FP8E4M3 || dst_dtype == JULES_DTYPE_FP8E5M2;
+  const int f = dst_dtype == JULES_DTYPE_FP8E5M2 ? jb::gemm8::kFmtE5M2 : jb::gemm8::kFmtE4M3;
+  if (to_f8 && (src_dtype == JULES_DTYPE_F32 || src_dtype == JULES_DTYPE_BF16) && n % 8 == 0 &&
+      aligned16(src) && aligned16(dst)) {
+    const int64_t n8 = n / 8;
+    const int grid = (int)std::min<int64_t>((n8 + 255) / 256, grid_cap);
+    if (src_dtype == JULES_DTYPE_F32)
+      jb::gemm8::cast_to_f8_vec_kernel<float><<<grid, 256, 0, st>>>(
+          static_cast<const float*>(src), static_cast<uint8_t*>(dst), n8, f);
+    else
+      jb::gemm8::cast_to_f8_vec_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+          static_cast<const __nv_bfloat16*>(src), static_cast<uint8_t*>(dst), n8, f);
+    return check_launch("cast_to_f8_vec_kernel launch");
+  }
+  const int grid = (int)std::min<int64_t>((n + 255) / 256, grid_cap);
+  jb::gemm8::cast_kernel<<<grid, 256, 0, st>>>(src, dst, n, src_dtype, dst_dtype);
+  return check_launch("cast_kernel launch");
 }
 
 int jules_softmax(const void* in, void* out, int64_t M, int64_t N, int in_dtype, int out_dtype,

@@ -34,6 +34,7 @@ _i32p = ctypes.POINTER(ctypes.c_int)
 _i64p = ctypes.POINTER(ctypes.c_int64)
 
 ACT = {"none": 0, "relu": 1, "sigmoid": 2, "tanh": 3, "gelu": 4}
+FP8_FMT = {"e4m3": 0, "e5m2": 1}
 
 
 def build(reference_root: str = "/root/reference") -> None:
@@ -120,6 +121,11 @@ class Restated:
             ctypes.c_int, ctypes.c_int]
         lib.orc_mlp_block.argtypes = [_f32p] * 8 + [ctypes.c_int64] * 3 + [ctypes.c_float, _i64p,
                                                                           ctypes.c_int64]
+        lib.orc_fp8_decode.argtypes = [ctypes.c_void_p, _f32p, ctypes.c_int64, ctypes.c_int]
+        lib.orc_fp8_encode.argtypes = [_f32p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int]
+        lib.orc_gemm_fp8.argtypes = [ctypes.c_void_p, ctypes.c_void_p, _f32p, _f32p, _f32p,
+                                     ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_float,
+                                     ctypes.c_int, ctypes.c_int, ctypes.c_int]
         lib.orc_matmul_int8.argtypes = [ctypes.c_void_p, ctypes.c_void_p, _f32p, ctypes.c_int64,
                                         ctypes.c_int64, ctypes.c_int64, ctypes.c_float,
                                         ctypes.c_float, _f32p]
@@ -174,6 +180,37 @@ class Restated:
         C = np.empty((M, N), np.float32)
         self.lib.orc_matmul_int8(_i8(A), _i8(B), _fp(C), M, N, K, scale_a, scale_b,
                                  _fp(None if bias is None else np.ascontiguousarray(bias, np.float32)))
+        return C
+
+    def fp8_decode(self, codes, fmt):
+        """8-bit float codes (uint8) -> fp32; fmt "e4m3" or "e5m2"."""
+        codes = np.ascontiguousarray(codes, np.uint8)
+        out = np.empty(codes.shape, np.float32)
+        self.lib.orc_fp8_decode(codes.ctypes.data_as(ctypes.c_void_p), _fp(out), codes.size,
+                                FP8_FMT[fmt])
+        return out
+
+    def fp8_encode(self, x, fmt):
+        """fp32 -> 8-bit float codes (uint8): nearest-even, saturating."""
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty(x.shape, np.uint8)
+        self.lib.orc_fp8_encode(_fp(x), out.ctypes.data_as(ctypes.c_void_p), x.size, FP8_FMT[fmt])
+        return out
+
+    def gemm_fp8(self, A, W, a_fmt="e4m3", w_fmt="e4m3", bias=None, residual=None, act="none",
+                 scale=1.0):
+        """A, W: uint8 codes of 8-bit floats.  Returns fp32 C."""
+        A = np.ascontiguousarray(A, np.uint8)
+        W = np.ascontiguousarray(W, np.uint8)
+        M, K = A.shape
+        N = W.shape[1]
+        C = np.empty((M, N), np.float32)
+        vp = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+        self.lib.orc_gemm_fp8(vp(A), vp(W),
+                              _fp(None if bias is None else np.ascontiguousarray(bias, np.float32)),
+                              _fp(None if residual is None else np.ascontiguousarray(residual, np.float32)),
+                              _fp(C), M, N, K, scale, ACT[act] if isinstance(act, str) else int(act),
+                              FP8_FMT[a_fmt], FP8_FMT[w_fmt])
         return C
 
     def cross_entropy(self, logits, targets):

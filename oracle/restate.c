@@ -260,6 +260,99 @@ void orc_matmul_int8(const int8_t* A, const int8_t* B, float* C, int64_t M, int6
 }
 
 /*
+ * 8-bit floats: the E4M3 and E5M2 types of the reference's mixed-precision
+ * pass (lib/Passes/MixedPrecisionPass.cpp:55-62; lib/Dialect/JulesDialect.cpp
+ * :41-77), which the reference names but never evaluates.  Restated from
+ * the OCP 8-bit floating point specification (v1.0): sign, exponent,
+ * mantissa = 1/4/3 bits with bias 7 (E4M3) or 1/5/2 bits with bias 15
+ * (E5M2); exponent field 0 holds subnormals m * 2^(1 - bias - mbits).  E4M3
+ * has no infinities: S.1111.111 is its only NaN and 448 its largest value.
+ * E5M2 follows IEEE 754: exponent 31 with mantissa 0 is infinity, else NaN;
+ * 57344 is its largest finite value.
+ * fmt: 0 = E4M3, 1 = E5M2.
+ */
+float orc_fp8_to_f32(uint8_t x, int fmt) {
+  const int mbits = fmt == 0 ? 3 : 2, bias = fmt == 0 ? 7 : 15;
+  const int e = (x & 0x7F) >> mbits, m = x & ((1 << mbits) - 1);
+  const double sign = (x & 0x80) ? -1.0 : 1.0;
+  if (fmt == 0 && e == 15 && m == 7) return NAN;
+  if (fmt == 1 && e == 31) return m ? NAN : (float)(sign * INFINITY);
+  if (e == 0) return (float)(sign * ldexp((double)m, 1 - bias - mbits));
+  return (float)(sign * ldexp((double)((1 << mbits) + m), e - bias - mbits));
+}
+
+/*
+ * fp32 -> 8-bit float: round to nearest, ties to even, saturating to the
+ * largest finite value (the conversion jules_cast documents); NaN -> the
+ * format's NaN (E4M3 S.1111.111, E5M2 S.11111.11).
+ */
+uint8_t orc_f32_to_fp8(float x, int fmt) {
+  const int mbits = fmt == 0 ? 3 : 2, bias = fmt == 0 ? 7 : 15;
+  const uint8_t sign = signbit(x) ? 0x80 : 0x00;
+  const uint8_t max_code = fmt == 0 ? 0x7E : 0x7B;
+  if (isnan(x)) return sign | 0x7F;
+  const double a = fabs((double)x);
+  if (a >= (double)orc_fp8_to_f32(max_code, fmt)) return sign | max_code;
+  const int emin = 1 - bias;  /* exponent of the smallest normal */
+  int e2;
+  frexp(a, &e2);              /* a = f * 2^e2, f in [0.5, 1) */
+  int e = e2 - 1;             /* a in [2^e, 2^(e+1)) */
+  if (a == 0.0 || e < emin) {
+    /* subnormal spacing 2^(emin - mbits); k = 2^mbits rolls into the smallest normal */
+    const double k = rint(ldexp(a, mbits - emin));
+    return sign | (uint8_t)k;
+  }
+  double k = rint(ldexp(a, mbits - e));   /* in [2^mbits, 2^(mbits+1)] */
+  if (k == (double)(1 << (mbits + 1))) {
+    k = (double)(1 << mbits);
+    e += 1;
+  }
+  const int code = ((e + bias) << mbits) | ((int)k - (1 << mbits));
+  return sign | (uint8_t)(code > max_code ? max_code : code);
+}
+
+void orc_fp8_decode(const uint8_t* in, float* out, int64_t n, int fmt) {
+  for (int64_t i = 0; i < n; i++) out[i] = orc_fp8_to_f32(in[i], fmt);
+}
+
+void orc_fp8_encode(const float* in, uint8_t* out, int64_t n, int fmt) {
+  for (int64_t i = 0; i < n; i++) out[i] = orc_f32_to_fp8(in[i], fmt);
+}
+
+/*
+ * fp8 GEMM, the matmul the mixed-precision pass forms at target "fp8"
+ * (MixedPrecisionPass.cpp:1-28: operands cast to fp8, accumulation in f32,
+ * result cast back), with the tiledMatmulWithActivation epilogue
+ * (FusedKernels.h:378-458): C = act((A . W) * scale + bias) (+ residual).
+ * Products of decoded operands summed in double (the exact sum, rounded
+ * once), then the fp32 epilogue.
+ */
+void orc_gemm_fp8(const uint8_t* A, const uint8_t* W, const float* bias, const float* residual,
+                  float* C, int64_t M, int64_t N, int64_t K, float scale, int act, int a_fmt,
+                  int w_fmt) {
+  float* wd = (float*)malloc((size_t)(K * N) * sizeof(float));
+  for (int64_t i = 0; i < K * N; i++) wd[i] = orc_fp8_to_f32(W[i], w_fmt);
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < M; i++) {
+    double* acc = (double*)calloc((size_t)N, sizeof(double));
+    for (int64_t k = 0; k < K; k++) {
+      const double a = orc_fp8_to_f32(A[i * K + k], a_fmt);
+      const float* w = wd + k * N;
+      for (int64_t j = 0; j < N; j++) acc[j] += a * (double)w[j];
+    }
+    for (int64_t j = 0; j < N; j++) {
+      float v = (float)acc[j] * scale;
+      if (bias) v += bias[j];
+      v = apply_act(v, act);
+      if (residual) v += residual[i * N + j];
+      C[i * N + j] = v;
+    }
+    free(acc);
+  }
+  free(wd);
+}
+
+/*
  * Row softmax.  FusedKernels.h:464-526, in the summation order of its
  * AVX-512 branch (:466-505): max over the row (from -FLT_MAX); e = exp(x -
  * max) stored and summed in 16 lanes over 16-wide chunks, the lanes reduced,
