@@ -118,6 +118,28 @@ int jules_flash_attention_fwd(const void* Q, const void* K, const void* V, void*
                               int dtype, void* stream);
 
 /*
+ * Flash-attention backward: dQ, dK, dV of O = softmax(scale * Q K^T [causal])
+ * V for a given dO, from the forward's O and logsumexp (lse [B,Hq,S] fp32,
+ * natural log, as jules_flash_attention_fwd writes it).  Q, O, dO, dQ
+ * [B,Hq,S,D]; K, V, dK, dV [B,Hkv,S,D]; all of `dtype` (JULES_DTYPE_BF16 or
+ * F32).  Grouped-query heads: dK / dV of a kv head sum over its Hq/Hkv
+ * query heads.  scale <= 0 means 1/sqrt(D).  bf16 with D == 128 (16-byte
+ * aligned buffers) runs on tcgen05 (bf16 P and dS, fp32 accumulation);
+ * fp32 and other head dims (<= 256) on CUDA cores in fp32.  No atomics: the
+ * result is deterministic.  workspace: caller-provided device memory of
+ * jules_flash_attention_bwd_workspace_bytes() bytes (16-byte aligned).
+ * The reference has no attention backward; this is the gradient of the
+ * forward that replaces flashAttention (FlashAttention.h:130-309), the
+ * training-side neighbour of interleavedMLPForwardBackward
+ * (InterleavedAutodiff.h:55-160).
+ */
+size_t jules_flash_attention_bwd_workspace_bytes(int B, int Hq, int S, int D, int dtype);
+int jules_flash_attention_bwd(const void* Q, const void* K, const void* V, const void* O,
+                              const void* dO, const float* lse, void* dQ, void* dK, void* dV,
+                              int B, int Hq, int Hkv, int S, int D, float scale, int causal,
+                              int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Row LayerNorm: out = (x - mean) * inv_std * gamma + beta, biased variance,
  * inv_std = 1/sqrt(var + eps).  in [M,N], gamma/beta [N] fp32, optional
  * mean_out / rstd_out [M] fp32.  gamma and beta may both be NULL (no affine

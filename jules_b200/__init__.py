@@ -18,7 +18,7 @@ __all__ = [
     "lib", "JulesError", "ACT", "gemm_bias_act", "flash_attention_fwd", "layernorm", "gelu",
     "mlp_block", "mlp_block_workspace_bytes", "sgemm", "device_error", "kernel_by_name",
     "kernel_names", "LIB_PATH", "gemm_fp8", "cast", "matmul_int8", "softmax",
-    "cross_entropy_loss", "custom_call", "mlp_fwd_bwd",
+    "cross_entropy_loss", "custom_call", "mlp_fwd_bwd", "flash_attention_bwd", "attention",
 ]
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libjules_b200.so")
@@ -40,6 +40,9 @@ _SIGNATURES = {
                              _c_int, _c_int, _c_vp], _c_int),
     "jules_sgemm": ([_c_int, _c_int, _c_i64, _c_i64, _c_i64, _c_f, _c_vp, _c_i64, _c_vp, _c_i64,
                      _c_f, _c_vp, _c_i64, _c_vp], _c_int),
+    "jules_flash_attention_bwd_workspace_bytes": ([_c_int] * 5, ctypes.c_size_t),
+    "jules_flash_attention_bwd": ([_c_vp] * 9 + [_c_int] * 5 + [_c_f, _c_int, _c_int, _c_vp,
+                                                               ctypes.c_size_t, _c_vp], _c_int),
     "jules_flash_attention_fwd": ([_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_int, _c_int,
                                    _c_int, _c_int, _c_f, _c_int, _c_int, _c_vp], _c_int),
     "jules_layernorm": ([_c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_f, _c_int, _c_int, _c_vp,
@@ -198,6 +201,67 @@ def flash_attention_fwd(Q, K, V, causal=False, scale=0.0, out=None, lse=True, st
                                          _stream(stream))
     _check(rc, "jules_flash_attention_fwd")
     return out, l
+
+
+def flash_attention_bwd(Q, K, V, O, dO, lse, causal=False, scale=0.0, workspace=None,
+                        out=None, stream=None):
+    """Gradients (dQ, dK, dV) of flash_attention_fwd for dO, from its O and
+    lse.  Q, O, dO [B,Hq,S,D]; K, V [B,Hkv,S,D]; one dtype (fp32 or bf16);
+    lse [B,Hq,S] fp32.  out: optional (dQ, dK, dV) tensors."""
+    import torch
+    for t, n in ((Q, "Q"), (K, "K"), (V, "V"), (O, "O"), (dO, "dO"), (lse, "lse")):
+        _dense(t, n)
+    B, Hq, S, D = Q.shape
+    Hkv = K.shape[1]
+    dt = _dtype_code(Q)
+    if any(t.dtype != Q.dtype for t in (K, V, O, dO)) or lse.dtype != torch.float32:
+        raise ValueError("flash_attention_bwd: Q, K, V, O, dO share one dtype; lse is fp32")
+    dQ, dK, dV = out if out is not None else (torch.empty_like(Q), torch.empty_like(K),
+                                              torch.empty_like(V))
+    need = lib().jules_flash_attention_bwd_workspace_bytes(B, Hq, S, D, dt)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=Q.device)
+    rc = lib().jules_flash_attention_bwd(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), _ptr(dO), _ptr(lse),
+                                         _ptr(dQ), _ptr(dK), _ptr(dV), B, Hq, Hkv, S, D,
+                                         float(scale), int(bool(causal)), dt, _ptr(workspace),
+                                         workspace.numel() * workspace.element_size(),
+                                         _stream(stream))
+    _check(rc, "jules_flash_attention_bwd")
+    return dQ, dK, dV
+
+
+def attention(Q, K, V, causal=False, scale=0.0):
+    """Differentiable attention: forward jules_flash_attention_fwd, backward
+    jules_flash_attention_bwd (torch.autograd.Function)."""
+    return _attention_fn().apply(Q, K, V, bool(causal), float(scale))
+
+
+_ATTN_FN = None
+
+
+def _attention_fn():
+    global _ATTN_FN
+    if _ATTN_FN is None:
+        import torch
+
+        class _Attention(torch.autograd.Function):
+            @staticmethod
+            def forward(ctx, Q, K, V, causal, scale):
+                Q, K, V = Q.contiguous(), K.contiguous(), V.contiguous()
+                O, lse = flash_attention_fwd(Q, K, V, causal=causal, scale=scale)
+                ctx.save_for_backward(Q, K, V, O, lse)
+                ctx.causal, ctx.scale = causal, scale
+                return O
+
+            @staticmethod
+            def backward(ctx, dO):
+                Q, K, V, O, lse = ctx.saved_tensors
+                dQ, dK, dV = flash_attention_bwd(Q, K, V, O, dO.contiguous(), lse,
+                                                 causal=ctx.causal, scale=ctx.scale)
+                return dQ, dK, dV, None, None
+
+        _ATTN_FN = _Attention
+    return _ATTN_FN
 
 
 def layernorm(x, gamma, beta, eps=1e-5, out=None, out_dtype=None, stats=False, stream=None):

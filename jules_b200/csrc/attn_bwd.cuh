@@ -1,0 +1,643 @@
+// Flash-attention backward on tcgen05 tensor cores (bf16, head_dim 128).
+//
+// Gradients of O = softmax(scale * Q K^T [causal mask]) V for dO given,
+// from the forward's logsumexp (no second softmax pass):
+//   P_ij  = exp(scale * q_i . k_j - lse_i)
+//   dV_j  = sum_i P_ij dO_i             dP_ij = dO_i . v_j
+//   dS_ij = P_ij (dP_ij - D_i),         D_i   = dO_i . O_i
+//   dQ_i  = scale * sum_j dS_ij k_j     dK_j  = scale * sum_i dS_ij q_i
+// Grouped-query heads: dK and dV of a kv head sum over the Hq/Hkv query
+// heads that read it.  (The reference has no backward for attention; this is
+// the gradient of the forward in attn_tc.cuh, whose recurrence follows the
+// reference's flashAttention, include/jules/Kernel/FlashAttention.h:130-309.)
+//
+// Three kernels, no atomics (the gradients are deterministic):
+//  * bwd_prep_kernel: per query row, lse2 = lse * log2(e) and D = dO . O
+//    into a workspace padded to whole 128-row tiles (padding rows get
+//    lse2 = +inf, so their P is 0, and D = 0).
+//  * bwd_dkdv_kernel: one CTA per (kv head, 128-key tile j), K_j and V_j
+//    resident; for each (query head of the group, query tile i):
+//      S^T = K_j Q_i^T and dP^T = V_j dO_i^T into TMEM (rows = keys),
+//      softmax warps: P^T, dS^T as bf16 back into TMEM over S^T / dP^T,
+//      dV += P^T dO_i and dK += dS^T Q_i with the A operand in TMEM.
+//  * bwd_dq_kernel: one CTA per (query head, 128-query tile i), Q_i and dO_i
+//    resident; for each key tile j: S = Q_i K_j^T, dP = dO_i V_j^T, dS into
+//    TMEM, dQ += dS K_j.
+// Warp roles (6 warps): 0-3 softmax/epilogue (thread = TMEM lane = tile row),
+// 4 TMA producer, 5 MMA issuer and TMEM owner.
+// TMEM (512 columns): S [0,128), dP [128,256), accumulators [256,384) and
+// (dK/dV kernel) [384,512).  The next S overwrites P / dS only after the
+// MMAs reading them: one thread issues all MMAs and the tensor core runs
+// them in issue order.
+#pragma once
+
+#include "attn_tc.cuh"
+#include "simt.cuh"
+#include "sm100.cuh"
+
+namespace jb {
+namespace attn_bwd {
+
+constexpr int HD = 128;
+constexpr int BT = 128;                 // rows per query / key tile
+constexpr int kThreads = 192;
+constexpr int kWarpProducer = 4;
+constexpr int kWarpMma = 5;
+constexpr int kChunk = 128 * 64 * 2;    // one 64-dim (128 B) swizzled box of 128 rows
+constexpr int QS = 2;                   // Q / dO ring depth (dK/dV kernel)
+constexpr int KS = 2;                   // K / V ring depth (dQ kernel)
+constexpr float kLog2e = 1.4426950408889634f;
+
+__host__ __device__ constexpr int padded_len(int S) { return (S + BT - 1) / BT * BT; }
+
+// ---------------------------------------------------------------------------
+// lse2[bh, q] = lse * log2(e), delta[bh, q] = sum_d dO * O (fp32); rows
+// q in [S, Sp) are padding.  One warp per row, 4 dims per lane.
+__global__ void __launch_bounds__(256) bwd_prep_kernel(const __nv_bfloat16* __restrict__ O,
+                                                       const __nv_bfloat16* __restrict__ dO,
+                                                       const float* __restrict__ lse,
+                                                       float* __restrict__ lse2,
+                                                       float* __restrict__ delta, int BH, int S,
+                                                       int Sp) {
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = (int64_t)BH * Sp;
+  for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows;
+       row += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int bh = (int)(row / Sp), q = (int)(row - (int64_t)bh * Sp);
+    float d = 0.0f;
+    if (q < S) {
+      const size_t off = ((size_t)bh * S + q) * HD + lane * 4;
+      const uint2 a = *reinterpret_cast<const uint2*>(O + off);
+      const uint2 b = *reinterpret_cast<const uint2*>(dO + off);
+      const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&b);
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const float2 x = __bfloat1622float2(a2[k]), y = __bfloat1622float2(b2[k]);
+        d = fmaf(x.x, y.x, d);
+        d = fmaf(x.y, y.y, d);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+    }
+    if (lane == 0) {
+      lse2[row] = q < S ? lse[(size_t)bh * S + q] * kLog2e : INFINITY;
+      delta[row] = d;
+    }
+  }
+}
+
+// 32 columns of S and dP (fp32) -> 16 columns of packed bf16 P and dS.
+// lse2 / delta: per column (dK/dV kernel) or the row's own value.
+// keep(c): column c survives the mask.
+template <typename LseF, typename DeltaF, typename KeepF>
+__device__ __forceinline__ void p_ds_chunk(const uint32_t (&s)[32], const uint32_t (&dp)[32],
+                                           float scale_log2, LseF lse_at, DeltaF delta_at,
+                                           KeepF keep, uint32_t (&pk_p)[16],
+                                           uint32_t (&pk_ds)[16]) {
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    float p[2], ds[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int c = 2 * e + h;
+      const float x = fmaf(__uint_as_float(s[c]), scale_log2, -lse_at(c));
+      p[h] = keep(c) ? ex2_approx(x) : 0.0f;
+      ds[h] = p[h] * (__uint_as_float(dp[c]) - delta_at(c));
+    }
+    pk_p[e] = pack_bf16x2(p[0], p[1]);
+    pk_ds[e] = pack_bf16x2(ds[0], ds[1]);
+  }
+}
+
+// Stores one 128-column fp32 accumulator row (TMEM) as bf16 times mul.
+__device__ __forceinline__ void store_row_bf16(uint32_t trow, __nv_bfloat16* dst, float mul,
+                                               bool ok) {
+#pragma unroll 1
+  for (int c = 0; c < HD; c += 32) {
+    uint32_t o[32];
+    tmem_ld32(trow + c, o);
+    tmem_ld_wait(o);
+    if (ok) {
+      uint4* d4 = reinterpret_cast<uint4*>(dst + c);
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        uint4 v;
+        v.x = pack_bf16x2(__uint_as_float(o[8 * g + 0]) * mul, __uint_as_float(o[8 * g + 1]) * mul);
+        v.y = pack_bf16x2(__uint_as_float(o[8 * g + 2]) * mul, __uint_as_float(o[8 * g + 3]) * mul);
+        v.z = pack_bf16x2(__uint_as_float(o[8 * g + 4]) * mul, __uint_as_float(o[8 * g + 5]) * mul);
+        v.w = pack_bf16x2(__uint_as_float(o[8 * g + 6]) * mul, __uint_as_float(o[8 * g + 7]) * mul);
+        d4[g] = v;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// dK / dV
+// ---------------------------------------------------------------------------
+struct SmemKV {
+  alignas(1024) uint8_t k[2][kChunk];
+  alignas(1024) uint8_t v[2][kChunk];
+  alignas(1024) uint8_t q[QS][2][kChunk];
+  alignas(1024) uint8_t dO[QS][2][kChunk];
+  alignas(16) float lse2[QS][BT];
+  alignas(16) float delta[QS][BT];
+  uint64_t kv_full;
+  uint64_t q_full[QS], q_empty[QS];
+  uint64_t s_full, p_full, acc_full;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+// Query tiles of one work item: (query head h of the group, tile i), i from
+// the diagonal (causal) or 0, heads outer.
+__device__ __forceinline__ void kv_item_tile(int it, int i0, int n_qt, int& hh, int& i) {
+  const int per_head = n_qt - i0;
+  hh = it / per_head;
+  i = i0 + (it - hh * per_head);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                    const float* __restrict__ lse2, const float* __restrict__ delta,
+                    __nv_bfloat16* __restrict__ dK, __nv_bfloat16* __restrict__ dV, int B, int Hq,
+                    int Hkv, int S, float scale, int causal) {
+  extern __shared__ uint8_t smem_raw[];
+  SmemKV& s = *reinterpret_cast<SmemKV*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                         ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int Sp = padded_len(S);
+  const int n_t = Sp / BT;
+  const int BHkv = B * Hkv;
+  const int group = Hq / Hkv;
+  // Work item: key tile j (0 = the longest under the causal mask) x kv head.
+  const int j = blockIdx.x / BHkv;
+  const int zkv = blockIdx.x - j * BHkv;
+  const int b = zkv / Hkv, g = zkv - b * Hkv;
+  const int i0 = causal ? j : 0;
+  const int n_it = group * (n_t - i0);
+  const float scale_log2 = scale * kLog2e;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&s.kv_full, 1);
+    for (int k = 0; k < QS; ++k) {
+      mbar_init(&s.q_full[k], 1);
+      mbar_init(&s.q_empty[k], 1);
+    }
+    mbar_init(&s.s_full, 1);
+    mbar_init(&s.p_full, 128);
+    mbar_init(&s.acc_full, 1);
+    s.abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+    prefetch_tmap(&tmdO);
+  }
+  if (warp == kWarpMma) {
+    tmem_alloc(&s.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = s.tmem_base;
+  volatile int* abort_flag = &s.abort_flag;
+
+  if (warp == kWarpProducer) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&s.kv_full, 4 * kChunk);
+      tma_load_3d(s.k[0], &tmK, &s.kv_full, 0, j * BT, zkv);
+      tma_load_3d(s.k[1], &tmK, &s.kv_full, 64, j * BT, zkv);
+      tma_load_3d(s.v[0], &tmV, &s.kv_full, 0, j * BT, zkv);
+      tma_load_3d(s.v[1], &tmV, &s.kv_full, 64, j * BT, zkv);
+      for (int it = 0; it < n_it; ++it) {
+        int hh, i;
+        kv_item_tile(it, i0, n_t, hh, i);
+        const int bhq = b * Hq + g * group + hh;
+        const int st = it % QS;
+        const uint32_t ph = (uint32_t)(it / QS) & 1u;
+        if (!mbar_wait(&s.q_empty[st], ph ^ 1u, 110, abort_flag)) break;
+        mbar_arrive_expect_tx(&s.q_full[st], 4 * kChunk + 2 * BT * 4);
+        tma_load_3d(s.q[st][0], &tmQ, &s.q_full[st], 0, i * BT, bhq);
+        tma_load_3d(s.q[st][1], &tmQ, &s.q_full[st], 64, i * BT, bhq);
+        tma_load_3d(s.dO[st][0], &tmdO, &s.q_full[st], 0, i * BT, bhq);
+        tma_load_3d(s.dO[st][1], &tmdO, &s.q_full[st], 64, i * BT, bhq);
+        const size_t off = (size_t)bhq * Sp + (size_t)i * BT;
+        bulk_load(s.lse2[st], lse2 + off, BT * 4, &s.q_full[st]);
+        bulk_load(s.delta[st], delta + off, BT * 4, &s.q_full[st]);
+      }
+    }
+  } else if (warp == kWarpMma) {
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16_f32(BT, BT, false, false);
+      constexpr uint32_t idG = idesc_bf16_f32(BT, HD, false, true);
+      constexpr uint64_t kChunkStep = kChunk >> 4;
+      constexpr uint64_t kStageStep = (2 * kChunk) >> 4;
+      // K-major descriptors (+2 per 32 bytes of K) and MN-major ones for
+      // Q / dO as the B operand of dK / dV (+128 per 16 rows of 128 bytes).
+      const uint64_t dk = sdesc_sw128(smem_u32(s.k[0]), 16, 1024);
+      const uint64_t dv = sdesc_sw128(smem_u32(s.v[0]), 16, 1024);
+      const uint64_t dq_k = sdesc_sw128(smem_u32(s.q[0][0]), 16, 1024);
+      const uint64_t ddo_k = sdesc_sw128(smem_u32(s.dO[0][0]), 16, 1024);
+      const uint64_t dq_mn = sdesc_sw128(smem_u32(s.q[0][0]), kChunk, 1024);
+      const uint64_t ddo_mn = sdesc_sw128(smem_u32(s.dO[0][0]), kChunk, 1024);
+      bool ok = mbar_wait(&s.kv_full, 0, 111, abort_flag);
+      for (int it = 0; it < n_it && ok; ++it) {
+        const int st = it % QS;
+        const uint32_t ph = (uint32_t)(it / QS) & 1u;
+        if (!mbar_wait(&s.q_full[st], ph, 112, abort_flag)) break;
+        tc_fence_after();
+        uint64_t a[8], bq[8];
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t o = (kk >> 2) * kChunkStep + (kk & 3) * 2;
+          a[kk] = dk + o;
+          bq[kk] = dq_k + st * kStageStep + o;
+        }
+        umma8_ss(tbase + 0, a, bq, 0u, idS);           // S^T = K Q^T
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t o = (kk >> 2) * kChunkStep + (kk & 3) * 2;
+          a[kk] = dv + o;
+          bq[kk] = ddo_k + st * kStageStep + o;
+        }
+        umma8_ss(tbase + 128, a, bq, 0u, idS);         // dP^T = V dO^T
+        umma_commit(&s.s_full);
+        if (!mbar_wait(&s.p_full, (uint32_t)it & 1u, 113, abort_flag)) break;
+        tc_fence_after();
+        uint32_t ta[8];
+        uint64_t bb[8];
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          ta[kk] = tbase + 0 + kk * 8;
+          bb[kk] = ddo_mn + st * kStageStep + kk * 128;
+        }
+        umma8_ts(tbase + 256, ta, bb, it > 0 ? 1u : 0u, idG);   // dV += P^T dO
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          ta[kk] = tbase + 128 + kk * 8;
+          bb[kk] = dq_mn + st * kStageStep + kk * 128;
+        }
+        umma8_ts(tbase + 384, ta, bb, it > 0 ? 1u : 0u, idG);   // dK += dS^T Q
+        umma_commit(&s.q_empty[st]);
+      }
+      umma_commit(&s.acc_full);
+    }
+  } else {
+    // ---------------- softmax / epilogue: thread = key row ----------------
+    const int r = warp * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t tS = tbase + lane_off, tP = tbase + 128 + lane_off;
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      int hh, i;
+      kv_item_tile(it, i0, n_t, hh, i);
+      const int st = it % QS;
+      const uint32_t ph = (uint32_t)(it / QS) & 1u;
+      // lse2 / delta arrived with q_full (async proxy): observe it directly.
+      if (!mbar_wait(&s.q_full[st], ph, 114, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(&s.s_full, (uint32_t)it & 1u, 115, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      const bool diag = causal && i == j;  // query c < key r is masked
+      const float* l2 = s.lse2[st];
+      const float* dl = s.delta[st];
+#pragma unroll 1
+      for (int c0 = 0; c0 < BT; c0 += 32) {
+        uint32_t sv[32], dv[32];
+        tmem_ld32(tS + c0, sv);
+        tmem_ld32(tP + c0, dv);
+        tmem_ld_wait(sv);
+        tmem_ld_wait(dv);
+        uint32_t pk_p[16], pk_ds[16];
+        p_ds_chunk(
+            sv, dv, scale_log2, [&](int c) { return l2[c0 + c]; },
+            [&](int c) { return dl[c0 + c]; }, [&](int c) { return !diag || c0 + c >= r; }, pk_p,
+            pk_ds);
+        tmem_st16(tS + c0 / 2, pk_p);
+        tmem_st16(tP + c0 / 2, pk_ds);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&s.p_full);
+    }
+    if (ok && mbar_wait(&s.acc_full, 0, 116, abort_flag)) {
+      tc_fence_after();
+      const int key = j * BT + r;
+      const bool row_ok = key < S;
+      const size_t off = ((size_t)zkv * S + (row_ok ? key : 0)) * HD;
+      store_row_bf16(tbase + 256 + lane_off, dV + off, 1.0f, row_ok);
+      store_row_bf16(tbase + 384 + lane_off, dK + off, scale, row_ok);
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kWarpMma) tmem_dealloc(tbase, 512);
+}
+
+// ---------------------------------------------------------------------------
+// dQ
+// ---------------------------------------------------------------------------
+struct SmemQ {
+  alignas(1024) uint8_t q[2][kChunk];
+  alignas(1024) uint8_t dO[2][kChunk];
+  alignas(1024) uint8_t k[KS][2][kChunk];
+  alignas(1024) uint8_t v[KS][2][kChunk];
+  uint64_t q_full;
+  uint64_t kv_full[KS], kv_empty[KS];
+  uint64_t s_full, p_full, acc_full;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                  const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                  const float* __restrict__ lse2, const float* __restrict__ delta,
+                  __nv_bfloat16* __restrict__ dQ, int B, int Hq, int Hkv, int S, float scale,
+                  int causal) {
+  extern __shared__ uint8_t smem_raw[];
+  SmemQ& s = *reinterpret_cast<SmemQ*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                       ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int Sp = padded_len(S);
+  const int n_t = Sp / BT;
+  const int BHq = B * Hq;
+  const int group = Hq / Hkv;
+  // Work item: query tile i (the longest under the causal mask first) x head.
+  const int ir = blockIdx.x / BHq;
+  const int bhq = blockIdx.x - ir * BHq;
+  const int i = causal ? n_t - 1 - ir : ir;
+  const int zkv = (bhq / Hq) * Hkv + (bhq % Hq) / group;
+  const int n_kv = causal ? i + 1 : n_t;
+  const float scale_log2 = scale * kLog2e;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&s.q_full, 1);
+    for (int k = 0; k < KS; ++k) {
+      mbar_init(&s.kv_full[k], 1);
+      mbar_init(&s.kv_empty[k], 1);
+    }
+    mbar_init(&s.s_full, 1);
+    mbar_init(&s.p_full, 128);
+    mbar_init(&s.acc_full, 1);
+    s.abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+    prefetch_tmap(&tmdO);
+  }
+  if (warp == kWarpMma) {
+    tmem_alloc(&s.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = s.tmem_base;
+  volatile int* abort_flag = &s.abort_flag;
+
+  if (warp == kWarpProducer) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&s.q_full, 4 * kChunk);
+      tma_load_3d(s.q[0], &tmQ, &s.q_full, 0, i * BT, bhq);
+      tma_load_3d(s.q[1], &tmQ, &s.q_full, 64, i * BT, bhq);
+      tma_load_3d(s.dO[0], &tmdO, &s.q_full, 0, i * BT, bhq);
+      tma_load_3d(s.dO[1], &tmdO, &s.q_full, 64, i * BT, bhq);
+      for (int jj = 0; jj < n_kv; ++jj) {
+        const int st = jj % KS;
+        const uint32_t ph = (uint32_t)(jj / KS) & 1u;
+        if (!mbar_wait(&s.kv_empty[st], ph ^ 1u, 120, abort_flag)) break;
+        mbar_arrive_expect_tx(&s.kv_full[st], 4 * kChunk);
+        tma_load_3d(s.k[st][0], &tmK, &s.kv_full[st], 0, jj * BT, zkv);
+        tma_load_3d(s.k[st][1], &tmK, &s.kv_full[st], 64, jj * BT, zkv);
+        tma_load_3d(s.v[st][0], &tmV, &s.kv_full[st], 0, jj * BT, zkv);
+        tma_load_3d(s.v[st][1], &tmV, &s.kv_full[st], 64, jj * BT, zkv);
+      }
+    }
+  } else if (warp == kWarpMma) {
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16_f32(BT, BT, false, false);
+      constexpr uint32_t idG = idesc_bf16_f32(BT, HD, false, true);
+      constexpr uint64_t kChunkStep = kChunk >> 4;
+      constexpr uint64_t kStageStep = (2 * kChunk) >> 4;
+      const uint64_t dq = sdesc_sw128(smem_u32(s.q[0]), 16, 1024);
+      const uint64_t ddo = sdesc_sw128(smem_u32(s.dO[0]), 16, 1024);
+      const uint64_t dk_k = sdesc_sw128(smem_u32(s.k[0][0]), 16, 1024);
+      const uint64_t dv_k = sdesc_sw128(smem_u32(s.v[0][0]), 16, 1024);
+      const uint64_t dk_mn = sdesc_sw128(smem_u32(s.k[0][0]), kChunk, 1024);
+      bool ok = mbar_wait(&s.q_full, 0, 121, abort_flag);
+      for (int jj = 0; jj < n_kv && ok; ++jj) {
+        const int st = jj % KS;
+        const uint32_t ph = (uint32_t)(jj / KS) & 1u;
+        if (!mbar_wait(&s.kv_full[st], ph, 122, abort_flag)) break;
+        tc_fence_after();
+        uint64_t a[8], bk[8];
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t o = (kk >> 2) * kChunkStep + (kk & 3) * 2;
+          a[kk] = dq + o;
+          bk[kk] = dk_k + st * kStageStep + o;
+        }
+        umma8_ss(tbase + 0, a, bk, 0u, idS);           // S = Q K^T
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t o = (kk >> 2) * kChunkStep + (kk & 3) * 2;
+          a[kk] = ddo + o;
+          bk[kk] = dv_k + st * kStageStep + o;
+        }
+        umma8_ss(tbase + 128, a, bk, 0u, idS);         // dP = dO V^T
+        umma_commit(&s.s_full);
+        if (!mbar_wait(&s.p_full, (uint32_t)jj & 1u, 123, abort_flag)) break;
+        tc_fence_after();
+        uint32_t ta[8];
+        uint64_t bb[8];
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          ta[kk] = tbase + 0 + kk * 8;
+          bb[kk] = dk_mn + st * kStageStep + kk * 128;
+        }
+        umma8_ts(tbase + 256, ta, bb, jj > 0 ? 1u : 0u, idG);   // dQ += dS K
+        umma_commit(&s.kv_empty[st]);
+      }
+      umma_commit(&s.acc_full);
+    }
+  } else {
+    // ---------------- softmax / epilogue: thread = query row ----------------
+    const int r = warp * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t tS = tbase + lane_off, tP = tbase + 128 + lane_off;
+    const size_t srow = (size_t)bhq * Sp + (size_t)i * BT + r;
+    const float l2 = lse2[srow], dl = delta[srow];
+    bool ok = true;
+    for (int jj = 0; jj < n_kv; ++jj) {
+      if (!mbar_wait(&s.s_full, (uint32_t)jj & 1u, 124, abort_flag)) { ok = false; break; }
+      tc_fence_after();
+      const bool diag = causal && jj == i;  // key c > query r is masked
+      const int kpad = S - jj * BT;         // keys c >= kpad are padding
+#pragma unroll 1
+      for (int c0 = 0; c0 < BT; c0 += 32) {
+        uint32_t sv[32], dv[32];
+        tmem_ld32(tS + c0, sv);
+        tmem_ld32(tP + c0, dv);
+        tmem_ld_wait(sv);
+        tmem_ld_wait(dv);
+        uint32_t pk_p[16], pk_ds[16];
+        p_ds_chunk(
+            sv, dv, scale_log2, [&](int) { return l2; }, [&](int) { return dl; },
+            [&](int c) { return c0 + c < kpad && (!diag || c0 + c <= r); }, pk_p, pk_ds);
+        tmem_st16(tS + c0 / 2, pk_ds);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&s.p_full);
+    }
+    if (ok && mbar_wait(&s.acc_full, 0, 125, abort_flag)) {
+      tc_fence_after();
+      const int q = i * BT + r;
+      const bool row_ok = q < S;
+      store_row_bf16(tbase + 256 + lane_off, dQ + ((size_t)bhq * S + (row_ok ? q : 0)) * HD,
+                     scale, row_ok);
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kWarpMma) tmem_dealloc(tbase, 512);
+}
+
+// ---------------------------------------------------------------------------
+// CUDA-core path (fp32 inputs, head dims other than 128, unaligned buffers):
+// one warp per query row (dQ) or key row (dK, dV), head dim spread over the
+// lanes (up to kSimtDPL per lane), exact exp, fp32 throughout.
+// ---------------------------------------------------------------------------
+constexpr int kSimtDPL = 8;  // head dim <= 256
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ void load_row(const T* p, int D, int lane, float (&x)[kSimtDPL]) {
+#pragma unroll
+  for (int k = 0; k < kSimtDPL; ++k) {
+    const int d = lane + 32 * k;
+    x[k] = d < D ? to_f32<T>(p[d]) : 0.0f;
+  }
+}
+
+__device__ __forceinline__ float dot_row(const float (&a)[kSimtDPL], const float (&b)[kSimtDPL]) {
+  float s = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kSimtDPL; ++k) s = fmaf(a[k], b[k], s);
+  return warp_sum(s);
+}
+
+// delta[bh, q] = sum_d dO * O
+template <typename T>
+__global__ void __launch_bounds__(256) bwd_simt_delta_kernel(const T* __restrict__ O,
+                                                             const T* __restrict__ dO,
+                                                             float* __restrict__ delta,
+                                                             int64_t rows, int D) {
+  const int lane = threadIdx.x & 31;
+  for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows;
+       row += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    float o[kSimtDPL], g[kSimtDPL];
+    load_row(O + row * D, D, lane, o);
+    load_row(dO + row * D, D, lane, g);
+    const float d = dot_row(o, g);
+    if (lane == 0) delta[row] = d;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) bwd_simt_dq_kernel(
+    const T* __restrict__ Q, const T* __restrict__ K, const T* __restrict__ V,
+    const T* __restrict__ dO, const float* __restrict__ lse, const float* __restrict__ delta,
+    T* __restrict__ dQ, int B, int Hq, int Hkv, int S, int D, float scale, int causal) {
+  const int lane = threadIdx.x & 31;
+  const int64_t rows = (int64_t)B * Hq * S;
+  for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows;
+       row += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int64_t bh = row / S;
+    const int q = (int)(row - bh * S);
+    const int64_t zkv = (bh / Hq) * Hkv + (bh % Hq) / (Hq / Hkv);
+    float qv[kSimtDPL], gv[kSimtDPL], acc[kSimtDPL] = {};
+    load_row(Q + row * D, D, lane, qv);
+    load_row(dO + row * D, D, lane, gv);
+    const float l = lse[row], dl = delta[row];
+    const int n_k = causal ? q + 1 : S;
+    for (int k = 0; k < n_k; ++k) {
+      float kv[kSimtDPL], vv[kSimtDPL];
+      load_row(K + (zkv * S + k) * D, D, lane, kv);
+      load_row(V + (zkv * S + k) * D, D, lane, vv);
+      const float p = expf(scale * dot_row(qv, kv) - l);
+      const float ds = p * (dot_row(gv, vv) - dl);
+#pragma unroll
+      for (int c = 0; c < kSimtDPL; ++c) acc[c] = fmaf(ds, kv[c], acc[c]);
+    }
+#pragma unroll
+    for (int c = 0; c < kSimtDPL; ++c) {
+      const int d = lane + 32 * c;
+      if (d < D) dQ[row * D + d] = from_f32<T>(acc[c] * scale);
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) bwd_simt_dkdv_kernel(
+    const T* __restrict__ Q, const T* __restrict__ K, const T* __restrict__ V,
+    const T* __restrict__ dO, const float* __restrict__ lse, const float* __restrict__ delta,
+    T* __restrict__ dK, T* __restrict__ dV, int B, int Hq, int Hkv, int S, int D, float scale,
+    int causal) {
+  const int lane = threadIdx.x & 31;
+  const int group = Hq / Hkv;
+  const int64_t rows = (int64_t)B * Hkv * S;
+  for (int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows;
+       row += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int64_t zkv = row / S;
+    const int k = (int)(row - zkv * S);
+    const int64_t b = zkv / Hkv, g = zkv % Hkv;
+    float kv[kSimtDPL], vv[kSimtDPL], ak[kSimtDPL] = {}, av[kSimtDPL] = {};
+    load_row(K + row * D, D, lane, kv);
+    load_row(V + row * D, D, lane, vv);
+    for (int hh = 0; hh < group; ++hh) {
+      const int64_t bh = b * Hq + g * group + hh;
+      for (int q = causal ? k : 0; q < S; ++q) {
+        float qv[kSimtDPL], gv[kSimtDPL];
+        load_row(Q + (bh * S + q) * D, D, lane, qv);
+        load_row(dO + (bh * S + q) * D, D, lane, gv);
+        const float p = expf(scale * dot_row(qv, kv) - lse[bh * S + q]);
+        const float ds = p * (dot_row(gv, vv) - delta[bh * S + q]);
+#pragma unroll
+        for (int c = 0; c < kSimtDPL; ++c) {
+          av[c] = fmaf(p, gv[c], av[c]);
+          ak[c] = fmaf(ds, qv[c], ak[c]);
+        }
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < kSimtDPL; ++c) {
+      const int d = lane + 32 * c;
+      if (d < D) {
+        dK[row * D + d] = from_f32<T>(ak[c] * scale);
+        dV[row * D + d] = from_f32<T>(av[c]);
+      }
+    }
+  }
+}
+
+}  // namespace attn_bwd
+}  // namespace jb

@@ -17,6 +17,7 @@
 
 #include "../../include/jules_kernels.h"
 #include "attn_tc.cuh"
+#include "attn_bwd.cuh"
 #include "gemm_tc.cuh"
 #include "gemm_i8.cuh"
 #include "sm100.cuh"
@@ -370,6 +371,94 @@ int attn_tc(const void* Q, const void* K, const void* V, void* O, float* lse, in
   return check_launch("attn_fwd_tc_kernel launch");
 }
 
+size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+
+size_t attn_bwd_ws_bytes(int64_t BH, int S, int tensor_path) {
+  const int64_t rows = BH * (tensor_path ? jb::attn_bwd::padded_len(S) : S);
+  return 2 * align256((size_t)rows * 4);
+}
+
+// Attention backward, tcgen05 path (bf16, D = 128, 16-byte aligned).
+int attn_bwd_tc(const void* Q, const void* K, const void* V, const void* O, const void* dO,
+                const float* lse, void* dQ, void* dK, void* dV, int B, int Hq, int Hkv, int S,
+                float scale, int causal, void* ws, cudaStream_t st) {
+  namespace ab = jb::attn_bwd;
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  const int Sp = ab::padded_len(S);
+  const int64_t BHq = (int64_t)B * Hq, BHkv = (int64_t)B * Hkv;
+  const int n_t = Sp / ab::BT;
+  if (BHq * n_t > INT32_MAX || BHkv * n_t > INT32_MAX)
+    return fail(JULES_ERR_SHAPE, "attention bwd: too many tiles");
+  float* lse2 = static_cast<float*>(ws);
+  float* delta = reinterpret_cast<float*>(static_cast<char*>(ws) + align256((size_t)BHq * Sp * 4));
+  {
+    const int64_t warps = BHq * Sp;
+    const int grid = (int)std::min<int64_t>((warps * 32 + 255) / 256, (int64_t)device_sms(dev) * 16);
+    ab::bwd_prep_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(O),
+                                              static_cast<const __nv_bfloat16*>(dO), lse, lse2,
+                                              delta, (int)BHq, S, Sp);
+    if (int rc = check_launch("bwd_prep_kernel launch")) return rc;
+  }
+  CUtensorMap tq, tk, tv, tdo;
+  const uint32_t box[3] = {64, (uint32_t)ab::BT, 1};
+  {
+    const uint64_t dims[3] = {(uint64_t)ab::HD, (uint64_t)S, (uint64_t)BHq};
+    const uint64_t strides[2] = {(uint64_t)ab::HD * 2, (uint64_t)S * ab::HD * 2};
+    if (int rc = make_tmap_bf16(&tq, Q, 3, dims, strides, box)) return rc;
+    if (int rc = make_tmap_bf16(&tdo, dO, 3, dims, strides, box)) return rc;
+  }
+  {
+    const uint64_t dims[3] = {(uint64_t)ab::HD, (uint64_t)S, (uint64_t)BHkv};
+    const uint64_t strides[2] = {(uint64_t)ab::HD * 2, (uint64_t)S * ab::HD * 2};
+    if (int rc = make_tmap_bf16(&tk, K, 3, dims, strides, box)) return rc;
+    if (int rc = make_tmap_bf16(&tv, V, 3, dims, strides, box)) return rc;
+  }
+  const size_t smem_kv = sizeof(ab::SmemKV) + 1024, smem_q = sizeof(ab::SmemQ) + 1024;
+  static bool attr_set[kMaxDevices] = {};
+  if (!attr_set[dev]) {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    cudaError_t e = cudaFuncSetAttribute(ab::bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_kv);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(ab::bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_q);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attention bwd)");
+    attr_set[dev] = true;
+  }
+  ab::bwd_dkdv_kernel<<<(unsigned)(BHkv * n_t), ab::kThreads, smem_kv, st>>>(
+      tq, tk, tv, tdo, lse2, delta, static_cast<__nv_bfloat16*>(dK),
+      static_cast<__nv_bfloat16*>(dV), B, Hq, Hkv, S, scale, causal);
+  if (int rc = check_launch("bwd_dkdv_kernel launch")) return rc;
+  ab::bwd_dq_kernel<<<(unsigned)(BHq * n_t), ab::kThreads, smem_q, st>>>(
+      tq, tk, tv, tdo, lse2, delta, static_cast<__nv_bfloat16*>(dQ), B, Hq, Hkv, S, scale, causal);
+  return check_launch("bwd_dq_kernel launch");
+}
+
+// Attention backward, CUDA cores (any dtype of T, head dim <= 256).
+template <typename T>
+int attn_bwd_simt(const void* Q, const void* K, const void* V, const void* O, const void* dO,
+                  const float* lse, void* dQ, void* dK, void* dV, int B, int Hq, int Hkv, int S,
+                  int D, float scale, int causal, void* ws, cudaStream_t st) {
+  namespace ab = jb::attn_bwd;
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  float* delta = static_cast<float*>(ws);
+  const int64_t rq = (int64_t)B * Hq * S, rk = (int64_t)B * Hkv * S;
+  const int cap = device_sms(dev) * 16;
+  auto grid_for = [&](int64_t rows) { return (int)std::min<int64_t>((rows * 32 + 255) / 256, cap); };
+  ab::bwd_simt_delta_kernel<T><<<grid_for(rq), 256, 0, st>>>(
+      static_cast<const T*>(O), static_cast<const T*>(dO), delta, rq, D);
+  if (int rc = check_launch("bwd_simt_delta_kernel launch")) return rc;
+  ab::bwd_simt_dq_kernel<T><<<grid_for(rq), 256, 0, st>>>(
+      static_cast<const T*>(Q), static_cast<const T*>(K), static_cast<const T*>(V),
+      static_cast<const T*>(dO), lse, delta, static_cast<T*>(dQ), B, Hq, Hkv, S, D, scale, causal);
+  if (int rc = check_launch("bwd_simt_dq_kernel launch")) return rc;
+  ab::bwd_simt_dkdv_kernel<T><<<grid_for(rk), 256, 0, st>>>(
+      static_cast<const T*>(Q), static_cast<const T*>(K), static_cast<const T*>(V),
+      static_cast<const T*>(dO), lse, delta, static_cast<T*>(dK), static_cast<T*>(dV), B, Hq, Hkv,
+      S, D, scale, causal);
+  return check_launch("bwd_simt_dkdv_kernel launch");
+}
+
 }  // namespace
 
 // ===========================================================================
@@ -654,6 +743,40 @@ int jules_flash_attention_fwd(const void* Q, const void* K, const void* V, void*
   if (D == jb::attn::HD && aligned16(Q) && aligned16(K) && aligned16(V) && aligned16(O))
     return attn_tc(Q, K, V, O, lse, B, Hq, Hkv, S, D, scale, causal ? 1 : 0, st);
   return attn_simt<__nv_bfloat16>(Q, K, V, O, lse, B, Hq, Hkv, S, D, scale, causal ? 1 : 0, st);
+}
+
+size_t jules_flash_attention_bwd_workspace_bytes(int B, int Hq, int S, int D, int dtype) {
+  if (B <= 0 || Hq <= 0 || S <= 0) return 0;
+  const int tensor_path = dtype == JULES_DTYPE_BF16 && D == jb::attn_bwd::HD;
+  return attn_bwd_ws_bytes((int64_t)B * Hq, S, tensor_path);
+}
+
+int jules_flash_attention_bwd(const void* Q, const void* K, const void* V, const void* O,
+                              const void* dO, const float* lse, void* dQ, void* dK, void* dV,
+                              int B, int Hq, int Hkv, int S, int D, float scale, int causal,
+                              int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!Q || !K || !V || !O || !dO || !lse || !dQ || !dK || !dV)
+    return fail(JULES_ERR_ARG, "attention bwd: NULL pointer");
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || S < 0 || D <= 0 || Hq % Hkv != 0)
+    return fail(JULES_ERR_SHAPE, "attention bwd: B=%d Hq=%d Hkv=%d S=%d D=%d", B, Hq, Hkv, S, D);
+  if (D > 32 * jb::attn_bwd::kSimtDPL) return fail(JULES_ERR_SHAPE, "attention bwd: head_dim %d > 256", D);
+  if (dtype != JULES_DTYPE_F32 && dtype != JULES_DTYPE_BF16)
+    return fail(JULES_ERR_DTYPE, "attention bwd: dtype %d", dtype);
+  if (B == 0 || S == 0) return ok();
+  const size_t need = jules_flash_attention_bwd_workspace_bytes(B, Hq, S, D, dtype);
+  if (!workspace || workspace_bytes < need || !aligned16(workspace))
+    return fail(JULES_ERR_WORKSPACE, "attention bwd: workspace %zu < %zu bytes (or unaligned)", workspace_bytes, need);
+  if (!(scale > 0.0f)) scale = 1.0f / sqrtf((float)D);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int c = causal ? 1 : 0;
+  if (dtype == JULES_DTYPE_F32)
+    return attn_bwd_simt<float>(Q, K, V, O, dO, lse, dQ, dK, dV, B, Hq, Hkv, S, D, scale, c, workspace, st);
+  if (D == jb::attn_bwd::HD && aligned16(Q) && aligned16(K) && aligned16(V) && aligned16(O) &&
+      aligned16(dO) && aligned16(dQ) && aligned16(dK) && aligned16(dV) && aligned16(lse))
+    return attn_bwd_tc(Q, K, V, O, dO, lse, dQ, dK, dV, B, Hq, Hkv, S, scale, c, workspace, st);
+  if (D == jb::attn_bwd::HD)
+    return fail(JULES_ERR_ALIGN, "attention bwd: bf16 head_dim 128 needs 16-byte aligned buffers");
+  return attn_bwd_simt<__nv_bfloat16>(Q, K, V, O, dO, lse, dQ, dK, dV, B, Hq, Hkv, S, D, scale, c, workspace, st);
 }
 
 int jules_layernorm(const void* in, const float* gamma, const float* beta, void* out, int64_t M,

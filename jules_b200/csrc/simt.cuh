@@ -5,6 +5,7 @@
 // All are GPU kernels; none falls back to the host.
 #pragma once
 
+#include "gemm_tc.cuh"  // act_fast
 #include "sm100.cuh"
 
 namespace jb {

@@ -121,6 +121,8 @@ class Restated:
             ctypes.c_int, ctypes.c_int]
         lib.orc_mlp_block.argtypes = [_f32p] * 8 + [ctypes.c_int64] * 3 + [ctypes.c_float, _i64p,
                                                                           ctypes.c_int64]
+        lib.orc_attention_bwd.argtypes = [_f32p] * 7 + [ctypes.c_int] * 5 + [ctypes.c_float,
+                                                                             ctypes.c_int]
         lib.orc_fp8_decode.argtypes = [ctypes.c_void_p, _f32p, ctypes.c_int64, ctypes.c_int]
         lib.orc_fp8_encode.argtypes = [_f32p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int]
         lib.orc_gemm_fp8.argtypes = [ctypes.c_void_p, ctypes.c_void_p, _f32p, _f32p, _f32p,
@@ -241,6 +243,19 @@ class Restated:
                                      float(scale), int(bool(causal)), up, nu, int(q_begin),
                                      int(q_end), int(tile_q), int(tile_k))
         return O, lse
+
+    def attention_bwd(self, Q, K, V, dO, causal=False, scale=None):
+        """Exact (double) gradients (dQ, dK, dV) of the attention forward for
+        dO; shapes as flash_attention."""
+        Q, K, V, dO = (np.ascontiguousarray(a, np.float32) for a in (Q, K, V, dO))
+        B, Hq, S, D = Q.shape
+        Hkv = K.shape[1]
+        if scale is None:
+            scale = 1.0 / np.sqrt(D)
+        dQ, dK, dV = np.empty_like(Q), np.empty_like(K), np.empty_like(V)
+        self.lib.orc_attention_bwd(_fp(dQ), _fp(dK), _fp(dV), _fp(Q), _fp(K), _fp(V), _fp(dO),
+                                   B, Hq, Hkv, S, D, float(scale), int(bool(causal)))
+        return dQ, dK, dV
 
     def mlp_block(self, X, gamma, beta, W1, b1, W2, b2, eps=1e-5, rows=None):
         T, d = X.shape

@@ -444,6 +444,89 @@ void orc_layernorm(float* out, const float* in, const float* gamma,
   }
 }
 
+/*
+ * Attention backward (no reference routine: the reference has no gradient
+ * for attention).  The exact gradient of the forward restated below,
+ * O = softmax(scale * Q K^T [causal]) V, for a given dO, in double:
+ *   P = softmax row by row (from the scores, not from a stored lse),
+ *   dV_j = sum_i P_ij dO_i, dP_ij = dO_i . v_j, D_i = sum_j P_ij dP_ij,
+ *   dS_ij = P_ij (dP_ij - D_i), dQ_i = scale sum_j dS_ij k_j,
+ *   dK_j = scale sum_i dS_ij q_i; grouped-query heads sum into their kv head.
+ * Layout as orc_flash_attention.  dK, dV are zeroed here.
+ */
+void orc_attention_bwd(float* dQ, float* dK, float* dV, const float* Q, const float* K,
+                       const float* V, const float* dO, int B, int Hq, int Hkv, int S, int D,
+                       float scale, int causal) {
+  const int group = Hq / Hkv;
+  const size_t nkv = (size_t)B * Hkv * S * D;
+  double* dk = (double*)calloc(nkv, sizeof(double));
+  double* dv = (double*)calloc(nkv, sizeof(double));
+  double* P = (double*)malloc(sizeof(double) * (size_t)S * S);   /* P_ij, row i */
+  double* dS = (double*)malloc(sizeof(double) * (size_t)S * S);  /* dS_ij */
+  for (int b = 0; b < B; b++)
+    for (int h = 0; h < Hq; h++) {
+      const size_t zq = (size_t)b * Hq + h, zk = (size_t)b * Hkv + h / group;
+      const float* q = Q + zq * S * D;
+      const float* g = dO + zq * S * D;
+      const float* k = K + zk * S * D;
+      const float* v = V + zk * S * D;
+#pragma omp parallel for schedule(dynamic, 4)
+      for (int i = 0; i < S; i++) {
+        double* pr = P + (size_t)i * S;
+        double* dsr = dS + (size_t)i * S;
+        const int n = causal ? i + 1 : S;
+        double m = -INFINITY, l = 0.0, dsum = 0.0;
+        for (int j = 0; j < S; j++) {
+          pr[j] = 0.0;
+          dsr[j] = 0.0;
+        }
+        for (int j = 0; j < n; j++) {
+          double t = 0.0;
+          for (int d = 0; d < D; d++) t += (double)q[(size_t)i * D + d] * k[(size_t)j * D + d];
+          pr[j] = t * scale;
+          if (pr[j] > m) m = pr[j];
+        }
+        for (int j = 0; j < n; j++) {
+          pr[j] = exp(pr[j] - m);
+          l += pr[j];
+        }
+        for (int j = 0; j < n; j++) {
+          double t = 0.0;
+          pr[j] /= l;
+          for (int d = 0; d < D; d++) t += (double)g[(size_t)i * D + d] * v[(size_t)j * D + d];
+          dsr[j] = t;            /* dP_ij for now */
+          dsum += pr[j] * t;
+        }
+        for (int j = 0; j < n; j++) dsr[j] = pr[j] * (dsr[j] - dsum);
+        for (int d = 0; d < D; d++) {
+          double t = 0.0;
+          for (int j = 0; j < n; j++) t += dsr[j] * k[(size_t)j * D + d];
+          dQ[(zq * S + i) * D + d] = (float)(t * scale);
+        }
+      }
+#pragma omp parallel for schedule(static)
+      for (int j = 0; j < S; j++) {
+        double* acck = dk + (zk * S + j) * D;
+        double* accv = dv + (zk * S + j) * D;
+        for (int i = causal ? j : 0; i < S; i++) {
+          const double pij = P[(size_t)i * S + j], dsij = dS[(size_t)i * S + j];
+          for (int d = 0; d < D; d++) {
+            accv[d] += pij * g[(size_t)i * D + d];
+            acck[d] += dsij * scale * q[(size_t)i * D + d];
+          }
+        }
+      }
+    }
+  for (size_t x = 0; x < nkv; x++) {
+    dK[x] = (float)dk[x];
+    dV[x] = (float)dv[x];
+  }
+  free(P);
+  free(dS);
+  free(dk);
+  free(dv);
+}
+
 /* ------------------------------------------------------------------ */
 /* Flash attention forward: FlashAttention.h:130-309.                   */
 /* Per (b,h) unit and query tile: running max/sum and an accumulator;   */
