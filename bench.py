@@ -50,7 +50,7 @@ def parse():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["jules", "reference"], default="jules")
     p.add_argument("--workload", choices=["gemm", "attn", "attn_gqa", "mlp", "attn_fp32",
-                                          "softmax", "xent", "int8", "fp8"],
+                                          "softmax", "xent", "int8", "fp8", "attn_bwd"],
                    default="gemm")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
@@ -115,7 +115,8 @@ def profiled_traffic(workload):
     summary (profiles/<kernel>_<workload>.md, line 'traffic_bytes_per_launch:')."""
     name = {"gemm": "gemm_tc_c2", "attn": "attn_tc_c3", "attn_gqa": "attn_tc_c5",
             "mlp": "gemm_tc_c4", "attn_fp32": "attn_simt_c1", "softmax": "rows_softmax",
-            "xent": "rows_xent", "int8": "gemm_s8_int8", "fp8": "gemm_f8_fp8"}[workload]
+            "xent": "rows_xent", "int8": "gemm_s8_int8", "fp8": "gemm_f8_fp8",
+            "attn_bwd": "attn_bwd_c3"}[workload]
     path = os.path.join(HERE, "profiles", f"{name}.md")
     try:
         with open(path) as f:
@@ -149,6 +150,12 @@ def describe(workload, world, extra_l2=None):
         c = {"workload": "int8 GEMM (matmulInt8): s8 x s8 -> s32 -> fp32 * scale + bias",
              "M_per_rank": 8192, "N": 8192, "K": 8192, "global_M": 8192 * world,
              "sharding": "rows of M", "op_convention": "2*M*N*K int8 ops"}
+    elif workload == "attn_bwd":
+        c = {"workload": "C3-shape causal flash-attention backward (dQ, dK, dV) bf16, from O and lse",
+             "B_per_rank": 8, "Hq": 32, "Hkv": 32, "S": 4096, "D": 128, "global_B": 8 * world,
+             "sharding": "batch x kv-head-group units",
+             "flop_convention": "2.5 x causal forward = 5*B*Hq*S^2*D (5 GEMMs; the kernels "
+                                "recompute S and dP for dQ, 7 GEMMs executed)"}
     elif workload == "fp8":
         c = {"workload": "fp8 GEMM + bias + GELU(tanh): e4m3 x e4m3 -> fp32 accumulate -> bf16",
              "M_per_rank": 8192, "N": 8192, "K": 8192, "global_M": 8192 * world,
@@ -588,6 +595,59 @@ class Fp8Gemm(Workload):
         self.hC.copy_(self.dC, non_blocking=True)
 
 
+class AttentionBwd(Workload):
+    """Causal flash-attention backward at the C3 shape (B=8, H=32, S=4096,
+    D=128, bf16): dQ, dK, dV from Q, K, V, O, dO and lse.  Timed unit: the
+    whole jules_flash_attention_bwd call (prep + dK/dV + dQ kernels)."""
+    dominant = "jules_flash_attention_bwd (bwd_dkdv_kernel + bwd_dq_kernel + bwd_prep_kernel)"
+    launches_per_step = 3
+
+    def __init__(self, jb, torch, rank, world, B=8, H=32, S=4096, D=128):
+        self.jb, self.torch = jb, torch
+        dev = torch.device("cuda")
+        g = torch.Generator(device=dev).manual_seed(77 + rank)
+        bf = torch.bfloat16
+        mk = lambda: torch.randn((B, H, S, D), generator=g, device=dev).to(bf)
+        self.Q, self.K, self.V, self.dO = mk(), mk(), mk(), mk()
+        self.O, self.lse = jb.flash_attention_fwd(self.Q, self.K, self.V, causal=True)
+        self.grads = (torch.empty_like(self.Q), torch.empty_like(self.K), torch.empty_like(self.V))
+        self.ws = torch.empty(jb.lib().jules_flash_attention_bwd_workspace_bytes(B, H, S, D, jb.DT_BF16),
+                              dtype=torch.uint8, device=dev)
+        self.nsets = 1
+        self.flops_per_step = 5.0 * B * H * S * S * D
+        self.flops_dominant = self.flops_per_step
+        self.config = {"l2": "inputs 1.6 GB per step (> L2)"}
+
+    def step(self, i, ev=None):
+        if ev:
+            ev[0].record()
+        self.jb.flash_attention_bwd(self.Q, self.K, self.V, self.O, self.dO, self.lse, causal=True,
+                                    workspace=self.ws, out=self.grads)
+        if ev:
+            ev[1].record()
+
+    def output(self, i):
+        return self.grads[0]
+
+    def e2e_setup(self):
+        t = self.torch
+        self.h_in = [x.cpu().pin_memory() for x in (self.Q, self.K, self.V, self.O, self.dO, self.lse)]
+        self.d_in = [t.empty_like(x) for x in (self.Q, self.K, self.V, self.O, self.dO, self.lse)]
+        self.h_out = [t.empty_like(x, device="cpu").pin_memory() for x in self.grads]
+        self.d_out = tuple(t.empty_like(x) for x in self.grads)
+        self.h2d = sum(x.numel() * x.element_size() for x in self.h_in)
+        self.d2h = sum(x.numel() * x.element_size() for x in self.h_out)
+
+    def e2e_step(self):
+        for h, d in zip(self.h_in, self.d_in):
+            d.copy_(h, non_blocking=True)
+        q, k, v, o, do, lse = self.d_in
+        self.jb.flash_attention_bwd(q, k, v, o, do, lse, causal=True, workspace=self.ws,
+                                    out=self.d_out)
+        for h, d in zip(self.h_out, self.d_out):
+            h.copy_(d, non_blocking=True)
+
+
 class RowWise(Workload):
     """Row softmax (softmax) or fused softmax + cross-entropy (xent), fp32,
     rows sharded across ranks.  HBM-bound: work is counted in bytes."""
@@ -657,12 +717,19 @@ METRIC = "Flash-attn fwd & fused-GEMM TFLOP/s at 1/2/4/8 B200; % of tensor peak"
 ROWS_METRIC = "Row softmax / fused cross-entropy GB/s (HBM bytes moved) per B200"
 INT8_METRIC = "int8 GEMM TOPS (matmulInt8) per B200"
 FP8_METRIC = "fp8 GEMM + bias + GELU TFLOP/s (mixed-precision matmul at fp8) per B200"
+BWD_METRIC = "Flash-attention backward (dQ, dK, dV) TFLOP/s per B200; % of tensor peak"
+
+
+def metric_for(workload):
+    if workload in ("softmax", "xent"):
+        return ROWS_METRIC
+    return {"int8": INT8_METRIC, "fp8": FP8_METRIC, "attn_bwd": BWD_METRIC}.get(workload, METRIC)
 # B200 datasheet dense int8 / fp8 tensor throughput (no measured figures on this pool).
 NOMINAL_INT8_TOPS = 4500.0
 NOMINAL_FP8_TFLOPS = 4500.0
 # The reference has no fp8 kernel (its mixed-precision pass only names the
 # types), so the fp8 CPU leg times the oracle's restatement ("port").
-CPU_KIND = {"fp8": "port"}
+CPU_KIND = {"fp8": "port", "attn_bwd": "port"}
 JSON_OUT = sys.stdout
 
 
@@ -720,6 +787,16 @@ def cpu_reference_sample(workload, reps=3, warm=1):
         flops = 2.0 * Ms * N * K
         desc = (f"oracle restatement orc_gemm_fp8 (oracle/restate.c; the reference has no fp8 "
                 f"kernel) on {Ms} of the 8192 rows; FLOPs 2*M*N*K")
+        reps = 2
+    elif workload == "attn_bwd":
+        Sx = 2048
+        R = oracle.Restated()
+        Q, K_, V, dO = (g.standard_normal((1, 1, Sx, 128), dtype=np.float32) for _ in range(4))
+        fn = lambda: R.attention_bwd(Q, K_, V, dO, causal=True)
+        flops = 5.0 * Sx * Sx * 128
+        desc = (f"oracle restatement orc_attention_bwd (oracle/restate.c, double; the reference "
+                f"has no attention backward) on one (b,h) unit at S={Sx}, D=128, causal; "
+                f"FLOPs 5*S^2*D")
         reps = 2
     elif workload in ("softmax", "xent"):
         if workload == "softmax":
@@ -789,7 +866,7 @@ def run_reference_arm(args):
     value = statistics.mean(vals)
     rowwise = args.workload in ("softmax", "xent")
     unit = "GB/s" if rowwise else ("TOPS" if args.workload == "int8" else "TFLOP/s")
-    metric = ROWS_METRIC if rowwise else {"int8": INT8_METRIC, "fp8": FP8_METRIC}.get(args.workload, METRIC)
+    metric = metric_for(args.workload)
     line = {"metric": metric, "value": round(value, 6), "unit": unit,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(wall / args.steps * 1e3, 3), "higher_is_better": True,
@@ -841,7 +918,8 @@ def main():
          "softmax": lambda: RowWise(jb, torch, rank, world, xent=False),
          "xent": lambda: RowWise(jb, torch, rank, world, xent=True),
          "int8": lambda: Int8Gemm(jb, torch, rank, world),
-         "fp8": lambda: Fp8Gemm(jb, torch, rank, world)}[args.workload]
+         "fp8": lambda: Fp8Gemm(jb, torch, rank, world),
+         "attn_bwd": lambda: AttentionBwd(jb, torch, rank, world)}[args.workload]
     wl = W()
     stream = torch.cuda.current_stream()
 
@@ -933,8 +1011,7 @@ def main():
 
     if rank == 0:
         line = {
-            "metric": (FP8_METRIC if isinstance(wl, Fp8Gemm) else
-                       {"TFLOP/s": METRIC, "GB/s": ROWS_METRIC, "TOPS": INT8_METRIC}[wl.unit]),
+            "metric": metric_for(args.workload),
             "value": round(tflops_total, 3), "unit": wl.unit,
             "n_gpus": world, "steps": K, "warmup": args.warmup,
             "ms_per_step": round(ms_total / K, 5), "higher_is_better": True, "scaling": "weak",
@@ -943,7 +1020,7 @@ def main():
             "config": describe(args.workload, world, wl.config.get("l2")),
             "roofline": roofline(wl, achieved, peak, peak_kind, traffic),
             **({"pct_of_dense_bf16_peak_2250": round(100 * tflops_total / world / 2250.0, 2)}
-               if wl.unit == "TFLOP/s" and not isinstance(wl, Fp8Gemm) else {}),
+               if wl.unit == "TFLOP/s" and not isinstance(wl, (Fp8Gemm, AttentionF32)) else {}),
             "clocks": clocks,
             "e2e": e2e,
             "gpu_launches": K * wl.launches_per_step,

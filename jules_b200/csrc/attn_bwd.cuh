@@ -12,9 +12,9 @@
 // reference's flashAttention, include/jules/Kernel/FlashAttention.h:130-309.)
 //
 // Three kernels, no atomics (the gradients are deterministic):
-//  * bwd_prep_kernel: per query row, lse2 = lse * log2(e) and D = dO . O
-//    into a workspace padded to whole 128-row tiles (padding rows get
-//    lse2 = +inf, so their P is 0, and D = 0).
+//  * bwd_prep_kernel: per query row, -lse * log2(e) and -D = -dO . O into a
+//    workspace padded to whole 128-row tiles (padding rows get -inf, so
+//    their P is 0, and 0).
 //  * bwd_dkdv_kernel: one CTA per (kv head, 128-key tile j), K_j and V_j
 //    resident; for each (query head of the group, query tile i):
 //      S^T = K_j Q_i^T and dP^T = V_j dO_i^T into TMEM (rows = keys),
@@ -23,12 +23,18 @@
 //  * bwd_dq_kernel: one CTA per (query head, 128-query tile i), Q_i and dO_i
 //    resident; for each key tile j: S = Q_i K_j^T, dP = dO_i V_j^T, dS into
 //    TMEM, dQ += dS K_j.
-// Warp roles (6 warps): 0-3 softmax/epilogue (thread = TMEM lane = tile row),
-// 4 TMA producer, 5 MMA issuer and TMEM owner.
+// Warp roles (10 warps): 0-7 softmax/epilogue (thread = TMEM lane = tile row;
+// warps w and w+4 share a lane quarter and split its 128 columns), 8 TMA
+// producer, 9 MMA issuer and TMEM owner.
 // TMEM (512 columns): S [0,128), dP [128,256), accumulators [256,384) and
-// (dK/dV kernel) [384,512).  The next S overwrites P / dS only after the
-// MMAs reading them: one thread issues all MMAs and the tensor core runs
-// them in issue order.
+// (dK/dV kernel) [384,512).  The two softmax warps of a lane quarter own
+// columns [64h, 64h+64) of S and of dP (h = 0, 1) and write their packed
+// bf16 results only there, into columns they have already read: P (dK/dV
+// kernel) or dS (dQ kernel) of score columns 64h + c at S column 64h + c/2,
+// dS of the dK/dV kernel at dP column 64h + c/2.  The MMA reading them takes
+// K-step kk (16 columns of scores) at 64 (kk / 4) + 8 (kk % 4).  The next S
+// overwrites them only after the MMAs reading them: one thread issues all
+// MMAs and the tensor core runs them in issue order.
 #pragma once
 
 #include "attn_tc.cuh"
@@ -40,9 +46,10 @@ namespace attn_bwd {
 
 constexpr int HD = 128;
 constexpr int BT = 128;                 // rows per query / key tile
-constexpr int kThreads = 192;
-constexpr int kWarpProducer = 4;
-constexpr int kWarpMma = 5;
+constexpr int kThreads = 320;
+constexpr int kSoftmaxThreads = 256;    // warps 0-7: two per TMEM lane quarter
+constexpr int kWarpProducer = 8;
+constexpr int kWarpMma = 9;
 constexpr int kChunk = 128 * 64 * 2;    // one 64-dim (128 B) swizzled box of 128 rows
 constexpr int QS = 2;                   // Q / dO ring depth (dK/dV kernel)
 constexpr int KS = 2;                   // K / V ring depth (dQ kernel)
@@ -51,8 +58,10 @@ constexpr float kLog2e = 1.4426950408889634f;
 __host__ __device__ constexpr int padded_len(int S) { return (S + BT - 1) / BT * BT; }
 
 // ---------------------------------------------------------------------------
-// lse2[bh, q] = lse * log2(e), delta[bh, q] = sum_d dO * O (fp32); rows
-// q in [S, Sp) are padding.  One warp per row, 4 dims per lane.
+// nlse2[bh, q] = -lse * log2(e), ndelta[bh, q] = -sum_d dO * O (fp32,
+// negated for the fused multiply-adds of the kernels below); rows q in
+// [S, Sp) are padding (nlse2 = -inf: their P is 0).  One warp per row, 4
+// dims per lane.
 __global__ void __launch_bounds__(256) bwd_prep_kernel(const __nv_bfloat16* __restrict__ O,
                                                        const __nv_bfloat16* __restrict__ dO,
                                                        const float* __restrict__ lse,
@@ -81,40 +90,64 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const __nv_bfloat16* __re
       for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
     }
     if (lane == 0) {
-      lse2[row] = q < S ? lse[(size_t)bh * S + q] * kLog2e : INFINITY;
-      delta[row] = d;
+      lse2[row] = q < S ? -lse[(size_t)bh * S + q] * kLog2e : -INFINITY;
+      delta[row] = -d;
     }
   }
 }
 
-// 32 columns of S and dP (fp32) -> 16 columns of packed bf16 P and dS.
-// lse2 / delta: per column (dK/dV kernel) or the row's own value.
-// keep(c): column c survives the mask.
-template <typename LseF, typename DeltaF, typename KeepF>
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// 32 columns of S and dP (fp32) -> 16 columns of packed bf16 P and dS, two
+// columns per f32x2 instruction:
+//   x = s * scale*log2(e) + nlse2,  p = 2^x,  ds = p * (dp + ndelta).
+// nl2 / nd2: the pair's -lse*log2(e) and -D (per column pair in the dK/dV
+// kernel, the row's own value twice in the dQ kernel).  Masked scores arrive
+// as -inf (p = 0).
+template <bool WANT_P, typename PairF>
 __device__ __forceinline__ void p_ds_chunk(const uint32_t (&s)[32], const uint32_t (&dp)[32],
-                                           float scale_log2, LseF lse_at, DeltaF delta_at,
-                                           KeepF keep, uint32_t (&pk_p)[16],
+                                           uint64_t scale2, PairF pair_at, uint32_t (&pk_p)[16],
                                            uint32_t (&pk_ds)[16]) {
 #pragma unroll
   for (int e = 0; e < 16; ++e) {
-    float p[2], ds[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int c = 2 * e + h;
-      const float x = fmaf(__uint_as_float(s[c]), scale_log2, -lse_at(c));
-      p[h] = keep(c) ? ex2_approx(x) : 0.0f;
-      ds[h] = p[h] * (__uint_as_float(dp[c]) - delta_at(c));
+    uint64_t nl2, nd2;
+    pair_at(2 * e, nl2, nd2);
+    const uint64_t x2 = attn::fma2(attn::pk2(__uint_as_float(s[2 * e]), __uint_as_float(s[2 * e + 1])),
+                                   scale2, nl2);
+    float x0, x1;
+    attn::upk2(x2, x0, x1);
+    const uint64_t p2 = attn::pk2(ex2_approx(x0), ex2_approx(x1));
+    const uint64_t g2 = attn::add2(attn::pk2(__uint_as_float(dp[2 * e]), __uint_as_float(dp[2 * e + 1])), nd2);
+    const uint64_t ds2 = mul2(p2, g2);
+    float a0, a1;
+    if (WANT_P) {
+      attn::upk2(p2, a0, a1);
+      pk_p[e] = pack_bf16x2(a0, a1);
     }
-    pk_p[e] = pack_bf16x2(p[0], p[1]);
-    pk_ds[e] = pack_bf16x2(ds[0], ds[1]);
+    attn::upk2(ds2, a0, a1);
+    pk_ds[e] = pack_bf16x2(a0, a1);
   }
 }
 
-// Stores one 128-column fp32 accumulator row (TMEM) as bf16 times mul.
+// Causal / padding mask of one 32-column chunk: columns with keep(c) false
+// get -inf scores.
+template <typename KeepF>
+__device__ __forceinline__ void mask_chunk(uint32_t (&s)[32], KeepF keep) {
+#pragma unroll
+  for (int c = 0; c < 32; ++c)
+    if (!keep(c)) s[c] = __float_as_uint(-INFINITY);
+}
+
+// Stores 64 columns [c_begin, c_begin + 64) of a fp32 accumulator row
+// (TMEM) as bf16 times mul.
 __device__ __forceinline__ void store_row_bf16(uint32_t trow, __nv_bfloat16* dst, float mul,
-                                               bool ok) {
+                                               bool ok, int c_begin) {
 #pragma unroll 1
-  for (int c = 0; c < HD; c += 32) {
+  for (int c = c_begin; c < c_begin + 64; c += 32) {
     uint32_t o[32];
     tmem_ld32(trow + c, o);
     tmem_ld_wait(o);
@@ -150,6 +183,23 @@ struct SmemKV {
   int abort_flag;
 };
 
+// Work order shared by both kernels: items (head, tile) come in groups of
+// G consecutive heads; inside a group the tiles run longest-causal-first and,
+// for each tile, the G heads back to back.  The ~148 CTAs resident at a time
+// then stream the operands of a few heads (2 MB per head at S = 4096), which
+// stay in L2, instead of one head each.  longest_first: tile 0 (key tiles,
+// the dK/dV kernel) or tile n_t - 1 (query tiles, the dQ kernel) first.
+__device__ __forceinline__ void decode_bwd_item(int w, int n_t, int heads, int G, bool causal,
+                                                bool low_first, int& tile, int& head) {
+  const int per_group = G * n_t;
+  const int g = w / per_group;
+  const int idx = w - g * per_group;
+  const int gh = min(G, heads - g * G);
+  const int r = idx / gh;
+  head = g * G + (idx - r * gh);
+  tile = (!causal || low_first) ? r : n_t - 1 - r;
+}
+
 // Query tiles of one work item: (query head h of the group, tile i), i from
 // the diagonal (causal) or 0, heads outer.
 __device__ __forceinline__ void kv_item_tile(int it, int i0, int n_qt, int& hh, int& i) {
@@ -174,8 +224,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int BHkv = B * Hkv;
   const int group = Hq / Hkv;
   // Work item: key tile j (0 = the longest under the causal mask) x kv head.
-  const int j = blockIdx.x / BHkv;
-  const int zkv = blockIdx.x - j * BHkv;
+  int j, zkv;
+  decode_bwd_item(blockIdx.x, n_t, BHkv, 8, causal != 0, true, j, zkv);
   const int b = zkv / Hkv, g = zkv - b * Hkv;
   const int i0 = causal ? j : 0;
   const int n_it = group * (n_t - i0);
@@ -188,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.q_empty[k], 1);
     }
     mbar_init(&s.s_full, 1);
-    mbar_init(&s.p_full, 128);
+    mbar_init(&s.p_full, kSoftmaxThreads);
     mbar_init(&s.acc_full, 1);
     s.abort_flag = 0;
     fence_mbar_init();
@@ -273,13 +323,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint64_t bb[8];
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          ta[kk] = tbase + 0 + kk * 8;
+          ta[kk] = tbase + 0 + 64 * (kk >> 2) + (kk & 3) * 8;
           bb[kk] = ddo_mn + st * kStageStep + kk * 128;
         }
         umma8_ts(tbase + 256, ta, bb, it > 0 ? 1u : 0u, idG);   // dV += P^T dO
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          ta[kk] = tbase + 128 + kk * 8;
+          ta[kk] = tbase + 128 + 64 * (kk >> 2) + (kk & 3) * 8;
           bb[kk] = dq_mn + st * kStageStep + kk * 128;
         }
         umma8_ts(tbase + 384, ta, bb, it > 0 ? 1u : 0u, idG);   // dK += dS^T Q
@@ -289,9 +339,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- softmax / epilogue: thread = key row ----------------
-    const int r = warp * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const int quarter = warp & 3, half = warp >> 2;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t tS = tbase + lane_off, tP = tbase + 128 + lane_off;
+    const uint64_t scale2 = attn::pk2(scale_log2, scale_log2);
     bool ok = true;
     for (int it = 0; it < n_it; ++it) {
       int hh, i;
@@ -303,22 +355,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&s.s_full, (uint32_t)it & 1u, 115, abort_flag)) { ok = false; break; }
       tc_fence_after();
       const bool diag = causal && i == j;  // query c < key r is masked
-      const float* l2 = s.lse2[st];
-      const float* dl = s.delta[st];
+      const uint64_t* nl = reinterpret_cast<const uint64_t*>(s.lse2[st]);
+      const uint64_t* nd = reinterpret_cast<const uint64_t*>(s.delta[st]);
 #pragma unroll 1
-      for (int c0 = 0; c0 < BT; c0 += 32) {
+      for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
         uint32_t sv[32], dv[32];
         tmem_ld32(tS + c0, sv);
         tmem_ld32(tP + c0, dv);
         tmem_ld_wait(sv);
         tmem_ld_wait(dv);
+        if (diag) mask_chunk(sv, [&](int c) { return c0 + c >= r; });
         uint32_t pk_p[16], pk_ds[16];
-        p_ds_chunk(
-            sv, dv, scale_log2, [&](int c) { return l2[c0 + c]; },
-            [&](int c) { return dl[c0 + c]; }, [&](int c) { return !diag || c0 + c >= r; }, pk_p,
-            pk_ds);
-        tmem_st16(tS + c0 / 2, pk_p);
-        tmem_st16(tP + c0 / 2, pk_ds);
+        p_ds_chunk<true>(sv, dv, scale2,
+                         [&](int c, uint64_t& l, uint64_t& d) {
+                           l = nl[(c0 + c) >> 1];
+                           d = nd[(c0 + c) >> 1];
+                         },
+                         pk_p, pk_ds);
+        // packed into this half's own, already-read columns (see below)
+        tmem_st16(tS + half * 64 + (c0 - half * 64) / 2, pk_p);
+        tmem_st16(tP + half * 64 + (c0 - half * 64) / 2, pk_ds);
       }
       tmem_st_wait();
       tc_fence_before();
@@ -329,8 +385,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int key = j * BT + r;
       const bool row_ok = key < S;
       const size_t off = ((size_t)zkv * S + (row_ok ? key : 0)) * HD;
-      store_row_bf16(tbase + 256 + lane_off, dV + off, 1.0f, row_ok);
-      store_row_bf16(tbase + 384 + lane_off, dK + off, scale, row_ok);
+      store_row_bf16(tbase + 256 + lane_off, dV + off, 1.0f, row_ok, half * 64);
+      store_row_bf16(tbase + 384 + lane_off, dK + off, scale, row_ok, half * 64);
     }
   }
 
@@ -371,10 +427,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_t = Sp / BT;
   const int BHq = B * Hq;
   const int group = Hq / Hkv;
-  // Work item: query tile i (the longest under the causal mask first) x head.
-  const int ir = blockIdx.x / BHq;
-  const int bhq = blockIdx.x - ir * BHq;
-  const int i = causal ? n_t - 1 - ir : ir;
+  // Work item: query tile i (the longest under the causal mask first) x head;
+  // groups of at least 8 heads, whole grouped-query sets.
+  int i, bhq;
+  decode_bwd_item(blockIdx.x, n_t, BHq, group >= 8 ? group : 8, causal != 0, false, i, bhq);
   const int zkv = (bhq / Hq) * Hkv + (bhq % Hq) / group;
   const int n_kv = causal ? i + 1 : n_t;
   const float scale_log2 = scale * kLog2e;
@@ -386,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.kv_empty[k], 1);
     }
     mbar_init(&s.s_full, 1);
-    mbar_init(&s.p_full, 128);
+    mbar_init(&s.p_full, kSoftmaxThreads);
     mbar_init(&s.acc_full, 1);
     s.abort_flag = 0;
     fence_mbar_init();
@@ -462,7 +518,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint64_t bb[8];
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          ta[kk] = tbase + 0 + kk * 8;
+          ta[kk] = tbase + 0 + 64 * (kk >> 2) + (kk & 3) * 8;
           bb[kk] = dk_mn + st * kStageStep + kk * 128;
         }
         umma8_ts(tbase + 256, ta, bb, jj > 0 ? 1u : 0u, idG);   // dQ += dS K
@@ -472,29 +528,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- softmax / epilogue: thread = query row ----------------
-    const int r = warp * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const int quarter = warp & 3, half = warp >> 2;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t tS = tbase + lane_off, tP = tbase + 128 + lane_off;
     const size_t srow = (size_t)bhq * Sp + (size_t)i * BT + r;
-    const float l2 = lse2[srow], dl = delta[srow];
+    const float nl = lse2[srow], nd = delta[srow];
+    const uint64_t nl2 = attn::pk2(nl, nl), nd2 = attn::pk2(nd, nd);
+    const uint64_t scale2 = attn::pk2(scale_log2, scale_log2);
     bool ok = true;
     for (int jj = 0; jj < n_kv; ++jj) {
       if (!mbar_wait(&s.s_full, (uint32_t)jj & 1u, 124, abort_flag)) { ok = false; break; }
       tc_fence_after();
       const bool diag = causal && jj == i;  // key c > query r is masked
       const int kpad = S - jj * BT;         // keys c >= kpad are padding
+      const bool masked = diag || kpad < BT;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BT; c0 += 32) {
+      for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
         uint32_t sv[32], dv[32];
         tmem_ld32(tS + c0, sv);
         tmem_ld32(tP + c0, dv);
         tmem_ld_wait(sv);
         tmem_ld_wait(dv);
+        if (masked) mask_chunk(sv, [&](int c) { return c0 + c < kpad && (!diag || c0 + c <= r); });
         uint32_t pk_p[16], pk_ds[16];
-        p_ds_chunk(
-            sv, dv, scale_log2, [&](int) { return l2; }, [&](int) { return dl; },
-            [&](int c) { return c0 + c < kpad && (!diag || c0 + c <= r); }, pk_p, pk_ds);
-        tmem_st16(tS + c0 / 2, pk_ds);
+        p_ds_chunk<false>(sv, dv, scale2,
+                          [&](int, uint64_t& l, uint64_t& d) {
+                            l = nl2;
+                            d = nd2;
+                          },
+                          pk_p, pk_ds);
+        tmem_st16(tS + half * 64 + (c0 - half * 64) / 2, pk_ds);
       }
       tmem_st_wait();
       tc_fence_before();
@@ -505,7 +569,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int q = i * BT + r;
       const bool row_ok = q < S;
       store_row_bf16(tbase + 256 + lane_off, dQ + ((size_t)bhq * S + (row_ok ? q : 0)) * HD,
-                     scale, row_ok);
+                     scale, row_ok, half * 64);
     }
   }
 
