@@ -26,15 +26,16 @@
 // Warp roles (10 warps): 0-7 softmax/epilogue (thread = TMEM lane = tile row;
 // warps w and w+4 share a lane quarter and split its 128 columns), 8 TMA
 // producer, 9 MMA issuer and TMEM owner.
-// TMEM (512 columns): S [0,128), dP [128,256), accumulators [256,384) and
-// (dK/dV kernel) [384,512).  The two softmax warps of a lane quarter own
-// columns [64h, 64h+64) of S and of dP (h = 0, 1) and write their packed
-// bf16 results only there, into columns they have already read: P (dK/dV
-// kernel) or dS (dQ kernel) of score columns 64h + c at S column 64h + c/2,
-// dS of the dK/dV kernel at dP column 64h + c/2.  The MMA reading them takes
-// K-step kk (16 columns of scores) at 64 (kk / 4) + 8 (kk % 4).  The next S
-// overwrites them only after the MMAs reading them: one thread issues all
-// MMAs and the tensor core runs them in issue order.
+// Ping-pong: each 128-row tile of the streamed operand is processed as two
+// 64-row halves h = 0, 1 with their own S and dP in TMEM, so softmax group h
+// (warps 4h..4h+3, thread = TMEM lane = tile row) works on half h while the
+// tensor core runs the other half's gradient MMAs and next-tile S / dP.
+// TMEM (512 columns): half h's S at [128h, +64) and dP at [128h + 64, +64);
+// accumulators at [256, 384) and (dK/dV kernel) [384, 512).  The softmax
+// writes its packed bf16 results into columns it has already read: P (dK/dV
+// kernel) or dS (dQ kernel) over S, dS of the dK/dV kernel over dP.  The
+// next S of a half overwrites them only after the MMAs reading them: one
+// thread issues all MMAs and the tensor core runs them in issue order.
 #pragma once
 
 #include "attn_tc.cuh"
@@ -46,6 +47,7 @@ namespace attn_bwd {
 
 constexpr int HD = 128;
 constexpr int BT = 128;                 // rows per query / key tile
+constexpr int BH2 = 64;                 // half tile: the unit of the softmax ping-pong
 constexpr int kThreads = 320;
 constexpr int kSoftmaxThreads = 256;    // warps 0-7: two per TMEM lane quarter
 constexpr int kWarpProducer = 8;
@@ -133,6 +135,16 @@ __device__ __forceinline__ void p_ds_chunk(const uint32_t (&s)[32], const uint32
   }
 }
 
+// D (+)= sum over 4 K-steps of A[tmem] * B[smem].
+__device__ __forceinline__ void umma4_ts(uint32_t d_tmem, const uint32_t (&a)[4],
+                                         const uint64_t (&b)[4], uint32_t acc_first,
+                                         uint32_t idesc) {
+  umma_f16_ts(d_tmem, a[0], b[0], idesc, acc_first);
+  umma_f16_ts(d_tmem, a[1], b[1], idesc, 1u);
+  umma_f16_ts(d_tmem, a[2], b[2], idesc, 1u);
+  umma_f16_ts(d_tmem, a[3], b[3], idesc, 1u);
+}
+
 // Causal / padding mask of one 32-column chunk: columns with keep(c) false
 // get -inf scores.
 template <typename KeepF>
@@ -178,7 +190,7 @@ struct SmemKV {
   alignas(16) float delta[QS][BT];
   uint64_t kv_full;
   uint64_t q_full[QS], q_empty[QS];
-  uint64_t s_full, p_full, acc_full;
+  uint64_t s_full[2], p_full[2], acc_full;
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -237,8 +249,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.q_full[k], 1);
       mbar_init(&s.q_empty[k], 1);
     }
-    mbar_init(&s.s_full, 1);
-    mbar_init(&s.p_full, kSoftmaxThreads);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&s.s_full[x], 1);
+      mbar_init(&s.p_full[x], kSoftmaxThreads / 2);
+    }
     mbar_init(&s.acc_full, 1);
     s.abort_flag = 0;
     fence_mbar_init();
@@ -283,10 +297,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kWarpMma) {
     if (lane == 0) {
-      constexpr uint32_t idS = idesc_bf16_f32(BT, BT, false, false);
+      constexpr uint32_t idS = idesc_bf16_f32(BT, BH2, false, false);
       constexpr uint32_t idG = idesc_bf16_f32(BT, HD, false, true);
       constexpr uint64_t kChunkStep = kChunk >> 4;
       constexpr uint64_t kStageStep = (2 * kChunk) >> 4;
+      constexpr uint64_t kHalfRows = (BH2 * 128) >> 4;  // 64 rows of 128 bytes
       // K-major descriptors (+2 per 32 bytes of K) and MN-major ones for
       // Q / dO as the B operand of dK / dV (+128 per 16 rows of 128 bytes).
       const uint64_t dk = sdesc_sw128(smem_u32(s.k[0]), 16, 1024);
@@ -295,54 +310,81 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t ddo_k = sdesc_sw128(smem_u32(s.dO[0][0]), 16, 1024);
       const uint64_t dq_mn = sdesc_sw128(smem_u32(s.q[0][0]), kChunk, 1024);
       const uint64_t ddo_mn = sdesc_sw128(smem_u32(s.dO[0][0]), kChunk, 1024);
-      bool ok = mbar_wait(&s.kv_full, 0, 111, abort_flag);
-      for (int it = 0; it < n_it && ok; ++it) {
-        const int st = it % QS;
-        const uint32_t ph = (uint32_t)(it / QS) & 1u;
-        if (!mbar_wait(&s.q_full[st], ph, 112, abort_flag)) break;
-        tc_fence_after();
-        uint64_t a[8], bq[8];
+      // S^T_x = K Q_x^T and dP^T_x = V dO_x^T for query half x of stage st.
+      auto issue_s = [&](int x, int st) {
+        uint64_t a[8], b[8];
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t o = (kk >> 2) * kChunkStep + (kk & 3) * 2;
           a[kk] = dk + o;
-          bq[kk] = dq_k + st * kStageStep + o;
+          b[kk] = dq_k + st * kStageStep + x * kHalfRows + o;
         }
-        umma8_ss(tbase + 0, a, bq, 0u, idS);           // S^T = K Q^T
+        umma8_ss(tbase + 128 * x, a, b, 0u, idS);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t o = (kk >> 2) * kChunkStep + (kk & 3) * 2;
           a[kk] = dv + o;
-          bq[kk] = ddo_k + st * kStageStep + o;
+          b[kk] = ddo_k + st * kStageStep + x * kHalfRows + o;
         }
-        umma8_ss(tbase + 128, a, bq, 0u, idS);         // dP^T = V dO^T
-        umma_commit(&s.s_full);
-        if (!mbar_wait(&s.p_full, (uint32_t)it & 1u, 113, abort_flag)) break;
+        umma8_ss(tbase + 128 * x + 64, a, b, 0u, idS);
+        umma_commit(&s.s_full[x]);
+      };
+      // dV += P^T_x dO_x, dK += dS^T_x Q_x (A in TMEM, K = the half's 64 queries).
+      auto issue_g = [&](int x, int st, uint32_t acc) {
+        uint32_t ta[4];
+        uint64_t b[4];
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          ta[kk] = tbase + 128 * x + kk * 8;
+          b[kk] = ddo_mn + st * kStageStep + x * kHalfRows + kk * 128;
+        }
+        umma4_ts(tbase + 256, ta, b, acc, idG);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          ta[kk] = tbase + 128 * x + 64 + kk * 8;
+          b[kk] = dq_mn + st * kStageStep + x * kHalfRows + kk * 128;
+        }
+        umma4_ts(tbase + 384, ta, b, acc, idG);
+      };
+      bool ok = mbar_wait(&s.kv_full, 0, 111, abort_flag) &&
+                mbar_wait(&s.q_full[0], 0, 112, abort_flag);
+      if (ok) {
         tc_fence_after();
-        uint32_t ta[8];
-        uint64_t bb[8];
+        issue_s(0, 0);
+        issue_s(1, 0);
+      }
+      // Ping-pong: while softmax group x works on half x of query tile it,
+      // the tensor core runs the other half's gradient and next-tile MMAs.
+      for (int it = 0; it < n_it && ok; ++it) {
+        const int st = it % QS;
+        const bool more = it + 1 < n_it;
+        const int st1 = (it + 1) % QS;
+        const uint32_t ph1 = (uint32_t)((it + 1) / QS) & 1u;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          ta[kk] = tbase + 0 + 64 * (kk >> 2) + (kk & 3) * 8;
-          bb[kk] = ddo_mn + st * kStageStep + kk * 128;
+        for (int x = 0; x < 2; ++x) {
+          if (!mbar_wait(&s.p_full[x], (uint32_t)it & 1u, 113, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          issue_g(x, st, (it > 0 || x > 0) ? 1u : 0u);
+          if (x == 1) umma_commit(&s.q_empty[st]);
+          if (more) {
+            if (x == 0) {
+              if (!mbar_wait(&s.q_full[st1], ph1, 117, abort_flag)) { ok = false; break; }
+              tc_fence_after();
+            }
+            issue_s(x, st1);
+          }
         }
-        umma8_ts(tbase + 256, ta, bb, it > 0 ? 1u : 0u, idG);   // dV += P^T dO
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          ta[kk] = tbase + 128 + 64 * (kk >> 2) + (kk & 3) * 8;
-          bb[kk] = dq_mn + st * kStageStep + kk * 128;
-        }
-        umma8_ts(tbase + 384, ta, bb, it > 0 ? 1u : 0u, idG);   // dK += dS^T Q
-        umma_commit(&s.q_empty[st]);
       }
       umma_commit(&s.acc_full);
     }
   } else {
     // ---------------- softmax / epilogue: thread = key row ----------------
+    // Group half (warps 4*half .. 4*half+3) owns query half `half` of every
+    // tile: S^T at TMEM columns [128 half, +64), dP^T at [128 half + 64, +64).
     const int quarter = warp & 3, half = warp >> 2;
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const uint32_t tS = tbase + lane_off, tP = tbase + 128 + lane_off;
+    const uint32_t tS = tbase + 128 * half + lane_off, tP = tS + 64;
     const uint64_t scale2 = attn::pk2(scale_log2, scale_log2);
     bool ok = true;
     for (int it = 0; it < n_it; ++it) {
@@ -352,19 +394,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t ph = (uint32_t)(it / QS) & 1u;
       // lse2 / delta arrived with q_full (async proxy): observe it directly.
       if (!mbar_wait(&s.q_full[st], ph, 114, abort_flag)) { ok = false; break; }
-      if (!mbar_wait(&s.s_full, (uint32_t)it & 1u, 115, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(&s.s_full[half], (uint32_t)it & 1u, 115, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      const bool diag = causal && i == j;  // query c < key r is masked
-      const uint64_t* nl = reinterpret_cast<const uint64_t*>(s.lse2[st]);
-      const uint64_t* nd = reinterpret_cast<const uint64_t*>(s.delta[st]);
+      const bool diag = causal && i == j;  // query q < key r is masked
+      const uint64_t* nl = reinterpret_cast<const uint64_t*>(s.lse2[st] + BH2 * half);
+      const uint64_t* nd = reinterpret_cast<const uint64_t*>(s.delta[st] + BH2 * half);
+      const int qh = BH2 * half;  // first query of this half within the tile
 #pragma unroll 1
-      for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
+      for (int c0 = 0; c0 < BH2; c0 += 32) {
         uint32_t sv[32], dv[32];
         tmem_ld32(tS + c0, sv);
         tmem_ld32(tP + c0, dv);
         tmem_ld_wait(sv);
         tmem_ld_wait(dv);
-        if (diag) mask_chunk(sv, [&](int c) { return c0 + c >= r; });
+        if (diag) mask_chunk(sv, [&](int c) { return qh + c0 + c >= r; });
         uint32_t pk_p[16], pk_ds[16];
         p_ds_chunk<true>(sv, dv, scale2,
                          [&](int c, uint64_t& l, uint64_t& d) {
@@ -372,13 +415,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                            d = nd[(c0 + c) >> 1];
                          },
                          pk_p, pk_ds);
-        // packed into this half's own, already-read columns (see below)
-        tmem_st16(tS + half * 64 + (c0 - half * 64) / 2, pk_p);
-        tmem_st16(tP + half * 64 + (c0 - half * 64) / 2, pk_ds);
+        // packed into this half's own, already-read columns
+        tmem_st16(tS + c0 / 2, pk_p);
+        tmem_st16(tP + c0 / 2, pk_ds);
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&s.p_full);
+      mbar_arrive(&s.p_full[half]);
     }
     if (ok && mbar_wait(&s.acc_full, 0, 116, abort_flag)) {
       tc_fence_after();
@@ -407,7 +450,7 @@ struct SmemQ {
   alignas(1024) uint8_t v[KS][2][kChunk];
   uint64_t q_full;
   uint64_t kv_full[KS], kv_empty[KS];
-  uint64_t s_full, p_full, acc_full;
+  uint64_t s_full[2], p_full[2], acc_full;
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -441,8 +484,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&s.kv_full[k], 1);
       mbar_init(&s.kv_empty[k], 1);
     }
-    mbar_init(&s.s_full, 1);
-    mbar_init(&s.p_full, kSoftmaxThreads);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&s.s_full[x], 1);
+      mbar_init(&s.p_full[x], kSoftmaxThreads / 2);
+    }
     mbar_init(&s.acc_full, 1);
     s.abort_flag = 0;
     fence_mbar_init();
@@ -481,76 +526,103 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kWarpMma) {
     if (lane == 0) {
-      constexpr uint32_t idS = idesc_bf16_f32(BT, BT, false, false);
+      constexpr uint32_t idS = idesc_bf16_f32(BT, BH2, false, false);
       constexpr uint32_t idG = idesc_bf16_f32(BT, HD, false, true);
       constexpr uint64_t kChunkStep = kChunk >> 4;
       constexpr uint64_t kStageStep = (2 * kChunk) >> 4;
+      constexpr uint64_t kHalfRows = (BH2 * 128) >> 4;  // 64 rows of 128 bytes
       const uint64_t dq = sdesc_sw128(smem_u32(s.q[0]), 16, 1024);
       const uint64_t ddo = sdesc_sw128(smem_u32(s.dO[0]), 16, 1024);
       const uint64_t dk_k = sdesc_sw128(smem_u32(s.k[0][0]), 16, 1024);
       const uint64_t dv_k = sdesc_sw128(smem_u32(s.v[0][0]), 16, 1024);
       const uint64_t dk_mn = sdesc_sw128(smem_u32(s.k[0][0]), kChunk, 1024);
-      bool ok = mbar_wait(&s.q_full, 0, 121, abort_flag);
-      for (int jj = 0; jj < n_kv && ok; ++jj) {
-        const int st = jj % KS;
-        const uint32_t ph = (uint32_t)(jj / KS) & 1u;
-        if (!mbar_wait(&s.kv_full[st], ph, 122, abort_flag)) break;
-        tc_fence_after();
-        uint64_t a[8], bk[8];
+      // S_x = Q K_x^T and dP_x = dO V_x^T for key half x of stage st.
+      auto issue_s = [&](int x, int st) {
+        uint64_t a[8], b[8];
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t o = (kk >> 2) * kChunkStep + (kk & 3) * 2;
           a[kk] = dq + o;
-          bk[kk] = dk_k + st * kStageStep + o;
+          b[kk] = dk_k + st * kStageStep + x * kHalfRows + o;
         }
-        umma8_ss(tbase + 0, a, bk, 0u, idS);           // S = Q K^T
+        umma8_ss(tbase + 128 * x, a, b, 0u, idS);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t o = (kk >> 2) * kChunkStep + (kk & 3) * 2;
           a[kk] = ddo + o;
-          bk[kk] = dv_k + st * kStageStep + o;
+          b[kk] = dv_k + st * kStageStep + x * kHalfRows + o;
         }
-        umma8_ss(tbase + 128, a, bk, 0u, idS);         // dP = dO V^T
-        umma_commit(&s.s_full);
-        if (!mbar_wait(&s.p_full, (uint32_t)jj & 1u, 123, abort_flag)) break;
-        tc_fence_after();
-        uint32_t ta[8];
-        uint64_t bb[8];
+        umma8_ss(tbase + 128 * x + 64, a, b, 0u, idS);
+        umma_commit(&s.s_full[x]);
+      };
+      // dQ += dS_x K_x (A in TMEM, K = the half's 64 keys).
+      auto issue_g = [&](int x, int st, uint32_t acc) {
+        uint32_t ta[4];
+        uint64_t b[4];
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          ta[kk] = tbase + 0 + 64 * (kk >> 2) + (kk & 3) * 8;
-          bb[kk] = dk_mn + st * kStageStep + kk * 128;
+        for (int kk = 0; kk < 4; ++kk) {
+          ta[kk] = tbase + 128 * x + kk * 8;
+          b[kk] = dk_mn + st * kStageStep + x * kHalfRows + kk * 128;
         }
-        umma8_ts(tbase + 256, ta, bb, jj > 0 ? 1u : 0u, idG);   // dQ += dS K
-        umma_commit(&s.kv_empty[st]);
+        umma4_ts(tbase + 256, ta, b, acc, idG);
+      };
+      bool ok = mbar_wait(&s.q_full, 0, 121, abort_flag) &&
+                mbar_wait(&s.kv_full[0], 0, 122, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+      }
+      for (int jj = 0; jj < n_kv && ok; ++jj) {
+        const int st = jj % KS;
+        const bool more = jj + 1 < n_kv;
+        const int st1 = (jj + 1) % KS;
+        const uint32_t ph1 = (uint32_t)((jj + 1) / KS) & 1u;
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+          if (!mbar_wait(&s.p_full[x], (uint32_t)jj & 1u, 123, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          issue_g(x, st, (jj > 0 || x > 0) ? 1u : 0u);
+          if (x == 1) umma_commit(&s.kv_empty[st]);
+          if (more) {
+            if (x == 0) {
+              if (!mbar_wait(&s.kv_full[st1], ph1, 126, abort_flag)) { ok = false; break; }
+              tc_fence_after();
+            }
+            issue_s(x, st1);
+          }
+        }
       }
       umma_commit(&s.acc_full);
     }
   } else {
     // ---------------- softmax / epilogue: thread = query row ----------------
+    // Group half owns key half `half` of every key tile: S at TMEM columns
+    // [128 half, +64), dP at [128 half + 64, +64).
     const int quarter = warp & 3, half = warp >> 2;
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const uint32_t tS = tbase + lane_off, tP = tbase + 128 + lane_off;
+    const uint32_t tS = tbase + 128 * half + lane_off, tP = tS + 64;
     const size_t srow = (size_t)bhq * Sp + (size_t)i * BT + r;
     const float nl = lse2[srow], nd = delta[srow];
     const uint64_t nl2 = attn::pk2(nl, nl), nd2 = attn::pk2(nd, nd);
     const uint64_t scale2 = attn::pk2(scale_log2, scale_log2);
     bool ok = true;
     for (int jj = 0; jj < n_kv; ++jj) {
-      if (!mbar_wait(&s.s_full, (uint32_t)jj & 1u, 124, abort_flag)) { ok = false; break; }
+      if (!mbar_wait(&s.s_full[half], (uint32_t)jj & 1u, 124, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      const bool diag = causal && jj == i;  // key c > query r is masked
-      const int kpad = S - jj * BT;         // keys c >= kpad are padding
-      const bool masked = diag || kpad < BT;
+      const int kh = BH2 * half;             // first key of this half within the tile
+      const bool diag = causal && jj == i;   // key k > query r is masked
+      const int kpad = S - jj * BT - kh;     // keys c >= kpad of this half are padding
+      const bool masked = (diag && kh + BH2 - 1 > r) || kpad < BH2;
 #pragma unroll 1
-      for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
+      for (int c0 = 0; c0 < BH2; c0 += 32) {
         uint32_t sv[32], dv[32];
         tmem_ld32(tS + c0, sv);
         tmem_ld32(tP + c0, dv);
         tmem_ld_wait(sv);
         tmem_ld_wait(dv);
-        if (masked) mask_chunk(sv, [&](int c) { return c0 + c < kpad && (!diag || c0 + c <= r); });
+        if (masked) mask_chunk(sv, [&](int c) { return c0 + c < kpad && (!diag || kh + c0 + c <= r); });
         uint32_t pk_p[16], pk_ds[16];
         p_ds_chunk<false>(sv, dv, scale2,
                           [&](int, uint64_t& l, uint64_t& d) {
@@ -558,11 +630,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                             d = nd2;
                           },
                           pk_p, pk_ds);
-        tmem_st16(tS + half * 64 + (c0 - half * 64) / 2, pk_ds);
+        tmem_st16(tS + c0 / 2, pk_ds);
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&s.p_full);
+      mbar_arrive(&s.p_full[half]);
     }
     if (ok && mbar_wait(&s.acc_full, 0, 125, abort_flag)) {
       tc_fence_after();
