@@ -386,7 +386,7 @@ class Attention(Workload):
 
 class AttentionF32(Workload):
     """C1: fp32 [1,8,512,64] non-causal (CUDA cores)."""
-    dominant = "attn_kernel<float>"
+    dominant = "attn_tile_kernel<float, float, 64>"
 
     def __init__(self, jb, torch, rank, world):
         self.jb, self.torch = jb, torch

@@ -326,9 +326,32 @@ int attn_simt_launch(const void* Q, const void* K, const void* V, void* O, float
   return check_launch("attn_kernel launch");
 }
 
+template <typename TIn, typename TOut, int D>
+int attn_tile_launch(const void* Q, const void* K, const void* V, void* O, float* lse, int B, int Hq,
+                     int Hkv, int S, float scale, int causal, cudaStream_t st) {
+  namespace sm = jb::simt;
+  const size_t smem = sizeof(float) * (D * sm::TBQ + D * (sm::TBK + 4) + sm::TBK * D + sm::TBK * sm::TBQ);
+  auto kern = sm::attn_tile_kernel<TIn, TOut, D>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn_tile)");
+  }
+  dim3 grid((unsigned)((S + sm::TBQ - 1) / sm::TBQ), (unsigned)(B * Hq));
+  kern<<<grid, 128, smem, st>>>(static_cast<const TIn*>(Q), static_cast<const TIn*>(K),
+                                static_cast<const TIn*>(V), static_cast<TOut*>(O), lse, Hq, Hkv, S,
+                                scale, causal);
+  return check_launch("attn_tile_kernel launch");
+}
+
 template <typename T>
 int attn_simt(const void* Q, const void* K, const void* V, void* O, float* lse, int B, int Hq,
               int Hkv, int S, int D, float scale, int causal, cudaStream_t st) {
+  // register-tiled kernel: vector loads of K / V need 16-byte aligned bases
+  if (aligned16(Q) && aligned16(K) && aligned16(V)) {
+    if (D == 32) return attn_tile_launch<T, T, 32>(Q, K, V, O, lse, B, Hq, Hkv, S, scale, causal, st);
+    if (D == 64) return attn_tile_launch<T, T, 64>(Q, K, V, O, lse, B, Hq, Hkv, S, scale, causal, st);
+    if (D == 128) return attn_tile_launch<T, T, 128>(Q, K, V, O, lse, B, Hq, Hkv, S, scale, causal, st);
+  }
   if (D <= 32) return attn_simt_launch<T, T, 1>(Q, K, V, O, lse, B, Hq, Hkv, S, D, scale, causal, st);
   if (D <= 64) return attn_simt_launch<T, T, 2>(Q, K, V, O, lse, B, Hq, Hkv, S, D, scale, causal, st);
   if (D <= 128) return attn_simt_launch<T, T, 4>(Q, K, V, O, lse, B, Hq, Hkv, S, D, scale, causal, st);

@@ -280,6 +280,169 @@ __global__ void __launch_bounds__(128)
 }
 
 // ---------------------------------------------------------------------------
+// Register-tiled attention forward for head dims 32, 64 and 128 (the fp32
+// path, C1's [1,8,512,64]): 16 query rows of one (b, h) per CTA, key tiles
+// of 64, 128 threads as 8 x 16.  Thread (ty, tx) computes the scores of
+// query rows 2ty, 2ty+1 against keys 4tx..4tx+3 of the tile (Q and K
+// staged transposed in shared memory, 8 FMAs per float2 + float4 load) and
+// accumulates output dims tx*DPT.. of its two rows from P (staged
+// key-major) and V.  Online softmax per row as attn_kernel (expf, running
+// max and sum reduced over the 16 threads of a half warp); causal and
+// padding masks; grouped-query heads.
+// ---------------------------------------------------------------------------
+constexpr int TBQ = 16, TBK = 64;
+
+// Four consecutive elements as fp32 (16-byte fp32 / 8-byte bf16 load).
+__device__ __forceinline__ float4 load4_f32(const float* p) {
+  return *reinterpret_cast<const float4*>(p);
+}
+__device__ __forceinline__ float4 load4_f32(const __nv_bfloat16* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+template <typename TIn, typename TOut, int D>
+__global__ void __launch_bounds__(128, 4)
+    attn_tile_kernel(const TIn* __restrict__ Q, const TIn* __restrict__ Kp,
+                     const TIn* __restrict__ Vp, TOut* __restrict__ O, float* __restrict__ lse,
+                     int Hq, int Hkv, int S, float scale, int causal) {
+  static_assert(D == 32 || D == 64 || D == 128, "head dim");
+  constexpr int DPT = D / 16;     // output dims per thread
+  constexpr int KT = TBK + 4;     // Kt row stride (16-byte multiple, fewer bank conflicts)
+  extern __shared__ float sm[];
+  float* Qt = sm;                 // [D][TBQ]
+  float* Kt = Qt + D * TBQ;       // [D][KT]
+  float* Vs = Kt + D * KT;        // [TBK][D]
+  float* Pt = Vs + TBK * D;       // [TBK][TBQ]
+
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int bh = blockIdx.y;
+  const int b = bh / Hq, h = bh % Hq;
+  const int hk = h / (Hq / Hkv);
+  const int q0 = blockIdx.x * TBQ;
+  const TIn* qb = Q + (size_t)bh * S * D;
+  const TIn* kb = Kp + ((size_t)b * Hkv + hk) * S * D;
+  const TIn* vb = Vp + ((size_t)b * Hkv + hk) * S * D;
+
+  for (int e = threadIdx.x; e < TBQ * D; e += 128) {
+    const int r = e / D, d = e % D;
+    Qt[d * TBQ + r] = (q0 + r < S) ? to_f32(qb[(size_t)(q0 + r) * D + d]) : 0.0f;
+  }
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f}, acc[2][DPT];
+#pragma unroll
+  for (int r = 0; r < 2; ++r)
+#pragma unroll
+    for (int i = 0; i < DPT; ++i) acc[r][i] = 0.0f;
+
+  const int qi0 = q0 + 2 * ty;  // this thread's first query row
+  const int kv_end = causal ? min(S, q0 + TBQ) : S;
+  // K / V tiles move through registers, 4 elements per load: the next
+  // tile's loads are issued before the current tile's arithmetic (head dims
+  // up to 64; at 128 the 32 registers per tensor would spill).
+  constexpr int NV4 = TBK * D / 4 / 128;
+  constexpr bool kPrefetch = D <= 64;
+  float4 kr[NV4], vr[NV4];
+  auto fetch = [&](int k0) {
+#pragma unroll
+    for (int u = 0; u < NV4; ++u) {
+      const int idx = threadIdx.x + 128 * u;
+      const int j = idx / (D / 4), d4 = idx % (D / 4);
+      const bool in = k0 + j < S;
+      kr[u] = in ? load4_f32(kb + (size_t)(k0 + j) * D + 4 * d4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      vr[u] = in ? load4_f32(vb + (size_t)(k0 + j) * D + 4 * d4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  auto stash = [&]() {
+#pragma unroll
+    for (int u = 0; u < NV4; ++u) {
+      const int idx = threadIdx.x + 128 * u;
+      const int j = idx / (D / 4), d4 = idx % (D / 4);
+      Kt[(4 * d4 + 0) * KT + j] = kr[u].x;
+      Kt[(4 * d4 + 1) * KT + j] = kr[u].y;
+      Kt[(4 * d4 + 2) * KT + j] = kr[u].z;
+      Kt[(4 * d4 + 3) * KT + j] = kr[u].w;
+      *reinterpret_cast<float4*>(Vs + j * D + 4 * d4) = vr[u];
+    }
+  };
+  if (kPrefetch && kv_end > 0) fetch(0);
+  for (int k0 = 0; k0 < kv_end; k0 += TBK) {
+    __syncthreads();  // previous tile's Kt / Vs / Pt fully consumed
+    if (!kPrefetch) fetch(k0);
+    stash();
+    __syncthreads();
+    if (kPrefetch && k0 + TBK < kv_end) fetch(k0 + TBK);  // in flight during this tile
+    float sc[2][4] = {};
+#pragma unroll 8
+    for (int d = 0; d < D; ++d) {
+      const float2 q = *reinterpret_cast<const float2*>(Qt + d * TBQ + 2 * ty);
+      const float4 k = *reinterpret_cast<const float4*>(Kt + d * KT + 4 * tx);
+      sc[0][0] = fmaf(q.x, k.x, sc[0][0]); sc[0][1] = fmaf(q.x, k.y, sc[0][1]);
+      sc[0][2] = fmaf(q.x, k.z, sc[0][2]); sc[0][3] = fmaf(q.x, k.w, sc[0][3]);
+      sc[1][0] = fmaf(q.y, k.x, sc[1][0]); sc[1][1] = fmaf(q.y, k.y, sc[1][1]);
+      sc[1][2] = fmaf(q.y, k.z, sc[1][2]); sc[1][3] = fmaf(q.y, k.w, sc[1][3]);
+    }
+    float p[2][4];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int qi = qi0 + r;
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int kj = k0 + 4 * tx + c;
+        const bool valid = kj < S && !(causal && kj > qi);
+        sc[r][c] = valid ? scale * sc[r][c] : -INFINITY;
+        tmax = fmaxf(tmax, sc[r][c]);
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+      const float mnew = fmaxf(m[r], tmax);
+      float psum = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        p[r][c] = (sc[r][c] == -INFINITY) ? 0.0f : expf(sc[r][c] - mnew);
+        psum += p[r][c];
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
+      const float alpha = (m[r] == -INFINITY) ? 0.0f : expf(m[r] - mnew);
+      l[r] = l[r] * alpha + psum;
+      m[r] = mnew;
+#pragma unroll
+      for (int i = 0; i < DPT; ++i) acc[r][i] *= alpha;
+    }
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      *reinterpret_cast<float2*>(Pt + (4 * tx + c) * TBQ + 2 * ty) = make_float2(p[0][c], p[1][c]);
+    __syncthreads();
+#pragma unroll 8
+    for (int j = 0; j < TBK; ++j) {
+      const float2 pj = *reinterpret_cast<const float2*>(Pt + j * TBQ + 2 * ty);
+      const float* vrow = Vs + j * D + tx * DPT;
+#pragma unroll
+      for (int i = 0; i < DPT; i += 2) {
+        const float2 v = *reinterpret_cast<const float2*>(vrow + i);
+        acc[0][i] = fmaf(pj.x, v.x, acc[0][i]);
+        acc[0][i + 1] = fmaf(pj.x, v.y, acc[0][i + 1]);
+        acc[1][i] = fmaf(pj.y, v.x, acc[1][i]);
+        acc[1][i + 1] = fmaf(pj.y, v.y, acc[1][i + 1]);
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int qi = qi0 + r;
+    if (qi >= S) continue;
+    const float inv = 1.0f / l[r];
+    TOut* orow = O + ((size_t)bh * S + qi) * D + tx * DPT;
+#pragma unroll
+    for (int i = 0; i < DPT; ++i) orow[i] = from_f32<TOut>(acc[r][i] * inv);
+    if (lse && tx == 0) lse[(size_t)bh * S + qi] = m[r] + logf(l[r]);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // LayerNorm over rows (include/jules/Kernel/FusedKernels.h:532-600): mean,
 // biased variance (second pass over (x-mean)^2), inv_std = 1/sqrt(var+eps),
 // y = (x-mean)*inv_std*gamma + beta.  One 256-thread block per row; fp32
