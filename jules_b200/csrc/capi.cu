@@ -330,16 +330,16 @@ template <typename TIn, typename TOut, int D>
 int attn_tile_launch(const void* Q, const void* K, const void* V, void* O, float* lse, int B, int Hq,
                      int Hkv, int S, float scale, int causal, cudaStream_t st) {
   namespace sm = jb::simt;
-  const size_t smem = sizeof(float) * (D * sm::TBQ + D * (sm::TBK + 4) + sm::TBK * D + sm::TBK * sm::TBQ);
+  const size_t smem = sizeof(float) * sm::attn_tile_smem_floats<D>();
   auto kern = sm::attn_tile_kernel<TIn, TOut, D>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn_tile)");
   }
   dim3 grid((unsigned)((S + sm::TBQ - 1) / sm::TBQ), (unsigned)(B * Hq));
-  kern<<<grid, 128, smem, st>>>(static_cast<const TIn*>(Q), static_cast<const TIn*>(K),
-                                static_cast<const TIn*>(V), static_cast<TOut*>(O), lse, Hq, Hkv, S,
-                                scale, causal);
+  kern<<<grid, sm::kTileThreads, smem, st>>>(static_cast<const TIn*>(Q), static_cast<const TIn*>(K),
+                                             static_cast<const TIn*>(V), static_cast<TOut*>(O), lse,
+                                             Hq, Hkv, S, scale, causal);
   return check_launch("attn_tile_kernel launch");
 }
 

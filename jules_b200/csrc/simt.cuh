@@ -282,7 +282,9 @@ __global__ void __launch_bounds__(128)
 // ---------------------------------------------------------------------------
 // Register-tiled attention forward for head dims 32, 64 and 128 (the fp32
 // path, C1's [1,8,512,64]): 16 query rows of one (b, h) per CTA, key tiles
-// of 64, 128 threads as 8 x 16.  Thread (ty, tx) computes the scores of
+// of 64, two groups of 128 threads taking alternate key tiles (each with its
+// own shared-memory tiles and named barrier), merged at the end.  Within a
+// group, 8 x 16 threads: thread (ty, tx) computes the scores of
 // query rows 2ty, 2ty+1 against keys 4tx..4tx+3 of the tile (Q and K
 // staged transposed in shared memory, 8 FMAs per float2 + float4 load) and
 // accumulates output dims tx*DPT.. of its two rows from P (staged
@@ -303,8 +305,15 @@ __device__ __forceinline__ float4 load4_f32(const __nv_bfloat16* p) {
   return make_float4(a.x, a.y, b.x, b.y);
 }
 
+constexpr int kTileThreads = 256;
+
+template <int D>
+constexpr size_t attn_tile_smem_floats() {
+  return D * TBQ + 2 * (D * (TBK + 4) + TBK * D + TBK * TBQ);
+}
+
 template <typename TIn, typename TOut, int D>
-__global__ void __launch_bounds__(128, 4)
+__global__ void __launch_bounds__(kTileThreads, 2)
     attn_tile_kernel(const TIn* __restrict__ Q, const TIn* __restrict__ Kp,
                      const TIn* __restrict__ Vp, TOut* __restrict__ O, float* __restrict__ lse,
                      int Hq, int Hkv, int S, float scale, int causal) {
@@ -312,12 +321,16 @@ __global__ void __launch_bounds__(128, 4)
   constexpr int DPT = D / 16;     // output dims per thread
   constexpr int KT = TBK + 4;     // Kt row stride (16-byte multiple, fewer bank conflicts)
   extern __shared__ float sm[];
-  float* Qt = sm;                 // [D][TBQ]
-  float* Kt = Qt + D * TBQ;       // [D][KT]
-  float* Vs = Kt + D * KT;        // [TBK][D]
-  float* Pt = Vs + TBK * D;       // [TBK][TBQ]
+  const int grp = threadIdx.x >> 7;  // key-tile group: tiles grp, grp + 2, ...
+  const int gt = threadIdx.x & 127;  // thread within the group
+  float* Qt = sm;                                    // [D][TBQ], shared by both groups
+  float* Kt = Qt + D * TBQ + grp * (D * KT + TBK * D + TBK * TBQ);  // [D][KT]
+  float* Vs = Kt + D * KT;                           // [TBK][D]
+  float* Pt = Vs + TBK * D;                          // [TBK][TBQ]
+  // group-local barrier (ids 1, 2), 128 threads
+  auto group_sync = [&]() { asm volatile("bar.sync %0, 128;" ::"r"(grp + 1) : "memory"); };
 
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int tx = gt & 15, ty = gt >> 4;
   const int bh = blockIdx.y;
   const int b = bh / Hq, h = bh % Hq;
   const int hk = h / (Hq / Hkv);
@@ -326,10 +339,11 @@ __global__ void __launch_bounds__(128, 4)
   const TIn* kb = Kp + ((size_t)b * Hkv + hk) * S * D;
   const TIn* vb = Vp + ((size_t)b * Hkv + hk) * S * D;
 
-  for (int e = threadIdx.x; e < TBQ * D; e += 128) {
+  for (int e = threadIdx.x; e < TBQ * D; e += kTileThreads) {
     const int r = e / D, d = e % D;
     Qt[d * TBQ + r] = (q0 + r < S) ? to_f32(qb[(size_t)(q0 + r) * D + d]) : 0.0f;
   }
+  __syncthreads();
   float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f}, acc[2][DPT];
 #pragma unroll
   for (int r = 0; r < 2; ++r)
@@ -347,7 +361,7 @@ __global__ void __launch_bounds__(128, 4)
   auto fetch = [&](int k0) {
 #pragma unroll
     for (int u = 0; u < NV4; ++u) {
-      const int idx = threadIdx.x + 128 * u;
+      const int idx = gt + 128 * u;
       const int j = idx / (D / 4), d4 = idx % (D / 4);
       const bool in = k0 + j < S;
       kr[u] = in ? load4_f32(kb + (size_t)(k0 + j) * D + 4 * d4) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -357,7 +371,7 @@ __global__ void __launch_bounds__(128, 4)
   auto stash = [&]() {
 #pragma unroll
     for (int u = 0; u < NV4; ++u) {
-      const int idx = threadIdx.x + 128 * u;
+      const int idx = gt + 128 * u;
       const int j = idx / (D / 4), d4 = idx % (D / 4);
       Kt[(4 * d4 + 0) * KT + j] = kr[u].x;
       Kt[(4 * d4 + 1) * KT + j] = kr[u].y;
@@ -366,13 +380,14 @@ __global__ void __launch_bounds__(128, 4)
       *reinterpret_cast<float4*>(Vs + j * D + 4 * d4) = vr[u];
     }
   };
-  if (kPrefetch && kv_end > 0) fetch(0);
-  for (int k0 = 0; k0 < kv_end; k0 += TBK) {
-    __syncthreads();  // previous tile's Kt / Vs / Pt fully consumed
+  const int k_first = grp * TBK;
+  if (kPrefetch && k_first < kv_end) fetch(k_first);
+  for (int k0 = k_first; k0 < kv_end; k0 += 2 * TBK) {
+    group_sync();  // previous tile's Kt / Vs / Pt fully consumed
     if (!kPrefetch) fetch(k0);
     stash();
-    __syncthreads();
-    if (kPrefetch && k0 + TBK < kv_end) fetch(k0 + TBK);  // in flight during this tile
+    group_sync();
+    if (kPrefetch && k0 + 2 * TBK < kv_end) fetch(k0 + 2 * TBK);  // in flight during this tile
     float sc[2][4] = {};
 #pragma unroll 8
     for (int d = 0; d < D; ++d) {
@@ -415,7 +430,7 @@ __global__ void __launch_bounds__(128, 4)
 #pragma unroll
     for (int c = 0; c < 4; ++c)
       *reinterpret_cast<float2*>(Pt + (4 * tx + c) * TBQ + 2 * ty) = make_float2(p[0][c], p[1][c]);
-    __syncthreads();
+    group_sync();
 #pragma unroll 8
     for (int j = 0; j < TBK; ++j) {
       const float2 pj = *reinterpret_cast<const float2*>(Pt + j * TBQ + 2 * ty);
@@ -428,6 +443,40 @@ __global__ void __launch_bounds__(128, 4)
         acc[1][i] = fmaf(pj.y, v.x, acc[1][i]);
         acc[1][i + 1] = fmaf(pj.y, v.y, acc[1][i + 1]);
       }
+    }
+  }
+  // Merge: group 1 hands (m, l, acc) of each of its rows to the group-0
+  // thread with the same (ty, tx) through its own (now free) tile memory.
+  __syncthreads();
+  float* xch = sm + D * TBQ + (D * KT + TBK * D + TBK * TBQ);  // group 1's tiles
+  constexpr int XS = 2 * DPT + 8;  // floats per thread: m, l at 4r, 4r+1; acc from 8
+  if (grp == 1) {
+    float* x = xch + gt * XS;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      x[4 * r] = m[r];
+      x[4 * r + 1] = l[r];
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int i = 0; i < DPT; ++i) x[8 + r * DPT + i] = acc[r][i];
+  }
+  __syncthreads();
+  if (grp == 1) return;
+  {
+    const float* x = xch + gt * XS;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const float m1 = x[4 * r], l1 = x[4 * r + 1];
+      const float mn = fmaxf(m[r], m1);
+      if (mn == -INFINITY) continue;  // row with no visible key (padding)
+      const float a0 = (m[r] == -INFINITY) ? 0.0f : expf(m[r] - mn);
+      const float a1 = (m1 == -INFINITY) ? 0.0f : expf(m1 - mn);
+      l[r] = l[r] * a0 + l1 * a1;
+      m[r] = mn;
+#pragma unroll
+      for (int i = 0; i < DPT; ++i) acc[r][i] = acc[r][i] * a0 + x[8 + r * DPT + i] * a1;
     }
   }
 #pragma unroll
