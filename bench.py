@@ -249,6 +249,67 @@ class Workload:
     def sets_for(self, bytes_per_set):
         return max(2, int((2 * L2_BYTES) // max(bytes_per_set, 1)) + 1)
 
+    def e2e_spec(self):
+        """(pinned host inputs, pinned host outputs, run(dev_inputs, dev_outputs)); run calls
+        the public API on the current stream."""
+        raise NotImplementedError
+
+
+class E2EPipeline:
+    """End-to-end steps through the public API with host buffers: each step
+    copies its inputs host -> device, runs, and copies its result device ->
+    host.  Two device buffer sets and three streams (H2D, compute, D2H)
+    ordered by events, so step i's copies overlap steps i-1 and i+1 the way a
+    serving loop overlaps them; every step still moves all of its bytes."""
+
+    def __init__(self, torch, wl):
+        self.t = torch
+        self.h_in, h_out, self.run = wl.e2e_spec()
+        self.h_out = [h_out, [torch.empty_like(h).pin_memory() for h in h_out]]
+        self.sets = [([torch.empty_like(h, device="cuda") for h in self.h_in],
+                      [torch.empty_like(h, device="cuda") for h in h_out]) for _ in range(2)]
+        self.s_in, self.s_comp, self.s_out = (torch.cuda.Stream() for _ in range(3))
+        E = torch.cuda.Event
+        self.ev_in, self.ev_comp, self.ev_out = ([E(), E()] for _ in range(3))
+        for k in range(2):  # first waits are satisfied
+            self.ev_comp[k].record(self.s_comp)
+            self.ev_out[k].record(self.s_out)
+        self.h2d = sum(h.numel() * h.element_size() for h in self.h_in)
+        self.d2h = sum(h.numel() * h.element_size() for h in h_out)
+        self.i = 0
+
+    def step(self):
+        t, k = self.t, self.i % 2
+        d_in, d_out = self.sets[k]
+        with t.cuda.stream(self.s_in):
+            self.s_in.wait_event(self.ev_comp[k])   # step i-2's compute has read d_in
+            for h, d in zip(self.h_in, d_in):
+                d.copy_(h, non_blocking=True)
+            self.ev_in[k].record(self.s_in)
+        with t.cuda.stream(self.s_comp):
+            self.s_comp.wait_event(self.ev_in[k])
+            self.s_comp.wait_event(self.ev_out[k])  # step i-2's D2H has read d_out
+            self.run(d_in, d_out)
+            self.ev_comp[k].record(self.s_comp)
+        with t.cuda.stream(self.s_out):
+            self.s_out.wait_event(self.ev_comp[k])
+            for h, d in zip(self.h_out[k], d_out):
+                h.copy_(d, non_blocking=True)
+            self.ev_out[k].record(self.s_out)
+        self.i += 1
+
+    def time_steps(self, n):
+        """Device time of n steps (first H2D start to last D2H end), ms."""
+        t = self.t
+        t.cuda.synchronize()
+        e0, e1 = t.cuda.Event(enable_timing=True), t.cuda.Event(enable_timing=True)
+        e0.record(self.s_in)
+        for _ in range(n):
+            self.step()
+        e1.record(self.s_out)  # after the last D2H, which follows every earlier op
+        t.cuda.synchronize()
+        return e0.elapsed_time(e1)
+
 
 class Gemm(Workload):
     """C2: C = GELU(A.W + bias), M=N=K=4096 per rank (rows of M sharded)."""
@@ -290,24 +351,12 @@ class Gemm(Workload):
         return self.C[i % self.nsets]
 
     # e2e through the C ABI with host buffers
-    def e2e_setup(self):
-        t = self.torch
-        self.hA = self.A[0].cpu().pin_memory()
-        self.hW = self.W[0].cpu().pin_memory()
-        self.hb = self.b[0].cpu().pin_memory()
-        self.hC = t.empty((self.M, self.N), dtype=t.bfloat16).pin_memory()
-        self.dA, self.dW, self.db = (t.empty_like(self.A[0]), t.empty_like(self.W[0]),
-                                     t.empty_like(self.b[0]))
-        self.dC = t.empty_like(self.C[0])
-        self.h2d = (self.hA.numel() + self.hW.numel()) * 2 + self.hb.numel() * 4
-        self.d2h = self.hC.numel() * 2
-
-    def e2e_step(self):
-        self.dA.copy_(self.hA, non_blocking=True)
-        self.dW.copy_(self.hW, non_blocking=True)
-        self.db.copy_(self.hb, non_blocking=True)
-        self.jb.gemm_bias_act(self.dA, self.dW, self.db, act="gelu", out=self.dC)
-        self.hC.copy_(self.dC, non_blocking=True)
+    def e2e_spec(self):
+        jb = self.jb
+        h_in = [self.A[0].cpu().pin_memory(), self.W[0].cpu().pin_memory(),
+                self.b[0].cpu().pin_memory()]
+        h_out = [self.torch.empty((self.M, self.N), dtype=self.torch.bfloat16).pin_memory()]
+        return h_in, h_out, lambda d, o: jb.gemm_bias_act(d[0], d[1], d[2], act="gelu", out=o[0])
 
 
 class Attention(Workload):
@@ -364,24 +413,12 @@ class Attention(Workload):
     def output(self, i):
         return self.O[i % self.nsets]
 
-    def e2e_setup(self):
-        t = self.torch
-        self.hQ = self.Q[0].cpu().pin_memory()
-        self.hK = self.Kt[0].cpu().pin_memory()
-        self.hV = self.V[0].cpu().pin_memory()
-        self.hO = t.empty_like(self.hQ).pin_memory()
-        self.dQ, self.dK, self.dV = (t.empty_like(self.Q[0]), t.empty_like(self.Kt[0]),
-                                     t.empty_like(self.V[0]))
-        self.dO = t.empty_like(self.Q[0])
-        self.h2d = (self.hQ.numel() + self.hK.numel() + self.hV.numel()) * 2
-        self.d2h = self.hO.numel() * 2
-
-    def e2e_step(self):
-        self.dQ.copy_(self.hQ, non_blocking=True)
-        self.dK.copy_(self.hK, non_blocking=True)
-        self.dV.copy_(self.hV, non_blocking=True)
-        self.jb.flash_attention_fwd(self.dQ, self.dK, self.dV, causal=True, out=self.dO, lse=False)
-        self.hO.copy_(self.dO, non_blocking=True)
+    def e2e_spec(self):
+        jb = self.jb
+        h_in = [x[0].cpu().pin_memory() for x in (self.Q, self.Kt, self.V)]
+        h_out = [self.torch.empty_like(h_in[0]).pin_memory()]
+        return h_in, h_out, lambda d, o: jb.flash_attention_fwd(d[0], d[1], d[2], causal=True,
+                                                                 out=o[0], lse=False)
 
 
 class AttentionF32(Workload):
@@ -417,20 +454,12 @@ class AttentionF32(Workload):
     def output(self, i):
         return self.O[i % self.nsets]
 
-    def e2e_setup(self):
-        t = self.torch
-        self.hQ, self.hK, self.hV = (x[0].cpu().pin_memory() for x in (self.Q, self.Kt, self.V))
-        self.hO = t.empty_like(self.hQ).pin_memory()
-        self.dQ, self.dK, self.dV, self.dO = (t.empty_like(self.Q[0]) for _ in range(4))
-        self.h2d = 3 * self.hQ.numel() * 4
-        self.d2h = self.hO.numel() * 4
-
-    def e2e_step(self):
-        self.dQ.copy_(self.hQ, non_blocking=True)
-        self.dK.copy_(self.hK, non_blocking=True)
-        self.dV.copy_(self.hV, non_blocking=True)
-        self.jb.flash_attention_fwd(self.dQ, self.dK, self.dV, causal=False, out=self.dO, lse=False)
-        self.hO.copy_(self.dO, non_blocking=True)
+    def e2e_spec(self):
+        jb = self.jb
+        h_in = [x[0].cpu().pin_memory() for x in (self.Q, self.Kt, self.V)]
+        h_out = [self.torch.empty_like(h_in[0]).pin_memory()]
+        return h_in, h_out, lambda d, o: jb.flash_attention_fwd(d[0], d[1], d[2], causal=False,
+                                                                 out=o[0], lse=False)
 
 
 class Mlp(Workload):
@@ -475,22 +504,14 @@ class Mlp(Workload):
     def output(self, i):
         return self.out
 
-    def e2e_setup(self):
-        t = self.torch
-        self.hX = self.X.cpu().pin_memory()
-        self.hO = t.empty_like(self.hX).pin_memory()
-        self.dX = t.empty_like(self.X)
-        self.dO = t.empty_like(self.X)
-        self.ws = t.empty(self.jb.mlp_block_workspace_bytes(self.T, self.d, self.dff),
-                          dtype=t.uint8, device="cuda")
-        self.h2d = self.hX.numel() * 2
-        self.d2h = self.hO.numel() * 2
-
-    def e2e_step(self):
-        self.dX.copy_(self.hX, non_blocking=True)
-        self.jb.mlp_block(self.dX, self.gam, self.bet, self.W1, self.b1, self.W2, self.b2,
-                          out=self.dO, workspace=self.ws)
-        self.hO.copy_(self.dO, non_blocking=True)
+    def e2e_spec(self):
+        jb, t = self.jb, self.torch
+        self.ws = t.empty(jb.mlp_block_workspace_bytes(self.T, self.d, self.dff), dtype=t.uint8,
+                          device="cuda")
+        h_in = [self.X.cpu().pin_memory()]   # weights stay resident
+        h_out = [t.empty_like(h_in[0]).pin_memory()]
+        return h_in, h_out, lambda d, o: jb.mlp_block(d[0], self.gam, self.bet, self.W1, self.b1,
+                                                       self.W2, self.b2, out=o[0], workspace=self.ws)
 
 
 class Int8Gemm(Workload):
@@ -528,19 +549,11 @@ class Int8Gemm(Workload):
     def output(self, i):
         return self.C[i % self.nsets]
 
-    def e2e_setup(self):
-        t = self.torch
-        self.hA, self.hB = self.A[0].cpu().pin_memory(), self.B[0].cpu().pin_memory()
-        self.hC = t.empty_like(self.C[0], device="cpu").pin_memory()
-        self.dA, self.dB, self.dC = t.empty_like(self.A[0]), t.empty_like(self.B[0]), t.empty_like(self.C[0])
-        self.h2d = self.hA.numel() + self.hB.numel()
-        self.d2h = self.hC.numel() * 4
-
-    def e2e_step(self):
-        self.dA.copy_(self.hA, non_blocking=True)
-        self.dB.copy_(self.hB, non_blocking=True)
-        self.jb.matmul_int8(self.dA, self.dB, 0.01, 0.02, self.bias, out=self.dC)
-        self.hC.copy_(self.dC, non_blocking=True)
+    def e2e_spec(self):
+        jb = self.jb
+        h_in = [self.A[0].cpu().pin_memory(), self.B[0].cpu().pin_memory()]
+        h_out = [self.torch.empty_like(self.C[0], device="cpu").pin_memory()]
+        return h_in, h_out, lambda d, o: jb.matmul_int8(d[0], d[1], 0.01, 0.02, self.bias, out=o[0])
 
 
 class Fp8Gemm(Workload):
@@ -580,19 +593,12 @@ class Fp8Gemm(Workload):
     def output(self, i):
         return self.C[i % self.nsets]
 
-    def e2e_setup(self):
-        t = self.torch
-        self.hA, self.hB = self.A[0].cpu().pin_memory(), self.B[0].cpu().pin_memory()
-        self.hC = t.empty_like(self.C[0], device="cpu").pin_memory()
-        self.dA, self.dB, self.dC = t.empty_like(self.A[0]), t.empty_like(self.B[0]), t.empty_like(self.C[0])
-        self.h2d = self.hA.numel() + self.hB.numel()
-        self.d2h = self.hC.numel() * 2
-
-    def e2e_step(self):
-        self.dA.copy_(self.hA, non_blocking=True)
-        self.dB.copy_(self.hB, non_blocking=True)
-        self.jb.gemm_fp8(self.dA, self.dB, self.bias, act="gelu", scale=self.scale, out=self.dC)
-        self.hC.copy_(self.dC, non_blocking=True)
+    def e2e_spec(self):
+        jb = self.jb
+        h_in = [self.A[0].cpu().pin_memory(), self.B[0].cpu().pin_memory()]
+        h_out = [self.torch.empty_like(self.C[0], device="cpu").pin_memory()]
+        return h_in, h_out, lambda d, o: jb.gemm_fp8(d[0], d[1], self.bias, act="gelu",
+                                                      scale=self.scale, out=o[0])
 
 
 class AttentionBwd(Workload):
@@ -629,23 +635,12 @@ class AttentionBwd(Workload):
     def output(self, i):
         return self.grads[0]
 
-    def e2e_setup(self):
-        t = self.torch
-        self.h_in = [x.cpu().pin_memory() for x in (self.Q, self.K, self.V, self.O, self.dO, self.lse)]
-        self.d_in = [t.empty_like(x) for x in (self.Q, self.K, self.V, self.O, self.dO, self.lse)]
-        self.h_out = [t.empty_like(x, device="cpu").pin_memory() for x in self.grads]
-        self.d_out = tuple(t.empty_like(x) for x in self.grads)
-        self.h2d = sum(x.numel() * x.element_size() for x in self.h_in)
-        self.d2h = sum(x.numel() * x.element_size() for x in self.h_out)
-
-    def e2e_step(self):
-        for h, d in zip(self.h_in, self.d_in):
-            d.copy_(h, non_blocking=True)
-        q, k, v, o, do, lse = self.d_in
-        self.jb.flash_attention_bwd(q, k, v, o, do, lse, causal=True, workspace=self.ws,
-                                    out=self.d_out)
-        for h, d in zip(self.h_out, self.d_out):
-            h.copy_(d, non_blocking=True)
+    def e2e_spec(self):
+        jb = self.jb
+        h_in = [x.cpu().pin_memory() for x in (self.Q, self.K, self.V, self.O, self.dO, self.lse)]
+        h_out = [self.torch.empty_like(x, device="cpu").pin_memory() for x in self.grads]
+        return h_in, h_out, lambda d, o: jb.flash_attention_bwd(*d, causal=True, workspace=self.ws,
+                                                                 out=tuple(o))
 
 
 class RowWise(Workload):
@@ -679,7 +674,7 @@ class RowWise(Workload):
         if self.xent:
             rc = self.jb.lib().jules_cross_entropy_loss(
                 self.jb._ptr(x), self.jb._ptr(t), self.jb._ptr(y), self.jb._ptr(self.loss),
-                self.M, self.N, self.jb.DT_F32, None)
+                self.M, self.N, self.jb.DT_F32, self.jb._stream(None))
             self.jb._check(rc, "jules_cross_entropy_loss")
         else:
             self.jb.softmax(x, out=y)
@@ -695,21 +690,10 @@ class RowWise(Workload):
     def output(self, i):
         return self.Y[i % self.nsets]
 
-    def e2e_setup(self):
-        t = self.torch
-        self.hX = self.X[0].cpu().pin_memory()
-        self.hT = self.T[0].cpu().pin_memory()
-        self.hY = t.empty_like(self.hX).pin_memory()
-        self.dX, self.dY, self.dT = t.empty_like(self.X[0]), t.empty_like(self.X[0]), t.empty_like(self.T[0])
-        self.h2d = self.hX.numel() * 4 + (self.hT.numel() * 4 if self.xent else 0)
-        self.d2h = self.hY.numel() * 4
-
-    def e2e_step(self):
-        self.dX.copy_(self.hX, non_blocking=True)
-        if self.xent:
-            self.dT.copy_(self.hT, non_blocking=True)
-        self._run(self.dX, self.dY, self.dT)
-        self.hY.copy_(self.dY, non_blocking=True)
+    def e2e_spec(self):
+        h_in = [self.X[0].cpu().pin_memory()] + ([self.T[0].cpu().pin_memory()] if self.xent else [])
+        h_out = [self.torch.empty_like(h_in[0]).pin_memory()]
+        return h_in, h_out, lambda d, o: self._run(d[0], o[0], d[1] if self.xent else None)
 
 
 METRIC = "Flash-attn fwd & fused-GEMM TFLOP/s at 1/2/4/8 B200; % of tensor peak"
@@ -979,24 +963,21 @@ def main():
     # ---------------- e2e through the C ABI with host buffers ----------------
     e2e = None
     if not args.no_e2e:
-        wl.e2e_setup()
-        for _ in range(2):
-            wl.e2e_step()
+        pipe = E2EPipeline(torch, wl)
+        for _ in range(3):
+            pipe.step()
         torch.cuda.synchronize()
-        Ke = max(3, min(K, 10))
+        Ke = max(4, min(K, 10))
         barrier()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(Ke):
-            wl.e2e_step()
-        e1.record(stream)
-        torch.cuda.synchronize()
+        ems = max_over_ranks(pipe.time_steps(Ke))
         barrier()
-        ems = max_over_ranks(e0.elapsed_time(e1))
         e2e = {"value": round(wl.flops_per_step * world * Ke / (ems * 1e-3) / wl.unit_scale, 3),
-               "unit": wl.unit, "h2d_bytes_per_step": int(wl.h2d), "d2h_bytes_per_step": int(wl.d2h),
-               "steps": Ke, "path": "pinned host -> cudaMemcpyAsync -> C ABI -> cudaMemcpyAsync -> host"}
+               "unit": wl.unit, "h2d_bytes_per_step": int(pipe.h2d),
+               "d2h_bytes_per_step": int(pipe.d2h), "steps": Ke,
+               "path": "pinned host -> cudaMemcpyAsync (H2D stream) -> public API (compute stream) "
+                       "-> cudaMemcpyAsync (D2H stream) -> host; 2 buffer sets, consecutive steps "
+                       "overlapped"}
+        del pipe
 
     # ---------------- CPU baseline (rank 0, N == 1) ----------------
     cpu = None
