@@ -665,8 +665,8 @@ class RowWise(Workload):
         self.loss = torch.empty((), dtype=torch.float32, device=dev)
         self.flops_per_step = 2.0 * M * N * 4 + (M * 4 if xent else 0)  # bytes
         self.flops_dominant = self.flops_per_step
-        self.dominant = ("softmax_cta_kernel<float,float,true> (cross-entropy)" if xent
-                         else "softmax_cta_kernel<float,float,false>")
+        self.dominant = ("softmax_stage_kernel<1024, 8, float, true> (cross-entropy)" if xent
+                         else "softmax_reg_kernel<256, 4, float, false>")
         self.config = {"l2": f"inputs {per_set / 2**20:.0f} MiB per step (> L2)"
                        if self.nsets == 1 else f"{self.nsets} rotating input sets"}
 

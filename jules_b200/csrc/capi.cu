@@ -615,6 +615,30 @@ void rows_reg_go(const T* x, T* y, const int32_t* targets, float* loss, int64_t 
       <<<(unsigned)blocks, THREADS, 0, st>>>(x, y, targets, loss, M, (int)N, inv_M);
 }
 
+// Rows of 32 KB and more: one persistent 1024-thread CTA per SM with the
+// next row staged in shared memory (softmax_stage_kernel).
+template <int THREADS, int NV, typename T, bool XENT>
+bool rows_stage_go(const T* x, T* y, const int32_t* targets, float* loss, int64_t M, int64_t N,
+                   float inv_M, int sms, cudaStream_t st) {
+  const size_t smem = (size_t)N * sizeof(T);
+  auto kern = jb::rows::softmax_stage_kernel<THREADS, NV, T, XENT>;
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return false;
+  if (!attr_set[dev]) {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    constexpr size_t kMax = (size_t)THREADS * NV * 16;  // the largest row this instance takes
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMax) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return false;
+    }
+    attr_set[dev] = true;
+  }
+  int64_t blocks = M < sms ? M : sms;
+  kern<<<(unsigned)blocks, THREADS, smem, st>>>(x, y, targets, loss, M, (int)N, inv_M);
+  return true;
+}
+
 template <typename TIn, typename TOut, bool XENT>
 bool rows_reg_launch(const TIn* x, TOut* y, const int32_t* targets, float* loss, int64_t M,
                      int64_t N, float inv_M, int sms, cudaStream_t st) {
@@ -625,9 +649,9 @@ bool rows_reg_launch(const TIn* x, TOut* y, const int32_t* targets, float* loss,
     if (N % E || !aligned16(x) || (y && !aligned16(y)) || (N * sizeof(TIn)) % 16) return false;
     if (N <= 256 * 4 * E) rows_reg_go<256, 4, TIn, XENT>(x, y, targets, loss, M, N, inv_M, sms, st);
     else if (N <= 512 * 4 * E) rows_reg_go<512, 4, TIn, XENT>(x, y, targets, loss, M, N, inv_M, sms, st);
-    else if (N <= 1024 * 4 * E) rows_reg_go<1024, 4, TIn, XENT>(x, y, targets, loss, M, N, inv_M, sms, st);
+    else if (N <= 1024 * 4 * E) return rows_stage_go<1024, 4, TIn, XENT>(x, y, targets, loss, M, N, inv_M, sms, st);
     else if (E == 4 && N <= 1024 * 8 * E)  // 8 vectors of bf16 would spill at 1024 threads
-      rows_reg_go<1024, (E == 4 ? 8 : 4), TIn, XENT>(x, y, targets, loss, M, N, inv_M, sms, st);
+      return rows_stage_go<1024, (E == 4 ? 8 : 4), TIn, XENT>(x, y, targets, loss, M, N, inv_M, sms, st);
     else return false;
     return true;
   }

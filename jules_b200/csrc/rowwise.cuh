@@ -183,8 +183,14 @@ struct Vec16;
 template <>
 struct Vec16<float> {
   static constexpr int kN = 4;
+  // load: read-only global memory (ld.global.nc); load_generic: any state
+  // space (the staged rows in shared memory).
   __device__ __forceinline__ static void load(const float* p, float (&f)[4]) {
     const float4 v = __ldg(reinterpret_cast<const float4*>(p));
+    f[0] = v.x; f[1] = v.y; f[2] = v.z; f[3] = v.w;
+  }
+  __device__ __forceinline__ static void load_generic(const float* p, float (&f)[4]) {
+    const float4 v = *reinterpret_cast<const float4*>(p);
     f[0] = v.x; f[1] = v.y; f[2] = v.z; f[3] = v.w;
   }
   __device__ __forceinline__ static void store(float* p, const float (&f)[4]) {
@@ -194,14 +200,19 @@ struct Vec16<float> {
 template <>
 struct Vec16<__nv_bfloat16> {
   static constexpr int kN = 8;
-  __device__ __forceinline__ static void load(const __nv_bfloat16* p, float (&f)[8]) {
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+  __device__ __forceinline__ static void unpack(const uint4 v, float (&f)[8]) {
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       f[2 * i] = __uint_as_float(w[i] << 16);
       f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
     }
+  }
+  __device__ __forceinline__ static void load(const __nv_bfloat16* p, float (&f)[8]) {
+    unpack(__ldg(reinterpret_cast<const uint4*>(p)), f);
+  }
+  __device__ __forceinline__ static void load_generic(const __nv_bfloat16* p, float (&f)[8]) {
+    unpack(*reinterpret_cast<const uint4*>(p), f);
   }
   __device__ __forceinline__ static void store(__nv_bfloat16* p, const float (&f)[8]) {
     uint4 v;
@@ -302,6 +313,104 @@ __global__ void __launch_bounds__(THREADS) softmax_reg_kernel(const T* __restric
     }
     if (XENT && threadIdx.x == 0 && tv) {
       const float p = __expf(to_f32(x[t]) - m) * inv;
+      loss_acc += -logf(p + 1e-10f) * inv_M;
+    }
+  }
+  if (XENT && threadIdx.x == 0 && loss_acc != 0.0f) atomicAdd(loss, loss_acc);
+}
+
+// As softmax_reg_kernel, for rows of 32 KB and more (one 1024-thread CTA per
+// SM): the CTA is persistent over rows and the next row is copied into
+// shared memory by one bulk copy (cp.async.bulk, completing on an mbarrier)
+// as soon as the current row has moved from shared memory into registers,
+// so the read of row r+1 overlaps the reductions and the output writes of
+// row r.  Needs 16-byte aligned rows (N * sizeof(T) a multiple of 16).
+constexpr int kStageChunk = 32768;  // bytes per bulk copy instruction
+
+template <int THREADS, int NV, typename T, bool XENT>
+__global__ void __launch_bounds__(THREADS) softmax_stage_kernel(const T* __restrict__ in,
+                                                                T* __restrict__ out,
+                                                                const int32_t* __restrict__ targets,
+                                                                float* __restrict__ loss,
+                                                                int64_t M, int N, float inv_M) {
+  constexpr int E = Vec16<T>::kN;
+  extern __shared__ __align__(16) uint8_t stage_raw[];
+  T* row_buf = reinterpret_cast<T*>(stage_raw);
+  __shared__ float red[THREADS / 32];
+  __shared__ uint64_t full;
+  __shared__ int abort_flag;
+  const uint32_t row_bytes = (uint32_t)N * sizeof(T);
+  const int nvec = N / E;
+  auto issue = [&](int64_t row) {  // thread 0: bring `row` into row_buf
+    mbar_arrive_expect_tx(&full, row_bytes);
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(in + row * N);
+    for (uint32_t o = 0; o < row_bytes; o += kStageChunk)
+      bulk_load(stage_raw + o, src + o, min((uint32_t)kStageChunk, row_bytes - o), &full);
+  };
+  if (threadIdx.x == 0) {
+    mbar_init(&full, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+    if (blockIdx.x < M) issue(blockIdx.x);
+  }
+  __syncthreads();
+  float loss_acc = 0.0f;
+  uint32_t phase = 0;
+  for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
+    const bool ok = mbar_wait(&full, phase, 91, &abort_flag);
+    if (__syncthreads_or(!ok)) break;  // uniform exit, no thread left at a barrier
+    phase ^= 1u;
+    float f[NV][E];
+    float m = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int vi = threadIdx.x + k * THREADS;
+      if (vi < nvec) {
+        Vec16<T>::load_generic(row_buf + (size_t)vi * E, f[k]);
+#pragma unroll
+        for (int e = 0; e < E; ++e) m = fmaxf(m, f[k][e]);
+      }
+    }
+    __syncthreads();  // row_buf fully read: the next row may land in it
+    if (threadIdx.x == 0 && row + gridDim.x < M) issue(row + gridDim.x);
+    m = block_max<THREADS>(m, red);
+    float sum = 0.0f;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int vi = threadIdx.x + k * THREADS;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        f[k][e] = (vi < nvec) ? __expf(f[k][e] - m) : 0.0f;
+        sum += f[k][e];
+      }
+    }
+    sum = block_sum<THREADS>(sum, red);
+    const float inv = 1.0f / sum;
+    int t = -1;
+    bool tv = false;
+    if (XENT) {
+      t = targets[row];
+      tv = t >= 0 && t < N;
+      if (threadIdx.x == 0 && !target_ok(t, N)) tv = false;
+    }
+    if (!XENT || out) {
+      T* y = out + row * N;
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        const int vi = threadIdx.x + k * THREADS;
+        if (vi < nvec) {
+          float o[E];
+#pragma unroll
+          for (int e = 0; e < E; ++e) {
+            const float p = f[k][e] * inv;
+            o[e] = XENT ? (p - (vi * E + e == t ? 1.0f : 0.0f)) * inv_M : p;
+          }
+          Vec16<T>::store(y + (size_t)vi * E, o);
+        }
+      }
+    }
+    if (XENT && threadIdx.x == 0 && tv) {
+      const float p = __expf(to_f32(in[row * N + t]) - m) * inv;
       loss_acc += -logf(p + 1e-10f) * inv_M;
     }
   }

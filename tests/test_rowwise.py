@@ -10,10 +10,11 @@ from helpers import to_dev, to_np
 pytestmark = pytest.mark.gpu
 
 # warp-per-row path (N <= 1024), the register-resident CTA path at each of its
-# sizes (N a multiple of the vector width), and the two-pass CTA path
-# (ragged N, or N beyond 32K fp32)
+# sizes (N a multiple of the vector width), the shared-memory-staged path
+# (rows of 32 KB and more; M > SM count so CTAs stage several rows), and the
+# two-pass CTA path (ragged N, or N beyond 32K fp32)
 SHAPES = [(64, 256), (64, 10), (2048, 2048), (7, 1000), (5, 1024), (5, 1025), (3, 5000),
-          (4, 8192), (4, 16384), (4, 32768), (2, 70000), (1, 1), (300, 1)]
+          (4, 8192), (4, 16384), (4, 32768), (300, 16384), (2, 70000), (1, 1), (300, 1)]
 
 
 def _logits(M, N, seed, scale=3.0):
@@ -52,7 +53,7 @@ def test_softmax_bf16(jb, orc, M, N):
 
 
 @pytest.mark.parametrize("M,N", [(64, 10), (64, 1000), (13, 37), (5, 3000), (2, 50257),
-                                 (300, 1024), (8, 32768), (3, 40000)])
+                                 (300, 1024), (8, 32768), (300, 32768), (3, 40000)])
 def test_cross_entropy_fp32_vs_reference(jb, ref, M, N):
     import torch
     x = _logits(M, N, seed=M + 7 * N)
