@@ -266,8 +266,10 @@ int gemm_tc2(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
   const int64_t tail = tiles % max_pairs;
   // Split the tail tiles along K (see gemm_bf16_tc2_kernel) only when the
   // last round would be nearly empty.  For larger tails the split measured
-  // slower (4096^3: 34 tail tiles on 74 pairs, 1118 vs 1190 TFLOP/s): the
-  // half-empty last round runs at higher clocks under the power cap.
+  // slower (4096^3: 34 tail tiles on 74 pairs, 1086 vs 1147 TFLOP/s at an
+  // unthrottled 1965 MHz): the fp32 partial write, the partner's partial
+  // read and the second TMEM readout of every split tile cost more than the
+  // half round they save.
   if (allow_split && tiles > max_pairs && tail > 0 && 4 * tail <= max_pairs && num_k >= 2) {
     whole = (int)(tiles - tail);
     units = whole + 2 * (int)tail;
