@@ -186,3 +186,28 @@ def test_gemm_bias_act_routes_fp8(jb):
     C1 = jb.gemm_bias_act(a, w, b, act="gelu")
     C2 = jb.gemm_fp8(a, w, b, act="gelu")
     assert C1.dtype == torch.bfloat16 and torch.equal(C1, C2)
+
+
+@pytest.mark.gpu
+def test_cast_other_pairs_bit_exact(jb):
+    """fp32 <-> bf16 (round to nearest even, as torch) and fp8 -> other fp8
+    (decode, then the saturating encode) through the scalar cast kernel."""
+    import torch
+    R = _oracle()
+    g = np.random.default_rng(3)
+    x = np.concatenate([g.standard_normal(100001).astype(np.float32) * 100,
+                        np.array([0.0, -0.0, np.inf, -np.inf, 1e38, -1e-40], np.float32)])
+    xt = torch.from_numpy(x).cuda()
+    b = jb.cast(xt, torch.bfloat16)
+    assert torch.equal(b.view(torch.int16).cpu(), xt.cpu().to(torch.bfloat16).view(torch.int16))
+    f = jb.cast(b, torch.float32)
+    assert torch.equal(f.cpu(), b.cpu().float())
+    codes = np.arange(256, dtype=np.uint8)
+    for src, dst in (("e4m3", "e5m2"), ("e5m2", "e4m3")):
+        d = torch.from_numpy(codes).cuda().view(_torch_f8(src))
+        got = jb.cast(d, _torch_f8(dst)).view(torch.uint8).cpu().numpy()
+        dec = R.fp8_decode(codes, src)
+        want = R.fp8_encode(dec, dst)
+        nan = np.isnan(dec)
+        assert np.array_equal(got[~nan], want[~nan])
+        assert np.isnan(R.fp8_decode(got[nan], dst)).all()
