@@ -125,7 +125,7 @@ int jules_flash_attention_fwd(const void* Q, const void* K, const void* V, void*
  * F32).  Grouped-query heads: dK / dV of a kv head sum over its Hq/Hkv
  * query heads.  scale <= 0 means 1/sqrt(D).  bf16 with D == 128 (16-byte
  * aligned buffers) runs on tcgen05 (bf16 P and dS, fp32 accumulation);
- * fp32 and other head dims (<= 256) on CUDA cores in fp32.  No atomics: the
+ * fp32, other head dims (<= 256) and unaligned buffers on CUDA cores in fp32.  No atomics: the
  * result is deterministic.  workspace: caller-provided device memory of
  * jules_flash_attention_bwd_workspace_bytes() bytes (16-byte aligned).
  * The reference has no attention backward; this is the gradient of the

@@ -11,7 +11,9 @@
 // uses the same stale max for O and the sum, so the result is unchanged).
 //
 // Work item = two 128-row query tiles (256 rows) of one (b, h); persistent
-// CTAs take items longest-causal-first.  12 warps (3 warpgroups):
+// CTAs take items longest-causal-first.  Under the causal mask tile 0 runs
+// one key step fewer than tile 1 (the last key tile is past all its rows).
+// 12 warps (3 warpgroups):
 //   warp 8     TMA producer: both Q tiles once per item; K and V tiles
 //              (128 keys x 128 dims as two 64-dim 128B-swizzled boxes) in
 //              2-deep rings shared by the two query tiles.
@@ -91,6 +93,14 @@ __device__ __forceinline__ void decode_item(int w, int n_pairs, int BH, int G, i
   pair = causal ? (n_pairs - 1 - r) : r;
 }
 
+// Key tiles query tile t of a pair needs (causal: up to its last row); the
+// item's count is tile 1's.  Under the causal mask tile 0 needs one fewer:
+// the pair's last key tile lies entirely after tile 0's rows.
+__device__ __forceinline__ int kv_tiles_t(int pair, int t, int n_kv_full, int causal) {
+  if (!causal) return n_kv_full;
+  const int n = 2 * pair + t + 1;
+  return n < n_kv_full ? n : n_kv_full;
+}
 __device__ __forceinline__ int kv_tiles(int pair, int n_kv_full, int causal) {
   if (!causal) return n_kv_full;
   const int n = 2 * pair + 2;
@@ -251,7 +261,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idS = idesc_bf16_f32(BQ, BKV, false, false);
       constexpr uint32_t idPV = idesc_bf16_f32(BQ, HD, false, true);
-      uint32_t kvi = 0, pvc = 0, wi = 0;
+      uint32_t kvi = 0, wi = 0;
+      uint32_t pvc_t[NQT] = {0, 0};  // completed key steps per tile (barrier phases)
       bool ok = true;
       // Descriptors for every operand slot, built once.  A K step moves the
       // start-address field (bytes >> 4): +2 per 32 bytes inside a 128-byte
@@ -289,6 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int pair, bh;
         decode_item(w, n_pairs, BH, hgroup, causal, pair, bh);
         const int n_kv = kv_tiles(pair, n_kv_full, causal);
+        const int nk[NQT] = {kv_tiles_t(pair, 0, n_kv_full, causal), n_kv};
         if (!mbar_wait(&s.q_full, wi & 1u, 20, abort_flag)) break;
         const uint32_t kv0 = kvi;
         {
@@ -302,24 +314,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int j = 0; j < n_kv && ok; ++j) {
           const uint32_t st = (kv0 + j) % KVS, ph = ((kv0 + j) / KVS) & 1u;
-          const uint32_t g = pvc + j;
-          const bool more = j + 1 < n_kv;
           const uint32_t st1 = (kv0 + j + 1) % KVS, ph1 = ((kv0 + j + 1) / KVS) & 1u;
 #pragma unroll
           for (int t = 0; t < NQT; ++t) {
+            if (j >= nk[t]) continue;  // tile 0's steps end one early under the causal mask
+            const uint32_t g = pvc_t[t] + j;
+            const bool more = j + 1 < nk[t];
+            // the first tile of this step waits for V; the first to issue the
+            // next step's S waits for K
+            const bool first = t == 0 || j >= nk[0];
+            const bool kfirst = t == 0 || j + 1 >= nk[0];
             bool kready = false;
             {
               // Poll every barrier this group needs at once; the slow path
               // (rare) waits on them one by one.
               const uint32_t r0 = mbar_try_wait(&s.p_full[t], g & 1u) ? 1u : 0u;
               const uint32_t r1 = (j != 0) ? 1u : (mbar_try_wait(&s.o_empty[t], (wi & 1u) ^ 1u) ? 1u : 0u);
-              const uint32_t r2 = (t != 0) ? 1u : (mbar_try_wait(&s.v_full[st], ph) ? 1u : 0u);
-              const uint32_t r3 = (t == 0 && more) ? (mbar_try_wait(&s.k_full[st1], ph1) ? 1u : 0u) : 0u;
+              const uint32_t r2 = !first ? 1u : (mbar_try_wait(&s.v_full[st], ph) ? 1u : 0u);
+              const uint32_t r3 = (kfirst && more) ? (mbar_try_wait(&s.k_full[st1], ph1) ? 1u : 0u) : 0u;
               kready = r3 != 0u;
               if ((r0 & r1 & r2) == 0u) {
                 if (!mbar_wait(&s.p_full[t], g & 1u, 22, abort_flag)) { ok = false; break; }
                 if (j == 0 && !mbar_wait(&s.o_empty[t], (wi & 1u) ^ 1u, 23, abort_flag)) { ok = false; break; }
-                if (t == 0 && !mbar_wait(&s.v_full[st], ph, 24, abort_flag)) { ok = false; break; }
+                if (first && !mbar_wait(&s.v_full[st], ph, 24, abort_flag)) { ok = false; break; }
               }
             }
             tc_fence_after();
@@ -327,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (t == NQT - 1) umma_commit(&s.v_empty[st]);
             if (!more) umma_commit(&s.o_full[t]);
             if (more) {
-              if (t == 0 && !kready) {
+              if (kfirst && !kready) {
                 if (!mbar_wait(&s.k_full[st1], ph1, 25, abort_flag)) { ok = false; break; }
                 tc_fence_after();
               }
@@ -340,7 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (!ok) break;
-        pvc += n_kv;
+        pvc_t[0] += nk[0];
+        pvc_t[1] += nk[1];
         kvi = kv0 + n_kv;
       }
     }
@@ -358,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int w = blockIdx.x; w < total; w += gridDim.x, ++wi) {
       int pair, bh;
       decode_item(w, n_pairs, BH, hgroup, causal, pair, bh);
-      const int n_kv = kv_tiles(pair, n_kv_full, causal);
+      const int n_kv = kv_tiles_t(pair, t, n_kv_full, causal);  // this tile's key steps
       const int qt0 = pair * NQT * BQ + t * BQ;  // first row of this tile
       const int q = qt0 + r;
       float m_run = -INFINITY, l_run = 0.0f;

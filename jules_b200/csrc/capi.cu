@@ -823,8 +823,7 @@ int jules_flash_attention_bwd(const void* Q, const void* K, const void* V, const
   if (D == jb::attn_bwd::HD && aligned16(Q) && aligned16(K) && aligned16(V) && aligned16(O) &&
       aligned16(dO) && aligned16(dQ) && aligned16(dK) && aligned16(dV) && aligned16(lse))
     return attn_bwd_tc(Q, K, V, O, dO, lse, dQ, dK, dV, B, Hq, Hkv, S, scale, c, workspace, st);
-  if (D == jb::attn_bwd::HD)
-    return fail(JULES_ERR_ALIGN, "attention bwd: bf16 head_dim 128 needs 16-byte aligned buffers");
+  // other head dims and unaligned buffers: CUDA cores (as the forward)
   return attn_bwd_simt<__nv_bfloat16>(Q, K, V, O, dO, lse, dQ, dK, dV, B, Hq, Hkv, S, D, scale, c, workspace, st);
 }
 

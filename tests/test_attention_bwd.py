@@ -146,3 +146,26 @@ def test_attention_bwd_long_sequence_sampled(jb):
     Q, K, V, dO = _inputs(1, 2, 1, 4096, 128, 41)
     got, (q, k, v, do) = _run_gpu(jb, Q, K, V, dO, True, torch.bfloat16)
     _check_bf16(got, _oracle().attention_bwd(q, k, v, do, True))
+
+
+@pytest.mark.gpu
+def test_attention_bwd_unaligned_bf16_falls_back(jb):
+    """bf16 head_dim 128 with buffers off 16-byte alignment: the CUDA-core
+    path (as the forward), same results bar."""
+    import torch
+    B, Hq, Hkv, S, D = 1, 2, 1, 96, 128
+
+    def off(a):  # a copy of `a` whose storage starts 2 bytes past an aligned address
+        buf = torch.empty(a.size + 8, dtype=torch.bfloat16, device="cuda")
+        t = buf[1:1 + a.size].view(a.shape)
+        t.copy_(torch.from_numpy(a).to(torch.bfloat16))
+        assert t.data_ptr() % 16 != 0
+        return t
+    Q, K, V, dO = _inputs(B, Hq, Hkv, S, D, 17)
+    q, k, v, do = off(Q), off(K), off(V), off(dO)
+    O, lse = jb.flash_attention_fwd(q, k, v, causal=True)
+    dq, dk, dv = jb.flash_attention_bwd(q, k, v, O, do, lse, causal=True)
+    torch.cuda.synchronize()
+    assert jb.device_error() == 0
+    want = _oracle().attention_bwd(*(x.float().cpu().numpy() for x in (q, k, v, do)), causal=True)
+    _check_bf16([x.float().cpu().numpy() for x in (dq, dk, dv)], want)
