@@ -281,18 +281,18 @@ __global__ void __launch_bounds__(128)
 
 // ---------------------------------------------------------------------------
 // Register-tiled attention forward for head dims 32, 64 and 128 (the fp32
-// path, C1's [1,8,512,64]): 16 query rows of one (b, h) per CTA, key tiles
+// path, C1's [1,8,512,64]): 32 query rows of one (b, h) per CTA, key tiles
 // of 64, two groups of 128 threads taking alternate key tiles (each with its
 // own shared-memory tiles and named barrier), merged at the end.  Within a
-// group, 8 x 16 threads: thread (ty, tx) computes the scores of
-// query rows 2ty, 2ty+1 against keys 4tx..4tx+3 of the tile (Q and K
-// staged transposed in shared memory, 8 FMAs per float2 + float4 load) and
-// accumulates output dims tx*DPT.. of its two rows from P (staged
-// key-major) and V.  Online softmax per row as attn_kernel (expf, running
+// group, 8 x 16 threads: thread (ty, tx) computes the scores of query rows
+// 4ty..4ty+3 against keys 4tx..4tx+3 of the tile (Q and K staged transposed
+// in shared memory, 16 FMAs per two float4 loads) and accumulates output
+// dims tx*DPT.. of its four rows from P (staged key-major) and V.  Online softmax per row as attn_kernel (expf, running
 // max and sum reduced over the 16 threads of a half warp); causal and
 // padding masks; grouped-query heads.
 // ---------------------------------------------------------------------------
-constexpr int TBQ = 16, TBK = 64;
+constexpr int TRT = 4;               // query rows per thread
+constexpr int TBQ = 8 * TRT, TBK = 64;  // query rows per CTA, keys per tile
 
 // Four consecutive elements as fp32 (16-byte fp32 / 8-byte bf16 load).
 __device__ __forceinline__ float4 load4_f32(const float* p) {
@@ -313,11 +313,12 @@ constexpr size_t attn_tile_smem_floats() {
 }
 
 template <typename TIn, typename TOut, int D>
-__global__ void __launch_bounds__(kTileThreads, 2)
+__global__ void __launch_bounds__(kTileThreads, 1)
     attn_tile_kernel(const TIn* __restrict__ Q, const TIn* __restrict__ Kp,
                      const TIn* __restrict__ Vp, TOut* __restrict__ O, float* __restrict__ lse,
                      int Hq, int Hkv, int S, float scale, int causal) {
   static_assert(D == 32 || D == 64 || D == 128, "head dim");
+  constexpr int RT = TRT;
   constexpr int DPT = D / 16;     // output dims per thread
   constexpr int KT = TBK + 4;     // Kt row stride (16-byte multiple, fewer bank conflicts)
   extern __shared__ float sm[];
@@ -344,13 +345,16 @@ __global__ void __launch_bounds__(kTileThreads, 2)
     Qt[d * TBQ + r] = (q0 + r < S) ? to_f32(qb[(size_t)(q0 + r) * D + d]) : 0.0f;
   }
   __syncthreads();
-  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f}, acc[2][DPT];
+  float m[RT], l[RT], acc[RT][DPT];
 #pragma unroll
-  for (int r = 0; r < 2; ++r)
+  for (int r = 0; r < RT; ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.0f;
 #pragma unroll
     for (int i = 0; i < DPT; ++i) acc[r][i] = 0.0f;
+  }
 
-  const int qi0 = q0 + 2 * ty;  // this thread's first query row
+  const int qi0 = q0 + RT * ty;  // this thread's first query row
   const int kv_end = causal ? min(S, q0 + TBQ) : S;
   // K / V tiles move through registers, 4 elements per load: the next
   // tile's loads are issued before the current tile's arithmetic (head dims
@@ -388,19 +392,23 @@ __global__ void __launch_bounds__(kTileThreads, 2)
     stash();
     group_sync();
     if (kPrefetch && k0 + 2 * TBK < kv_end) fetch(k0 + 2 * TBK);  // in flight during this tile
-    float sc[2][4] = {};
+    float sc[RT][4] = {};
 #pragma unroll 8
     for (int d = 0; d < D; ++d) {
-      const float2 q = *reinterpret_cast<const float2*>(Qt + d * TBQ + 2 * ty);
+      const float4 q = *reinterpret_cast<const float4*>(Qt + d * TBQ + RT * ty);
       const float4 k = *reinterpret_cast<const float4*>(Kt + d * KT + 4 * tx);
-      sc[0][0] = fmaf(q.x, k.x, sc[0][0]); sc[0][1] = fmaf(q.x, k.y, sc[0][1]);
-      sc[0][2] = fmaf(q.x, k.z, sc[0][2]); sc[0][3] = fmaf(q.x, k.w, sc[0][3]);
-      sc[1][0] = fmaf(q.y, k.x, sc[1][0]); sc[1][1] = fmaf(q.y, k.y, sc[1][1]);
-      sc[1][2] = fmaf(q.y, k.z, sc[1][2]); sc[1][3] = fmaf(q.y, k.w, sc[1][3]);
-    }
-    float p[2][4];
+      const float qv[RT] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
+      for (int r = 0; r < RT; ++r) {
+        sc[r][0] = fmaf(qv[r], k.x, sc[r][0]);
+        sc[r][1] = fmaf(qv[r], k.y, sc[r][1]);
+        sc[r][2] = fmaf(qv[r], k.z, sc[r][2]);
+        sc[r][3] = fmaf(qv[r], k.w, sc[r][3]);
+      }
+    }
+    float p[RT][4];
+#pragma unroll
+    for (int r = 0; r < RT; ++r) {
       const int qi = qi0 + r;
       float tmax = -INFINITY;
 #pragma unroll
@@ -429,19 +437,22 @@ __global__ void __launch_bounds__(kTileThreads, 2)
     }
 #pragma unroll
     for (int c = 0; c < 4; ++c)
-      *reinterpret_cast<float2*>(Pt + (4 * tx + c) * TBQ + 2 * ty) = make_float2(p[0][c], p[1][c]);
+      *reinterpret_cast<float4*>(Pt + (4 * tx + c) * TBQ + RT * ty) =
+          make_float4(p[0][c], p[1][c], p[2][c], p[3][c]);
     group_sync();
-#pragma unroll 8
+#pragma unroll 4
     for (int j = 0; j < TBK; ++j) {
-      const float2 pj = *reinterpret_cast<const float2*>(Pt + j * TBQ + 2 * ty);
+      const float4 pq = *reinterpret_cast<const float4*>(Pt + j * TBQ + RT * ty);
+      const float pv[RT] = {pq.x, pq.y, pq.z, pq.w};
       const float* vrow = Vs + j * D + tx * DPT;
 #pragma unroll
       for (int i = 0; i < DPT; i += 2) {
         const float2 v = *reinterpret_cast<const float2*>(vrow + i);
-        acc[0][i] = fmaf(pj.x, v.x, acc[0][i]);
-        acc[0][i + 1] = fmaf(pj.x, v.y, acc[0][i + 1]);
-        acc[1][i] = fmaf(pj.y, v.x, acc[1][i]);
-        acc[1][i + 1] = fmaf(pj.y, v.y, acc[1][i + 1]);
+#pragma unroll
+        for (int r = 0; r < RT; ++r) {
+          acc[r][i] = fmaf(pv[r], v.x, acc[r][i]);
+          acc[r][i + 1] = fmaf(pv[r], v.y, acc[r][i + 1]);
+        }
       }
     }
   }
@@ -449,26 +460,24 @@ __global__ void __launch_bounds__(kTileThreads, 2)
   // thread with the same (ty, tx) through its own (now free) tile memory.
   __syncthreads();
   float* xch = sm + D * TBQ + (D * KT + TBK * D + TBK * TBQ);  // group 1's tiles
-  constexpr int XS = 2 * DPT + 8;  // floats per thread: m, l at 4r, 4r+1; acc from 8
+  constexpr int XS = 2 * RT + RT * DPT;  // floats per thread: m, l at 2r, 2r+1; acc after
   if (grp == 1) {
     float* x = xch + gt * XS;
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      x[4 * r] = m[r];
-      x[4 * r + 1] = l[r];
+    for (int r = 0; r < RT; ++r) {
+      x[2 * r] = m[r];
+      x[2 * r + 1] = l[r];
+#pragma unroll
+      for (int i = 0; i < DPT; ++i) x[2 * RT + r * DPT + i] = acc[r][i];
     }
-#pragma unroll
-    for (int r = 0; r < 2; ++r)
-#pragma unroll
-      for (int i = 0; i < DPT; ++i) x[8 + r * DPT + i] = acc[r][i];
   }
   __syncthreads();
   if (grp == 1) return;
   {
     const float* x = xch + gt * XS;
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const float m1 = x[4 * r], l1 = x[4 * r + 1];
+    for (int r = 0; r < RT; ++r) {
+      const float m1 = x[2 * r], l1 = x[2 * r + 1];
       const float mn = fmaxf(m[r], m1);
       if (mn == -INFINITY) continue;  // row with no visible key (padding)
       const float a0 = (m[r] == -INFINITY) ? 0.0f : expf(m[r] - mn);
@@ -476,11 +485,11 @@ __global__ void __launch_bounds__(kTileThreads, 2)
       l[r] = l[r] * a0 + l1 * a1;
       m[r] = mn;
 #pragma unroll
-      for (int i = 0; i < DPT; ++i) acc[r][i] = acc[r][i] * a0 + x[8 + r * DPT + i] * a1;
+      for (int i = 0; i < DPT; ++i) acc[r][i] = acc[r][i] * a0 + x[2 * RT + r * DPT + i] * a1;
     }
   }
 #pragma unroll
-  for (int r = 0; r < 2; ++r) {
+  for (int r = 0; r < RT; ++r) {
     const int qi = qi0 + r;
     if (qi >= S) continue;
     const float inv = 1.0f / l[r];
