@@ -24,8 +24,7 @@
 //              warpgroup's registers low.
 //   warps 0-3  softmax group 0 (query tile 0), one row per thread (TMEM lane
 //   warps 4-7  = row); group 1 (query tile 1).  Each reads S from TMEM, masks,
-//              takes the row max and the exponentials (3/4 on the MUFU ex2
-//              unit, 1/4 as a polynomial on the FMA pipe), writes P as bf16
+//              takes the row max and the exponentials (MUFU ex2), writes P as bf16
 //              back over S in TMEM, rescales O when needed, and at the end
 //              normalises O and writes O and lse.
 // PV runs with P as the TMEM A operand (no shared-memory round trip).
@@ -130,29 +129,6 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
-}
-
-// 2^x for a pair, on the FMA pipe.  Inputs are clamped to >= -125, so keys
-// that the mask removed get 2^-125 (~2e-38) instead of 0 on this path.
-// Cody-Waite split x = n + f, n = rint(x) via the 1.5*2^23 shifter, 2^f from a
-// degree-3 polynomial fitted on [-0.5, 0.5] (max relative error 7.5e-5; see
-// fit_exp2.py), 2^n added into the exponent field.
-__device__ __forceinline__ void exp2_fma_pair(uint64_t x2, float& e0, float& e1) {
-  float x0, x1;
-  upk2(x2, x0, x1);
-  x2 = pk2(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
-  const uint64_t t2 = add2(x2, pk2(12582912.0f, 12582912.0f));
-  const uint64_t n2 = add2(t2, pk2(-12582912.0f, -12582912.0f));
-  const uint64_t f2 = fma2(n2, pk2(-1.0f, -1.0f), x2);
-  uint64_t p2 = fma2(pk2(0.05517137795686722f, 0.05517137795686722f), f2,
-                     pk2(0.24261121451854706f, 0.24261121451854706f));
-  p2 = fma2(p2, f2, pk2(0.6932610273361206f, 0.6932610273361206f));
-  p2 = fma2(p2, f2, pk2(0.9999280571937561f, 0.9999280571937561f));
-  float p0, p1, t0, t1;
-  upk2(p2, p0, p1);
-  upk2(t2, t0, t1);
-  e0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
-  e1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
 #define JB_W128(r)                                                                     \
@@ -432,15 +408,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             // x = s * scale*log2(e) - m, two lanes per instruction
             const uint64_t x2 =
                 fma2(pk2(__uint_as_float(sr[e]), __uint_as_float(sr[e + 1])), scale2, negm2);
-            float e0, e1;
-            if ((c & 3) == 3) {
-              exp2_fma_pair(x2, e0, e1);
-            } else {
-              float x0, x1;
-              upk2(x2, x0, x1);
-              e0 = ex2_approx(x0);
-              e1 = ex2_approx(x1);
-            }
+            float x0, x1;
+            upk2(x2, x0, x1);
+            const float e0 = ex2_approx(x0), e1 = ex2_approx(x1);
             sum2[c & 1] = add2(sum2[c & 1], pk2(e0, e1));
             pk[c] = pack_bf16x2(e0, e1);
           }
