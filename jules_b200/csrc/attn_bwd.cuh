@@ -21,8 +21,10 @@
 //      softmax warps: P^T, dS^T as bf16 back into TMEM over S^T / dP^T,
 //      dV += P^T dO_i and dK += dS^T Q_i with the A operand in TMEM.
 //  * bwd_dq_kernel: one CTA per (query head, 128-query tile i), Q_i and dO_i
-//    resident; for each key tile j: S = Q_i K_j^T, dP = dO_i V_j^T, dS into
-//    TMEM, dQ += dS K_j.
+//    resident in TMEM; for each key tile j: S = Q_i K_j^T, dP = dO_i V_j^T,
+//    dS into TMEM, dQ += dS K_j.
+// (dQ kernel: Q_i and dO_i are copied into TMEM [384, 512) by the softmax
+// warps, so S and dP read only K and V from shared memory.)
 // Warp roles (10 warps): 0-7 softmax/epilogue (thread = TMEM lane = tile row;
 // warps w and w+4 share a lane quarter and split its 128 columns), 8 TMA
 // producer, 9 MMA issuer and TMEM owner.
@@ -448,12 +450,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 // dQ
 // ---------------------------------------------------------------------------
+// Q_i and dO_i live in TMEM (columns [384, 448) and [448, 512), packed
+// bf16 in the A-operand layout), written once per CTA by the softmax warps,
+// so S and dP are TS MMAs that read only K and V from shared memory.
 struct SmemQ {
-  alignas(1024) uint8_t q[2][kChunk];
-  alignas(1024) uint8_t dO[2][kChunk];
   alignas(1024) uint8_t k[KS][2][kChunk];
   alignas(1024) uint8_t v[KS][2][kChunk];
-  uint64_t q_full;
+  uint64_t q_full;  // Q and dO in TMEM
   uint64_t kv_full[KS], kv_empty[KS];
   uint64_t s_full[2], p_full[2], acc_full;
   uint32_t tmem_base;
@@ -464,6 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                   const float* __restrict__ lse2, const float* __restrict__ delta,
+                  const __nv_bfloat16* __restrict__ Qg, const __nv_bfloat16* __restrict__ dOg,
                   __nv_bfloat16* __restrict__ dQ, int B, int Hq, int Hkv, int S, float scale,
                   int causal) {
   extern __shared__ uint8_t smem_raw[];
@@ -484,7 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const float scale_log2 = scale * kLog2e;
 
   if (threadIdx.x == 0) {
-    mbar_init(&s.q_full, 1);
+    mbar_init(&s.q_full, kSoftmaxThreads);
     for (int k = 0; k < KS; ++k) {
       mbar_init(&s.kv_full[k], 1);
       mbar_init(&s.kv_empty[k], 1);
@@ -496,10 +500,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&s.acc_full, 1);
     s.abort_flag = 0;
     fence_mbar_init();
-    prefetch_tmap(&tmQ);
     prefetch_tmap(&tmK);
     prefetch_tmap(&tmV);
-    prefetch_tmap(&tmdO);
   }
   if (warp == kWarpMma) {
     tmem_alloc(&s.tmem_base, 512);
@@ -513,11 +515,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kWarpProducer) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(&s.q_full, 4 * kChunk);
-      tma_load_3d(s.q[0], &tmQ, &s.q_full, 0, i * BT, bhq);
-      tma_load_3d(s.q[1], &tmQ, &s.q_full, 64, i * BT, bhq);
-      tma_load_3d(s.dO[0], &tmdO, &s.q_full, 0, i * BT, bhq);
-      tma_load_3d(s.dO[1], &tmdO, &s.q_full, 64, i * BT, bhq);
       for (int jj = 0; jj < n_kv; ++jj) {
         const int st = jj % KS;
         const uint32_t ph = (uint32_t)(jj / KS) & 1u;
@@ -536,28 +533,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint64_t kChunkStep = kChunk >> 4;
       constexpr uint64_t kStageStep = (2 * kChunk) >> 4;
       constexpr uint64_t kHalfRows = (BH2 * 128) >> 4;  // 64 rows of 128 bytes
-      const uint64_t dq = sdesc_sw128(smem_u32(s.q[0]), 16, 1024);
-      const uint64_t ddo = sdesc_sw128(smem_u32(s.dO[0]), 16, 1024);
       const uint64_t dk_k = sdesc_sw128(smem_u32(s.k[0][0]), 16, 1024);
       const uint64_t dv_k = sdesc_sw128(smem_u32(s.v[0][0]), 16, 1024);
       const uint64_t dk_mn = sdesc_sw128(smem_u32(s.k[0][0]), kChunk, 1024);
-      // S_x = Q K_x^T and dP_x = dO V_x^T for key half x of stage st.
+      // S_x = Q K_x^T and dP_x = dO V_x^T for key half x of stage st; Q and
+      // dO (A) from TMEM, 8 columns per K-step of 16 dims.
       auto issue_s = [&](int x, int st) {
-        uint64_t a[8], b[8];
+        uint32_t a[8];
+        uint64_t b[8];
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t o = (kk >> 2) * kChunkStep + (kk & 3) * 2;
-          a[kk] = dq + o;
+          a[kk] = tbase + 384 + kk * 8;
           b[kk] = dk_k + st * kStageStep + x * kHalfRows + o;
         }
-        umma8_ss(tbase + 128 * x, a, b, 0u, idS);
+        umma8_ts(tbase + 128 * x, a, b, 0u, idS);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t o = (kk >> 2) * kChunkStep + (kk & 3) * 2;
-          a[kk] = ddo + o;
+          a[kk] = tbase + 448 + kk * 8;
           b[kk] = dv_k + st * kStageStep + x * kHalfRows + o;
         }
-        umma8_ss(tbase + 128 * x + 64, a, b, 0u, idS);
+        umma8_ts(tbase + 128 * x + 64, a, b, 0u, idS);
         umma_commit(&s.s_full[x]);
       };
       // dQ += dS_x K_x (A in TMEM, K = the half's 64 keys).
@@ -608,6 +605,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t tS = tbase + 128 * half + lane_off, tP = tS + 64;
+    {
+      // this thread's row of Q_i and dO_i, dims [64 half, +64), into TMEM
+      const int q = i * BT + r;
+      const bool row_ok = q < S;
+      const size_t off = ((size_t)bhq * S + (row_ok ? q : 0)) * HD + half * 64;
+      const uint4* qs = reinterpret_cast<const uint4*>(Qg + off);
+      const uint4* ds = reinterpret_cast<const uint4*>(dOg + off);
+      uint32_t qa[32], da[32];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const uint4 a = row_ok ? qs[u] : make_uint4(0u, 0u, 0u, 0u);
+        const uint4 d = row_ok ? ds[u] : make_uint4(0u, 0u, 0u, 0u);
+        qa[4 * u] = a.x; qa[4 * u + 1] = a.y; qa[4 * u + 2] = a.z; qa[4 * u + 3] = a.w;
+        da[4 * u] = d.x; da[4 * u + 1] = d.y; da[4 * u + 2] = d.z; da[4 * u + 3] = d.w;
+      }
+      tmem_st32(tbase + 384 + 32 * half + lane_off, qa);
+      tmem_st32(tbase + 448 + 32 * half + lane_off, da);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&s.q_full);
+    }
     const size_t srow = (size_t)bhq * Sp + (size_t)i * BT + r;
     const float nl = lse2[srow], nd = delta[srow];
     const uint64_t nl2 = attn::pk2(nl, nl), nd2 = attn::pk2(nd, nd);

@@ -454,7 +454,9 @@ int attn_bwd_tc(const void* Q, const void* K, const void* V, const void* O, cons
       static_cast<__nv_bfloat16*>(dV), B, Hq, Hkv, S, scale, causal);
   if (int rc = check_launch("bwd_dkdv_kernel launch")) return rc;
   ab::bwd_dq_kernel<<<(unsigned)(BHq * n_t), ab::kThreads, smem_q, st>>>(
-      tq, tk, tv, tdo, lse2, delta, static_cast<__nv_bfloat16*>(dQ), B, Hq, Hkv, S, scale, causal);
+      tq, tk, tv, tdo, lse2, delta, static_cast<const __nv_bfloat16*>(Q),
+      static_cast<const __nv_bfloat16*>(dO), static_cast<__nv_bfloat16*>(dQ), B, Hq, Hkv, S, scale,
+      causal);
   return check_launch("bwd_dq_kernel launch");
 }
 
