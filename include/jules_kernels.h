@@ -74,6 +74,17 @@ const char* jules_status_string(int status);
 int jules_device_error(uint32_t* word, int clear);
 
 /*
+ * Failure-detection self-test: launches one thread that waits, with a limit
+ * of limit_ns (0 < limit_ns <= 2 s), on a pipeline barrier that nothing
+ * completes.  The wait gives up the way every pipeline wait of the library
+ * does (the device error word gets JULES_ERR_TIMEOUT's kind with site 250)
+ * and the kernel returns, so jules_device_error() then reports
+ * JULES_ERR_TIMEOUT and the context stays usable.  No counterpart in the
+ * reference, whose kernels have no bounded waits.
+ */
+int jules_selftest_bounded_wait(uint64_t limit_ns, void* stream);
+
+/*
  * C = act(A . W + bias) (+ residual)
  *   A [M,K], W [K,N], C and residual [M,N], bias [N] (fp32, nullable),
  *   residual nullable (same dtype as A and W).

@@ -36,6 +36,7 @@ _SIGNATURES = {
     "jules_last_error_string": ([], ctypes.c_char_p),
     "jules_status_string": ([_c_int], ctypes.c_char_p),
     "jules_device_error": ([ctypes.POINTER(ctypes.c_uint32), _c_int], _c_int),
+    "jules_selftest_bounded_wait": ([ctypes.c_uint64, _c_vp], _c_int),
     "jules_gemm_bias_act": ([_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_int,
                              _c_int, _c_int, _c_vp], _c_int),
     "jules_sgemm": ([_c_int, _c_int, _c_i64, _c_i64, _c_i64, _c_f, _c_vp, _c_i64, _c_vp, _c_i64,

@@ -179,45 +179,11 @@ int gemm_tc(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
   return check_launch("gemm_bf16_tc_kernel launch");
 }
 
-// Scratch of the split tail: per (device, stream) so launches on different
-// streams never share it; grown on demand, counters zeroed once (the kernel
-// leaves them at zero).  Layout: a fixed counter area (kSplitMaxRegions x
-// u32, the same for every request so counters never move), then per region
-// two halves of 128 x tn fp32.
-constexpr int kSplitMaxRegions = 1024;  // regions = 2 x tail tiles <= resident pairs
-struct SplitScratch {
-  void* ptr = nullptr;
-  size_t bytes = 0;
-};
-std::map<std::pair<int, cudaStream_t>, SplitScratch> g_split_scratch;
-
-int split_scratch(int dev, cudaStream_t st, int regions, int tn, float** partial,
-                  unsigned** counters) {
-  if (regions > kSplitMaxRegions) return fail(JULES_ERR_SHAPE, "split tail: %d regions", regions);
-  const size_t cbytes = (size_t)kSplitMaxRegions * 4;
-  const size_t need = cbytes + (size_t)regions * 2 * 128 * tn * 4;
-  std::lock_guard<std::mutex> lk(g_dev_mu);
-  SplitScratch& sc = g_split_scratch[{dev, st}];
-  if (sc.bytes < need) {
-    if (sc.ptr) cudaFree(sc.ptr);
-    sc.ptr = nullptr;
-    sc.bytes = 0;
-    cudaError_t e = cudaMalloc(&sc.ptr, need);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(split scratch)");
-    e = cudaMemset(sc.ptr, 0, need);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(split scratch)");
-    sc.bytes = need;
-  }
-  *counters = static_cast<unsigned*>(sc.ptr);
-  *partial = reinterpret_cast<float*>(static_cast<char*>(sc.ptr) + cbytes);
-  return JULES_OK;
-}
-
 // CTA-pair tcgen05 GEMM (256 x 256 tiles, cluster of 2).
 template <int TN, typename TOut>
 int gemm_tc2(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
              const __nv_bfloat16* res, TOut* C, int64_t M, int64_t N, int64_t K, int act,
-             cudaStream_t st, bool allow_split) {
+             cudaStream_t st) {
   int dev;
   if (int rc = current_device(&dev)) return rc;
   CUtensorMap ta, tw;
@@ -259,26 +225,17 @@ int gemm_tc2(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
     max_pairs = clusters;
   }
   const int64_t tiles = ((M + 255) / 256) * ((N + TN - 1) / TN);
-  const int num_k = (int)((K + 63) / 64);
-  int whole = (int)tiles, units = (int)tiles;
-  float* partial = nullptr;
-  unsigned* counters = nullptr;
+  // Tail split (see gemm_bf16_tc2_kernel): the r tiles of the last, partial
+  // round run as 2r half-width units when they fit in one round.  At C2
+  // (4096^3: 256 tiles on 74 pairs) the last round's 34 tiles become 68
+  // halves; with 512 rows per GPU (32 tiles) every tile is split.
   const int64_t tail = tiles % max_pairs;
-  // Split the tail tiles along K (see gemm_bf16_tc2_kernel) only when the
-  // last round would be nearly empty.  For larger tails the split measured
-  // slower (4096^3: 34 tail tiles on 74 pairs, 1086 vs 1147 TFLOP/s at an
-  // unthrottled 1965 MHz): the fp32 partial write, the partner's partial
-  // read and the second TMEM readout of every split tile cost more than the
-  // half round they save.
-  if (allow_split && tiles > max_pairs && tail > 0 && 4 * tail <= max_pairs && num_k >= 2) {
-    whole = (int)(tiles - tail);
-    units = whole + 2 * (int)tail;
-    if (int rc = split_scratch(dev, st, 2 * (int)tail, TN, &partial, &counters)) return rc;
-  }
+  const int whole = (int)(tiles - (2 * tail <= max_pairs ? tail : 0));
+  const int units = (int)(whole + 2 * (tiles - whole));
   const int pairs = units < max_pairs ? units : max_pairs;
   cfg.gridDim = dim3(2 * pairs);
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tw, bias, res, C, (int)M, (int)N, (int)K, act,
-                                     whole, units, partial, counters);
+                                     whole, units);
   if (e != cudaSuccess) return cuda_fail(e, "gemm_bf16_tc2_kernel launch");
   return check_launch("gemm_bf16_tc2_kernel launch");
 }
@@ -290,9 +247,9 @@ int gemm_tc2(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
 template <typename TOut>
 int gemm_tc_dispatch(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
                      const __nv_bfloat16* res, TOut* C, int64_t M, int64_t N, int64_t K, int act,
-                     cudaStream_t st, bool allow_split = true) {
+                     cudaStream_t st) {
   if (M < 256 || N < 256) return gemm_tc(A, W, bias, res, C, M, N, K, act, st);
-  return gemm_tc2<256>(A, W, bias, res, C, M, N, K, act, st, allow_split);
+  return gemm_tc2<256>(A, W, bias, res, C, M, N, K, act, st);
 }
 
 template <typename TIn, typename TOut>
@@ -484,6 +441,23 @@ int attn_bwd_simt(const void* Q, const void* K, const void* V, const void* O, co
       static_cast<const T*>(dO), lse, delta, static_cast<T*>(dK), static_cast<T*>(dV), B, Hq, Hkv,
       S, D, scale, causal);
   return check_launch("bwd_simt_dkdv_kernel launch");
+}
+
+// Self-test of the bounded wait: one thread waits on an mbarrier that nothing
+// arrives on, with the given limit.  The wait gives up, records
+// kDevErrTimeout with site kSelftestWaitSite in the device error word and the
+// kernel returns; the context stays usable.
+constexpr uint32_t kSelftestWaitSite = 250;
+__global__ void wait_selftest_kernel(uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    jb::mbar_init(&bar, 1);
+    abort_flag = 0;
+    jb::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) (void)jb::mbar_wait_for(&bar, 0, kSelftestWaitSite, &abort_flag, limit_ns);
 }
 
 }  // namespace
@@ -727,6 +701,14 @@ int jules_device_error(uint32_t* word, int clear) {
     return fail(JULES_ERR_TIMEOUT, "device wait timed out (site %u)", (w >> 8) & 0xffu);
   if (w) return fail(JULES_ERR_SHAPE, "device reported error word 0x%x", w);
   return ok();
+}
+
+int jules_selftest_bounded_wait(uint64_t limit_ns, void* stream) {
+  if (limit_ns == 0 || limit_ns > jb::kWaitLimitNs)
+    return fail(JULES_ERR_ARG, "selftest_bounded_wait: limit %llu ns outside (0, %llu]",
+                (unsigned long long)limit_ns, (unsigned long long)jb::kWaitLimitNs);
+  wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_ns);
+  return check_launch("wait_selftest_kernel launch");
 }
 
 int jules_gemm_bias_act(const void* A, const void* W, const float* bias, const void* residual,
@@ -1184,28 +1166,6 @@ int noalloc_scratch(void** out) {
   return JULES_OK;
 }
 
-// bf16 GEMM for the no-allocation path: the same kernels as
-// jules_gemm_bias_act, but never the K-split tail (whose scratch is
-// allocated on demand).
-int gemm_noalloc(const void* A, const void* W, const float* bias, const void* residual, void* C,
-                 int64_t M, int64_t N, int64_t K, int act, int out_dtype, cudaStream_t st) {
-  const bool out_bf = out_dtype == JULES_DTYPE_BF16;
-  if (N % 8 == 0 && K % 8 == 0 && aligned16(A) && aligned16(W) && aligned16(C) &&
-      (!bias || aligned16(bias)) && (!residual || aligned16(residual))) {
-    const auto* a = static_cast<const __nv_bfloat16*>(A);
-    const auto* w = static_cast<const __nv_bfloat16*>(W);
-    const auto* r = static_cast<const __nv_bfloat16*>(residual);
-    if (out_bf)
-      return gemm_tc_dispatch(a, w, bias, r, static_cast<__nv_bfloat16*>(C), M, N, K, act, st,
-                              /*allow_split=*/false);
-    return gemm_tc_dispatch(a, w, bias, r, static_cast<float*>(C), M, N, K, act, st,
-                            /*allow_split=*/false);
-  }
-  if (out_bf)
-    return gemm_simt<__nv_bfloat16, __nv_bfloat16>(A, W, bias, residual, C, M, N, K, act, 0, st);
-  return gemm_simt<__nv_bfloat16, float>(A, W, bias, residual, C, M, N, K, act, 1, st);
-}
-
 }  // namespace
 
 extern "C" {
@@ -1232,17 +1192,18 @@ int jules_mlp_block_noalloc(const void* X, const float* gamma, const float* beta
   if (T == 0) return ok();
   void* ws = nullptr;
   if (int rc = noalloc_scratch(&ws)) return rc;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   const size_t xn_bytes = ((size_t)T * d * 2 + 255) & ~size_t(255);
   void* xn = ws;
   void* hid = static_cast<char*>(ws) + xn_bytes;
   if (int rc = jules_layernorm(X, gamma, beta, xn, T, d, eps, JULES_DTYPE_BF16, JULES_DTYPE_BF16,
                                nullptr, nullptr, stream))
     return rc;
-  if (int rc = gemm_noalloc(xn, W1, b1, nullptr, hid, T, dff, d, JULES_ACT_GELU, JULES_DTYPE_BF16,
-                            st))
+  // The GEMMs allocate nothing (their tail split needs no scratch).
+  if (int rc = jules_gemm_bias_act(xn, W1, b1, nullptr, hid, T, dff, d, JULES_ACT_GELU,
+                                   JULES_DTYPE_BF16, JULES_DTYPE_BF16, stream))
     return rc;
-  return gemm_noalloc(hid, W2, b2, X, out, T, d, dff, JULES_ACT_NONE, out_dtype, st);
+  return jules_gemm_bias_act(hid, W2, b2, X, out, T, d, dff, JULES_ACT_NONE, JULES_DTYPE_BF16,
+                             out_dtype, stream);
 }
 
 }  // extern "C"

@@ -275,11 +275,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 //                       accumulator on the leader's barrier (256 arrivals).
 //
 // Tail split.  With T tiles on P resident pairs, the last round holds only
-// T mod P tiles.  When that is at most P/2, those tiles are split in two
-// halves along K ("units"), so the last round takes half as long.  Each half
-// writes its fp32 partial tile to the scratch buffer and bumps a per-tile
-// counter; the half that arrives second adds the other half's partial to its
-// own accumulator and runs the epilogue.  Nothing waits on another CTA.
+// r = T mod P tiles (all T when T < P).  When 2r <= P, those r tiles are run
+// as 2r half-width units of 256 x 128 (M=256, N=128 MMAs over the full K), so
+// the last round takes about half as long.  The halves are independent
+// output tiles: nothing is combined, no scratch memory, no counters.
 // ---------------------------------------------------------------------------
 template <int STAGES, int TN>
 struct Smem2 {
@@ -293,35 +292,29 @@ struct Smem2 {
   uint64_t tempty[2];
   uint32_t tmem_base;
   int abort_flag;
-  int split_last;
 };
 
 // Work unit u of the tail-split schedule: whole tiles first, then the two
-// K-halves of each tail tile.
+// column halves of each tail tile.  n_off is the unit's first column inside
+// its tile, cols its width (TN or TN/2).
 struct PairUnit {
-  int tile, k0, k1, split, half;
+  int tile, n_off, cols;
 };
-__device__ __forceinline__ PairUnit pair_unit(int u, int whole_units, int num_k) {
+template <int TN>
+__device__ __forceinline__ PairUnit pair_unit(int u, int whole_units) {
   PairUnit r;
   if (u < whole_units) {
     r.tile = u;
-    r.k0 = 0;
-    r.k1 = num_k;
-    r.split = 0;
-    r.half = 0;
+    r.n_off = 0;
+    r.cols = TN;
   } else {
     const int v = u - whole_units;
     r.tile = whole_units + (v >> 1);
-    r.half = v & 1;
-    r.k0 = r.half ? num_k / 2 : 0;
-    r.k1 = r.half ? num_k : num_k / 2;
-    r.split = 1;
+    r.n_off = (v & 1) * (TN / 2);
+    r.cols = TN / 2;
   }
   return r;
 }
-
-// Named barrier over the four epilogue warps (128 threads).
-__device__ __forceinline__ void epilogue_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 // Epilogue math for 8 consecutive columns: bias, activation, residual, store.
 template <typename TOut>
@@ -349,14 +342,15 @@ __device__ __forceinline__ void epilogue8(float (&v)[8], const float* bias,
   store8(crow + col, v);
 }
 
+// whole_units: tiles run at full width; num_units: whole_units + 2 x the
+// number of tail tiles run as halves (== whole_units when nothing is split).
 template <int STAGES, int TN, typename TOut>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc2_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmW, const float* __restrict__ bias,
                          const __nv_bfloat16* __restrict__ residual, TOut* __restrict__ C, int M,
-                         int N, int K, int act, int whole_units, int num_units,
-                         float* __restrict__ partial, unsigned* __restrict__ counters) {
-  static_assert(TN == 128 || TN == 256, "pair tile N is 128 or 256");
+                         int N, int K, int act, int whole_units, int num_units) {
+  static_assert(TN == 256, "pair tile N is 256 (its halves are 128)");
   constexpr int TM = 256;
   constexpr uint32_t kTmemCols = 2 * TN;  // two accumulators
   using S = Smem2<STAGES, TN>;
@@ -404,17 +398,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int u = pair_id; u < num_units && ok; u += num_pairs) {
-        const PairUnit pu = pair_unit(u, whole_units, num_k);
+        const PairUnit pu = pair_unit<TN>(u, whole_units);
         int mi, ni;
         tile_coords(pu.tile, num_m, num_n, mi, ni);
+        const int cta_cols = pu.cols / 2;  // this CTA's share of the unit's W columns
         const int m0 = mi * TM + (int)rank * 128;
-        const int n0 = ni * TN + (int)rank * (TN / 2);
-        for (int kb = pu.k0; kb < pu.k1; ++kb) {
+        const int n0 = ni * TN + pu.n_off + (int)rank * cta_cols;
+        const uint32_t tx = 2u * (uint32_t)(S::kABytes + BK * cta_cols * 2);
+        for (int kb = 0; kb < num_k; ++kb) {
           if (!mbar_wait(&s.empty[stage], phase ^ 1u, 41, abort_flag)) { ok = false; break; }
-          if (leader) mbar_arrive_expect_tx(&s.full[stage], 2 * (S::kABytes + S::kBBytes));
+          if (leader) mbar_arrive_expect_tx(&s.full[stage], tx);
           tma_load_2d_pair(s.a[stage], &tmA, &s.full[stage], kb * BK, m0);
-#pragma unroll
-          for (int j = 0; j < TN / 128; ++j)
+          for (int j = 0; j < cta_cols / 64; ++j)
             tma_load_2d_pair(s.b[stage] + j * (BK * 64 * 2), &tmW, &s.full[stage], n0 + j * 64, kb * BK);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -423,7 +418,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer (leader CTA) ----------------
     if (leader && lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(TM, TN, false, true);
+      constexpr uint32_t idesc_full = idesc_bf16_f32(TM, TN, false, true);
+      constexpr uint32_t idesc_half = idesc_bf16_f32(TM, TN / 2, false, true);
       const uint32_t empty0 = smem_u32(&s.empty[0]);
       const uint32_t tfull0 = smem_u32(&s.tfull[0]);
       const uint32_t empty0_peer = mapa_shared(empty0, 1);
@@ -434,11 +430,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int u = pair_id; u < num_units && ok; u += num_pairs) {
-        const PairUnit pu = pair_unit(u, whole_units, num_k);
+        const PairUnit pu = pair_unit<TN>(u, whole_units);
+        const uint32_t idesc = pu.cols == TN ? idesc_full : idesc_half;
         if (!mbar_wait(&s.tempty[acc], acc_phase ^ 1u, 42, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * TN;
-        for (int kb = pu.k0; kb < pu.k1; ++kb) {
+        for (int kb = 0; kb < num_k; ++kb) {
           if (!mbar_wait(&s.full[stage], phase, 43, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint64_t a0 = sdesc_sw128(smem_u32(s.a[stage]), 16, 1024);
@@ -449,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ad[kk] = a0 + kk * 2;    // +32 bytes inside the swizzle row
             bd[kk] = b0 + kk * 128;  // +16 K rows of 128 bytes
           }
-          umma4_pair_ss(d_tmem, ad, bd, kb > pu.k0 ? 1u : 0u, idesc);
+          umma4_pair_ss(d_tmem, ad, bd, kb > 0 ? 1u : 0u, idesc);
           umma_commit_pair(empty0 + stage * 8);
           umma_commit_pair(empty0_peer + stage * 8);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -468,75 +465,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int u = pair_id; u < num_units; u += num_pairs) {
-      const PairUnit pu = pair_unit(u, whole_units, num_k);
+      const PairUnit pu = pair_unit<TN>(u, whole_units);
       int mi, ni;
       tile_coords(pu.tile, num_m, num_n, mi, ni);
       const int m0 = mi * TM + (int)rank * 128;
-      const int n0 = ni * TN;
+      const int n0 = ni * TN + pu.n_off;
       if (!mbar_wait(&s.tfull[acc], acc_phase, 44, abort_flag)) break;
       tc_fence_after();
       const int row = m0 + row_in_tile;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * TN;
       TOut* crow = C + (size_t)(row < M ? row : 0) * N;
       const __nv_bfloat16* rrow = residual ? residual + (size_t)(row < M ? row : 0) * N : nullptr;
-      const float* other = nullptr;  // the other K-half's partial row (split units)
-      bool finish = true;
-      if (pu.split) {
-        // This CTA's slice of the tile, one region per (tail tile, rank),
-        // two halves per region, 128 rows x TN fp32 per half.
-        const int region = (pu.tile - whole_units) * 2 + (int)rank;
-        float* mine = partial + ((size_t)(region * 2 + pu.half) * 128 + row_in_tile) * TN;
 #pragma unroll 1
-        for (int c = 0; c < TN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(t_row + c * 32, r);
-          tmem_ld_wait(r);
-          float4* dst = reinterpret_cast<float4*>(mine + c * 32);
+      for (int c = 0; c < pu.cols / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(t_row + c * 32, r);
+        tmem_ld_wait(r);
+        const int col0 = n0 + c * 32;
+        if (row < M && col0 < N) {
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            dst[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                                 __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
-        }
-        __threadfence();
-        epilogue_bar();
-        if (threadIdx.x == 64) {  // first epilogue thread
-          const unsigned prev = atomicAdd(&counters[region], 1u);
-          s.split_last = prev == 1u;
-          if (prev == 1u) counters[region] = 0u;  // ready for the next launch
-        }
-        epilogue_bar();
-        finish = s.split_last != 0;
-        __threadfence();
-        other = partial + ((size_t)(region * 2 + (pu.half ^ 1)) * 128 + row_in_tile) * TN;
-      }
-      if (finish) {
-#pragma unroll 1
-        for (int c = 0; c < TN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(t_row + c * 32, r);
-          tmem_ld_wait(r);
-          if (other) {
-            const float4* src = reinterpret_cast<const float4*>(other + c * 32);
+          for (int g = 0; g < 4; ++g) {
+            const int col = col0 + g * 8;
+            if (col < N) {
+              float v[8];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const float4 o = __ldcg(src + q);
-              r[4 * q] = __float_as_uint(__uint_as_float(r[4 * q]) + o.x);
-              r[4 * q + 1] = __float_as_uint(__uint_as_float(r[4 * q + 1]) + o.y);
-              r[4 * q + 2] = __float_as_uint(__uint_as_float(r[4 * q + 2]) + o.z);
-              r[4 * q + 3] = __float_as_uint(__uint_as_float(r[4 * q + 3]) + o.w);
-            }
-          }
-          const int col0 = n0 + c * 32;
-          if (row < M && col0 < N) {
-#pragma unroll
-            for (int g = 0; g < 4; ++g) {
-              const int col = col0 + g * 8;
-              if (col < N) {
-                float v[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[g * 8 + j]);
-                epilogue8(v, bias, rrow, crow, col, act);
-              }
+              for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[g * 8 + j]);
+              epilogue8(v, bias, rrow, crow, col, act);
             }
           }
         }

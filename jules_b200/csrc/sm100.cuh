@@ -94,23 +94,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait until the phase with the given parity has completed.  Returns false
-// (and records kDevErrTimeout | site) if that takes longer than
-// kWaitLimitNs, or immediately if *abort is already set by another warp.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t site,
-                                          volatile int* abort_flag) {
+// (and records kDevErrTimeout | site) if that takes longer than limit_ns,
+// or soon after *abort is set by another warp.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, uint32_t site,
+                                              volatile int* abort_flag, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 255u) == 0) {
       if (abort_flag && *abort_flag) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) {
+      if (globaltimer() - t0 > limit_ns) {
         record_error(kDevErrTimeout, site);
         if (abort_flag) *abort_flag = 1;
         return false;
       }
     }
   }
+}
+
+// The pipelines' wait: bounded by kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t site,
+                                          volatile int* abort_flag) {
+  return mbar_wait_for(bar, parity, site, abort_flag, kWaitLimitNs);
 }
 
 // ---------------------------------------------------------------------------

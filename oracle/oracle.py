@@ -37,9 +37,16 @@ ACT = {"none": 0, "relu": 1, "sigmoid": 2, "tanh": 3, "gelu": 4}
 FP8_FMT = {"e4m3": 0, "e5m2": 1}
 
 
-def build(reference_root: str = "/root/reference") -> None:
+def reference_dir() -> str:
+    """Checkout of the reference project: $JULES_REFERENCE_DIR, else a
+    `reference` directory beside this repository."""
+    return os.environ.get("JULES_REFERENCE_DIR") or os.path.join(os.path.dirname(os.path.dirname(HERE)),
+                                                                 "reference")
+
+
+def build(reference_root: str | None = None) -> None:
     """Compile the oracle (restatement always; reference when present)."""
-    subprocess.run(["make", "-s", f"REF={reference_root}"], cwd=HERE, check=True)
+    subprocess.run(["make", "-s", f"REF={reference_root or reference_dir()}"], cwd=HERE, check=True)
 
 
 def _fp(a: np.ndarray | None):

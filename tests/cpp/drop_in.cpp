@@ -22,6 +22,13 @@ static std::vector<float> load(const std::string& p, size_t n) {
   std::fclose(f);
   return v;
 }
+static std::vector<int8_t> load_i8(const std::string& p, size_t n) {
+  std::vector<int8_t> v(n);
+  FILE* f = std::fopen(p.c_str(), "rb");
+  if (!f || std::fread(v.data(), 1, n, f) != n) { std::fprintf(stderr, "read %s\n", p.c_str()); std::exit(2); }
+  std::fclose(f);
+  return v;
+}
 static void save(const std::string& p, const std::vector<float>& v) {
   FILE* f = std::fopen(p.c_str(), "wb");
   std::fwrite(v.data(), 4, v.size(), f);
@@ -40,6 +47,8 @@ int main(int argc, char** argv) {
   save(d + "/out_flash.bin", O);
   attention(O.data(), Q.data(), K.data(), V.data(), B, H, S, D, arena, planner);
   save(d + "/out_attention.bin", O);
+  standardAttention(O.data(), Q.data(), K.data(), V.data(), B, H, S, D, arena);
+  save(d + "/out_standard.bin", O);
   // tiled matmul + GELU [96,200]x[200,136]
   const int M = 96, Kd = 200, N = 136;
   auto A = load(d + "/in_a.bin", M * Kd), W = load(d + "/in_w.bin", Kd * N);
@@ -50,6 +59,8 @@ int main(int argc, char** argv) {
   save(d + "/out_tiled_gelu.bin", C);
   fusedMatmulBiasRelu(A.data(), W.data(), bias.data(), C.data(), M, Kd, N);
   save(d + "/out_bias_relu.bin", C);
+  fusedMatmulRelu(A.data(), W.data(), C.data(), M, Kd, N);  // argument order (M, K, N)
+  save(d + "/out_relu.bin", C);
   blasMatmul(A.data(), W.data(), C.data(), M, N, Kd);
   save(d + "/out_blas.bin", C);
   // layernorm [96,200] and gelu
@@ -86,6 +97,22 @@ int main(int argc, char** argv) {
     save(d + "/out_train_dW1.bin", gW1);
     save(d + "/out_train_dX.bin", gX);
     save(d + "/out_train_loss.bin", std::vector<float>(1, r.loss));
+  }
+  // matmulInt8: [96,200]x[200,136] (CUDA cores: N not a multiple of 16) and
+  // [256,256]x[256,512] (tcgen05 kind::i8), scales 0.5 / 0.25, with bias
+  {
+    auto A8 = load_i8(d + "/in_a8.bin", M * Kd), B8 = load_i8(d + "/in_b8.bin", Kd * N);
+    std::vector<float> C8(M * N);
+    matmulInt8(A8.data(), B8.data(), C8.data(), M, N, Kd, 0.5f, 0.25f, bias.data());
+    save(d + "/out_int8_small.bin", C8);
+    const int M2 = 256, K2 = 256, N2 = 512;
+    auto A9 = load_i8(d + "/in_a9.bin", M2 * K2), B9 = load_i8(d + "/in_b9.bin", K2 * N2);
+    auto b9 = load(d + "/in_b9bias.bin", N2);
+    std::vector<float> C9(M2 * N2);
+    matmulInt8(A9.data(), B9.data(), C9.data(), M2, N2, K2, 0.5f, 0.25f, b9.data());
+    save(d + "/out_int8_tc.bin", C9);
+    matmulInt8(A9.data(), B9.data(), C9.data(), M2, N2, K2, 1.0f, 1.0f);  // no bias
+    save(d + "/out_int8_tc_nobias.bin", C9);
   }
   std::printf("drop-in ok\n");
   return 0;

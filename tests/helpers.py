@@ -46,3 +46,25 @@ def attn_inputs(B, Hq, Hkv, S, D, seed=0, bf16=True):
     if bf16:
         Q, K, V = bf16_np(Q), bf16_np(K), bf16_np(V)
     return Q, K, V
+
+
+_KEEP = []
+
+
+def arg_buffer(nbytes=1 << 20):
+    """Pointer for argument-validation tests, whose calls must fail before
+    any kernel runs.  With a GPU present it is a real device allocation of
+    nbytes (kept alive for the session), so that a validation regression
+    would launch on valid memory instead of a made-up address; without one
+    the library cannot launch anything and a placeholder address is used."""
+    import ctypes
+    try:
+        import torch
+        gpu = torch.cuda.is_available()
+    except Exception:
+        gpu = False
+    if not gpu:
+        return ctypes.c_void_p(256)
+    t = torch.zeros(max(int(nbytes), 256), dtype=torch.uint8, device="cuda")
+    _KEEP.append(t)
+    return ctypes.c_void_p(t.data_ptr())

@@ -9,6 +9,7 @@ import subprocess
 import pytest
 
 from conftest import ROOT
+from helpers import arg_buffer
 
 INC = os.path.join(ROOT, "include")
 
@@ -69,10 +70,12 @@ def test_registry(jb):
     assert h.jules_kernel_name(-1) is None
 
 
-FAKE = ctypes.c_void_p(256)  # never dereferenced: validation fails first
+@pytest.fixture(scope="module")
+def FAKE():
+    return arg_buffer()  # the calls below fail validation before any launch
 
 
-def test_gemm_argument_errors(jb):
+def test_gemm_argument_errors(jb, FAKE):
     h = jb.lib()
     assert h.jules_gemm_bias_act(None, FAKE, None, None, FAKE, 4, 4, 4, 0, 1, 1, None) == 6
     assert h.jules_gemm_bias_act(FAKE, FAKE, None, None, FAKE, 4, 0, 4, 0, 1, 1, None) == 1
@@ -83,7 +86,7 @@ def test_gemm_argument_errors(jb):
     assert b"NULL" in h.jules_last_error_string() or h.jules_last_error_string() == b""
 
 
-def test_attention_argument_errors(jb):
+def test_attention_argument_errors(jb, FAKE):
     h = jb.lib()
     f = h.jules_flash_attention_fwd
     assert f(None, FAKE, FAKE, FAKE, None, 1, 1, 1, 8, 64, 0.0, 0, 1, None) == 6
@@ -93,7 +96,7 @@ def test_attention_argument_errors(jb):
     assert f(FAKE, FAKE, FAKE, FAKE, None, 1, 2, 2, 0, 64, 0.0, 0, 1, None) == 0   # empty
 
 
-def test_norm_mlp_argument_errors(jb):
+def test_norm_mlp_argument_errors(jb, FAKE):
     h = jb.lib()
     assert h.jules_layernorm(None, FAKE, FAKE, FAKE, 4, 4, 1e-5, 0, 0, None, None, None) == 6
     assert h.jules_gelu(FAKE, FAKE, -1, 0, None) == 1
@@ -104,14 +107,47 @@ def test_norm_mlp_argument_errors(jb):
                            None, 0, None)
     assert rc == 8
     rc = h.jules_mlp_block(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 1, 16, 64, 256, 1e-5,
-                           ctypes.c_void_p(264), need, None)
+                           ctypes.c_void_p(FAKE.value + 8), need, None)
     assert rc == 2  # workspace misaligned
     rc = h.jules_mlp_block(FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 5, 16, 64, 256, 1e-5,
-                           ctypes.c_void_p(256), need, None)
+                           FAKE, need, None)
     assert rc == 3  # bad out dtype
 
 
-def test_sgemm_argument_errors(jb):
+def test_sgemm_argument_errors(jb, FAKE):
     h = jb.lib()
     assert h.jules_sgemm(0, 0, 4, 4, 4, 1.0, None, 4, FAKE, 4, 0.0, FAKE, 4, None) == 6
     assert h.jules_sgemm(0, 0, 4, 4, 4, 1.0, FAKE, 2, FAKE, 4, 0.0, FAKE, 4, None) == 1  # lda < K
+
+
+def test_selftest_wait_rejects_bad_limits(jb):
+    h = jb.lib()
+    assert h.jules_selftest_bounded_wait(0, None) == 6
+    assert h.jules_selftest_bounded_wait(3_000_000_000, None) == 6
+
+
+@pytest.mark.gpu
+def test_bounded_wait_expires_and_context_survives(jb):
+    """A pipeline wait on a barrier that nothing completes gives up after its
+    limit, reports JULES_ERR_TIMEOUT with its site through the device error
+    word, and the kernel returns: the next launch on the same context works."""
+    import time
+
+    import torch
+    h = jb.lib()
+    assert jb.device_error() == 0
+    limit_ns = 50_000_000  # 50 ms
+    t0 = time.perf_counter()
+    assert h.jules_selftest_bounded_wait(limit_ns, None) == 0
+    word = ctypes.c_uint32(0)
+    assert h.jules_device_error(ctypes.byref(word), 1) == 5  # JULES_ERR_TIMEOUT
+    elapsed = time.perf_counter() - t0
+    assert word.value & 0xff == 1 and (word.value >> 8) & 0xff == 250, hex(word.value)
+    assert elapsed >= limit_ns * 1e-9
+    assert elapsed < 10.0
+    assert jb.device_error() == 0  # cleared
+    a = torch.ones((256, 256), dtype=torch.bfloat16, device="cuda")
+    c = jb.gemm_bias_act(a, a)
+    torch.cuda.synchronize()
+    assert jb.device_error() == 0
+    assert bool((c.float() == 256.0).all())

@@ -8,13 +8,15 @@ import numpy as np
 import pytest
 
 from conftest import F32_REL_L2, rel_l2
+from helpers import arg_buffer
 
 JULES_ERR_ARG, JULES_ERR_UNSUPPORTED = 6, 7
 
 
 def _raw_call(jb, name, n_buffers=2, opaque_len=None):
     d = jb.CallDesc()
-    bufs = (ctypes.c_void_p * n_buffers)(*([256] * n_buffers))  # never dereferenced
+    fake = arg_buffer().value  # the calls fail validation before any launch
+    bufs = (ctypes.c_void_p * n_buffers)(*([fake] * n_buffers))
     return jb.lib().jules_custom_call(name.encode(), None, bufs, n_buffers,
                                       ctypes.cast(ctypes.pointer(d), ctypes.c_void_p),
                                       ctypes.sizeof(d) if opaque_len is None else opaque_len)

@@ -7,6 +7,8 @@ import subprocess
 import numpy as np
 import pytest
 
+import oracle
+
 from conftest import F32_REL_L2, ROOT, rel_l2
 
 def _compile(tmp, jb):
@@ -34,7 +36,13 @@ def test_drop_in_matches_reference(tmp_path, jb, ref):
     bias = g.uniform(-1, 1, 136).astype(np.float32)
     W2 = g.uniform(-1, 1, (136, 24)).astype(np.float32)
     b2 = g.uniform(-1, 1, 24).astype(np.float32)
-    for name, arr in dict(q=Q, k=K, v=V, a=A, w=W, bias=bias, w2=W2, b2=b2).items():
+    A8 = g.integers(-128, 128, (96, 200)).astype(np.int8)
+    B8 = g.integers(-128, 128, (200, 136)).astype(np.int8)
+    A9 = g.integers(-128, 128, (256, 256)).astype(np.int8)
+    B9 = g.integers(-128, 128, (256, 512)).astype(np.int8)
+    b9 = g.standard_normal(512).astype(np.float32)
+    for name, arr in dict(q=Q, k=K, v=V, a=A, w=W, bias=bias, w2=W2, b2=b2, a8=A8, b8=B8, a9=A9,
+                          b9=B9, b9bias=b9).items():
         arr.tofile(os.path.join(d, f"in_{name}.bin"))
     subprocess.run([exe, d], check=True)
     out = lambda n, shape: np.fromfile(os.path.join(d, f"out_{n}.bin"), np.float32).reshape(shape)
@@ -42,6 +50,15 @@ def test_drop_in_matches_reference(tmp_path, jb, ref):
     assert rel_l2(out("attention", Q.shape), ref.attention(Q, K, V)) <= F32_REL_L2
     assert rel_l2(out("tiled_gelu", (96, 136)), ref.tiled_matmul_act(A, W, "gelu")) <= F32_REL_L2
     assert rel_l2(out("bias_relu", (96, 136)), ref.fused_matmul_bias_relu(A, W, bias)) <= F32_REL_L2
+    assert rel_l2(out("standard", Q.shape), ref.standard_attention(Q, K, V)) <= F32_REL_L2
+    # fusedMatmulRelu takes (M, K, N); a swapped order would not match (M, K, N all differ)
+    assert rel_l2(out("relu", (96, 136)), ref.fused_matmul_relu(A, W)) <= F32_REL_L2
+    # matmulInt8: int32 accumulation is exact, so the results equal the
+    # reference's scalar branch (oracle/_ref avx2 build) bit for bit
+    ref8 = oracle.Reference(variant="avx2")
+    assert np.array_equal(out("int8_small", (96, 136)), ref8.matmul_int8(A8, B8, 0.5, 0.25, bias))
+    assert np.array_equal(out("int8_tc", (256, 512)), ref8.matmul_int8(A9, B9, 0.5, 0.25, b9))
+    assert np.array_equal(out("int8_tc_nobias", (256, 512)), ref8.matmul_int8(A9, B9))
     assert rel_l2(out("blas", (96, 136)), ref.blas_matmul(A, W)) <= F32_REL_L2
     ln = ref.layernorm(A, np.ones(200, np.float32), np.zeros(200, np.float32))
     assert rel_l2(out("layernorm", (96, 200)), ln) <= F32_REL_L2
