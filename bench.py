@@ -49,9 +49,10 @@ def parse():
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["jules", "reference"], default="jules")
-    p.add_argument("--workload", choices=["gemm", "attn", "attn_gqa", "mlp", "attn_fp32",
-                                          "softmax", "xent", "int8", "fp8", "attn_bwd"],
-                   default="gemm")
+    p.add_argument("--workload", choices=["headline", "gemm", "attn", "attn_gqa", "mlp",
+                                          "attn_fp32", "softmax", "xent", "int8", "fp8",
+                                          "attn_bwd"],
+                   default="headline")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     a = p.parse_args()
@@ -130,18 +131,28 @@ def profiled_traffic(workload):
 
 def describe(workload, world, extra_l2=None):
     """The config object of the JSON line (shared by both arms)."""
-    if workload == "gemm":
-        c = {"workload": "C2 fused GEMM+bias+GELU(tanh)", "M_per_rank": 4096, "N": 4096,
-             "K": 4096, "global_M": 4096 * world, "sharding": "rows of M", "dtype_in": "bf16",
-             "accumulate": "fp32", "dtype_out": "bf16"}
+    if workload in ("gemm", "headline"):
+        c = {"workload": "C2 fused GEMM+bias+GELU(tanh)", "M": 4096, "N": 4096, "K": 4096,
+             "M_per_rank": 4096 // world, "sharding": "rows of M (strong scaling: the global "
+             "config split over the ranks)", "dtype_in": "bf16", "accumulate": "fp32",
+             "dtype_out": "bf16"}
+        if world > 1:
+            c["gather"] = ("C gathered into every rank inside the timed step: fused into the GEMM "
+                           "epilogue as NVLink stores to each rank's C (jules_dist_gemm_bias_act)")
     elif workload in ("attn", "attn_gqa"):
         gqa = workload == "attn_gqa"
         B, Hq, Hkv, S = (4, 64, 8, 16384) if gqa else (8, 32, 32, 4096)
-        c = {"workload": ("C5 GQA causal flash-attention fwd" if gqa else
+        c = {"workload": ("C5 GQA causal flash-attention fwd + lse" if gqa else
                           "C3 causal flash-attention fwd + lse"),
-             "B_per_rank": B, "Hq": Hq, "Hkv": Hkv, "S": S, "D": 128, "global_B": B * world,
-             "sharding": "batch x kv-head-group units",
+             "B": B, "Hq": Hq, "Hkv": Hkv, "S": S, "D": 128,
+             "units_per_rank": B * Hkv // world,
+             "sharding": "(batch, kv head) units (strong scaling: the global config split over "
+                         "the ranks)",
              "flop_convention": "causal = 2*B*Hq*S^2*D"}
+        if world > 1:
+            c["gather"] = ("O and lse gathered into every rank inside the timed step: fused into "
+                           "the attention epilogue as NVLink stores to each rank's O and lse "
+                           "(jules_dist_flash_attention_fwd)")
     elif workload == "mlp":
         c = {"workload": "C4 MLP block LN->GEMM+b+GELU->GEMM+b+residual", "T_per_rank": 16384,
              "d": 4096, "dff": 16384, "global_T": 16384 * world, "sharding": "token rows",
@@ -312,15 +323,23 @@ class E2EPipeline:
 
 
 class Gemm(Workload):
-    """C2: C = GELU(A.W + bias), M=N=K=4096 per rank (rows of M sharded)."""
+    """C2: C = GELU(A.W + bias), M=N=K=4096.  With N GPUs the same global
+    problem is split by rows of M (strong scaling): each rank computes its
+    4096/N rows and the gather of C into every rank is fused into the GEMM
+    (jules_dist_gemm_bias_act on shared output buffers), so a step is the
+    whole distributed op, gather included."""
     dominant = "gemm_bf16_tc2_kernel (CTA pair)"
+    global_work = True
 
-    def __init__(self, jb, torch, rank, world, M=4096, N=4096, K=4096):
+    def __init__(self, jb, torch, rank, world, M=4096, N=4096, K=4096, dist=None):
         self.jb, self.torch = jb, torch
         self.M, self.N, self.K = M, N, K
-        self.world = world
+        self.world, self.dist = world, dist
+        if world > 1:
+            self.dominant = "gemm_bf16_tc2_kernel (CTA pair) + fused gather to every rank"
+            self.launches_per_step = 2  # the GEMM and the one-thread signal/wait kernel
         dev = torch.device("cuda")
-        g = torch.Generator(device=dev).manual_seed(1234 + rank)
+        g = torch.Generator(device=dev).manual_seed(1234)  # the same problem on every rank
         per_set = (M * K + K * N + M * N) * 2
         self.nsets = self.sets_for(per_set)
         s = 1.0 / K ** 0.5
@@ -331,21 +350,39 @@ class Gemm(Workload):
         self.W = [((torch.rand((K, N), generator=g, device=dev) * 2 - 1) * s).to(torch.bfloat16)
                   for _ in range(self.nsets)]
         self.b = [torch.randn(N, generator=g, device=dev) * 0.02 for _ in range(self.nsets)]
-        self.C = [torch.empty((M, N), dtype=torch.bfloat16, device=dev) for _ in range(self.nsets)]
-        self.flops_per_step = 2.0 * M * N * K
-        self.flops_dominant = self.flops_per_step
-        self.config = {"workload": "C2 fused GEMM+bias+GELU(tanh)", "M_per_rank": M, "N": N,
-                       "K": K, "global_M": M * world, "sharding": "rows of M",
-                       "dtype_in": "bf16", "accumulate": "fp32", "dtype_out": "bf16",
-                       "l2": f"{self.nsets} rotating input sets ({self.nsets * per_set / 2**20:.0f} MiB > L2)"}
+        if world > 1:
+            self.C = [dist.alloc_shared((M, N), torch.bfloat16) for _ in range(self.nsets)]
+        else:
+            self.C = [torch.empty((M, N), dtype=torch.bfloat16, device=dev) for _ in range(self.nsets)]
+        self.rows = jb.dist_shard(M, world, rank)
+        self.flops_per_step = 2.0 * M * N * K  # the whole job's work per step
+        self.flops_dominant = 2.0 * (self.rows[1] - self.rows[0]) * N * K  # this rank's GEMM
+        self.config = {"l2": f"{self.nsets} rotating input sets ({self.nsets * per_set / 2**20:.0f} MiB > L2)"}
 
     def step(self, i, ev=None):
         k = i % self.nsets
         if ev:
             ev[0].record()
-        self.jb.gemm_bias_act(self.A[k], self.W[k], self.b[k], act="gelu", out=self.C[k])
+        if self.world > 1:
+            self.dist.gemm_bias_act(self.A[k], self.W[k], self.b[k], act="gelu", out=self.C[k])
+        else:
+            self.jb.gemm_bias_act(self.A[k], self.W[k], self.b[k], act="gelu", out=self.C[k])
         if ev:
             ev[1].record()
+
+    def compute_only(self, i):
+        """This rank's rows without the gather (the compute half of a step)."""
+        k = i % self.nsets
+        a, b = self.rows
+        if not hasattr(self, "Cl"):
+            self.Cl = self.torch.empty((b - a, self.N), dtype=self.torch.bfloat16, device="cuda")
+        self.jb.gemm_bias_act(self.A[k][a:b], self.W[k], self.b[k], act="gelu", out=self.Cl)
+
+    def release(self):
+        if self.world > 1:
+            for c in self.C:
+                self.dist.free_shared(c)
+            self.C = []
 
     def output(self, i):
         return self.C[i % self.nsets]
@@ -358,14 +395,40 @@ class Gemm(Workload):
         h_out = [self.torch.empty((self.M, self.N), dtype=self.torch.bfloat16).pin_memory()]
         return h_in, h_out, lambda d, o: jb.gemm_bias_act(d[0], d[1], d[2], act="gelu", out=o[0])
 
+    def e2e_dist_spec(self):
+        """N > 1: each step copies this rank's rows of A in, runs the sharded
+        call (gather fused) and rank 0 reads the whole C back; W and bias are
+        replicated once, outside timing."""
+        a, b = self.rows
+        d_in = self.A[0]
+        ins = [(d_in[a:b].cpu().pin_memory(), d_in[a:b])]
+        # Two output buffers in turn: while rank 0 reads step s's C, the other
+        # ranks may already write step s+1's into the other buffer (they
+        # cannot reach step s+2 before rank 0 has signalled s+1, which it
+        # does only after its read of step s).
+        h_out = self.torch.empty((self.M, self.N), dtype=self.torch.bfloat16).pin_memory()
+        outs = [(h_out, self.C[0])]
+        state = {"i": 0}
+
+        def run():
+            k = state["i"] % 2
+            state["i"] += 1
+            outs[0] = (h_out, self.C[k])
+            self.dist.gemm_bias_act(d_in, self.W[0], self.b[0], act="gelu", out=self.C[k])
+
+        return ins, outs, run
+
 
 class Attention(Workload):
     """C3 (attn) / C5 (attn_gqa): causal bf16 flash-attention fwd + lse;
     (batch, kv-head group) units sharded across ranks."""
     dominant = "attn_fwd_tc_kernel"
 
-    def __init__(self, jb, torch, rank, world, gqa=False):
+    global_work = True
+
+    def __init__(self, jb, torch, rank, world, gqa=False, dist=None):
         self.jb, self.torch = jb, torch
+        self.world, self.dist = world, dist
         if gqa:
             B, Hq, Hkv, S = 4, 64, 8, 16384
             # 32 (b, kv-group) units; each rank owns 32/world of them, run as
@@ -376,10 +439,11 @@ class Attention(Workload):
             self.units = B
         D = 128
         self.global_shape = (B, Hq, Hkv, S, D)
-        # per-rank shard, same size for every world size (weak scaling)
+        # the global problem on every rank; with N GPUs each computes its
+        # (batch, kv head) units and the outputs are gathered (strong scaling)
         self.B, self.Hq, self.Hkv, self.S, self.D = B, Hq, Hkv, S, D
         dev = torch.device("cuda")
-        g = torch.Generator(device=dev).manual_seed(77 + rank)
+        g = torch.Generator(device=dev).manual_seed(77)
         per_set = (B * Hq * S * D * 2 + 2 * B * Hkv * S * D) * 2
         self.nsets = 1 if per_set > L2_BYTES else self.sets_for(per_set)
         self.Q = [torch.randn((B, Hq, S, D), generator=g, device=dev).to(torch.bfloat16)
@@ -388,12 +452,19 @@ class Attention(Workload):
                    for _ in range(self.nsets)]
         self.V = [torch.randn((B, Hkv, S, D), generator=g, device=dev).to(torch.bfloat16)
                   for _ in range(self.nsets)]
-        self.O = [torch.empty_like(q) for q in self.Q]
-        self.L = [torch.empty((B, Hq, S), dtype=torch.float32, device=dev) for _ in self.Q]
+        if world > 1:  # every rank's O and lse writable by all: the gather fused in
+            self.O = [dist.alloc_shared((B, Hq, S, D), torch.bfloat16) for _ in self.Q]
+            self.L = [dist.alloc_shared((B, Hq, S), torch.float32) for _ in self.Q]
+        else:
+            self.O = [torch.empty_like(q) for q in self.Q]
+            self.L = [torch.empty((B, Hq, S), dtype=torch.float32, device=dev) for _ in self.Q]
         # causal FLOPs, FlashAttention convention: 2 * B*H*S^2*D
         self.flops_per_step = 2.0 * B * Hq * S * S * D
-        self.flops_dominant = self.flops_per_step
-        self.config = {"workload": ("C5 GQA causal flash-attention fwd" if gqa else
+        self.flops_dominant = self.flops_per_step / world
+        if world > 1:
+            self.dominant = "attn_fwd_tc_kernel + fused gather to every rank"
+            self.launches_per_step = 2  # attention and the one-thread signal/wait kernel
+        self.config = {"workload": ("C5 GQA causal flash-attention fwd + lse" if gqa else
                                     "C3 causal flash-attention fwd + lse"),
                        "B_per_rank": B, "Hq": Hq, "Hkv": Hkv, "S": S, "D": D,
                        "global_B": B * world, "sharding": "batch x kv-head-group units",
@@ -401,12 +472,59 @@ class Attention(Workload):
                        "l2": f"inputs {per_set / 2**20:.0f} MiB per step (> L2)"
                        if self.nsets == 1 else f"{self.nsets} rotating input sets"}
 
+    def _run(self, Q, K, V, O, L):
+        """The C ABI call: causal forward writing O and the fp32 logsumexp
+        (sharded over the ranks, O and lse gathered, when N > 1)."""
+        jb = self.jb
+        if self.world > 1:
+            self.dist.flash_attention_fwd(Q, K, V, causal=True, out=O, lse=L)
+            return
+        rc = jb.lib().jules_flash_attention_fwd(
+            jb._ptr(Q), jb._ptr(K), jb._ptr(V), jb._ptr(O), jb._ptr(L), self.B, self.Hq,
+            self.Hkv, self.S, self.D, 0.0, 1, jb.DT_BF16, jb._stream(None))
+        jb._check(rc, "jules_flash_attention_fwd")
+
+    def release(self):
+        if self.world > 1:
+            for t in self.O + self.L:
+                self.dist.free_shared(t)
+            self.O, self.L = [], []
+
+    def compute_only(self, i):
+        """This rank's (batch, kv head) units without the gather."""
+        units = self.B * self.Hkv
+        a, b = self.jb.dist_shard(units, self.world, self.dist.rank)
+        G = self.Hq // self.Hkv
+        v4 = lambda x, g: x.view(units, g, self.S, self.D)[a:b]
+        k = i % self.nsets
+        jb = self.jb
+        rc = jb.lib().jules_flash_attention_fwd(
+            jb._ptr(v4(self.Q[k], G)), jb._ptr(v4(self.Kt[k], 1)), jb._ptr(v4(self.V[k], 1)),
+            jb._ptr(v4(self.O[k], G)), jb._ptr(self.L[k].view(units, G, self.S)[a:b]), b - a, G, 1,
+            self.S, self.D, 0.0, 1, jb.DT_BF16, jb._stream(None))
+        jb._check(rc, "jules_flash_attention_fwd")
+
+    def e2e_dist_spec(self):
+        """N > 1: each step copies this rank's units of Q, K, V in, runs the
+        sharded call and rank 0 reads the whole O and lse back."""
+        t = self.torch
+        units = self.B * self.Hkv
+        a, b = self.jb.dist_shard(units, self.world, self.dist.rank)
+        G = self.Hq // self.Hkv
+        q = self.Q[0].view(units, G, self.S, self.D)
+        kv = lambda x: x.view(units, 1, self.S, self.D)
+        ins = [(q[a:b].cpu().pin_memory(), q[a:b]), (kv(self.Kt[0])[a:b].cpu().pin_memory(), kv(self.Kt[0])[a:b]),
+               (kv(self.V[0])[a:b].cpu().pin_memory(), kv(self.V[0])[a:b])]
+        outs = [(t.empty_like(self.O[0], device="cpu").pin_memory(), self.O[0]),
+                (t.empty_like(self.L[0], device="cpu").pin_memory(), self.L[0])]
+        run = lambda: self._run(self.Q[0], self.Kt[0], self.V[0], self.O[0], self.L[0])
+        return ins, outs, run
+
     def step(self, i, ev=None):
         k = i % self.nsets
         if ev:
             ev[0].record()
-        self.jb.flash_attention_fwd(self.Q[k], self.Kt[k], self.V[k], causal=True, out=self.O[k],
-                                    lse=False)
+        self._run(self.Q[k], self.Kt[k], self.V[k], self.O[k], self.L[k])
         if ev:
             ev[1].record()
 
@@ -414,11 +532,10 @@ class Attention(Workload):
         return self.O[i % self.nsets]
 
     def e2e_spec(self):
-        jb = self.jb
         h_in = [x[0].cpu().pin_memory() for x in (self.Q, self.Kt, self.V)]
-        h_out = [self.torch.empty_like(h_in[0]).pin_memory()]
-        return h_in, h_out, lambda d, o: jb.flash_attention_fwd(d[0], d[1], d[2], causal=True,
-                                                                 out=o[0], lse=False)
+        h_out = [self.torch.empty_like(h_in[0]).pin_memory(),
+                 self.torch.empty_like(self.L[0], device="cpu").pin_memory()]
+        return h_in, h_out, lambda d, o: self._run(d[0], d[1], d[2], o[0], o[1])
 
 
 class AttentionF32(Workload):
@@ -835,32 +952,42 @@ def run_reference_arm(args):
     rank, _, world = dist_env()
     if rank != 0:
         return 0
-    # Each step is one bounded sample of the workload on the CPU.
-    import numpy as np  # noqa: F401
-    vals = []
-    desc = ""
-    threads = os.cpu_count() or 1
-    for _ in range(args.warmup):
-        cpu_reference_sample(args.workload, reps=1, warm=0)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        v, desc, threads = cpu_reference_sample(args.workload, reps=1, warm=0)
-        vals.append(v)
-    wall = time.perf_counter() - t0
-    value = statistics.mean(vals)
-    rowwise = args.workload in ("softmax", "xent")
-    unit = "GB/s" if rowwise else ("TOPS" if args.workload == "int8" else "TFLOP/s")
-    metric = metric_for(args.workload)
-    line = {"metric": metric, "value": round(value, 6), "unit": unit,
+    headline = args.workload == "headline"
+    workload = "gemm" if headline else args.workload
+
+    def timed(wkey, steps, warmup):
+        """Each step is one bounded sample of the workload on the CPU."""
+        for _ in range(warmup):
+            cpu_reference_sample(wkey, reps=1, warm=0)
+        vals, desc, threads = [], "", os.cpu_count() or 1
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            v, desc, threads = cpu_reference_sample(wkey, reps=1, warm=0)
+            vals.append(v)
+        return statistics.mean(vals), (time.perf_counter() - t0) / steps, desc, threads
+
+    value, step_s, desc, threads = timed(workload, args.steps, args.warmup)
+    rowwise = workload in ("softmax", "xent")
+    unit = "GB/s" if rowwise else ("TOPS" if workload == "int8" else "TFLOP/s")
+    line = {"metric": metric_for(args.workload), "value": round(value, 6), "unit": unit,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(wall / args.steps * 1e3, 3), "higher_is_better": True,
+            "ms_per_step": round(step_s * 1e3, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": describe(args.workload, world, "CPU: bounded sample per step"),
+            "config": describe(workload, world, "CPU: bounded sample per step"),
             "impl": "reference",
             "cpu_baseline": {"value": round(value, 6), "unit": unit, "cores": threads,
-                             "kind": CPU_KIND.get(args.workload, "reference"), "sample": desc},
+                             "kind": CPU_KIND.get(workload, "reference"), "sample": desc},
             "e2e": {"value": round(value, 6), "unit": unit, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
+    if headline:
+        # the attention half (C3): a few samples, each ~1 s of CPU work
+        av, astep, adesc, athreads = timed("attn", 3, 1)
+        line["attn"] = {"value": round(av, 6), "unit": "TFLOP/s",
+                        "ms_per_step": round(astep * 1e3, 3), "steps": 3,
+                        "config": describe("attn", world, "CPU: bounded sample per step"),
+                        "cpu_baseline": {"value": round(av, 6), "unit": "TFLOP/s",
+                                         "cores": athreads, "kind": "reference",
+                                         "sample": adesc}}
     emit(line)
     return 0
 
@@ -894,111 +1021,168 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    W = {"gemm": lambda: Gemm(jb, torch, rank, world),
-         "attn": lambda: Attention(jb, torch, rank, world, gqa=False),
-         "attn_gqa": lambda: Attention(jb, torch, rank, world, gqa=True),
-         "mlp": lambda: Mlp(jb, torch, rank, world),
-         "attn_fp32": lambda: AttentionF32(jb, torch, rank, world),
-         "softmax": lambda: RowWise(jb, torch, rank, world, xent=False),
-         "xent": lambda: RowWise(jb, torch, rank, world, xent=True),
-         "int8": lambda: Int8Gemm(jb, torch, rank, world),
-         "fp8": lambda: Fp8Gemm(jb, torch, rank, world),
-         "attn_bwd": lambda: AttentionBwd(jb, torch, rank, world)}[args.workload]
-    wl = W()
-    stream = torch.cuda.current_stream()
+    # The communicator of the library's multi-GPU entry points (strong-scaled
+    # C2 / C3 / C5); torch.distributed above is the bench's own plumbing
+    # (barriers, max over ranks).
+    dist_comm = jb.Dist.from_torch() if world > 1 and args.workload in (
+        "headline", "gemm", "attn", "attn_gqa") else None
 
-    for i in range(args.warmup):
-        wl.step(i)
-    torch.cuda.synchronize()
-    if jb.device_error() != 0:
-        raise RuntimeError("device error during warm-up")
+    def make(workload):
+        return {"gemm": lambda: Gemm(jb, torch, rank, world, dist=dist_comm),
+                "attn": lambda: Attention(jb, torch, rank, world, gqa=False, dist=dist_comm),
+                "attn_gqa": lambda: Attention(jb, torch, rank, world, gqa=True, dist=dist_comm),
+                "mlp": lambda: Mlp(jb, torch, rank, world),
+                "attn_fp32": lambda: AttentionF32(jb, torch, rank, world),
+                "softmax": lambda: RowWise(jb, torch, rank, world, xent=False),
+                "xent": lambda: RowWise(jb, torch, rank, world, xent=True),
+                "int8": lambda: Int8Gemm(jb, torch, rank, world),
+                "fp8": lambda: Fp8Gemm(jb, torch, rank, world),
+                "attn_bwd": lambda: AttentionBwd(jb, torch, rank, world)}[workload]()
 
-    # ---------------- timed region (device) ----------------
-    K = args.steps
-    dom = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(K)]
-    sampler = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
-                           else local_rank)
-    barrier()
-    torch.cuda.synchronize()
-    sampler.start()
-    t_begin = torch.cuda.Event(enable_timing=True)
-    t_end = torch.cuda.Event(enable_timing=True)
-    t_begin.record(stream)
-    for i in range(K):
-        wl.step(i, dom[i])
-    t_end.record(stream)
-    torch.cuda.synchronize()
-    barrier()
-    clocks = sampler.stop()
-    ms_total = max_over_ranks(t_begin.elapsed_time(t_end))
-    dom_ms = statistics.mean(a.elapsed_time(b) for a, b in dom)
-    dom_ms = max_over_ranks(dom_ms)
-    if jb.device_error() != 0:
-        raise RuntimeError("device error in timed region")
+    def measure(workload):
+        """Warm-up, the K timed steps, the gather, e2e and the CPU leg of one
+        workload; returns the fields of its JSON object."""
+        wl = make(workload)
+        stream = torch.cuda.current_stream()
+        for i in range(args.warmup):
+            wl.step(i)
+        torch.cuda.synchronize()
+        if jb.device_error() != 0:
+            raise RuntimeError(f"device error during warm-up ({workload})")
 
-    tflops_total = wl.flops_per_step * world * K / (ms_total * 1e-3) / wl.unit_scale
-    peak, hbm, peak_kind = measured_peaks()
-    achieved = wl.flops_dominant / (dom_ms * 1e-3) / wl.unit_scale
-    traffic = profiled_traffic(args.workload)
-
-    # ---------------- output gather (N > 1), timed separately ----------------
-    gather = None
-    if world > 1:
-        out = wl.output(0).contiguous()
-        full = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device="cuda")
-        dist.all_gather_into_tensor(full, out)  # warm
+        # ---------------- timed region (device) ----------------
+        K = args.steps
+        dom = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(K)]
+        sampler = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
+                               else local_rank)
+        barrier()
+        torch.cuda.synchronize()
+        sampler.start()
+        t_begin = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_begin.record(stream)
+        for i in range(K):
+            wl.step(i, dom[i])
+        t_end.record(stream)
         torch.cuda.synchronize()
         barrier()
-        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        g0.record()
-        dist.all_gather_into_tensor(full, out)
-        g1.record()
-        torch.cuda.synchronize()
-        gms = max_over_ranks(g0.elapsed_time(g1))
-        gather = {"collective": "ncclAllGather of each rank's output shard (not in value)",
-                  "bytes_per_rank": out.numel() * out.element_size(), "ms": round(gms, 4)}
-        del full
+        clocks = sampler.stop()
+        ms_total = max_over_ranks(t_begin.elapsed_time(t_end))
+        dom_ms = statistics.mean(a.elapsed_time(b) for a, b in dom)
+        dom_ms = max_over_ranks(dom_ms)
+        if jb.device_error() != 0:
+            raise RuntimeError(f"device error in timed region ({workload})")
 
-    # ---------------- e2e through the C ABI with host buffers ----------------
-    e2e = None
-    if not args.no_e2e:
-        pipe = E2EPipeline(torch, wl)
-        for _ in range(3):
-            pipe.step()
-        torch.cuda.synchronize()
-        Ke = max(4, min(K, 10))
-        barrier()
-        ems = max_over_ranks(pipe.time_steps(Ke))
-        barrier()
-        e2e = {"value": round(wl.flops_per_step * world * Ke / (ems * 1e-3) / wl.unit_scale, 3),
-               "unit": wl.unit, "h2d_bytes_per_step": int(pipe.h2d),
-               "d2h_bytes_per_step": int(pipe.d2h), "steps": Ke,
-               "path": "pinned host -> cudaMemcpyAsync (H2D stream) -> public API (compute stream) "
-                       "-> cudaMemcpyAsync (D2H stream) -> host; 2 buffer sets, consecutive steps "
-                       "overlapped"}
-        del pipe
+        strong = getattr(wl, "global_work", False)
+        per_job = 1 if strong else world  # flops_per_step is the whole job's when strong
+        tflops_total = wl.flops_per_step * per_job * K / (ms_total * 1e-3) / wl.unit_scale
+        peak, hbm, peak_kind = measured_peaks()
+        achieved = wl.flops_dominant / (dom_ms * 1e-3) / wl.unit_scale
+        traffic = profiled_traffic(workload)
 
-    # ---------------- CPU baseline (rank 0, N == 1) ----------------
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        try:
-            v, desc, threads = cpu_reference_sample(args.workload)
-            cpu = {"value": round(v, 6), "unit": wl.unit, "cores": threads,
-                   "kind": CPU_KIND.get(args.workload, "reference"), "sample": desc}
-        except Exception as ex:  # the GPU number stands without it
-            cpu = {"value": None, "unit": wl.unit, "cores": None, "kind": "reference",
-                   "sample": f"unavailable: {ex}"}
+        # ---------------- output gather (N > 1), timed separately ----------------
+        gather = None
+        compute_only = None
+        if world > 1 and strong:
+            # the same steps without the gather: this rank's share of the work alone
+            for i in range(3):
+                wl.compute_only(i)
+            torch.cuda.synchronize()
+            barrier()
+            c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            c0.record(stream)
+            for i in range(K):
+                wl.compute_only(i)
+            c1.record(stream)
+            torch.cuda.synchronize()
+            cms = max_over_ranks(c0.elapsed_time(c1))
+            compute_only = {"value": round(wl.flops_per_step * K / (cms * 1e-3) / wl.unit_scale, 3),
+                            "ms_per_step": round(cms / K, 5),
+                            "what": "each rank's share without the gather (max over ranks)"}
+        elif world > 1:
+            out = wl.output(0).contiguous()
+            full = torch.empty((world,) + tuple(out.shape), dtype=out.dtype, device="cuda")
+            dist.all_gather_into_tensor(full, out)  # warm
+            torch.cuda.synchronize()
+            barrier()
+            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            g0.record()
+            dist.all_gather_into_tensor(full, out)
+            g1.record()
+            torch.cuda.synchronize()
+            gms = max_over_ranks(g0.elapsed_time(g1))
+            gather = {"collective": "ncclAllGather of each rank's output shard (not in value)",
+                      "bytes_per_rank": out.numel() * out.element_size(), "ms": round(gms, 4)}
+            del full
 
-    if rank == 0:
-        line = {
-            "metric": metric_for(args.workload),
+        # ---------------- e2e through the C ABI with host buffers ----------------
+        e2e = None
+        if not args.no_e2e and world > 1 and strong:
+            ins, outs, run = wl.e2e_dist_spec()
+
+            def e2e_step():
+                for h, d in ins:
+                    d.copy_(h, non_blocking=True)
+                run()
+                if rank == 0:
+                    for h, d in outs:
+                        h.copy_(d, non_blocking=True)
+
+            for _ in range(3):
+                e2e_step()
+            torch.cuda.synchronize()
+            Ke = max(4, min(K, 10))
+            barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(Ke):
+                e2e_step()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ems = max_over_ranks(e0.elapsed_time(e1))
+            barrier()
+            h2d = sum(h.numel() * h.element_size() for h, _ in ins) * world  # all ranks' inputs
+            d2h = sum(h.numel() * h.element_size() for h, _ in outs)         # rank 0 reads the result
+            e2e = {"value": round(wl.flops_per_step * Ke / (ems * 1e-3) / wl.unit_scale, 3),
+                   "unit": wl.unit, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                   "steps": Ke,
+                   "path": "each rank: pinned host -> cudaMemcpyAsync of its shard of the inputs -> "
+                           "sharded public API call (gather included) -> rank 0 cudaMemcpyAsync of "
+                           "the whole result -> host; one stream; replicated weights resident"}
+        elif not args.no_e2e:
+            pipe = E2EPipeline(torch, wl)
+            for _ in range(3):
+                pipe.step()
+            torch.cuda.synchronize()
+            Ke = max(4, min(K, 10))
+            barrier()
+            ems = max_over_ranks(pipe.time_steps(Ke))
+            barrier()
+            e2e = {"value": round(wl.flops_per_step * world * Ke / (ems * 1e-3) / wl.unit_scale, 3),
+                   "unit": wl.unit, "h2d_bytes_per_step": int(pipe.h2d),
+                   "d2h_bytes_per_step": int(pipe.d2h), "steps": Ke,
+                   "path": "pinned host -> cudaMemcpyAsync (H2D stream) -> public API (compute "
+                           "stream) -> cudaMemcpyAsync (D2H stream) -> host; 2 buffer sets, "
+                           "consecutive steps overlapped"}
+            del pipe
+
+        # ---------------- CPU baseline (rank 0, N == 1) ----------------
+        cpu = None
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            try:
+                v, desc, threads = cpu_reference_sample(workload)
+                cpu = {"value": round(v, 6), "unit": wl.unit, "cores": threads,
+                       "kind": CPU_KIND.get(workload, "reference"), "sample": desc}
+            except Exception as ex:  # the GPU number stands without it
+                cpu = {"value": None, "unit": wl.unit, "cores": None, "kind": "reference",
+                       "sample": f"unavailable: {ex}"}
+
+        res = {
             "value": round(tflops_total, 3), "unit": wl.unit,
-            "n_gpus": world, "steps": K, "warmup": args.warmup,
-            "ms_per_step": round(ms_total / K, 5), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32" if args.workload == "attn_fp32" else wl.dtype,
-            "data": "synthetic (seeded; config shapes and distributions)",
-            "config": describe(args.workload, world, wl.config.get("l2")),
+            "ms_per_step": round(ms_total / K, 5),
+            "dtype": "f32" if workload == "attn_fp32" else wl.dtype,
+            "config": describe(workload, world, wl.config.get("l2")),
             "roofline": roofline(wl, achieved, peak, peak_kind, traffic),
             **({"pct_of_dense_bf16_peak_2250": round(100 * tflops_total / world / 2250.0, 2)}
                if wl.unit == "TFLOP/s" and not isinstance(wl, (Fp8Gemm, AttentionF32)) else {}),
@@ -1006,10 +1190,46 @@ def main():
             "e2e": e2e,
             "gpu_launches": K * wl.launches_per_step,
             "cpu_baseline": cpu,
+            "scaling": "strong" if strong else "weak",
         }
         if gather:
-            line["gather"] = gather
+            res["gather"] = gather
+        if compute_only:
+            res["compute_only"] = compute_only
+        if hasattr(wl, "release"):
+            torch.cuda.synchronize()
+            barrier()
+            wl.release()
+        del wl
+        torch.cuda.empty_cache()
+        return res
+
+    headline = args.workload == "headline"
+    main_res = measure("gemm" if headline else args.workload)
+    attn_res = measure("attn") if headline else None
+    if rank == 0:
+        line = {"metric": metric_for(args.workload), "value": main_res["value"],
+                "unit": main_res["unit"], "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": main_res["ms_per_step"],
+                "higher_is_better": True, "scaling": main_res["scaling"], "vs_baseline": None,
+                "dtype": main_res["dtype"],
+                "data": "synthetic (seeded; config shapes and distributions)"}
+        for k in ("config", "roofline", "pct_of_dense_bf16_peak_2250", "clocks", "e2e",
+                  "gpu_launches", "cpu_baseline", "gather", "compute_only"):
+            if k in main_res:
+                line[k] = main_res[k]
+        if attn_res:
+            # The attention half of the headline metric (config C3), measured in
+            # the same process right after the GEMM half; the line's own
+            # gpu_launches counts both.
+            line["gpu_launches"] += attn_res["gpu_launches"]
+            line["attn"] = {k: v for k, v in attn_res.items() if k not in ("dtype",)}
         emit(line)
+
+    if dist_comm is not None:
+        torch.cuda.synchronize()
+        barrier()
+        dist_comm.close()
 
     if world > 1:
         barrier()

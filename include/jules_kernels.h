@@ -39,6 +39,7 @@ extern "C" {
 #define JULES_ERR_ARG 6         /* NULL pointer or bad enum */
 #define JULES_ERR_UNSUPPORTED 7 /* name known but not implemented */
 #define JULES_ERR_WORKSPACE 8   /* caller workspace too small */
+#define JULES_ERR_COMM 9        /* NCCL missing or a collective failed */
 
 /* Element types. */
 #define JULES_DTYPE_F32 0
@@ -335,6 +336,73 @@ int jules_kernel_by_name(const char* name);
 const char* jules_kernel_name(int id);
 int jules_kernel_count(void);
 int jules_kernel_implemented(int id);
+
+/*
+ * ---------------------------------------------------------------------------
+ * Multi-GPU: one process per GPU (1 <= world <= 8, one node).  The hot path is
+ * split into independent units - token rows of the GEMM, (batch, kv head)
+ * units of attention - and the outputs are gathered over NVLink, the one
+ * exchange the partition needs.  The reference names that exchange only as an
+ * IR collective (include/jules/Dialect/JulesOps.td:660-684, lowering in
+ * lib/Passes/StableHLOLowering.cpp:1100-1170 that never runs); these entry
+ * points are what a dispatch table binds for it.  NCCL is loaded at run time
+ * (libnccl.so.2); without it these calls return JULES_ERR_COMM.
+ *
+ * All dist calls are collective: every rank makes the same calls in the same
+ * order, with the same shapes.  Buffers use the single-GPU layouts; each rank
+ * reads only its own units of the inputs and every rank's output holds the
+ * whole result when the call's work on `stream` has finished.
+ * ---------------------------------------------------------------------------
+ */
+#define JULES_DIST_ID_BYTES 128
+
+/* Balanced contiguous partition: rank's units are [*begin, *end) of units. */
+int jules_dist_shard(int64_t units, int world, int rank, int64_t* begin, int64_t* end);
+
+/* Rank 0 creates the id (JULES_DIST_ID_BYTES bytes) and passes it to every
+ * rank out of band; each rank then calls jules_dist_init with its own device
+ * current.  jules_dist_destroy releases the communicator and its buffers. */
+int jules_dist_unique_id(void* id);
+int jules_dist_init(void** comm, int world, int rank, const void* id);
+int jules_dist_destroy(void* comm);
+
+/* Stream-ordered barrier over all ranks (an 8-byte all-reduce). */
+int jules_dist_barrier(void* comm, void* stream);
+
+/* Output buffer that every rank can write: each rank allocates `bytes`, and
+ * the peers' buffers are mapped into every process (CUDA IPC, handles
+ * exchanged over the communicator).  Collective.  The memory is zeroed. */
+int jules_dist_alloc_shared(void* comm, size_t bytes, void** local);
+int jules_dist_free_shared(void* comm, void* local);
+
+/*
+ * Sharded jules_gemm_bias_act: rank r computes rows jules_dist_shard(M) of
+ * C = act(A . W + bias) (+ residual) from its rows of A (and residual); W and
+ * bias are replicated.  When C comes from jules_dist_alloc_shared (bf16
+ * operands, N % 8 == 0, K % 8 == 0, M / world >= 256, N >= 256), the gather
+ * is fused into the GEMM: the epilogue stores every finished tile into all
+ * ranks' C over NVLink while later tiles compute, then the ranks signal each
+ * other through counters in peer memory (a bounded wait; an expired wait
+ * reports JULES_ERR_TIMEOUT through jules_device_error).  Otherwise the rows
+ * are computed locally and gathered with an in-place ncclAllGather.
+ * Replaces tiledMatmulWithActivation (FusedKernels.h:378-458) run across the
+ * GPUs of one node.
+ */
+int jules_dist_gemm_bias_act(void* comm, const void* A, const void* W, const float* bias,
+                             const void* residual, void* C, int64_t M, int64_t N, int64_t K,
+                             int act, int in_dtype, int out_dtype, void* stream);
+
+/*
+ * Sharded jules_flash_attention_fwd: the B x Hkv (batch, kv head) units are
+ * split evenly over the ranks (B * Hkv % world == 0, and each rank's units
+ * whole batches or a part of one); each rank computes O (and lse) of its
+ * units, then O and lse are gathered in place with ncclAllGather.
+ * Replaces flashAttention (FlashAttention.h:130-309) run across the GPUs of
+ * one node.
+ */
+int jules_dist_flash_attention_fwd(void* comm, const void* Q, const void* K, const void* V, void* O,
+                                   float* lse, int B, int Hq, int Hkv, int S, int D, float scale,
+                                   int causal, int dtype, void* stream);
 
 #ifdef __cplusplus
 }

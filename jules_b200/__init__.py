@@ -19,6 +19,7 @@ __all__ = [
     "mlp_block", "mlp_block_workspace_bytes", "sgemm", "device_error", "kernel_by_name",
     "kernel_names", "LIB_PATH", "gemm_fp8", "cast", "matmul_int8", "softmax",
     "cross_entropy_loss", "custom_call", "mlp_fwd_bwd", "flash_attention_bwd", "attention",
+    "Dist",
 ]
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libjules_b200.so")
@@ -67,6 +68,18 @@ _SIGNATURES = {
     "jules_kernel_name": ([_c_int], ctypes.c_char_p),
     "jules_kernel_count": ([], _c_int),
     "jules_kernel_implemented": ([_c_int], _c_int),
+    "jules_dist_shard": ([_c_i64, _c_int, _c_int, ctypes.POINTER(_c_i64), ctypes.POINTER(_c_i64)],
+                         _c_int),
+    "jules_dist_unique_id": ([_c_vp], _c_int),
+    "jules_dist_init": ([ctypes.POINTER(_c_vp), _c_int, _c_int, _c_vp], _c_int),
+    "jules_dist_destroy": ([_c_vp], _c_int),
+    "jules_dist_barrier": ([_c_vp, _c_vp], _c_int),
+    "jules_dist_alloc_shared": ([_c_vp, ctypes.c_size_t, ctypes.POINTER(_c_vp)], _c_int),
+    "jules_dist_free_shared": ([_c_vp, _c_vp], _c_int),
+    "jules_dist_gemm_bias_act": ([_c_vp] * 6 + [_c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int,
+                                                _c_vp], _c_int),
+    "jules_dist_flash_attention_fwd": ([_c_vp] * 6 + [_c_int] * 5 + [_c_f, _c_int, _c_int, _c_vp],
+                                       _c_int),
 }
 
 
@@ -457,3 +470,119 @@ def kernel_by_name(name: str) -> int:
 def kernel_names():
     h = lib()
     return [h.jules_kernel_name(i).decode() for i in range(h.jules_kernel_count())]
+
+
+# ---------------------------------------------------------------------------
+# Multi-GPU (one process per GPU): the jules_dist_* entry points.
+# ---------------------------------------------------------------------------
+DIST_ID_BYTES = 128
+
+
+def dist_shard(units: int, world: int, rank: int) -> tuple[int, int]:
+    """[begin, end) of `units` owned by `rank` (the library's partition)."""
+    b, e = _c_i64(0), _c_i64(0)
+    _check(lib().jules_dist_shard(units, world, rank, ctypes.byref(b), ctypes.byref(e)),
+           "jules_dist_shard")
+    return b.value, e.value
+
+
+class _DevArray:
+    """__cuda_array_interface__ over library-owned device memory."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+
+class Dist:
+    """A communicator of the multi-GPU entry points.  Every rank constructs
+    one with the same id (see unique_id / from_torch) and its own device
+    current; all methods are collective."""
+
+    def __init__(self, world: int, rank: int, uid: bytes):
+        self.world, self.rank = world, rank
+        self.h = _c_vp()
+        buf = ctypes.create_string_buffer(bytes(uid), DIST_ID_BYTES)
+        _check(lib().jules_dist_init(ctypes.byref(self.h), world, rank, buf), "jules_dist_init")
+        self._shared = {}
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(DIST_ID_BYTES)
+        _check(lib().jules_dist_unique_id(buf), "jules_dist_unique_id")
+        return buf.raw
+
+    @classmethod
+    def from_torch(cls, group=None):
+        """Rank 0's id sent to all ranks over an initialised torch.distributed
+        group (plumbing only)."""
+        import torch.distributed as tdist
+        obj = [cls.unique_id() if tdist.get_rank(group) == 0 else None]
+        tdist.broadcast_object_list(obj, src=0, group=group)
+        return cls(tdist.get_world_size(group), tdist.get_rank(group), obj[0])
+
+    def close(self):
+        if self.h:
+            lib().jules_dist_destroy(self.h)
+            self.h = _c_vp()
+            self._shared.clear()
+
+    def barrier(self, stream=None):
+        _check(lib().jules_dist_barrier(self.h, _stream(stream)), "jules_dist_barrier")
+
+    def alloc_shared(self, shape, dtype):
+        """A zeroed tensor whose memory every rank can write (the output of a
+        fused-gather call).  Valid until free_shared / close."""
+        import torch
+        elt = torch.empty((), dtype=dtype).element_size()
+        n = 1
+        for d in shape:
+            n *= int(d)
+        p = _c_vp()
+        _check(lib().jules_dist_alloc_shared(self.h, max(n * elt, 16), ctypes.byref(p)),
+               "jules_dist_alloc_shared")
+        code = {1: "|u1", 2: "<i2", 4: "<f4"}[elt]
+        t = torch.as_tensor(_DevArray(p.value, shape, code))
+        if t.dtype != dtype:
+            t = t.view(dtype)
+        self._shared[p.value] = t
+        return t
+
+    def free_shared(self, t):
+        ptr = t.data_ptr()
+        self._shared.pop(ptr, None)
+        _check(lib().jules_dist_free_shared(self.h, _c_vp(ptr)), "jules_dist_free_shared")
+
+    def gemm_bias_act(self, A, W, bias=None, residual=None, act="none", out=None, out_dtype=None,
+                      stream=None):
+        """Sharded jules_gemm_bias_act: this rank computes its rows of C and every
+        rank's `out` holds the whole C afterwards (fused gather when `out` came
+        from alloc_shared)."""
+        import torch
+        _dense(A, "A"), _dense(W, "W")
+        M, K = A.shape
+        N = W.shape[1]
+        if out is None:
+            out = torch.empty((M, N), dtype=out_dtype or A.dtype, device=A.device)
+        rc = lib().jules_dist_gemm_bias_act(self.h, _ptr(A), _ptr(W), _ptr(bias), _ptr(residual),
+                                            _ptr(out), M, N, K,
+                                            ACT[act] if isinstance(act, str) else int(act),
+                                            _dtype_code(A), _dtype_code(out), _stream(stream))
+        _check(rc, "jules_dist_gemm_bias_act")
+        return out
+
+    def flash_attention_fwd(self, Q, K, V, causal=False, scale=0.0, out=None, lse=None,
+                            stream=None):
+        """Sharded jules_flash_attention_fwd over (batch, kv head) units; every
+        rank's `out` (and `lse`) holds the whole result afterwards."""
+        import torch
+        B, Hq, S, D = Q.shape
+        Hkv = K.shape[1]
+        if out is None:
+            out = torch.empty_like(Q)
+        rc = lib().jules_dist_flash_attention_fwd(self.h, _ptr(Q), _ptr(K), _ptr(V), _ptr(out),
+                                                  _ptr(lse), B, Hq, Hkv, S, D, float(scale),
+                                                  int(bool(causal)), _dtype_code(Q),
+                                                  _stream(stream))
+        _check(rc, "jules_dist_flash_attention_fwd")
+        return out, lse

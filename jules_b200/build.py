@@ -60,7 +60,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
         subprocess.run(cmd, check=True)
         objs.append(obj)
     tmp = LIB + ".tmp"
-    cmd = [nvcc()] + ARCH + ["-shared", "-o", tmp] + objs
+    cmd = [nvcc()] + ARCH + ["-shared", "-o", tmp] + objs + ["-ldl"]
     subprocess.run(cmd, check=True)
     os.replace(tmp, LIB)
     for o in objs:

@@ -60,6 +60,16 @@ constexpr int kWarpMma = 9;
 constexpr int kChunk = 128 * 64 * 2;  // one 64-dim (128 B) swizzled box of 128 rows
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
+// Where the epilogue writes O and lse: the local buffers (index 0) and, for
+// the sharded call with the gather fused in, the same (b, h) rows of every
+// other rank's buffers mapped into this process.  lse entries are null when
+// no logsumexp is wanted.
+struct AttnOut {
+  __nv_bfloat16* o[kMaxPeers];
+  float* lse[kMaxPeers];
+  int n;
+};
+
 struct Smem {
   alignas(1024) uint8_t q[NQT][2][kChunk];
   alignas(1024) uint8_t k[KVS][2][kChunk];
@@ -67,6 +77,9 @@ struct Smem {
   uint64_t q_full, q_empty;
   uint64_t k_full[KVS], k_empty[KVS];
   uint64_t v_full[KVS], v_empty[KVS];
+  // Epilogue staging, 2 KB per softmax warp: 32 rows x 64 bytes (32 bf16
+  // columns of O), 16-byte chunks XOR-swizzled by (row >> 1) & 3.
+  alignas(128) uint4 epi[8][32 * 4];
   uint64_t s_full[NQT], p_full[NQT], o_full[NQT], o_empty[NQT];
   uint32_t tmem_base;
   int abort_flag;
@@ -152,9 +165,8 @@ __device__ __forceinline__ void tmem_ld32_at(uint32_t taddr, uint32_t* r) {
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                        const __grid_constant__ CUtensorMap tmK,
-                       const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O,
-                       float* __restrict__ lse, int B, int Hq, int Hkv, int S, float scale_log2,
-                       int causal) {
+                       const __grid_constant__ CUtensorMap tmV, const AttnOut out, int B,
+                       int Hq, int Hkv, int S, float scale_log2, int causal) {
   extern __shared__ uint8_t smem_raw[];
   Smem& s = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                      ~uintptr_t(1023));
@@ -443,34 +455,57 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ----- epilogue: O / l -> bf16, lse -----
       if (!mbar_wait(&s.o_full[t], wi & 1u, 32, abort_flag)) break;
       tc_fence_after();
+      // O / l as bf16, 32 columns at a time through shared memory: lane t
+      // holds row t after tcgen05.ld, and after the exchange 4 lanes write
+      // 64 contiguous bytes of one row (8 rows per store instruction), to
+      // the local O and, when the gather is fused in, every rank's O.
       const float inv_l = 1.0f / l_run;
       const bool row_ok = q < S;
-      __nv_bfloat16* orow = O + ((size_t)bh * S + (row_ok ? q : 0)) * HD;
+      const int row0 = qt0 + quarter * 32;  // first row of this warp
+      uint4* stg = s.epi[warp];
 #pragma unroll 1
       for (int c = 0; c < HD; c += 32) {
         uint32_t o[32];
         tmem_ld32(tO + c, o);
         tmem_ld_wait(o);
-        if (row_ok) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c);
 #pragma unroll
-          for (int g8 = 0; g8 < 4; ++g8) {
-            uint4 v;
-            v.x = pack_bf16x2(__uint_as_float(o[8 * g8 + 0]) * inv_l, __uint_as_float(o[8 * g8 + 1]) * inv_l);
-            v.y = pack_bf16x2(__uint_as_float(o[8 * g8 + 2]) * inv_l, __uint_as_float(o[8 * g8 + 3]) * inv_l);
-            v.z = pack_bf16x2(__uint_as_float(o[8 * g8 + 4]) * inv_l, __uint_as_float(o[8 * g8 + 5]) * inv_l);
-            v.w = pack_bf16x2(__uint_as_float(o[8 * g8 + 6]) * inv_l, __uint_as_float(o[8 * g8 + 7]) * inv_l);
-            dst[g8] = v;
+        for (int g8 = 0; g8 < 4; ++g8) {
+          uint4 v;
+          v.x = pack_bf16x2(__uint_as_float(o[8 * g8 + 0]) * inv_l, __uint_as_float(o[8 * g8 + 1]) * inv_l);
+          v.y = pack_bf16x2(__uint_as_float(o[8 * g8 + 2]) * inv_l, __uint_as_float(o[8 * g8 + 3]) * inv_l);
+          v.z = pack_bf16x2(__uint_as_float(o[8 * g8 + 4]) * inv_l, __uint_as_float(o[8 * g8 + 5]) * inv_l);
+          v.w = pack_bf16x2(__uint_as_float(o[8 * g8 + 6]) * inv_l, __uint_as_float(o[8 * g8 + 7]) * inv_l);
+          stg[lane * 4 + (g8 ^ ((lane >> 1) & 3))] = v;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int rr = (lane >> 2) + 8 * i;
+          if (row0 + rr < S) {
+            const uint4 v = stg[rr * 4 + ((lane & 3) ^ ((rr >> 1) & 3))];
+            const size_t off = ((size_t)bh * S + row0 + rr) * HD + c + (lane & 3) * 8;
+#pragma unroll
+            for (int p = 0; p < kMaxPeers; ++p)
+              if (p < out.n) *reinterpret_cast<uint4*>(out.o[p] + off) = v;
           }
         }
+        __syncwarp();
       }
-      if (lse && row_ok) lse[(size_t)bh * S + q] = (m_run + log2f(l_run)) * 0.69314718055994531f;
+      if (out.lse[0] && row_ok) {
+        const float l = (m_run + log2f(l_run)) * 0.69314718055994531f;
+#pragma unroll
+        for (int p = 0; p < kMaxPeers; ++p)
+          if (p < out.n) out.lse[p][(size_t)bh * S + q] = l;
+      }
       tc_fence_before();
       mbar_arrive(&s.o_empty[t]);
       pvc += n_kv;
     }
   }
 
+  // Peer stores must be visible system-wide before this rank signals the
+  // others that its units are in place (dist_signal_wait_kernel).
+  if (out.n > 1) __threadfence_system();
   __syncwarp();
   tc_fence_before();
   __syncthreads();

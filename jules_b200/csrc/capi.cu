@@ -180,10 +180,12 @@ int gemm_tc(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
 }
 
 // CTA-pair tcgen05 GEMM (256 x 256 tiles, cluster of 2).
+// out: the local C, or every rank's C for the sharded GEMM with the gather
+// fused into the epilogue (M = this rank's rows).
 template <int TN, typename TOut>
 int gemm_tc2(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
-             const __nv_bfloat16* res, TOut* C, int64_t M, int64_t N, int64_t K, int act,
-             cudaStream_t st) {
+             const __nv_bfloat16* res, const jb::gemm::OutDest<TOut>& out, int64_t M, int64_t N,
+             int64_t K, int act, cudaStream_t st) {
   int dev;
   if (int rc = current_device(&dev)) return rc;
   CUtensorMap ta, tw;
@@ -234,8 +236,8 @@ int gemm_tc2(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
   const int units = (int)(whole + 2 * (tiles - whole));
   const int pairs = units < max_pairs ? units : max_pairs;
   cfg.gridDim = dim3(2 * pairs);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tw, bias, res, C, (int)M, (int)N, (int)K, act,
-                                     whole, units);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tw, bias, res, out, (int)M, (int)N, (int)K,
+                                     act, whole, units);
   if (e != cudaSuccess) return cuda_fail(e, "gemm_bf16_tc2_kernel launch");
   return check_launch("gemm_bf16_tc2_kernel launch");
 }
@@ -249,7 +251,11 @@ int gemm_tc_dispatch(const __nv_bfloat16* A, const __nv_bfloat16* W, const float
                      const __nv_bfloat16* res, TOut* C, int64_t M, int64_t N, int64_t K, int act,
                      cudaStream_t st) {
   if (M < 256 || N < 256) return gemm_tc(A, W, bias, res, C, M, N, K, act, st);
-  return gemm_tc2<256>(A, W, bias, res, C, M, N, K, act, st);
+  jb::gemm::OutDest<TOut> out{};
+  out.c[0] = C;
+  out.n = 1;
+  out.row_off = 0;
+  return gemm_tc2<256>(A, W, bias, res, out, M, N, K, act, st);
 }
 
 template <typename TIn, typename TOut>
@@ -317,8 +323,10 @@ int attn_simt(const void* Q, const void* K, const void* V, void* O, float* lse, 
   return attn_simt_launch<T, T, 8>(Q, K, V, O, lse, B, Hq, Hkv, S, D, scale, causal, st);
 }
 
-int attn_tc(const void* Q, const void* K, const void* V, void* O, float* lse, int B, int Hq, int Hkv,
-            int S, int D, float scale, int causal, cudaStream_t st) {
+// out: the local O / lse, or every rank's for the sharded call with the
+// gather fused in (B, Hq, Hkv: this rank's units).
+int attn_tc(const void* Q, const void* K, const void* V, const jb::attn::AttnOut& out, int B, int Hq,
+            int Hkv, int S, int D, float scale, int causal, cudaStream_t st) {
   int dev;
   if (int rc = current_device(&dev)) return rc;
   CUtensorMap tq, tk, tv;
@@ -348,8 +356,7 @@ int attn_tc(const void* Q, const void* K, const void* V, void* O, float* lse, in
   const int64_t work = (int64_t)n_pairs * B * Hq;
   const int grid = (int)(work < device_sms(dev) ? work : device_sms(dev));
   const float scale_log2 = scale * 1.4426950408889634f;
-  kern<<<grid, jb::attn::kThreads, smem, st>>>(tq, tk, tv, static_cast<__nv_bfloat16*>(O), lse, B,
-                                               Hq, Hkv, S, scale_log2, causal);
+  kern<<<grid, jb::attn::kThreads, smem, st>>>(tq, tk, tv, out, B, Hq, Hkv, S, scale_log2, causal);
   return check_launch("attn_fwd_tc_kernel launch");
 }
 
@@ -461,6 +468,8 @@ __global__ void wait_selftest_kernel(uint64_t limit_ns) {
 }
 
 }  // namespace
+
+#include "dist.cuh"
 
 // ===========================================================================
 // Exported C ABI
@@ -681,6 +690,7 @@ const char* jules_status_string(int s) {
     case JULES_ERR_ARG: return "bad argument";
     case JULES_ERR_UNSUPPORTED: return "not implemented";
     case JULES_ERR_WORKSPACE: return "workspace too small";
+    case JULES_ERR_COMM: return "collective communication error";
     default: return "unknown status";
   }
 }
@@ -773,8 +783,13 @@ int jules_flash_attention_fwd(const void* Q, const void* K, const void* V, void*
   if (dtype == JULES_DTYPE_F32)
     return attn_simt<float>(Q, K, V, O, lse, B, Hq, Hkv, S, D, scale, causal ? 1 : 0, st);
   if (dtype != JULES_DTYPE_BF16) return fail(JULES_ERR_DTYPE, "attention: dtype %d", dtype);
-  if (D == jb::attn::HD && aligned16(Q) && aligned16(K) && aligned16(V) && aligned16(O))
-    return attn_tc(Q, K, V, O, lse, B, Hq, Hkv, S, D, scale, causal ? 1 : 0, st);
+  if (D == jb::attn::HD && aligned16(Q) && aligned16(K) && aligned16(V) && aligned16(O)) {
+    jb::attn::AttnOut out{};
+    out.o[0] = static_cast<__nv_bfloat16*>(O);
+    out.lse[0] = lse;
+    out.n = 1;
+    return attn_tc(Q, K, V, out, B, Hq, Hkv, S, D, scale, causal ? 1 : 0, st);
+  }
   return attn_simt<__nv_bfloat16>(Q, K, V, O, lse, B, Hq, Hkv, S, D, scale, causal ? 1 : 0, st);
 }
 
@@ -1204,6 +1219,261 @@ int jules_mlp_block_noalloc(const void* X, const float* gamma, const float* beta
     return rc;
   return jules_gemm_bias_act(hid, W2, b2, X, out, T, d, dff, JULES_ACT_NONE, JULES_DTYPE_BF16,
                              out_dtype, stream);
+}
+
+}  // extern "C"
+
+// ===========================================================================
+// Multi-GPU entry points (dist.cuh).
+// ===========================================================================
+extern "C" {
+
+int jules_dist_shard(int64_t units, int world, int rank, int64_t* begin, int64_t* end) {
+  if (!begin || !end) return fail(JULES_ERR_ARG, "dist_shard: NULL output");
+  if (units < 0 || world <= 0 || rank < 0 || rank >= world)
+    return fail(JULES_ERR_ARG, "dist_shard: units=%lld world=%d rank=%d", (long long)units, world, rank);
+  const int64_t base = units / world, extra = units % world;
+  *begin = rank * base + (rank < extra ? rank : extra);
+  *end = *begin + base + (rank < extra ? 1 : 0);
+  return ok();
+}
+
+int jules_dist_unique_id(void* id) {
+  if (!id) return fail(JULES_ERR_ARG, "dist_unique_id: NULL");
+  if (int rc = need_nccl()) return rc;
+  ncclUniqueId u;
+  ncclResult_t r = nccl().get_unique_id(&u);
+  if (r != ncclSuccess) return nccl_fail(r, "ncclGetUniqueId");
+  static_assert(sizeof(u) == JULES_DIST_ID_BYTES, "NCCL unique id size");
+  std::memcpy(id, &u, sizeof(u));
+  return ok();
+}
+
+int jules_dist_init(void** comm, int world, int rank, const void* id) {
+  if (!comm || !id) return fail(JULES_ERR_ARG, "dist_init: NULL");
+  *comm = nullptr;
+  if (world < 1 || world > jb::dist::kMaxRanks || rank < 0 || rank >= world)
+    return fail(JULES_ERR_ARG, "dist_init: world=%d rank=%d (1 <= world <= %d)", world, rank,
+                jb::dist::kMaxRanks);
+  if (int rc = need_nccl()) return rc;
+  auto* c = new DistComm();
+  c->world = world;
+  c->rank = rank;
+  if (int rc = current_device(&c->dev)) {
+    delete c;
+    return rc;
+  }
+  ncclUniqueId u;
+  std::memcpy(&u, id, sizeof(u));
+  ncclResult_t r = nccl().comm_init_rank(&c->comm, world, u, rank);
+  if (r != ncclSuccess) {
+    delete c;
+    return nccl_fail(r, "ncclCommInitRank");
+  }
+  int rc = shared_alloc(c, 256, &c->flags);
+  if (!rc) {
+    unsigned long long* h[jb::dist::kMaxRanks];
+    for (int q = 0; q < world; ++q) h[q] = static_cast<unsigned long long*>(c->flags.peers[q]);
+    cudaError_t e = cudaMalloc(&c->d_counters, sizeof(h));
+    if (e == cudaSuccess) e = cudaMemcpy(c->d_counters, h, sizeof(h), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) rc = cuda_fail(e, "dist_init: counter table");
+  }
+  if (rc) {
+    jules_dist_destroy(c);
+    return rc;
+  }
+  *comm = c;
+  return ok();
+}
+
+int jules_dist_destroy(void* comm) {
+  if (!comm) return ok();
+  auto* c = static_cast<DistComm*>(comm);
+  cudaDeviceSynchronize();
+  for (auto& b : c->shared) shared_release(c, b);
+  shared_release(c, c->flags);
+  if (c->d_counters) cudaFree(c->d_counters);
+  if (c->comm) nccl().comm_destroy(c->comm);
+  delete c;
+  return ok();
+}
+
+int jules_dist_barrier(void* comm, void* stream) {
+  DistComm* c;
+  if (int rc = dist_check(comm, &c)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // one in-place all-reduce of the spare word after the counter
+  auto* w = reinterpret_cast<unsigned long long*>(static_cast<char*>(c->flags.local) + 64);
+  ncclResult_t r = nccl().all_reduce(w, w, 1, ncclUint64, ncclSum, c->comm, st);
+  return r == ncclSuccess ? ok() : nccl_fail(r, "ncclAllReduce(barrier)");
+}
+
+int jules_dist_alloc_shared(void* comm, size_t bytes, void** local) {
+  if (!local) return fail(JULES_ERR_ARG, "dist_alloc_shared: NULL");
+  *local = nullptr;
+  DistComm* c;
+  if (int rc = dist_check(comm, &c)) return rc;
+  if (bytes == 0) return fail(JULES_ERR_ARG, "dist_alloc_shared: 0 bytes");
+  SharedBuf b;
+  if (int rc = shared_alloc(c, bytes, &b)) return rc;
+  std::lock_guard<std::mutex> lk(c->mu);
+  c->shared.push_back(b);
+  *local = b.local;
+  return ok();
+}
+
+int jules_dist_free_shared(void* comm, void* local) {
+  DistComm* c;
+  if (int rc = dist_check(comm, &c)) return rc;
+  std::lock_guard<std::mutex> lk(c->mu);
+  for (size_t i = 0; i < c->shared.size(); ++i) {
+    if (c->shared[i].local == local) {
+      cudaDeviceSynchronize();
+      shared_release(c, c->shared[i]);
+      c->shared.erase(c->shared.begin() + (long)i);
+      return ok();
+    }
+  }
+  return fail(JULES_ERR_ARG, "dist_free_shared: not a shared buffer of this communicator");
+}
+
+int jules_dist_gemm_bias_act(void* comm, const void* A, const void* W, const float* bias,
+                             const void* residual, void* C, int64_t M, int64_t N, int64_t K,
+                             int act, int in_dtype, int out_dtype, void* stream) {
+  DistComm* c;
+  if (int rc = dist_check(comm, &c)) return rc;
+  if (!A || !W || !C) return fail(JULES_ERR_ARG, "dist_gemm: NULL A, W or C");
+  if (M < 0 || N <= 0 || K <= 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+    return fail(JULES_ERR_SHAPE, "dist_gemm: M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+  if (out_dtype != JULES_DTYPE_F32 && out_dtype != JULES_DTYPE_BF16)
+    return fail(JULES_ERR_DTYPE, "dist_gemm: out dtype %d", out_dtype);
+  if (in_dtype != JULES_DTYPE_F32 && in_dtype != JULES_DTYPE_BF16 && in_dtype != JULES_DTYPE_FP8E4M3 &&
+      in_dtype != JULES_DTYPE_FP8E5M2)
+    return fail(JULES_ERR_DTYPE, "dist_gemm: in dtype %d", in_dtype);
+  if (M == 0) return ok();
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int64_t b, e;
+  jules_dist_shard(M, c->world, c->rank, &b, &e);
+  const size_t ein = dtype_bytes(in_dtype), eout = dtype_bytes(out_dtype);
+  const size_t eres = in_dtype == JULES_DTYPE_F32 ? 4 : 2;  // fp8 operands take a bf16 residual
+  const char* A_l = static_cast<const char*>(A) + (size_t)b * K * ein;
+  const char* R_l = residual ? static_cast<const char*>(residual) + (size_t)b * N * eres : nullptr;
+  SharedBuf shared_c;  // C's peer mappings when it is a shared buffer
+  const bool is_shared = find_shared(c, C, (size_t)M * N * eout, &shared_c);
+  // The fused path depends only on values every rank shares, so all ranks
+  // take the same path.
+  const bool fused = is_shared && in_dtype == JULES_DTYPE_BF16 && N % 8 == 0 && K % 8 == 0 && N >= 256 &&
+                     M / c->world >= 256 && aligned16(A) && aligned16(W) && aligned16(C) &&
+                     (!bias || aligned16(bias)) && (!residual || aligned16(residual));
+  if (fused) {
+    const auto* a = reinterpret_cast<const __nv_bfloat16*>(A_l);
+    const auto* w = static_cast<const __nv_bfloat16*>(W);
+    const auto* r = reinterpret_cast<const __nv_bfloat16*>(R_l);
+    int rc;
+    if (out_dtype == JULES_DTYPE_BF16) {
+      jb::gemm::OutDest<__nv_bfloat16> od{};
+      od.n = c->world;
+      od.row_off = (int)b;
+      od.c[0] = static_cast<__nv_bfloat16*>(C);
+      for (int q = 1; q < c->world; ++q)
+        od.c[q] = static_cast<__nv_bfloat16*>(shared_c.peers[(c->rank + q) % c->world]);
+      rc = gemm_tc2<256>(a, w, bias, r, od, e - b, N, K, act, st);
+    } else {
+      jb::gemm::OutDest<float> od{};
+      od.n = c->world;
+      od.row_off = (int)b;
+      od.c[0] = static_cast<float*>(C);
+      for (int q = 1; q < c->world; ++q)
+        od.c[q] = static_cast<float*>(shared_c.peers[(c->rank + q) % c->world]);
+      rc = gemm_tc2<256>(a, w, bias, r, od, e - b, N, K, act, st);
+    }
+    if (rc) return rc;
+    const unsigned long long target = (++c->calls) * (unsigned long long)c->world;
+    jb::dist::dist_signal_wait_kernel<<<1, 32, 0, st>>>(
+        c->d_counters, c->world, static_cast<const unsigned long long*>(c->flags.local), target,
+        jb::kWaitLimitNs);
+    return check_launch("dist_signal_wait_kernel launch");
+  }
+  if (e > b) {
+    char* C_l = static_cast<char*>(C) + (size_t)b * N * eout;
+    if (int rc = jules_gemm_bias_act(A_l, W, bias, R_l, C_l, e - b, N, K, act, in_dtype, out_dtype, stream))
+      return rc;
+  }
+  ncclDataType_t t;
+  if (int rc = nccl_type(out_dtype, &t)) return rc;
+  return gather_in_place(c, C, M, N, t, eout, st);
+}
+
+int jules_dist_flash_attention_fwd(void* comm, const void* Q, const void* K, const void* V, void* O,
+                                   float* lse, int B, int Hq, int Hkv, int S, int D, float scale,
+                                   int causal, int dtype, void* stream) {
+  DistComm* c;
+  if (int rc = dist_check(comm, &c)) return rc;
+  if (!Q || !K || !V || !O) return fail(JULES_ERR_ARG, "dist_attention: NULL Q, K, V or O");
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || S < 0 || D <= 0 || Hq % Hkv != 0)
+    return fail(JULES_ERR_SHAPE, "dist_attention: B=%d Hq=%d Hkv=%d S=%d D=%d", B, Hq, Hkv, S, D);
+  if (dtype != JULES_DTYPE_F32 && dtype != JULES_DTYPE_BF16)
+    return fail(JULES_ERR_DTYPE, "dist_attention: dtype %d", dtype);
+  if (B == 0 || S == 0) return ok();
+  // Units: (batch, kv head) pairs, each one kv head and the Hq/Hkv query
+  // heads reading it, contiguous in every tensor.  Each rank's units must
+  // form whole batches or lie inside one batch, so its share is one call.
+  const int64_t units = (int64_t)B * Hkv;
+  const int w = c->world;
+  if (units % w != 0)
+    return fail(JULES_ERR_SHAPE, "dist_attention: %lld units do not split over %d ranks", (long long)units, w);
+  const int64_t upr = units / w, u0 = upr * c->rank;
+  if (upr % Hkv != 0 && Hkv % upr != 0)
+    return fail(JULES_ERR_SHAPE, "dist_attention: %lld units per rank neither whole batches nor a part of one", (long long)upr);
+  const int G = Hq / Hkv;
+  const int64_t b0 = u0 / Hkv, g0 = u0 % Hkv;
+  const int Bl = upr % Hkv == 0 ? (int)(upr / Hkv) : 1;
+  const int Hkvl = upr % Hkv == 0 ? Hkv : (int)upr;
+  const int Hql = Hkvl * G;
+  const size_t elt = dtype_bytes(dtype);
+  const size_t q_off = ((size_t)b0 * Hq + (size_t)g0 * G) * S * D;
+  const size_t kv_off = ((size_t)b0 * Hkv + (size_t)g0) * S * D;
+  const char* q = static_cast<const char*>(Q) + q_off * elt;
+  const char* k = static_cast<const char*>(K) + kv_off * elt;
+  const char* v = static_cast<const char*>(V) + kv_off * elt;
+  char* o = static_cast<char*>(O) + q_off * elt;
+  float* l = lse ? lse + ((size_t)b0 * Hq + (size_t)g0 * G) * S : nullptr;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  SharedBuf so, sl;
+  const bool o_shared = find_shared(c, O, (size_t)B * Hq * S * D * elt, &so);
+  const bool l_shared = !lse || find_shared(c, lse, (size_t)B * Hq * S * 4, &sl);
+  if (o_shared && l_shared && dtype == JULES_DTYPE_BF16 && D == jb::attn::HD && aligned16(Q) &&
+      aligned16(K) && aligned16(V) && aligned16(O)) {
+    // Gather fused into the attention epilogue: each finished O tile (and
+    // its lse) is stored into every rank's buffers.
+    jb::attn::AttnOut out{};
+    out.n = w;
+    for (int qq = 0; qq < w; ++qq) {
+      const int peer = (c->rank + qq) % w;
+      out.o[qq] = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(so.peers[peer]) + q_off * elt);
+      out.lse[qq] = lse ? reinterpret_cast<float*>(static_cast<char*>(sl.peers[peer]) +
+                                                   ((size_t)b0 * Hq + (size_t)g0 * G) * S * 4)
+                        : nullptr;
+    }
+    if (!(scale > 0.0f)) scale = 1.0f / sqrtf((float)D);
+    if (int rc = attn_tc(q, k, v, out, Bl, Hql, Hkvl, S, D, scale, causal ? 1 : 0, st)) return rc;
+    const unsigned long long target = (++c->calls) * (unsigned long long)w;
+    jb::dist::dist_signal_wait_kernel<<<1, 32, 0, st>>>(
+        c->d_counters, w, static_cast<const unsigned long long*>(c->flags.local), target,
+        jb::kWaitLimitNs);
+    return check_launch("dist_signal_wait_kernel launch");
+  }
+  if (int rc = jules_flash_attention_fwd(q, k, v, o, l, Bl, Hql, Hkvl, S, D, scale, causal, dtype, stream))
+    return rc;
+  ncclDataType_t t;
+  if (int rc = nccl_type(dtype, &t)) return rc;
+  ncclResult_t r = nccl().group_start();
+  if (r != ncclSuccess) return nccl_fail(r, "ncclGroupStart");
+  int rc = gather_in_place(c, O, units, (int64_t)G * S * D, t, elt, st);
+  if (!rc && lse) rc = gather_in_place(c, lse, units, (int64_t)G * S, ncclFloat32, 4, st);
+  r = nccl().group_end();
+  if (rc) return rc;
+  return r == ncclSuccess ? ok() : nccl_fail(r, "ncclGroupEnd");
 }
 
 }  // extern "C"

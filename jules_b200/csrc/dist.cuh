@@ -1,0 +1,260 @@
+// Multi-GPU layer: one process per GPU, the hot path sharded into independent
+// units (token rows of the GEMM, (batch, kv-head group) units of attention)
+// and the outputs gathered over NVLink.  The reference names this exchange
+// only as an IR collective (include/jules/Dialect/JulesOps.td:660-684) whose
+// lowering is dead code; the partition follows its shapes.
+//
+// Plumbing: NCCL, loaded at run time (dlopen "libnccl.so.2": in a process that
+// already holds one, e.g. PyTorch's, that library is reused), for the
+// communicator, the exchange of peer-memory handles and the attention gather.
+//
+// Gather fused into the kernel: when the output is a "shared" buffer
+// (cudaMalloc + CUDA IPC handles exchanged over the communicator), the GEMM
+// (or attention) epilogue stores each finished tile of this rank's rows (or
+// units) into every rank's output over NVLink while later tiles are still
+// being computed.  A one-thread kernel then signals every rank (system-scope
+// atomics on a counter in each rank's memory) and waits, with a bounded
+// spin, until all ranks have signalled: after it, every rank's output holds
+// the whole result.  Outputs that are not shared fall back to computing the
+// local share and an in-place ncclAllGather.
+#pragma once
+
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <vector>
+
+namespace jb {
+namespace dist {
+
+constexpr int kMaxRanks = 8;  // == gemm::kMaxOutDest
+constexpr uint32_t kSiteSignalWait = 251;
+
+// Adds one to every rank's completion counter, then waits until this rank's
+// counter reaches `target` (= world x calls so far).  One thread.  The
+// fence before the signals orders this rank's earlier peer stores (the
+// GEMM epilogue also fences them system-wide before its kernel ends).
+__global__ void dist_signal_wait_kernel(unsigned long long* const* counters, int world,
+                                        const unsigned long long* mine,
+                                        unsigned long long target, uint64_t limit_ns) {
+  if (threadIdx.x != 0) return;
+  __threadfence_system();
+  for (int r = 0; r < world; ++r) atomicAdd_system(counters[r], 1ull);
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(mine) : "memory");
+    if (v >= target) break;
+    if ((it & 63u) == 0 && globaltimer() - t0 > limit_ns) {
+      record_error(kDevErrTimeout, kSiteSignalWait);
+      return;
+    }
+    __nanosleep(64);
+  }
+  __threadfence_system();
+}
+
+}  // namespace dist
+}  // namespace jb
+
+namespace {
+
+// ---------------------------------------------------------------------------
+// NCCL entry points, resolved once.
+// ---------------------------------------------------------------------------
+struct NcclApi {
+  decltype(&ncclGetUniqueId) get_unique_id = nullptr;
+  decltype(&ncclCommInitRank) comm_init_rank = nullptr;
+  decltype(&ncclCommDestroy) comm_destroy = nullptr;
+  decltype(&ncclAllGather) all_gather = nullptr;
+  decltype(&ncclAllReduce) all_reduce = nullptr;
+  decltype(&ncclBroadcast) broadcast = nullptr;
+  decltype(&ncclGroupStart) group_start = nullptr;
+  decltype(&ncclGroupEnd) group_end = nullptr;
+  decltype(&ncclGetErrorString) error_string = nullptr;
+  bool loaded = false;
+  std::string why;
+};
+
+NcclApi& nccl() {
+  static NcclApi api;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_LOCAL);
+    if (!h) {
+      const char* e = dlerror();
+      api.why = e ? e : "dlopen(libnccl.so.2) failed";
+      return;
+    }
+    bool ok = true;
+    auto sym = [&](auto& fn, const char* name) {
+      fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(h, name));
+      if (!fn) ok = false;
+    };
+    sym(api.get_unique_id, "ncclGetUniqueId");
+    sym(api.comm_init_rank, "ncclCommInitRank");
+    sym(api.comm_destroy, "ncclCommDestroy");
+    sym(api.all_gather, "ncclAllGather");
+    sym(api.all_reduce, "ncclAllReduce");
+    sym(api.broadcast, "ncclBroadcast");
+    sym(api.group_start, "ncclGroupStart");
+    sym(api.group_end, "ncclGroupEnd");
+    sym(api.error_string, "ncclGetErrorString");
+    api.loaded = ok;
+    if (!ok) api.why = "libnccl.so.2 lacks an expected symbol";
+  });
+  return api;
+}
+
+int nccl_fail(ncclResult_t r, const char* what) {
+  return fail(JULES_ERR_COMM, "%s: %s", what, nccl().error_string ? nccl().error_string(r) : "?");
+}
+
+int need_nccl() {
+  if (!nccl().loaded) return fail(JULES_ERR_COMM, "NCCL unavailable: %s", nccl().why.c_str());
+  return JULES_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Communicator state.
+// ---------------------------------------------------------------------------
+struct SharedBuf {
+  void* local = nullptr;
+  size_t bytes = 0;
+  void* peers[jb::dist::kMaxRanks] = {};  // peers[rank] == local
+};
+
+struct DistComm {
+  ncclComm_t comm = nullptr;
+  int world = 1, rank = 0, dev = 0;
+  unsigned long long calls = 0;             // signal/wait rounds issued (same on every rank)
+  SharedBuf flags;                          // one u64 completion counter per rank
+  unsigned long long** d_counters = nullptr;  // device array: every rank's counter
+  std::vector<SharedBuf> shared;            // buffers from jules_dist_alloc_shared
+  std::mutex mu;
+};
+
+void shared_release(DistComm* c, SharedBuf& b) {
+  for (int r = 0; r < c->world; ++r)
+    if (r != c->rank && b.peers[r]) cudaIpcCloseMemHandle(b.peers[r]);
+  if (b.local) cudaFree(b.local);
+  b = SharedBuf{};
+}
+
+// Collective: every rank allocates `bytes`, exports a CUDA IPC handle, the
+// handles are all-gathered over NCCL and each rank maps the others'.
+int shared_alloc(DistComm* c, size_t bytes, SharedBuf* out) {
+  SharedBuf b;
+  b.bytes = bytes;
+  cudaError_t e = cudaMalloc(&b.local, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(shared buffer)");
+  e = cudaMemset(b.local, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();  // zeroed before any peer can map it
+  if (e != cudaSuccess) {
+    cudaFree(b.local);
+    return cuda_fail(e, "cudaMemset(shared buffer)");
+  }
+  cudaIpcMemHandle_t mine;
+  e = cudaIpcGetMemHandle(&mine, b.local);
+  const size_t hb = sizeof(cudaIpcMemHandle_t);
+  char* d_handles = nullptr;
+  if (e == cudaSuccess) e = cudaMalloc(&d_handles, hb * c->world);
+  if (e != cudaSuccess) {
+    cudaFree(b.local);
+    return cuda_fail(e, "cudaIpcGetMemHandle / handle exchange buffer");
+  }
+  std::vector<cudaIpcMemHandle_t> all(c->world);
+  int rc = JULES_OK;
+  cudaStream_t st = nullptr;
+  if ((e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking)) != cudaSuccess) {
+    rc = cuda_fail(e, "cudaStreamCreate");
+  } else if ((e = cudaMemcpy(d_handles + hb * c->rank, &mine, hb, cudaMemcpyHostToDevice)) != cudaSuccess) {
+    rc = cuda_fail(e, "copy IPC handle");
+  } else {
+    ncclResult_t r = nccl().all_gather(d_handles + hb * c->rank, d_handles, hb, ncclUint8, c->comm, st);
+    if (r != ncclSuccess) rc = nccl_fail(r, "ncclAllGather(IPC handles)");
+    else if ((e = cudaStreamSynchronize(st)) != cudaSuccess) rc = cuda_fail(e, "handle exchange");
+    else if ((e = cudaMemcpy(all.data(), d_handles, hb * c->world, cudaMemcpyDeviceToHost)) != cudaSuccess)
+      rc = cuda_fail(e, "copy IPC handles");
+  }
+  if (st) cudaStreamDestroy(st);
+  cudaFree(d_handles);
+  if (rc) {
+    cudaFree(b.local);
+    return rc;
+  }
+  for (int r = 0; r < c->world; ++r) {
+    if (r == c->rank) {
+      b.peers[r] = b.local;
+      continue;
+    }
+    e = cudaIpcOpenMemHandle(&b.peers[r], all[r], cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      b.peers[r] = nullptr;
+      shared_release(c, b);
+      return cuda_fail(e, "cudaIpcOpenMemHandle");
+    }
+  }
+  *out = b;
+  return JULES_OK;
+}
+
+// The shared buffer starting at ptr with at least `bytes`, if any.
+bool find_shared(DistComm* c, const void* ptr, size_t bytes, SharedBuf* out) {
+  std::lock_guard<std::mutex> lk(c->mu);
+  for (const auto& s : c->shared)
+    if (s.local == ptr && s.bytes >= bytes) {
+      *out = s;
+      return true;
+    }
+  return false;
+}
+
+int dist_check(void* comm, DistComm** c) {
+  if (!comm) return fail(JULES_ERR_ARG, "dist: NULL communicator");
+  *c = static_cast<DistComm*>(comm);
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  if (dev != (*c)->dev) return fail(JULES_ERR_ARG, "dist: device %d is current, the communicator is on %d", dev, (*c)->dev);
+  return JULES_OK;
+}
+
+int nccl_type(int dtype, ncclDataType_t* t) {
+  switch (dtype) {
+    case JULES_DTYPE_F32: *t = ncclFloat32; return JULES_OK;
+    case JULES_DTYPE_BF16: *t = ncclBfloat16; return JULES_OK;
+    case JULES_DTYPE_FP8E4M3:
+    case JULES_DTYPE_FP8E5M2: *t = ncclUint8; return JULES_OK;
+    default: return fail(JULES_ERR_DTYPE, "dist: dtype %d", dtype);
+  }
+}
+
+size_t dtype_bytes(int dtype) { return dtype == JULES_DTYPE_F32 ? 4 : (dtype == JULES_DTYPE_BF16 ? 2 : 1); }
+
+// Gathers rank slices of `elems_total` elements (rank r owns [begin_r, end_r)
+// of a balanced contiguous partition of `units` units of `unit_elems` each)
+// in place: an ncclAllGather when the partition is equal, else one
+// broadcast per rank in a group.
+int gather_in_place(DistComm* c, void* buf, int64_t units, int64_t unit_elems, ncclDataType_t t,
+                    size_t elt, cudaStream_t st) {
+  const int w = c->world;
+  char* base = static_cast<char*>(buf);
+  if (units % w == 0) {
+    const size_t cnt = (size_t)(units / w) * unit_elems;
+    ncclResult_t r = nccl().all_gather(base + (size_t)c->rank * cnt * elt, base, cnt, t, c->comm, st);
+    return r == ncclSuccess ? JULES_OK : nccl_fail(r, "ncclAllGather");
+  }
+  ncclResult_t r = nccl().group_start();
+  for (int q = 0; q < w && r == ncclSuccess; ++q) {
+    int64_t b, e;
+    jules_dist_shard(units, w, q, &b, &e);
+    void* p = base + (size_t)b * unit_elems * elt;
+    r = nccl().broadcast(p, p, (size_t)(e - b) * unit_elems, t, q, c->comm, st);
+  }
+  ncclResult_t r2 = nccl().group_end();
+  if (r != ncclSuccess) return nccl_fail(r, "ncclBroadcast");
+  return r2 == ncclSuccess ? JULES_OK : nccl_fail(r2, "ncclGroupEnd");
+}
+
+}  // namespace

@@ -286,12 +286,27 @@ struct Smem2 {
   static constexpr int kBBytes = BK * (TN / 2) * 2;  // this CTA's TN/2 columns of W
   alignas(1024) uint8_t a[STAGES][kABytes];
   alignas(1024) uint8_t b[STAGES][kBBytes];
+  // Epilogue staging: 4 KB per epilogue warp (32 rows of 128 bytes, their
+  // 16-byte chunks XOR-swizzled by row & 7).
+  alignas(128) float epi[4][32][32];
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint32_t tmem_base;
   int abort_flag;
+};
+
+// Where the pair kernel's epilogue writes C: the local C (c[0]) and, for the
+// sharded GEMM with the gather fused in, the same rows of every other rank's
+// C mapped into this process (c[1..n-1]).  Local row r of the tile grid is
+// row row_off + r of every C; A and the residual use local rows.
+constexpr int kMaxOutDest = kMaxPeers;
+template <typename TOut>
+struct OutDest {
+  TOut* c[kMaxOutDest];
+  int n;
+  int row_off;
 };
 
 // Work unit u of the tail-split schedule: whole tiles first, then the two
@@ -316,7 +331,8 @@ __device__ __forceinline__ PairUnit pair_unit(int u, int whole_units) {
   return r;
 }
 
-// Epilogue math for 8 consecutive columns: bias, activation, residual, store.
+// Per-thread epilogue math for 8 consecutive columns of one row: bias,
+// activation, residual, store (the 8-bit pair kernels).
 template <typename TOut>
 __device__ __forceinline__ void epilogue8(float (&v)[8], const float* bias,
                                           const __nv_bfloat16* rrow, TOut* crow, int col,
@@ -348,8 +364,8 @@ template <int STAGES, int TN, typename TOut>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc2_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmW, const float* __restrict__ bias,
-                         const __nv_bfloat16* __restrict__ residual, TOut* __restrict__ C, int M,
-                         int N, int K, int act, int whole_units, int num_units) {
+                         const __nv_bfloat16* __restrict__ residual, const OutDest<TOut> out,
+                         int M, int N, int K, int act, int whole_units, int num_units) {
   static_assert(TN == 256, "pair tile N is 256 (its halves are 128)");
   constexpr int TM = 256;
   constexpr uint32_t kTmemCols = 2 * TN;  // two accumulators
@@ -459,8 +475,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- epilogue (warps 2..5, both CTAs) ----------------
+    // Each warp owns 32 rows (its TMEM lane quarter).  tcgen05.ld gives lane t
+    // row t; bias, activation and residual are applied in that layout, the
+    // results go through shared memory (4 KB per warp, 16-byte chunks
+    // XOR-swizzled by row) and are read back so that 8 lanes cover 128
+    // contiguous bytes of one row: every store writes 16 bytes, every
+    // 8 lanes a whole 128-byte line, local or across NVLink.
+    //   bf16 C: blocks of 64 columns (32 rows x 128 B); fp32 C: 32 columns.
+    constexpr int kBlk = sizeof(TOut) == 2 ? 64 : 32;  // columns per staged block
     const int quarter = warp & 3;
-    const int row_in_tile = quarter * 32 + lane;
+    uint4* stage = reinterpret_cast<uint4*>(s.epi[quarter]);  // [32 rows][8 chunks of 16 B]
+    const int g = lane & 7;      // chunk (8 bf16 / 4 fp32 columns) this lane stores
+    const int rsub = lane >> 3;  // first row this lane stores
     const uint32_t tempty0_leader = mapa_shared(smem_u32(&s.tempty[0]), 0);
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -468,37 +494,92 @@ __global__ void __launch_bounds__(kThreads, 1)
       const PairUnit pu = pair_unit<TN>(u, whole_units);
       int mi, ni;
       tile_coords(pu.tile, num_m, num_n, mi, ni);
-      const int m0 = mi * TM + (int)rank * 128;
+      const int m0 = mi * TM + (int)rank * 128 + quarter * 32;  // first row of this warp
       const int n0 = ni * TN + pu.n_off;
       if (!mbar_wait(&s.tfull[acc], acc_phase, 44, abort_flag)) break;
       tc_fence_after();
-      const int row = m0 + row_in_tile;
-      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * TN;
-      TOut* crow = C + (size_t)(row < M ? row : 0) * N;
-      const __nv_bfloat16* rrow = residual ? residual + (size_t)(row < M ? row : 0) * N : nullptr;
+      const uint32_t t_warp = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * TN;
+      const int my_row = m0 + lane;  // row of this lane in the TMEM layout
+      const __nv_bfloat16* rrow =
+          residual ? residual + (size_t)(my_row < M ? my_row : 0) * N : nullptr;
 #pragma unroll 1
-      for (int c = 0; c < pu.cols / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(t_row + c * 32, r);
-        tmem_ld_wait(r);
-        const int col0 = n0 + c * 32;
-        if (row < M && col0 < N) {
+      for (int cb = 0; cb < pu.cols; cb += kBlk) {
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            const int col = col0 + g * 8;
-            if (col < N) {
-              float v[8];
+        for (int h = 0; h < kBlk / 32; ++h) {
+          const int c0 = n0 + cb + h * 32;  // first column of these 32
+          uint32_t r[32];
+          tmem_ld32(t_warp + cb + h * 32, r);
+          tmem_ld_wait(r);
+          float v[32];
 #pragma unroll
-              for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[g * 8 + j]);
-              epilogue8(v, bias, rrow, crow, col, act);
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          if (c0 < N) {  // N is a multiple of 8: a 32-column group is all in or starts past N
+            if (bias) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                if (c0 + j < N) {
+                  const float4 bv = *reinterpret_cast<const float4*>(bias + c0 + j);
+                  v[j] += bv.x; v[j + 1] += bv.y; v[j + 2] += bv.z; v[j + 3] += bv.w;
+                }
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = act_fast(v[j], act);
+            if (rrow) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) {
+                if (c0 + j < N) {
+                  const uint4 rv = *reinterpret_cast<const uint4*>(rrow + c0 + j);
+                  const __nv_bfloat162* rp = reinterpret_cast<const __nv_bfloat162*>(&rv);
+#pragma unroll
+                  for (int q = 0; q < 4; ++q) {
+                    const float2 f = __bfloat1622float2(rp[q]);
+                    v[j + 2 * q] += f.x;
+                    v[j + 2 * q + 1] += f.y;
+                  }
+                }
+              }
             }
           }
+          // this lane's row, chunks h*4 .. h*4+3 (bf16) or 0 .. 7 (fp32)
+          if constexpr (sizeof(TOut) == 2) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              stage[lane * 8 + ((h * 4 + q) ^ (lane & 7))] =
+                  make_uint4(pack_bf16x2(v[8 * q], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
+                             pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+          } else {
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              stage[lane * 8 + (q ^ (lane & 7))] =
+                  make_uint4(__float_as_uint(v[4 * q]), __float_as_uint(v[4 * q + 1]),
+                             __float_as_uint(v[4 * q + 2]), __float_as_uint(v[4 * q + 3]));
+          }
         }
+        __syncwarp();
+        const int col = n0 + cb + g * (16 / (int)sizeof(TOut));
+        if (col < N) {
+#pragma unroll 4
+          for (int i = 0; i < 8; ++i) {
+            const int rr = rsub + 4 * i;
+            const int row = m0 + rr;
+            if (row >= M) break;  // rows only grow with i
+            const uint4 val = stage[rr * 8 + (g ^ (rr & 7))];
+            const size_t off = (size_t)(out.row_off + row) * N + col;
+#pragma unroll
+            for (int p = 0; p < kMaxOutDest; ++p)
+              if (p < out.n) *reinterpret_cast<uint4*>(out.c[p] + off) = val;
+          }
+        }
+        __syncwarp();
       }
       tc_fence_before();
       mbar_arrive_cluster(tempty0_leader + acc * 8);
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
     }
+    // Peer stores must be visible system-wide before this rank signals the
+    // others that its rows are in place (dist_signal_wait_kernel).
+    if (out.n > 1) __threadfence_system();
   }
 
   __syncwarp();

@@ -29,6 +29,11 @@ __device__ __forceinline__ void record_error(uint32_t kind, uint32_t site) {
   atomicOr(&g_dev_error, kind | (site << 8));
 }
 
+// Most output buffers a kernel epilogue writes the same tile to: the local
+// one and, for the multi-GPU entry points with the gather fused in, every
+// other rank's (mapped into this process) - at most 8 GPUs of one node.
+constexpr int kMaxPeers = 8;
+
 // Wall-clock limit for any single mbarrier wait (ns).  Generous: a healthy
 // pipeline stage completes in microseconds.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
