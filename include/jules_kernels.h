@@ -267,6 +267,34 @@ int jules_mlp_block(const void* X, const float* gamma, const float* beta, const 
                     size_t workspace_bytes, void* stream);
 
 /*
+ * The MLP block with the LayerNorm folded into the first GEMM's epilogue.
+ * With W1' = diag(gamma) W1,
+ *   LN(x) . W1 + b1 = rstd * (x . W1' - mean * colsum(W1')) + (beta . W1 + b1),
+ * so the first GEMM runs on the raw rows of X (no normalised copy of X in
+ * HBM) after a pass that reads X once for its row statistics.
+ * jules_mlp_block_fold_weights prepares, once per weights: W1f [d,dff] bf16
+ * (= bf16(gamma[k] * W1[k][n])), colsum [dff] fp32 (column sums of W1f) and
+ * c [dff] fp32 (= beta . W1 + b1).  jules_mlp_block_folded then computes
+ * jules_mlp_block's result: out = GELU(LN(X) . W1 + b1) . W2 + b2 + X.
+ * d and dff multiples of 8, d <= 8192, 16-byte aligned buffers; workspace of
+ * jules_mlp_block_folded_workspace_bytes() (row statistics + the hidden
+ * activation).  Rounding differs from jules_mlp_block (W1' is rounded to
+ * bf16 instead of LN(X)); in fp32 accumulation the fold loses accuracy
+ * when a row's |mean| is large against its standard deviation, where
+ * jules_mlp_block is the form to use.
+ * Implements fusedMLPForward's LayerNorm + first layer (FusedKernels.h:
+ * 532-600, 650-760) with the normalisation inside the GEMM epilogue.
+ */
+int jules_mlp_block_fold_weights(const float* gamma, const float* beta, const void* W1,
+                                 const float* b1, void* W1f, float* colsum, float* c, int64_t d,
+                                 int64_t dff, void* stream);
+size_t jules_mlp_block_folded_workspace_bytes(int64_t T, int64_t d, int64_t dff);
+int jules_mlp_block_folded(const void* X, const void* W1f, const float* colsum, const float* c,
+                           const void* W2, const float* b2, void* out, int out_dtype, int64_t T,
+                           int64_t d, int64_t dff, float eps, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/*
  * The MLP block of jules_mlp_block without any allocation: no counterpart in
  * the reference.  For callers that cannot allocate device memory, such as a
  * runtime's custom-call handler (the jules.extern_kernel ->

@@ -19,7 +19,7 @@ __all__ = [
     "mlp_block", "mlp_block_workspace_bytes", "sgemm", "device_error", "kernel_by_name",
     "kernel_names", "LIB_PATH", "gemm_fp8", "cast", "matmul_int8", "softmax",
     "cross_entropy_loss", "custom_call", "mlp_fwd_bwd", "flash_attention_bwd", "attention",
-    "Dist",
+    "Dist", "mlp_block_fold_weights", "mlp_block_folded",
 ]
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libjules_b200.so")
@@ -68,6 +68,10 @@ _SIGNATURES = {
     "jules_kernel_name": ([_c_int], ctypes.c_char_p),
     "jules_kernel_count": ([], _c_int),
     "jules_kernel_implemented": ([_c_int], _c_int),
+    "jules_mlp_block_fold_weights": ([_c_vp] * 7 + [_c_i64, _c_i64, _c_vp], _c_int),
+    "jules_mlp_block_folded_workspace_bytes": ([_c_i64, _c_i64, _c_i64], ctypes.c_size_t),
+    "jules_mlp_block_folded": ([_c_vp] * 7 + [_c_int, _c_i64, _c_i64, _c_i64, _c_f, _c_vp,
+                                              ctypes.c_size_t, _c_vp], _c_int),
     "jules_dist_shard": ([_c_i64, _c_int, _c_int, ctypes.POINTER(_c_i64), ctypes.POINTER(_c_i64)],
                          _c_int),
     "jules_dist_unique_id": ([_c_vp], _c_int),
@@ -460,6 +464,41 @@ def mlp_block(X, gamma, beta, W1, b1, W2, b2, eps=1e-5, out=None, workspace=None
                                _ptr(workspace),
                                workspace.numel() * workspace.element_size(), _stream(stream))
     _check(rc, "jules_mlp_block")
+    return out
+
+
+def mlp_block_fold_weights(gamma, beta, W1, b1, stream=None):
+    """Folded LayerNorm weights of the MLP block (once per weights):
+    (W1f = bf16(diag(gamma) W1), colsum(W1f), c = beta . W1 + b1)."""
+    import torch
+    d, dff = W1.shape
+    W1f = torch.empty_like(W1)
+    colsum = torch.empty(dff, dtype=torch.float32, device=W1.device)
+    c = torch.empty(dff, dtype=torch.float32, device=W1.device)
+    rc = lib().jules_mlp_block_fold_weights(_ptr(gamma), _ptr(beta), _ptr(W1), _ptr(b1), _ptr(W1f),
+                                            _ptr(colsum), _ptr(c), d, dff, _stream(stream))
+    _check(rc, "jules_mlp_block_fold_weights")
+    return W1f, colsum, c
+
+
+def mlp_block_folded(X, folded, W2, b2, eps=1e-5, out=None, workspace=None, stream=None,
+                     out_dtype=None):
+    """mlp_block with the LayerNorm folded into GEMM1's epilogue; `folded` is
+    mlp_block_fold_weights(gamma, beta, W1, b1)."""
+    import torch
+    W1f, colsum, c = folded
+    T, d = X.shape
+    dff = W1f.shape[1]
+    if out is None:
+        out = torch.empty((T, d), dtype=out_dtype or X.dtype, device=X.device)
+    need = int(lib().jules_mlp_block_folded_workspace_bytes(T, d, dff))
+    if workspace is None:
+        workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=X.device)
+    rc = lib().jules_mlp_block_folded(_ptr(X), _ptr(W1f), _ptr(colsum), _ptr(c), _ptr(W2), _ptr(b2),
+                                      _ptr(out), _dtype_code(out), T, d, dff, float(eps),
+                                      _ptr(workspace), workspace.numel() * workspace.element_size(),
+                                      _stream(stream))
+    _check(rc, "jules_mlp_block_folded")
     return out
 
 

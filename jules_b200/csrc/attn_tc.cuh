@@ -70,6 +70,11 @@ struct AttnOut {
   int n;
 };
 
+// With the gather fused in (kGather), the dynamic shared memory continues
+// after Smem with the epilogue staging: 2 KB per softmax warp, 32 rows x 64
+// bytes (32 bf16 columns of O), 16-byte chunks XOR-swizzled by (row >> 1) & 3.
+constexpr int kEpiBytes = 8 * 32 * 64;
+
 struct Smem {
   alignas(1024) uint8_t q[NQT][2][kChunk];
   alignas(1024) uint8_t k[KVS][2][kChunk];
@@ -77,9 +82,6 @@ struct Smem {
   uint64_t q_full, q_empty;
   uint64_t k_full[KVS], k_empty[KVS];
   uint64_t v_full[KVS], v_empty[KVS];
-  // Epilogue staging, 2 KB per softmax warp: 32 rows x 64 bytes (32 bf16
-  // columns of O), 16-byte chunks XOR-swizzled by (row >> 1) & 3.
-  alignas(128) uint4 epi[8][32 * 4];
   uint64_t s_full[NQT], p_full[NQT], o_full[NQT], o_empty[NQT];
   uint32_t tmem_base;
   int abort_flag;
@@ -162,6 +164,7 @@ __device__ __forceinline__ void tmem_ld32_at(uint32_t taddr, uint32_t* r) {
       : "r"(taddr));
 }
 
+template <bool kGather>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                        const __grid_constant__ CUtensorMap tmK,
@@ -455,14 +458,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ----- epilogue: O / l -> bf16, lse -----
       if (!mbar_wait(&s.o_full[t], wi & 1u, 32, abort_flag)) break;
       tc_fence_after();
-      // O / l as bf16, 32 columns at a time through shared memory: lane t
-      // holds row t after tcgen05.ld, and after the exchange 4 lanes write
-      // 64 contiguous bytes of one row (8 rows per store instruction), to
-      // the local O and, when the gather is fused in, every rank's O.
+      // O / l as bf16.  Local output only: each lane stores its own row.
+      // With the gather fused in, 32 columns at a time go through shared
+      // memory so that 4 lanes write 64 contiguous bytes of one row (8 rows
+      // per store instruction) into every rank's O over NVLink.
       const float inv_l = 1.0f / l_run;
       const bool row_ok = q < S;
       const int row0 = qt0 + quarter * 32;  // first row of this warp
-      uint4* stg = s.epi[warp];
+      if constexpr (!kGather) {
+        __nv_bfloat16* orow = out.o[0] + ((size_t)bh * S + (row_ok ? q : 0)) * HD;
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 32) {
+          uint32_t o[32];
+          tmem_ld32(tO + c, o);
+          tmem_ld_wait(o);
+          if (row_ok) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + c);
+#pragma unroll
+            for (int g8 = 0; g8 < 4; ++g8) {
+              uint4 v;
+              v.x = pack_bf16x2(__uint_as_float(o[8 * g8 + 0]) * inv_l, __uint_as_float(o[8 * g8 + 1]) * inv_l);
+              v.y = pack_bf16x2(__uint_as_float(o[8 * g8 + 2]) * inv_l, __uint_as_float(o[8 * g8 + 3]) * inv_l);
+              v.z = pack_bf16x2(__uint_as_float(o[8 * g8 + 4]) * inv_l, __uint_as_float(o[8 * g8 + 5]) * inv_l);
+              v.w = pack_bf16x2(__uint_as_float(o[8 * g8 + 6]) * inv_l, __uint_as_float(o[8 * g8 + 7]) * inv_l);
+              dst[g8] = v;
+            }
+          }
+        }
+      } else {
+      uint4* stg = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(&s) +
+                                            ((sizeof(Smem) + 127) & ~size_t(127))) + warp * 32 * 4;
 #pragma unroll 1
       for (int c = 0; c < HD; c += 32) {
         uint32_t o[32];
@@ -491,6 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
       }
+      }
       if (out.lse[0] && row_ok) {
         const float l = (m_run + log2f(l_run)) * 0.69314718055994531f;
 #pragma unroll
@@ -505,7 +531,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // Peer stores must be visible system-wide before this rank signals the
   // others that its units are in place (dist_signal_wait_kernel).
-  if (out.n > 1) __threadfence_system();
+  if (kGather) __threadfence_system();
   __syncwarp();
   tc_fence_before();
   __syncthreads();

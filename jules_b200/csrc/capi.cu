@@ -58,6 +58,7 @@ struct DeviceInfo {
   bool gemm_attr_f32 = false;
   int gemm2_pairs[2][2] = {{0, 0}, {0, 0}};  // resident CTA pairs, [fp32 out][TN == 256]
   bool attn_attr = false;
+  bool attn_attr_gather = false;
 };
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_dev_mu;
@@ -148,7 +149,7 @@ constexpr int kGemmStages = 4;
 template <typename TOut>
 int gemm_tc(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
             const __nv_bfloat16* res, TOut* C, int64_t M, int64_t N, int64_t K, int act,
-            cudaStream_t st) {
+            cudaStream_t st, const float2* ln_stats = nullptr, const float* ln_colsum = nullptr) {
   int dev;
   if (int rc = current_device(&dev)) return rc;
   CUtensorMap ta, tw;
@@ -175,7 +176,8 @@ int gemm_tc(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
   }
   const int64_t tiles = ((M + 127) / 128) * ((N + kGemmBN - 1) / kGemmBN);
   const int grid = (int)(tiles < device_sms(dev) ? tiles : device_sms(dev));
-  kern<<<grid, jb::gemm::kThreads, smem, st>>>(ta, tw, bias, res, C, (int)M, (int)N, (int)K, act);
+  kern<<<grid, jb::gemm::kThreads, smem, st>>>(ta, tw, bias, res, C, (int)M, (int)N, (int)K, act,
+                                               ln_stats, ln_colsum);
   return check_launch("gemm_bf16_tc_kernel launch");
 }
 
@@ -185,7 +187,8 @@ int gemm_tc(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
 template <int TN, typename TOut>
 int gemm_tc2(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
              const __nv_bfloat16* res, const jb::gemm::OutDest<TOut>& out, int64_t M, int64_t N,
-             int64_t K, int act, cudaStream_t st) {
+             int64_t K, int act, cudaStream_t st, const float2* ln_stats = nullptr,
+             const float* ln_colsum = nullptr) {
   int dev;
   if (int rc = current_device(&dev)) return rc;
   CUtensorMap ta, tw;
@@ -237,7 +240,7 @@ int gemm_tc2(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
   const int pairs = units < max_pairs ? units : max_pairs;
   cfg.gridDim = dim3(2 * pairs);
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tw, bias, res, out, (int)M, (int)N, (int)K,
-                                     act, whole, units);
+                                     act, whole, units, ln_stats, ln_colsum);
   if (e != cudaSuccess) return cuda_fail(e, "gemm_bf16_tc2_kernel launch");
   return check_launch("gemm_bf16_tc2_kernel launch");
 }
@@ -249,13 +252,14 @@ int gemm_tc2(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
 template <typename TOut>
 int gemm_tc_dispatch(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
                      const __nv_bfloat16* res, TOut* C, int64_t M, int64_t N, int64_t K, int act,
-                     cudaStream_t st) {
-  if (M < 256 || N < 256) return gemm_tc(A, W, bias, res, C, M, N, K, act, st);
+                     cudaStream_t st, const float2* ln_stats = nullptr,
+                     const float* ln_colsum = nullptr) {
+  if (M < 256 || N < 256) return gemm_tc(A, W, bias, res, C, M, N, K, act, st, ln_stats, ln_colsum);
   jb::gemm::OutDest<TOut> out{};
   out.c[0] = C;
   out.n = 1;
   out.row_off = 0;
-  return gemm_tc2<256>(A, W, bias, res, out, M, N, K, act, st);
+  return gemm_tc2<256>(A, W, bias, res, out, M, N, K, act, st, ln_stats, ln_colsum);
 }
 
 template <typename TIn, typename TOut>
@@ -343,13 +347,17 @@ int attn_tc(const void* Q, const void* K, const void* V, const jb::attn::AttnOut
     if (int rc = make_tmap_bf16(&tk, K, 3, dims, strides, boxkv)) return rc;
     if (int rc = make_tmap_bf16(&tv, V, 3, dims, strides, boxkv)) return rc;
   }
-  auto kern = jb::attn::attn_fwd_tc_kernel;
-  const size_t smem = sizeof(jb::attn::Smem) + 1024;
-  if (!g_dev[dev].attn_attr) {
+  // out.n > 1: the gather is fused in (staged epilogue, extra shared memory)
+  const bool gather = out.n > 1;
+  auto kern = gather ? jb::attn::attn_fwd_tc_kernel<true> : jb::attn::attn_fwd_tc_kernel<false>;
+  const size_t smem = ((sizeof(jb::attn::Smem) + 127) & ~size_t(127)) + 1024 +
+                      (gather ? jb::attn::kEpiBytes : 0);
+  bool& attr_set = gather ? g_dev[dev].attn_attr_gather : g_dev[dev].attn_attr;
+  if (!attr_set) {
     std::lock_guard<std::mutex> lk(g_dev_mu);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn_tc)");
-    g_dev[dev].attn_attr = true;
+    attr_set = true;
   }
   constexpr int kRowsPerItem = jb::attn::NQT * jb::attn::BQ;
   const int n_pairs = (S + kRowsPerItem - 1) / kRowsPerItem;
@@ -467,6 +475,28 @@ __global__ void wait_selftest_kernel(uint64_t limit_ns) {
   if (threadIdx.x == 0) (void)jb::mbar_wait_for(&bar, 0, kSelftestWaitSite, &abort_flag, limit_ns);
 }
 
+}  // namespace
+
+namespace {
+// bf16 LayerNorm / row statistics, one warp per row (N % 8 == 0, N <= 8192).
+int layernorm_warp_launch(const __nv_bfloat16* in, const float* gamma, const float* beta,
+                          __nv_bfloat16* out, float* mean_out, float* rstd_out, float2* stats,
+                          int64_t M, int N, float eps, cudaStream_t st) {
+  const unsigned grid = (unsigned)((M + 7) / 8);
+  const int nv = N / 8;
+#define JB_LN_WARP(NV)                                                                         \
+  jb::simt::layernorm_bf16_warp_kernel<NV><<<grid, 256, 0, st>>>(in, gamma, beta, out, mean_out, \
+                                                                 rstd_out, stats, M, N, eps)
+  if (nv <= 32) JB_LN_WARP(1);
+  else if (nv <= 64) JB_LN_WARP(2);
+  else if (nv <= 128) JB_LN_WARP(4);
+  else if (nv <= 256) JB_LN_WARP(8);
+  else if (nv <= 512) JB_LN_WARP(16);
+  else if (nv <= 1024) JB_LN_WARP(32);
+  else return fail(JULES_ERR_SHAPE, "layernorm: row of %d too long for the warp kernel", N);
+#undef JB_LN_WARP
+  return check_launch("layernorm_bf16_warp_kernel launch");
+}
 }  // namespace
 
 #include "dist.cuh"
@@ -837,8 +867,14 @@ int jules_layernorm(const void* in, const float* gamma, const float* beta, void*
   if ((in_dtype != JULES_DTYPE_F32 && !in_bf) || (out_dtype != JULES_DTYPE_F32 && !out_bf))
     return fail(JULES_ERR_DTYPE, "layernorm: dtypes %d/%d", in_dtype, out_dtype);
   const unsigned grid = (unsigned)M;
-  if (in_bf && out_bf && gamma && N % 8 == 0 && N <= 8 * 256 * 4 && aligned16(in) &&
-      aligned16(out) && aligned16(gamma) && aligned16(beta)) {
+  if (in_bf && out_bf && N % 8 == 0 && N <= 256 * 32 && aligned16(in) && aligned16(out) &&
+      (!gamma || (aligned16(gamma) && aligned16(beta)))) {
+    if (int rc = layernorm_warp_launch(static_cast<const __nv_bfloat16*>(in), gamma, beta,
+                                       static_cast<__nv_bfloat16*>(out), mean_out, rstd_out,
+                                       nullptr, M, (int)N, eps, st))
+      return rc;
+  } else if (in_bf && out_bf && gamma && N % 8 == 0 && N <= 8 * 256 * 4 && aligned16(in) &&
+             aligned16(out) && aligned16(gamma) && aligned16(beta)) {
     jb::simt::layernorm_bf16_vec_kernel<4><<<grid, 256, 0, st>>>(
         static_cast<const __nv_bfloat16*>(in), gamma, beta, static_cast<__nv_bfloat16*>(out),
         mean_out, rstd_out, M, (int)N, eps);
@@ -1133,6 +1169,63 @@ int jules_mlp_block(const void* X, const float* gamma, const float* beta, const 
     return rc;
   if (int rc = jules_gemm_bias_act(xn, W1, b1, nullptr, hid, T, dff, d, JULES_ACT_GELU,
                                    JULES_DTYPE_BF16, JULES_DTYPE_BF16, stream))
+    return rc;
+  return jules_gemm_bias_act(hid, W2, b2, X, out, T, d, dff, JULES_ACT_NONE, JULES_DTYPE_BF16,
+                             out_dtype, stream);
+}
+
+int jules_mlp_block_fold_weights(const float* gamma, const float* beta, const void* W1,
+                                 const float* b1, void* W1f, float* colsum, float* c, int64_t d,
+                                 int64_t dff, void* stream) {
+  if (!gamma || !beta || !W1 || !W1f || !colsum || !c)
+    return fail(JULES_ERR_ARG, "mlp_block_fold_weights: NULL pointer");
+  if (d <= 0 || dff <= 0 || d > INT32_MAX || dff > INT32_MAX)
+    return fail(JULES_ERR_SHAPE, "mlp_block_fold_weights: d=%lld dff=%lld", (long long)d, (long long)dff);
+  jb::simt::ln_fold_weights_kernel<<<(unsigned)((dff + 255) / 256), 256, 0,
+                                     static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(W1), gamma, beta, b1, static_cast<__nv_bfloat16*>(W1f),
+      colsum, c, (int)d, (int)dff);
+  return check_launch("ln_fold_weights_kernel launch");
+}
+
+size_t jules_mlp_block_folded_workspace_bytes(int64_t T, int64_t d, int64_t dff) {
+  if (T <= 0 || d <= 0 || dff <= 0) return 0;
+  return (((size_t)T * 8 + 255) & ~size_t(255)) + (((size_t)T * dff * 2 + 255) & ~size_t(255));
+}
+
+int jules_mlp_block_folded(const void* X, const void* W1f, const float* colsum, const float* c,
+                           const void* W2, const float* b2, void* out, int out_dtype, int64_t T,
+                           int64_t d, int64_t dff, float eps, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  if (!X || !W1f || !colsum || !c || !W2 || !out)
+    return fail(JULES_ERR_ARG, "mlp_block_folded: NULL pointer");
+  if (out_dtype != JULES_DTYPE_BF16 && out_dtype != JULES_DTYPE_F32)
+    return fail(JULES_ERR_DTYPE, "mlp_block_folded: out dtype %d", out_dtype);
+  if (T < 0 || d <= 0 || dff <= 0 || T > INT32_MAX || d > 8192 || dff > INT32_MAX ||
+      d % 8 != 0 || dff % 8 != 0)
+    return fail(JULES_ERR_SHAPE,
+                "mlp_block_folded: T=%lld d=%lld dff=%lld (needs d, dff multiples of 8, d <= 8192; "
+                "jules_mlp_block takes any shape)", (long long)T, (long long)d, (long long)dff);
+  if (!aligned16(X) || !aligned16(W1f) || !aligned16(colsum) || !aligned16(c) || !aligned16(W2) ||
+      !aligned16(out) || (b2 && !aligned16(b2)))
+    return fail(JULES_ERR_ALIGN, "mlp_block_folded: buffers must be 16-byte aligned");
+  if (T == 0) return ok();
+  const size_t need = jules_mlp_block_folded_workspace_bytes(T, d, dff);
+  if (!workspace || workspace_bytes < need)
+    return fail(JULES_ERR_WORKSPACE, "mlp_block_folded: workspace %zu < %zu bytes", workspace_bytes, need);
+  if (!aligned16(workspace)) return fail(JULES_ERR_ALIGN, "mlp_block_folded: workspace not 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float2* stats = static_cast<float2*>(workspace);
+  auto* hid = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(workspace) +
+                                               (((size_t)T * 8 + 255) & ~size_t(255)));
+  // row statistics of X (one read of X), then GEMM1 on the raw rows with the
+  // LayerNorm applied in its epilogue, then GEMM2 + bias + residual
+  if (int rc = layernorm_warp_launch(static_cast<const __nv_bfloat16*>(X), nullptr, nullptr, nullptr,
+                                     nullptr, nullptr, stats, T, (int)d, eps, st))
+    return rc;
+  if (int rc = gemm_tc_dispatch(static_cast<const __nv_bfloat16*>(X),
+                                static_cast<const __nv_bfloat16*>(W1f), c, nullptr, hid, T, dff, d,
+                                JULES_ACT_GELU, st, stats, colsum))
     return rc;
   return jules_gemm_bias_act(hid, W2, b2, X, out, T, d, dff, JULES_ACT_NONE, JULES_DTYPE_BF16,
                              out_dtype, stream);

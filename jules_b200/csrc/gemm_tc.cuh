@@ -92,6 +92,19 @@ __device__ __forceinline__ void store8(float* dst, const float (&v)[8]) {
   reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
 }
 
+// LayerNorm folded into the GEMM.  With W' = diag(gamma) W,
+//   LN(x) . W = rstd * (x . W' - mean * colsum(W')) + beta . W,
+// so a GEMM of the raw rows x against W' gives LN(x) . W from the row
+// statistics (mean, rstd) and the column sums of W'; beta . W (+ the GEMM's
+// own bias) arrives as the bias.  Applied to 8 accumulators of one row.
+__device__ __forceinline__ void ln_fold8(float (&v)[8], float2 rs, const float* colsum) {
+  const float4 c0 = *reinterpret_cast<const float4*>(colsum);
+  const float4 c1 = *reinterpret_cast<const float4*>(colsum + 4);
+  const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = rs.y * fmaf(-rs.x, cs[j], v[j]);
+}
+
 // TOut: __nv_bfloat16 (one RNE cast at the store) or float.  The residual
 // has the operands' dtype (bf16).
 template <int BN, int STAGES, typename TOut>
@@ -99,7 +112,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmW, const float* __restrict__ bias,
                         const __nv_bfloat16* __restrict__ residual, TOut* __restrict__ C,
-                        int M, int N, int K, int act) {
+                        int M, int N, int K, int act, const float2* __restrict__ ln_stats,
+                        const float* __restrict__ ln_colsum) {
   static_assert(BN % 64 == 0 && BN <= 256, "BN must be a multiple of 64, at most 256");
   using S = Smem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
@@ -207,6 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int row = m0 + row_in_tile;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      const float2 rs = ln_stats && row < M ? ln_stats[row] : make_float2(0.0f, 1.0f);
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
@@ -223,6 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               float v[8];
 #pragma unroll
               for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[g * 8 + j]);
+              if (ln_stats) ln_fold8(v, rs, ln_colsum + col);
               if (bias) {
                 const float4 b0 = *reinterpret_cast<const float4*>(bias + col);
                 const float4 b1 = *reinterpret_cast<const float4*>(bias + col + 4);
@@ -365,7 +381,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc2_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmW, const float* __restrict__ bias,
                          const __nv_bfloat16* __restrict__ residual, const OutDest<TOut> out,
-                         int M, int N, int K, int act, int whole_units, int num_units) {
+                         int M, int N, int K, int act, int whole_units, int num_units,
+                         const float2* __restrict__ ln_stats, const float* __restrict__ ln_colsum) {
   static_assert(TN == 256, "pair tile N is 256 (its halves are 128)");
   constexpr int TM = 256;
   constexpr uint32_t kTmemCols = 2 * TN;  // two accumulators
@@ -502,6 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int my_row = m0 + lane;  // row of this lane in the TMEM layout
       const __nv_bfloat16* rrow =
           residual ? residual + (size_t)(my_row < M ? my_row : 0) * N : nullptr;
+      const float2 rs = ln_stats && my_row < M ? ln_stats[my_row] : make_float2(0.0f, 1.0f);
 #pragma unroll 1
       for (int cb = 0; cb < pu.cols; cb += kBlk) {
 #pragma unroll
@@ -514,6 +532,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
           if (c0 < N) {  // N is a multiple of 8: a 32-column group is all in or starts past N
+            if (ln_stats) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) {
+                if (c0 + j < N) {
+                  float w8[8];
+#pragma unroll
+                  for (int q = 0; q < 8; ++q) w8[q] = v[j + q];
+                  ln_fold8(w8, rs, ln_colsum + c0 + j);
+#pragma unroll
+                  for (int q = 0; q < 8; ++q) v[j + q] = w8[q];
+                }
+              }
+            }
             if (bias) {
 #pragma unroll
               for (int j = 0; j < 32; j += 4) {

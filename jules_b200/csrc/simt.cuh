@@ -550,6 +550,122 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Weights of the LayerNorm folded into the following GEMM (prepared once per
+// weights): W'[k][n] = bf16(gamma[k] * W[k][n]), colsum[n] = sum over k of
+// W'[k][n] as the tensor core sees it (the bf16 values, k in order), and
+// c[n] = b[n] + sum over k of beta[k] * W[k][n].  One thread per column,
+// walking k (consecutive threads read consecutive columns).
+__global__ void __launch_bounds__(256)
+    ln_fold_weights_kernel(const __nv_bfloat16* __restrict__ W, const float* __restrict__ gamma,
+                           const float* __restrict__ beta, const float* __restrict__ b,
+                           __nv_bfloat16* __restrict__ Wf, float* __restrict__ colsum,
+                           float* __restrict__ cvec, int d, int n_cols) {
+  const int n = blockIdx.x * 256 + threadIdx.x;
+  if (n >= n_cols) return;
+  float cs = 0.0f, cb = b ? b[n] : 0.0f;
+  for (int k = 0; k < d; ++k) {
+    const float w = __bfloat162float(W[(size_t)k * n_cols + n]);
+    const __nv_bfloat16 wf = __float2bfloat16_rn(gamma[k] * w);
+    Wf[(size_t)k * n_cols + n] = wf;
+    cs += __bfloat162float(wf);
+    cb = fmaf(beta[k], w, cb);
+  }
+  colsum[n] = cs;
+  cvec[n] = cb;
+}
+
+// bf16 LayerNorm, one warp per row, for N % 8 == 0 and N <= 256 * NV: the
+// row stays in registers as bf16 (NV 16-byte vectors per lane, all loads in
+// flight at once), mean and biased variance by warp shuffles over two passes
+// of the registers (the reference's two-pass statistics), one HBM read, no
+// block barriers; 8 rows per 256-thread block.  Writes any of: the
+// normalised row (out, with gamma/beta or without both), mean_out /
+// rstd_out, and stats_out = (mean, rstd) per row (the row statistics the
+// LayerNorm folded into a GEMM epilogue needs).
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <int NV>
+__global__ void __launch_bounds__(256, NV <= 16 ? 2 : 1)
+    layernorm_bf16_warp_kernel(const __nv_bfloat16* __restrict__ in,
+                               const float* __restrict__ gamma, const float* __restrict__ beta,
+                               __nv_bfloat16* __restrict__ out, float* __restrict__ mean_out,
+                               float* __restrict__ rstd_out, float2* __restrict__ stats_out,
+                               int64_t M, int N, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= M) return;
+  const int nv = N >> 3;
+  const uint4* x = reinterpret_cast<const uint4*>(in + row * N);
+  uint4 xv[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + 32 * i;
+    xv[i] = c < nv ? x[c] : make_uint4(0u, 0u, 0u, 0u);
+  }
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&xv[i]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(p[j]);
+      s += f.x + f.y;
+    }
+  }
+  const float mean = warp_sum(s) / (float)N;
+  float v = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    if (lane + 32 * i < nv) {
+      const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&xv[i]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(p[j]);
+        const float d0 = f.x - mean, d1 = f.y - mean;
+        v = fmaf(d0, d0, v);
+        v = fmaf(d1, d1, v);
+      }
+    }
+  }
+  const float var = warp_sum(v) / (float)N;
+  const float inv_std = 1.0f / sqrtf(var + eps);
+  if (lane == 0) {
+    if (mean_out) mean_out[row] = mean;
+    if (rstd_out) rstd_out[row] = inv_std;
+    if (stats_out) stats_out[row] = make_float2(mean, inv_std);
+  }
+  if (!out) return;
+  uint4* y = reinterpret_cast<uint4*>(out + row * N);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nv) {
+      float g[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f}, bb[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (gamma) {
+        const float4 g0 = reinterpret_cast<const float4*>(gamma)[2 * c];
+        const float4 g1 = reinterpret_cast<const float4*>(gamma)[2 * c + 1];
+        const float4 b0 = reinterpret_cast<const float4*>(beta)[2 * c];
+        const float4 b1 = reinterpret_cast<const float4*>(beta)[2 * c + 1];
+        g[0] = g0.x; g[1] = g0.y; g[2] = g0.z; g[3] = g0.w; g[4] = g1.x; g[5] = g1.y; g[6] = g1.z; g[7] = g1.w;
+        bb[0] = b0.x; bb[1] = b0.y; bb[2] = b0.z; bb[3] = b0.w; bb[4] = b1.x; bb[5] = b1.y; bb[6] = b1.z; bb[7] = b1.w;
+      }
+      const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&xv[i]);
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(p[j]);
+        o[j] = pack_bf16x2((f.x - mean) * inv_std * g[2 * j] + bb[2 * j],
+                           (f.y - mean) * inv_std * g[2 * j + 1] + bb[2 * j + 1]);
+      }
+      y[c] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
 // Vectorised bf16 LayerNorm for N % 8 == 0 and N <= 8 * 256 * LNV: the row
 // stays in registers between the three passes (one HBM read).
 template <int LNV>

@@ -83,6 +83,30 @@ def half_ulp_bf16(x):
     return 2.0 ** (e - 8)
 
 
+def c4_bf16_model(X, gam, bet, W1, b1, W2, b2, rows, W1f=None, eps=1e-5):
+    """The block on the sampled rows in float64 with exactly the roundings a
+    bf16 pipeline makes: the GEMM1 operand (LN(X) rounded to bf16, or, for
+    the folded form, W1f = bf16(diag(gamma) W1) given) and the hidden
+    activation rounded to bf16; everything else exact.  At C4 these
+    roundings alone put the output 0.021-0.027 (max-abs) away from the fp32
+    reference on 48 rows (rel-L2 0.0022), so max-abs is checked against
+    this model (what is left is accumulation order) and rel-L2 against the
+    fp32 oracle."""
+    x = X[rows].astype(np.float64)
+    mu = x.mean(1, keepdims=True)
+    r = 1.0 / np.sqrt(((x - mu) ** 2).mean(1, keepdims=True) + eps)
+    W1d = W1.astype(np.float64)
+    if W1f is None:
+        ln = bf16_np(((x - mu) * r * gam + bet).astype(np.float32)).astype(np.float64)
+        v = ln @ W1d + b1
+    else:
+        Wf = W1f.astype(np.float64)
+        v = r * (x @ Wf - mu * Wf.sum(0)) + (bet.astype(np.float64) @ W1d + b1)
+    h = 0.5 * v * (1 + np.tanh(0.7978845608 * (v + 0.044715 * v ** 3)))
+    hb = bf16_np(h.astype(np.float32)).astype(np.float64)
+    return hb @ W2.astype(np.float64) + b2 + x
+
+
 def check_bf16_output(got, want):
     """bf16 output vs the fp32 oracle: rel-L2 <= 5e-3 and max-abs <= 2e-2
     beyond the output's own rounding (values >= 8 cannot be stored in bf16
@@ -125,9 +149,84 @@ def test_mlp_block_config_c4_sampled(jb, orc):
                          b1.cpu().numpy(), to_np(W2), b2.cpu().numpy(), rows=rows)
     idx = torch.from_numpy(rows).cuda()
     got32 = to_np(out32[idx])
-    assert max_abs(got32, want) <= BF16_MAX_ABS
     assert rel_l2(got32, want) <= BF16_REL_L2
-    check_bf16_output(to_np(out[idx]), want)
+    model = c4_bf16_model(to_np(X), gam.cpu().numpy(), bet.cpu().numpy(), to_np(W1),
+                          b1.cpu().numpy(), to_np(W2), b2.cpu().numpy(), rows)
+    assert max_abs(got32, model) <= BF16_MAX_ABS
+    assert max_abs(got32, want) <= 2 * BF16_MAX_ABS  # the format's own floor is ~0.025 here
     # every row: the bf16 output is the fp32 output rounded once
     assert torch.equal(out, out32.to(torch.bfloat16))
     assert bool(torch.isfinite(out32).all())
+
+
+# --- LayerNorm folded into GEMM1's epilogue (jules_mlp_block_folded) -------
+def _mlp_gpu_folded(jb, X, gam, bet, W1, b1, W2, b2, out_dtype=None):
+    import torch
+    f = lambda a: torch.from_numpy(a).cuda()
+    folded = jb.mlp_block_fold_weights(f(gam), f(bet), to_dev(W1), f(b1))
+    out = jb.mlp_block_folded(to_dev(X), folded, to_dev(W2), f(b2), out_dtype=out_dtype)
+    torch.cuda.synchronize()
+    assert jb.device_error() == 0
+    return out, folded
+
+
+# (256, 512, 2048): pair GEMMs; (200, 256, 1024): T < 256, the 1-CTA GEMM;
+# (520, 1024, 3072): ragged rows in the pair GEMM's last tile
+@pytest.mark.parametrize("T,d,dff", [(256, 512, 2048), (200, 256, 1024), (520, 1024, 3072)])
+def test_mlp_block_folded_vs_oracle(jb, orc, T, d, dff):
+    import torch
+    ins = _mlp_inputs(T, d, dff, seed=T + d + 1)
+    want = orc.mlp_block(*ins)
+    got32, folded = _mlp_gpu_folded(jb, *ins, out_dtype=torch.float32)
+    assert max_abs(to_np(got32), want) <= BF16_MAX_ABS
+    assert rel_l2(to_np(got32), want) <= BF16_REL_L2
+    got, _ = _mlp_gpu_folded(jb, *ins)
+    check_bf16_output(to_np(got), want)
+    # the folded weights themselves: W1f = bf16(gamma[k] W1[k, n]), colsum, c
+    X, gam, bet, W1, b1, W2, b2 = ins
+    W1f, colsum, c = (to_np(t) for t in folded)
+    assert np.array_equal(W1f, bf16_np(gam[:, None] * W1))
+    assert max_abs(colsum, W1f.astype(np.float64).sum(0)) <= 1e-4
+    assert max_abs(c, (bet.astype(np.float64) @ W1) + b1) <= 1e-4
+
+
+def test_mlp_block_folded_rejects_unsupported_shapes(jb):
+    import torch
+    h = jb.lib()
+    buf = torch.zeros(1 << 16, dtype=torch.uint8, device="cuda")
+    p = jb._ptr(buf)
+    assert h.jules_mlp_block_folded(p, p, p, p, p, p, p, 1, 16, 100, 256, 1e-5, p, 1 << 16, None) == 1
+    assert h.jules_mlp_block_folded(p, p, p, p, p, p, p, 1, 16, 64, 256, 1e-5, p, 16, None) == 8
+    assert h.jules_mlp_block_folded_workspace_bytes(16, 64, 256) == 256 + 16 * 256 * 2
+
+
+@pytest.mark.slow
+def test_mlp_block_folded_config_c4_sampled(jb, orc):
+    """Config C4 at full size through the folded path: 48 rows vs the oracle."""
+    import torch
+    T, d, dff = 16384, 4096, 16384
+    g = torch.Generator(device="cuda").manual_seed(4)
+    X = torch.randn((T, d), generator=g, device="cuda").to(torch.bfloat16)
+    gam = 1 + 0.02 * torch.randn(d, generator=g, device="cuda")
+    bet = 0.02 * torch.randn(d, generator=g, device="cuda")
+    W1 = (0.02 * torch.randn((d, dff), generator=g, device="cuda")).to(torch.bfloat16)
+    b1 = 0.02 * torch.randn(dff, generator=g, device="cuda")
+    W2 = (0.02 * torch.randn((dff, d), generator=g, device="cuda")).to(torch.bfloat16)
+    b2 = 0.02 * torch.randn(d, generator=g, device="cuda")
+    folded = jb.mlp_block_fold_weights(gam, bet, W1, b1)
+    out32 = jb.mlp_block_folded(X, folded, W2, b2, out_dtype=torch.float32)
+    out = jb.mlp_block_folded(X, folded, W2, b2)
+    torch.cuda.synchronize()
+    assert jb.device_error() == 0
+    rows = np.linspace(0, T - 1, 48).astype(np.int64)
+    want = orc.mlp_block(to_np(X), gam.cpu().numpy(), bet.cpu().numpy(), to_np(W1),
+                         b1.cpu().numpy(), to_np(W2), b2.cpu().numpy(), rows=rows)
+    idx = torch.from_numpy(rows).cuda()
+    got32 = to_np(out32[idx])
+    assert rel_l2(got32, want) <= BF16_REL_L2
+    model = c4_bf16_model(to_np(X), gam.cpu().numpy(), bet.cpu().numpy(), to_np(W1),
+                          b1.cpu().numpy(), to_np(W2), b2.cpu().numpy(), rows,
+                          W1f=to_np(folded[0]))
+    assert max_abs(got32, model) <= BF16_MAX_ABS
+    assert max_abs(got32, want) <= 2 * BF16_MAX_ABS  # the format's own floor is ~0.025 here
+    assert torch.equal(out, out32.to(torch.bfloat16))
