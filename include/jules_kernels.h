@@ -49,6 +49,9 @@ extern "C" {
  * (lib/Passes/MixedPrecisionPass.cpp:55-62, lib/Dialect/JulesDialect.cpp:41). */
 #define JULES_DTYPE_FP8E4M3 2
 #define JULES_DTYPE_FP8E5M2 3
+/* IEEE half: the other 16-bit type of the reference's mixed-precision pass,
+ * which treats f16 like bf16 (lib/Passes/MixedPrecisionPass.cpp:76). */
+#define JULES_DTYPE_F16 4
 
 /* Activations: same order as jules::kernel::ActivationType
  * (include/jules/Kernel/FusedKernels.h:61-67). */
@@ -90,9 +93,10 @@ int jules_selftest_bounded_wait(uint64_t limit_ns, void* stream);
  *   A [M,K], W [K,N], C and residual [M,N], bias [N] (fp32, nullable),
  *   residual nullable (same dtype as A and W).
  *   in_dtype: dtype of A, W and residual; out_dtype: dtype of C.
- * bf16 in (bf16 or fp32 out) with N % 8 == 0, K % 8 == 0 and 16-byte
- * aligned pointers runs on tcgen05 tensor cores (fp32 accumulate, fp32
- * epilogue, one cast at the store); everything else on CUDA cores in fp32.
+ * bf16 in (bf16 or fp32 out) or f16 in (f16 or fp32 out) with N % 8 == 0,
+ * K % 8 == 0 and 16-byte aligned pointers runs on tcgen05 tensor cores (fp32
+ * accumulate, fp32 epilogue, one cast at the store); everything else on CUDA
+ * cores in fp32.
  * in_dtype JULES_DTYPE_FP8E4M3 / FP8E5M2 runs jules_gemm_fp8 with scale 1
  * (residual then bf16).
  * Replaces tiledMatmulWithActivation (FusedKernels.h:378-458),
@@ -119,8 +123,9 @@ int jules_sgemm(int transA, int transB, int64_t M, int64_t N, int64_t K, float a
  *   lse = log(sum_j exp(scale * q.k_j)) per query row, natural log.
  *   Hq % Hkv == 0 (grouped-query heads: kv head = h / (Hq/Hkv)).
  *   causal != 0 masks key j > query i.  scale <= 0 means 1/sqrt(D).
- *   dtype F32 (fp32 in/out, CUDA cores) or BF16 (bf16 in/out, fp32
- *   softmax statistics; D == 128 runs on tcgen05).
+ *   dtype F32 (fp32 in/out, CUDA cores), BF16 or F16 (16-bit in/out, fp32
+ *   softmax statistics; D == 128 or 64 with 16-byte aligned buffers runs on
+ *   tcgen05, P in the operand type).
  * Replaces flashAttention (FlashAttention.h:130-309), standardAttention
  * (:52-100) and attention (:114-124), which are the non-causal, Hq == Hkv,
  * fp32 special case.

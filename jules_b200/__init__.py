@@ -25,7 +25,7 @@ __all__ = [
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libjules_b200.so")
 
 ACT = {"none": 0, "relu": 1, "sigmoid": 2, "tanh": 3, "gelu": 4}
-DT_F32, DT_BF16, DT_FP8E4M3, DT_FP8E5M2 = 0, 1, 2, 3
+DT_F32, DT_BF16, DT_FP8E4M3, DT_FP8E5M2, DT_F16 = 0, 1, 2, 3, 4
 
 _c_vp = ctypes.c_void_p
 _c_i64 = ctypes.c_int64
@@ -135,6 +135,8 @@ def _dtype_code(t) -> int:
         return DT_F32
     if t.dtype == torch.bfloat16:
         return DT_BF16
+    if t.dtype == torch.float16:
+        return DT_F16
     if t.dtype == torch.float8_e4m3fn:
         return DT_FP8E4M3
     if t.dtype == torch.float8_e5m2:

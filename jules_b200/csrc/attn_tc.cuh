@@ -1,4 +1,5 @@
-// Flash-attention forward on tcgen05 tensor cores (bf16, head_dim 128).
+// Flash-attention forward on tcgen05 tensor cores (bf16 or fp16, head_dim
+// 128 or 64: template parameters TEl and HDIM).
 //
 // Computes, per (batch, query head) and query row i,
 //   O_i = sum_j softmax_j(scale * q_i . k_j) v_j,   lse_i = log sum_j exp(...)
@@ -39,7 +40,7 @@
 namespace jb {
 namespace attn {
 
-constexpr int HD = 128;   // head dim handled here
+constexpr int HD = 128;   // largest head dim handled here (64 is the other)
 constexpr int BQ = 128;   // query rows per tile (MMA M)
 constexpr int NQT = 2;    // query tiles per work item
 constexpr int BKV = 128;  // keys per tile (MMA N of S, K of PV)
@@ -164,7 +165,7 @@ __device__ __forceinline__ void tmem_ld32_at(uint32_t taddr, uint32_t* r) {
       : "r"(taddr));
 }
 
-template <bool kGather>
+template <int HDIM, typename TEl, bool kGather>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                        const __grid_constant__ CUtensorMap tmK,
@@ -228,30 +229,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int n_kv = kv_tiles(pair, n_kv_full, causal);
         const int q0 = pair * NQT * BQ;
         if (!mbar_wait(&s.q_empty, (wi & 1u) ^ 1u, 10, abort_flag)) break;
-        mbar_arrive_expect_tx(&s.q_full, NQT * 2 * kChunk);
+        constexpr int kBoxes = HDIM / 64;  // 64-dim boxes per row
+        mbar_arrive_expect_tx(&s.q_full, NQT * kBoxes * kChunk);
 #pragma unroll
         for (int t = 0; t < NQT; ++t) {
           tma_load_3d(s.q[t][0], &tmQ, &s.q_full, 0, q0 + t * BQ, bh);
-          tma_load_3d(s.q[t][1], &tmQ, &s.q_full, 64, q0 + t * BQ, bh);
+          if (kBoxes == 2) tma_load_3d(s.q[t][1], &tmQ, &s.q_full, 64, q0 + t * BQ, bh);
         }
         for (int j = 0; j < n_kv; ++j, ++kvi) {
           const uint32_t st = kvi % KVS, ph = (kvi / KVS) & 1u;
           if (!mbar_wait(&s.k_empty[st], ph ^ 1u, 11, abort_flag)) { ok = false; break; }
-          mbar_arrive_expect_tx(&s.k_full[st], 2 * kChunk);
+          mbar_arrive_expect_tx(&s.k_full[st], kBoxes * kChunk);
           tma_load_3d(s.k[st][0], &tmK, &s.k_full[st], 0, j * BKV, zkv);
-          tma_load_3d(s.k[st][1], &tmK, &s.k_full[st], 64, j * BKV, zkv);
+          if (kBoxes == 2) tma_load_3d(s.k[st][1], &tmK, &s.k_full[st], 64, j * BKV, zkv);
           if (!mbar_wait(&s.v_empty[st], ph ^ 1u, 12, abort_flag)) { ok = false; break; }
-          mbar_arrive_expect_tx(&s.v_full[st], 2 * kChunk);
+          mbar_arrive_expect_tx(&s.v_full[st], kBoxes * kChunk);
           tma_load_3d(s.v[st][0], &tmV, &s.v_full[st], 0, j * BKV, zkv);
-          tma_load_3d(s.v[st][1], &tmV, &s.v_full[st], 64, j * BKV, zkv);
+          if (kBoxes == 2) tma_load_3d(s.v[st][1], &tmV, &s.v_full[st], 64, j * BKV, zkv);
         }
       }
     }
   } else if (warp == kWarpMma) {
     // ------------------------------ MMA issuer ------------------------------
     if (lane == 0) {
-      constexpr uint32_t idS = idesc_bf16_f32(BQ, BKV, false, false);
-      constexpr uint32_t idPV = idesc_bf16_f32(BQ, HD, false, true);
+      constexpr uint32_t idS = idesc_f16kind<TEl>(BQ, BKV, false, false);
+      constexpr uint32_t idPV = idesc_f16kind<TEl>(BQ, HDIM, false, true);
       uint32_t kvi = 0, wi = 0;
       uint32_t pvc_t[NQT] = {0, 0};  // completed key steps per tile (barrier phases)
       bool ok = true;
@@ -266,14 +268,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint64_t kChunkStep = kChunk >> 4;           // next 64-dim chunk
       constexpr uint64_t kStageStep = (2 * kChunk) >> 4;     // next Q tile / ring slot
       auto issue_s = [&](int t, uint32_t st) {
-        uint64_t a[8], b[8];
         const uint64_t qa = dq0 + t * kStageStep, kb = dk0 + st * kStageStep;
+        if constexpr (HDIM == 128) {
+          uint64_t a[8], b[8];
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          a[kk] = qa + (kk >> 2) * kChunkStep + (kk & 3) * 2;
-          b[kk] = kb + (kk >> 2) * kChunkStep + (kk & 3) * 2;
+          for (int kk = 0; kk < 8; ++kk) {
+            a[kk] = qa + (kk >> 2) * kChunkStep + (kk & 3) * 2;
+            b[kk] = kb + (kk >> 2) * kChunkStep + (kk & 3) * 2;
+          }
+          umma8_ss(tbase + t * BKV, a, b, 0u, idS);
+        } else {  // one 64-dim chunk: 4 K-steps
+          uint64_t a[4], b[4];
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            a[kk] = qa + kk * 2;
+            b[kk] = kb + kk * 2;
+          }
+          umma4_ss(tbase + t * BKV, a, b, 0u, idS);
         }
-        umma8_ss(tbase + t * BKV, a, b, 0u, idS);
         umma_commit(&s.s_full[t]);
       };
       auto issue_pv = [&](int t, uint32_t st, bool accumulate) {
@@ -285,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           pa[kk] = tbase + t * BKV + kk * 8;
           b[kk] = vb + kk * 128;
         }
-        umma8_ts(tbase + 256 + t * HD, pa, b, accumulate ? 1u : 0u, idPV);
+        umma8_ts(tbase + 256 + t * HDIM, pa, b, accumulate ? 1u : 0u, idPV);
       };
       for (int w = blockIdx.x; w < total && ok; w += gridDim.x, ++wi) {
         int pair, bh;
@@ -362,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = quarter * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t tS = tbase + t * BKV + lane_off;
-    const uint32_t tO = tbase + 256 + t * HD + lane_off;
+    const uint32_t tO = tbase + 256 + t * HDIM + lane_off;
     uint32_t pvc = 0, wi = 0;
     for (int w = blockIdx.x; w < total; w += gridDim.x, ++wi) {
       int pair, bh;
@@ -427,9 +439,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             upk2(x2, x0, x1);
             const float e0 = ex2_approx(x0), e1 = ex2_approx(x1);
             sum2[c & 1] = add2(sum2[c & 1], pk2(e0, e1));
-            pk[c] = pack_bf16x2(e0, e1);
+            pk[c] = pack2<TEl>(e0, e1);
           }
-          // P (bf16 pairs) over the first 64 columns of this tile's S.
+          // P (pairs of the operand type) over the first 64 columns of this tile's S.
           tmem_st32(tS + half * 32, pk);
         }
         float sa, sb, sc2, sd;
@@ -439,7 +451,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j > 0 && __any_sync(0xffffffffu, need)) {
           // PV(t, j-1) has completed: its commit precedes S(t, j)'s.
 #pragma unroll 1
-          for (int c = 0; c < HD; c += 32) {
+          for (int c = 0; c < HDIM; c += 32) {
             uint32_t o[32];
             tmem_ld32(tO + c, o);
             tmem_ld_wait(o);
@@ -466,9 +478,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = q < S;
       const int row0 = qt0 + quarter * 32;  // first row of this warp
       if constexpr (!kGather) {
-        __nv_bfloat16* orow = out.o[0] + ((size_t)bh * S + (row_ok ? q : 0)) * HD;
+        __nv_bfloat16* orow = out.o[0] + ((size_t)bh * S + (row_ok ? q : 0)) * HDIM;
 #pragma unroll 1
-        for (int c = 0; c < HD; c += 32) {
+        for (int c = 0; c < HDIM; c += 32) {
           uint32_t o[32];
           tmem_ld32(tO + c, o);
           tmem_ld_wait(o);
@@ -477,10 +489,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int g8 = 0; g8 < 4; ++g8) {
               uint4 v;
-              v.x = pack_bf16x2(__uint_as_float(o[8 * g8 + 0]) * inv_l, __uint_as_float(o[8 * g8 + 1]) * inv_l);
-              v.y = pack_bf16x2(__uint_as_float(o[8 * g8 + 2]) * inv_l, __uint_as_float(o[8 * g8 + 3]) * inv_l);
-              v.z = pack_bf16x2(__uint_as_float(o[8 * g8 + 4]) * inv_l, __uint_as_float(o[8 * g8 + 5]) * inv_l);
-              v.w = pack_bf16x2(__uint_as_float(o[8 * g8 + 6]) * inv_l, __uint_as_float(o[8 * g8 + 7]) * inv_l);
+              v.x = pack2<TEl>(__uint_as_float(o[8 * g8 + 0]) * inv_l, __uint_as_float(o[8 * g8 + 1]) * inv_l);
+              v.y = pack2<TEl>(__uint_as_float(o[8 * g8 + 2]) * inv_l, __uint_as_float(o[8 * g8 + 3]) * inv_l);
+              v.z = pack2<TEl>(__uint_as_float(o[8 * g8 + 4]) * inv_l, __uint_as_float(o[8 * g8 + 5]) * inv_l);
+              v.w = pack2<TEl>(__uint_as_float(o[8 * g8 + 6]) * inv_l, __uint_as_float(o[8 * g8 + 7]) * inv_l);
               dst[g8] = v;
             }
           }
@@ -489,17 +501,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint4* stg = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(&s) +
                                             ((sizeof(Smem) + 127) & ~size_t(127))) + warp * 32 * 4;
 #pragma unroll 1
-      for (int c = 0; c < HD; c += 32) {
+      for (int c = 0; c < HDIM; c += 32) {
         uint32_t o[32];
         tmem_ld32(tO + c, o);
         tmem_ld_wait(o);
 #pragma unroll
         for (int g8 = 0; g8 < 4; ++g8) {
           uint4 v;
-          v.x = pack_bf16x2(__uint_as_float(o[8 * g8 + 0]) * inv_l, __uint_as_float(o[8 * g8 + 1]) * inv_l);
-          v.y = pack_bf16x2(__uint_as_float(o[8 * g8 + 2]) * inv_l, __uint_as_float(o[8 * g8 + 3]) * inv_l);
-          v.z = pack_bf16x2(__uint_as_float(o[8 * g8 + 4]) * inv_l, __uint_as_float(o[8 * g8 + 5]) * inv_l);
-          v.w = pack_bf16x2(__uint_as_float(o[8 * g8 + 6]) * inv_l, __uint_as_float(o[8 * g8 + 7]) * inv_l);
+          v.x = pack2<TEl>(__uint_as_float(o[8 * g8 + 0]) * inv_l, __uint_as_float(o[8 * g8 + 1]) * inv_l);
+          v.y = pack2<TEl>(__uint_as_float(o[8 * g8 + 2]) * inv_l, __uint_as_float(o[8 * g8 + 3]) * inv_l);
+          v.z = pack2<TEl>(__uint_as_float(o[8 * g8 + 4]) * inv_l, __uint_as_float(o[8 * g8 + 5]) * inv_l);
+          v.w = pack2<TEl>(__uint_as_float(o[8 * g8 + 6]) * inv_l, __uint_as_float(o[8 * g8 + 7]) * inv_l);
           stg[lane * 4 + (g8 ^ ((lane >> 1) & 3))] = v;
         }
         __syncwarp();
@@ -508,7 +520,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int rr = (lane >> 2) + 8 * i;
           if (row0 + rr < S) {
             const uint4 v = stg[rr * 4 + ((lane & 3) ^ ((rr >> 1) & 3))];
-            const size_t off = ((size_t)bh * S + row0 + rr) * HD + c + (lane & 3) * 8;
+            const size_t off = ((size_t)bh * S + row0 + rr) * HDIM + c + (lane & 3) * 8;
 #pragma unroll
             for (int p = 0; p < kMaxPeers; ++p)
               if (p < out.n) *reinterpret_cast<uint4*>(out.o[p] + off) = v;

@@ -10,6 +10,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <set>
 #include <mutex>
 #include <string>
 #include <utility>
@@ -54,11 +55,6 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 constexpr int kMaxDevices = 64;
 struct DeviceInfo {
   int sms = 0;
-  bool gemm_attr = false;
-  bool gemm_attr_f32 = false;
-  int gemm2_pairs[2][2] = {{0, 0}, {0, 0}};  // resident CTA pairs, [fp32 out][TN == 256]
-  bool attn_attr = false;
-  bool attn_attr_gather = false;
 };
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_dev_mu;
@@ -96,9 +92,10 @@ PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
   return fn;
 }
 
-// rank-2 or rank-3 bf16 map with 128-byte swizzle.
+// rank-2 or rank-3 map of 16-bit elements (bf16 or f16) with 128-byte swizzle.
 int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
-                   const uint64_t* strides_bytes, const uint32_t* box) {
+                   const uint64_t* strides_bytes, const uint32_t* box,
+                   CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
   auto enc = tmap_encoder();
   if (!enc) return fail(JULES_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   cuuint64_t d[3];
@@ -110,7 +107,7 @@ int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const uint64_t*
     bx[i] = box[i];
   }
   for (int i = 0; i < rank - 1; ++i) st[i] = strides_bytes[i];
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, st,
+  CUresult r = enc(map, dt, rank, const_cast<void*>(base), d, st,
                    bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(JULES_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -134,6 +131,17 @@ int make_tmap_i8(CUtensorMap* map, const void* base, uint64_t cols, uint64_t row
   return JULES_OK;
 }
 
+// Dynamic shared memory limit of a kernel, raised once per (device, kernel).
+int ensure_smem_attr(const void* kern, size_t smem, int dev) {
+  static std::set<std::pair<int, const void*>> done;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (done.count({dev, kern})) return JULES_OK;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+  done.insert({dev, kern});
+  return JULES_OK;
+}
+
 int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, what);
@@ -146,10 +154,17 @@ int check_launch(const char* what) {
 constexpr int kGemmBN = 256;
 constexpr int kGemmStages = 4;
 
-template <typename TOut>
-int gemm_tc(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
-            const __nv_bfloat16* res, TOut* C, int64_t M, int64_t N, int64_t K, int act,
-            cudaStream_t st, const float2* ln_stats = nullptr, const float* ln_colsum = nullptr) {
+template <typename TIn>
+constexpr CUtensorMapDataType tmap_dtype() {
+  return std::is_same<TIn, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                          : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+}
+
+// TIn: __nv_bfloat16 or __half operands (and residual); TOut: TIn or float.
+template <typename TIn, typename TOut>
+int gemm_tc(const TIn* A, const TIn* W, const float* bias, const TIn* res, TOut* C, int64_t M,
+            int64_t N, int64_t K, int act, cudaStream_t st, const float2* ln_stats = nullptr,
+            const float* ln_colsum = nullptr) {
   int dev;
   if (int rc = current_device(&dev)) return rc;
   CUtensorMap ta, tw;
@@ -157,23 +172,17 @@ int gemm_tc(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
     const uint64_t strides[1] = {(uint64_t)K * 2};
     const uint32_t box[2] = {64, 128};
-    if (int rc = make_tmap_bf16(&ta, A, 2, dims, strides, box)) return rc;
+    if (int rc = make_tmap_bf16(&ta, A, 2, dims, strides, box, tmap_dtype<TIn>())) return rc;
   }
   {
     const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
     const uint64_t strides[1] = {(uint64_t)N * 2};
     const uint32_t box[2] = {64, 64};
-    if (int rc = make_tmap_bf16(&tw, W, 2, dims, strides, box)) return rc;
+    if (int rc = make_tmap_bf16(&tw, W, 2, dims, strides, box, tmap_dtype<TIn>())) return rc;
   }
-  auto kern = jb::gemm::gemm_bf16_tc_kernel<kGemmBN, kGemmStages, TOut>;
+  auto kern = jb::gemm::gemm_bf16_tc_kernel<kGemmBN, kGemmStages, TIn, TOut>;
   const size_t smem = sizeof(jb::gemm::Smem<kGemmBN, kGemmStages>) + 1024;
-  bool& attr_set = std::is_same<TOut, float>::value ? g_dev[dev].gemm_attr_f32 : g_dev[dev].gemm_attr;
-  if (!attr_set) {
-    std::lock_guard<std::mutex> lk(g_dev_mu);
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm)");
-    attr_set = true;
-  }
+  if (int rc = ensure_smem_attr((const void*)kern, smem, dev)) return rc;
   const int64_t tiles = ((M + 127) / 128) * ((N + kGemmBN - 1) / kGemmBN);
   const int grid = (int)(tiles < device_sms(dev) ? tiles : device_sms(dev));
   kern<<<grid, jb::gemm::kThreads, smem, st>>>(ta, tw, bias, res, C, (int)M, (int)N, (int)K, act,
@@ -184,9 +193,9 @@ int gemm_tc(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
 // CTA-pair tcgen05 GEMM (256 x 256 tiles, cluster of 2).
 // out: the local C, or every rank's C for the sharded GEMM with the gather
 // fused into the epilogue (M = this rank's rows).
-template <int TN, typename TOut>
-int gemm_tc2(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
-             const __nv_bfloat16* res, const jb::gemm::OutDest<TOut>& out, int64_t M, int64_t N,
+template <int TN, typename TIn, typename TOut>
+int gemm_tc2(const TIn* A, const TIn* W, const float* bias,
+             const TIn* res, const jb::gemm::OutDest<TOut>& out, int64_t M, int64_t N,
              int64_t K, int act, cudaStream_t st, const float2* ln_stats = nullptr,
              const float* ln_colsum = nullptr) {
   int dev;
@@ -196,16 +205,16 @@ int gemm_tc2(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
     const uint64_t strides[1] = {(uint64_t)K * 2};
     const uint32_t box[2] = {64, 128};
-    if (int rc = make_tmap_bf16(&ta, A, 2, dims, strides, box)) return rc;
+    if (int rc = make_tmap_bf16(&ta, A, 2, dims, strides, box, tmap_dtype<TIn>())) return rc;
   }
   {
     const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
     const uint64_t strides[1] = {(uint64_t)N * 2};
     const uint32_t box[2] = {64, 64};
-    if (int rc = make_tmap_bf16(&tw, W, 2, dims, strides, box)) return rc;
+    if (int rc = make_tmap_bf16(&tw, W, 2, dims, strides, box, tmap_dtype<TIn>())) return rc;
   }
   constexpr int kStages = TN == 256 ? 6 : 8;
-  auto kern = jb::gemm::gemm_bf16_tc2_kernel<kStages, TN, TOut>;
+  auto kern = jb::gemm::gemm_bf16_tc2_kernel<kStages, TN, TIn, TOut>;
   const size_t smem = sizeof(jb::gemm::Smem2<kStages, TN>) + 1024;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
@@ -218,16 +227,26 @@ int gemm_tc2(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  int& max_pairs = g_dev[dev].gemm2_pairs[std::is_same<TOut, float>::value ? 1 : 0][TN == 256 ? 1 : 0];
-  if (max_pairs == 0) {
+  // resident CTA pairs of this kernel, queried once per device
+  static std::map<std::pair<int, const void*>, int> pairs_of;
+  int max_pairs = 0;
+  {
     std::lock_guard<std::mutex> lk(g_dev_mu);
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm2)");
+    auto it = pairs_of.find({dev, (const void*)kern});
+    if (it != pairs_of.end()) max_pairs = it->second;
+  }
+  if (max_pairs == 0) {
+    if (int rc = ensure_smem_attr((const void*)kern, smem, dev)) return rc;
     cfg.gridDim = dim3(2 * (device_sms(dev) / 2));
     int clusters = 0;
-    e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
-    if (e != cudaSuccess || clusters <= 0) clusters = device_sms(dev) / 2;
+    cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+    if (e != cudaSuccess || clusters <= 0) {
+      (void)cudaGetLastError();
+      clusters = device_sms(dev) / 2;
+    }
     max_pairs = clusters;
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    pairs_of[{dev, (const void*)kern}] = clusters;
   }
   const int64_t tiles = ((M + 255) / 256) * ((N + TN - 1) / TN);
   // Tail split (see gemm_bf16_tc2_kernel): the r tiles of the last, partial
@@ -249,9 +268,9 @@ int gemm_tc2(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
 // N fill them, 128 x 256 single-CTA tiles below that.  (256 x 128 pair tiles
 // measured slower: their N=128 MMAs leave the tensor pipe idle between
 // instructions.)
-template <typename TOut>
-int gemm_tc_dispatch(const __nv_bfloat16* A, const __nv_bfloat16* W, const float* bias,
-                     const __nv_bfloat16* res, TOut* C, int64_t M, int64_t N, int64_t K, int act,
+template <typename TIn, typename TOut>
+int gemm_tc_dispatch(const TIn* A, const TIn* W, const float* bias,
+                     const TIn* res, TOut* C, int64_t M, int64_t N, int64_t K, int act,
                      cudaStream_t st, const float2* ln_stats = nullptr,
                      const float* ln_colsum = nullptr) {
   if (M < 256 || N < 256) return gemm_tc(A, W, bias, res, C, M, N, K, act, st, ln_stats, ln_colsum);
@@ -328,44 +347,55 @@ int attn_simt(const void* Q, const void* K, const void* V, void* O, float* lse, 
 }
 
 // out: the local O / lse, or every rank's for the sharded call with the
-// gather fused in (B, Hq, Hkv: this rank's units).
+// gather fused in (B, Hq, Hkv: this rank's units).  D is 64 or 128; f16
+// selects fp16 operands and output (else bf16).
+template <int HDIM, typename TEl, bool G>
+int attn_tc_launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                   const jb::attn::AttnOut& out, int B, int Hq, int Hkv, int S, float scale_log2,
+                   int causal, int dev, int grid, cudaStream_t st) {
+  auto kern = jb::attn::attn_fwd_tc_kernel<HDIM, TEl, G>;
+  // with the gather fused in: the staged epilogue's shared memory after Smem
+  const size_t smem = ((sizeof(jb::attn::Smem) + 127) & ~size_t(127)) + 1024 +
+                      (G ? jb::attn::kEpiBytes : 0);
+  if (int rc = ensure_smem_attr((const void*)kern, smem, dev)) return rc;
+  kern<<<grid, jb::attn::kThreads, smem, st>>>(tq, tk, tv, out, B, Hq, Hkv, S, scale_log2, causal);
+  return check_launch("attn_fwd_tc_kernel launch");
+}
+
 int attn_tc(const void* Q, const void* K, const void* V, const jb::attn::AttnOut& out, int B, int Hq,
-            int Hkv, int S, int D, float scale, int causal, cudaStream_t st) {
+            int Hkv, int S, int D, float scale, int causal, bool f16, cudaStream_t st) {
   int dev;
   if (int rc = current_device(&dev)) return rc;
   CUtensorMap tq, tk, tv;
   const uint32_t box[3] = {64, (uint32_t)jb::attn::BQ, 1};
   const uint32_t boxkv[3] = {64, (uint32_t)jb::attn::BKV, 1};
+  const CUtensorMapDataType dt = f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   {
     const uint64_t dims[3] = {(uint64_t)D, (uint64_t)S, (uint64_t)B * Hq};
     const uint64_t strides[2] = {(uint64_t)D * 2, (uint64_t)S * D * 2};
-    if (int rc = make_tmap_bf16(&tq, Q, 3, dims, strides, box)) return rc;
+    if (int rc = make_tmap_bf16(&tq, Q, 3, dims, strides, box, dt)) return rc;
   }
   {
     const uint64_t dims[3] = {(uint64_t)D, (uint64_t)S, (uint64_t)B * Hkv};
     const uint64_t strides[2] = {(uint64_t)D * 2, (uint64_t)S * D * 2};
-    if (int rc = make_tmap_bf16(&tk, K, 3, dims, strides, boxkv)) return rc;
-    if (int rc = make_tmap_bf16(&tv, V, 3, dims, strides, boxkv)) return rc;
-  }
-  // out.n > 1: the gather is fused in (staged epilogue, extra shared memory)
-  const bool gather = out.n > 1;
-  auto kern = gather ? jb::attn::attn_fwd_tc_kernel<true> : jb::attn::attn_fwd_tc_kernel<false>;
-  const size_t smem = ((sizeof(jb::attn::Smem) + 127) & ~size_t(127)) + 1024 +
-                      (gather ? jb::attn::kEpiBytes : 0);
-  bool& attr_set = gather ? g_dev[dev].attn_attr_gather : g_dev[dev].attn_attr;
-  if (!attr_set) {
-    std::lock_guard<std::mutex> lk(g_dev_mu);
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(attn_tc)");
-    attr_set = true;
+    if (int rc = make_tmap_bf16(&tk, K, 3, dims, strides, boxkv, dt)) return rc;
+    if (int rc = make_tmap_bf16(&tv, V, 3, dims, strides, boxkv, dt)) return rc;
   }
   constexpr int kRowsPerItem = jb::attn::NQT * jb::attn::BQ;
   const int n_pairs = (S + kRowsPerItem - 1) / kRowsPerItem;
   const int64_t work = (int64_t)n_pairs * B * Hq;
   const int grid = (int)(work < device_sms(dev) ? work : device_sms(dev));
   const float scale_log2 = scale * 1.4426950408889634f;
-  kern<<<grid, jb::attn::kThreads, smem, st>>>(tq, tk, tv, out, B, Hq, Hkv, S, scale_log2, causal);
-  return check_launch("attn_fwd_tc_kernel launch");
+  const bool g = out.n > 1;
+#define JB_ATTN(HDIM, T, G) \
+  attn_tc_launch<HDIM, T, G>(tq, tk, tv, out, B, Hq, Hkv, S, scale_log2, causal, dev, grid, st)
+  if (D == 128) {
+    if (f16) return g ? JB_ATTN(128, __half, true) : JB_ATTN(128, __half, false);
+    return g ? JB_ATTN(128, __nv_bfloat16, true) : JB_ATTN(128, __nv_bfloat16, false);
+  }
+  if (f16) return g ? JB_ATTN(64, __half, true) : JB_ATTN(64, __half, false);
+  return g ? JB_ATTN(64, __nv_bfloat16, true) : JB_ATTN(64, __nv_bfloat16, false);
+#undef JB_ATTN
 }
 
 size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
@@ -763,6 +793,21 @@ int jules_gemm_bias_act(const void* A, const void* W, const float* bias, const v
     return jules_gemm_fp8(A, W, bias, residual, C, M, N, K, 1.0f, act, in_dtype, in_dtype,
                           out_dtype, stream);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (in_dtype == JULES_DTYPE_F16 || out_dtype == JULES_DTYPE_F16) {
+    if (in_dtype != JULES_DTYPE_F16 || (out_dtype != JULES_DTYPE_F16 && out_dtype != JULES_DTYPE_F32))
+      return fail(JULES_ERR_DTYPE, "gemm: dtypes %d/%d (f16 operands give f16 or fp32 C)", in_dtype, out_dtype);
+    const bool out_h = out_dtype == JULES_DTYPE_F16;
+    if (N % 8 == 0 && K % 8 == 0 && aligned16(A) && aligned16(W) && aligned16(C) &&
+        (!bias || aligned16(bias)) && (!residual || aligned16(residual))) {
+      const auto* a = static_cast<const __half*>(A);
+      const auto* w = static_cast<const __half*>(W);
+      const auto* r = static_cast<const __half*>(residual);
+      if (out_h) return gemm_tc_dispatch(a, w, bias, r, static_cast<__half*>(C), M, N, K, act, st);
+      return gemm_tc_dispatch(a, w, bias, r, static_cast<float*>(C), M, N, K, act, st);
+    }
+    if (out_h) return gemm_simt<__half, __half>(A, W, bias, residual, C, M, N, K, act, 0, st);
+    return gemm_simt<__half, float>(A, W, bias, residual, C, M, N, K, act, 1, st);
+  }
   const bool in_bf = in_dtype == JULES_DTYPE_BF16, out_bf = out_dtype == JULES_DTYPE_BF16;
   if ((in_dtype != JULES_DTYPE_F32 && !in_bf) || (out_dtype != JULES_DTYPE_F32 && !out_bf))
     return fail(JULES_ERR_DTYPE, "gemm: dtypes %d/%d", in_dtype, out_dtype);
@@ -812,14 +857,16 @@ int jules_flash_attention_fwd(const void* Q, const void* K, const void* V, void*
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == JULES_DTYPE_F32)
     return attn_simt<float>(Q, K, V, O, lse, B, Hq, Hkv, S, D, scale, causal ? 1 : 0, st);
-  if (dtype != JULES_DTYPE_BF16) return fail(JULES_ERR_DTYPE, "attention: dtype %d", dtype);
-  if (D == jb::attn::HD && aligned16(Q) && aligned16(K) && aligned16(V) && aligned16(O)) {
+  const bool f16 = dtype == JULES_DTYPE_F16;
+  if (dtype != JULES_DTYPE_BF16 && !f16) return fail(JULES_ERR_DTYPE, "attention: dtype %d", dtype);
+  if ((D == 128 || D == 64) && aligned16(Q) && aligned16(K) && aligned16(V) && aligned16(O)) {
     jb::attn::AttnOut out{};
     out.o[0] = static_cast<__nv_bfloat16*>(O);
     out.lse[0] = lse;
     out.n = 1;
-    return attn_tc(Q, K, V, out, B, Hq, Hkv, S, D, scale, causal ? 1 : 0, st);
+    return attn_tc(Q, K, V, out, B, Hq, Hkv, S, D, scale, causal ? 1 : 0, f16, st);
   }
+  if (f16) return attn_simt<__half>(Q, K, V, O, lse, B, Hq, Hkv, S, D, scale, causal ? 1 : 0, st);
   return attn_simt<__nv_bfloat16>(Q, K, V, O, lse, B, Hq, Hkv, S, D, scale, causal ? 1 : 0, st);
 }
 
@@ -1223,9 +1270,9 @@ int jules_mlp_block_folded(const void* X, const void* W1f, const float* colsum, 
   if (int rc = layernorm_warp_launch(static_cast<const __nv_bfloat16*>(X), nullptr, nullptr, nullptr,
                                      nullptr, nullptr, stats, T, (int)d, eps, st))
     return rc;
-  if (int rc = gemm_tc_dispatch(static_cast<const __nv_bfloat16*>(X),
-                                static_cast<const __nv_bfloat16*>(W1f), c, nullptr, hid, T, dff, d,
-                                JULES_ACT_GELU, st, stats, colsum))
+  if (int rc = gemm_tc_dispatch<__nv_bfloat16, __nv_bfloat16>(
+          static_cast<const __nv_bfloat16*>(X), static_cast<const __nv_bfloat16*>(W1f), c,
+          nullptr, hid, T, dff, d, JULES_ACT_GELU, st, stats, colsum))
     return rc;
   return jules_gemm_bias_act(hid, W2, b2, X, out, T, d, dff, JULES_ACT_NONE, JULES_DTYPE_BF16,
                              out_dtype, stream);
@@ -1505,7 +1552,7 @@ int jules_dist_flash_attention_fwd(void* comm, const void* Q, const void* K, con
   if (!Q || !K || !V || !O) return fail(JULES_ERR_ARG, "dist_attention: NULL Q, K, V or O");
   if (B < 0 || Hq <= 0 || Hkv <= 0 || S < 0 || D <= 0 || Hq % Hkv != 0)
     return fail(JULES_ERR_SHAPE, "dist_attention: B=%d Hq=%d Hkv=%d S=%d D=%d", B, Hq, Hkv, S, D);
-  if (dtype != JULES_DTYPE_F32 && dtype != JULES_DTYPE_BF16)
+  if (dtype != JULES_DTYPE_F32 && dtype != JULES_DTYPE_BF16 && dtype != JULES_DTYPE_F16)
     return fail(JULES_ERR_DTYPE, "dist_attention: dtype %d", dtype);
   if (B == 0 || S == 0) return ok();
   // Units: (batch, kv head) pairs, each one kv head and the Hq/Hkv query
@@ -1535,7 +1582,8 @@ int jules_dist_flash_attention_fwd(void* comm, const void* Q, const void* K, con
   SharedBuf so, sl;
   const bool o_shared = find_shared(c, O, (size_t)B * Hq * S * D * elt, &so);
   const bool l_shared = !lse || find_shared(c, lse, (size_t)B * Hq * S * 4, &sl);
-  if (o_shared && l_shared && dtype == JULES_DTYPE_BF16 && D == jb::attn::HD && aligned16(Q) &&
+  if (o_shared && l_shared && (dtype == JULES_DTYPE_BF16 || dtype == JULES_DTYPE_F16) &&
+      (D == 128 || D == 64) && aligned16(Q) &&
       aligned16(K) && aligned16(V) && aligned16(O)) {
     // Gather fused into the attention epilogue: each finished O tile (and
     // its lse) is stored into every rank's buffers.
@@ -1549,7 +1597,9 @@ int jules_dist_flash_attention_fwd(void* comm, const void* Q, const void* K, con
                         : nullptr;
     }
     if (!(scale > 0.0f)) scale = 1.0f / sqrtf((float)D);
-    if (int rc = attn_tc(q, k, v, out, Bl, Hql, Hkvl, S, D, scale, causal ? 1 : 0, st)) return rc;
+    if (int rc = attn_tc(q, k, v, out, Bl, Hql, Hkvl, S, D, scale, causal ? 1 : 0,
+                         dtype == JULES_DTYPE_F16, st))
+      return rc;
     const unsigned long long target = (++c->calls) * (unsigned long long)w;
     jb::dist::dist_signal_wait_kernel<<<1, 32, 0, st>>>(
         c->d_counters, w, static_cast<const unsigned long long*>(c->flags.local), target,

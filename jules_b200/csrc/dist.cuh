@@ -224,13 +224,16 @@ int nccl_type(int dtype, ncclDataType_t* t) {
   switch (dtype) {
     case JULES_DTYPE_F32: *t = ncclFloat32; return JULES_OK;
     case JULES_DTYPE_BF16: *t = ncclBfloat16; return JULES_OK;
+    case JULES_DTYPE_F16: *t = ncclFloat16; return JULES_OK;
     case JULES_DTYPE_FP8E4M3:
     case JULES_DTYPE_FP8E5M2: *t = ncclUint8; return JULES_OK;
     default: return fail(JULES_ERR_DTYPE, "dist: dtype %d", dtype);
   }
 }
 
-size_t dtype_bytes(int dtype) { return dtype == JULES_DTYPE_F32 ? 4 : (dtype == JULES_DTYPE_BF16 ? 2 : 1); }
+size_t dtype_bytes(int dtype) {
+  return dtype == JULES_DTYPE_F32 ? 4 : ((dtype == JULES_DTYPE_BF16 || dtype == JULES_DTYPE_F16) ? 2 : 1);
+}
 
 // Gathers rank slices of `elems_total` elements (rank r owns [begin_r, end_r)
 // of a balanced contiguous partition of `units` units of `unit_elems` each)

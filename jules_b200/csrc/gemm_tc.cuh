@@ -87,6 +87,14 @@ __device__ __forceinline__ void store8(__nv_bfloat16* dst, const float (&v)[8]) 
   o.w = pack_bf16x2(v[6], v[7]);
   *reinterpret_cast<uint4*>(dst) = o;
 }
+__device__ __forceinline__ void store8(__half* dst, const float (&v)[8]) {
+  uint4 o;
+  o.x = pack_f16x2(v[0], v[1]);
+  o.y = pack_f16x2(v[2], v[3]);
+  o.z = pack_f16x2(v[4], v[5]);
+  o.w = pack_f16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(dst) = o;
+}
 __device__ __forceinline__ void store8(float* dst, const float (&v)[8]) {
   reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
   reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
@@ -105,13 +113,13 @@ __device__ __forceinline__ void ln_fold8(float (&v)[8], float2 rs, const float* 
   for (int j = 0; j < 8; ++j) v[j] = rs.y * fmaf(-rs.x, cs[j], v[j]);
 }
 
-// TOut: __nv_bfloat16 (one RNE cast at the store) or float.  The residual
-// has the operands' dtype (bf16).
-template <int BN, int STAGES, typename TOut>
+// TIn: the operands' type, __nv_bfloat16 or __half (the residual has it
+// too).  TOut: TIn (one RNE cast at the store) or float.
+template <int BN, int STAGES, typename TIn, typename TOut>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmW, const float* __restrict__ bias,
-                        const __nv_bfloat16* __restrict__ residual, TOut* __restrict__ C,
+                        const TIn* __restrict__ residual, TOut* __restrict__ C,
                         int M, int N, int K, int act, const float2* __restrict__ ln_stats,
                         const float* __restrict__ ln_colsum) {
   static_assert(BN % 64 == 0 && BN <= 256, "BN must be a multiple of 64, at most 256");
@@ -176,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, false, true);
+      constexpr uint32_t idesc = idesc_f16kind<TIn>(BM, BN, false, true);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -230,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int col0 = n0 + c * 32;
         if (row < M && col0 < N) {
           TOut* crow = C + (size_t)row * N;
-          const __nv_bfloat16* rrow = residual ? residual + (size_t)row * N : nullptr;
+          const TIn* rrow = residual ? residual + (size_t)row * N : nullptr;
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
             const int col = col0 + g * 8;
@@ -249,10 +257,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int j = 0; j < 8; ++j) v[j] = act_fast(v[j], act);
               if (rrow) {
                 const uint4 rv = *reinterpret_cast<const uint4*>(rrow + col);
-                const __nv_bfloat162* rp = reinterpret_cast<const __nv_bfloat162*>(&rv);
+                const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                  const float2 f = __bfloat1622float2(rp[j]);
+                  const float2 f = unpack2<TIn>(rw[j]);
                   v[2 * j] += f.x;
                   v[2 * j + 1] += f.y;
                 }
@@ -376,11 +384,11 @@ __device__ __forceinline__ void epilogue8(float (&v)[8], const float* bias,
 
 // whole_units: tiles run at full width; num_units: whole_units + 2 x the
 // number of tail tiles run as halves (== whole_units when nothing is split).
-template <int STAGES, int TN, typename TOut>
+template <int STAGES, int TN, typename TIn, typename TOut>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_tc2_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmW, const float* __restrict__ bias,
-                         const __nv_bfloat16* __restrict__ residual, const OutDest<TOut> out,
+                         const TIn* __restrict__ residual, const OutDest<TOut> out,
                          int M, int N, int K, int act, int whole_units, int num_units,
                          const float2* __restrict__ ln_stats, const float* __restrict__ ln_colsum) {
   static_assert(TN == 256, "pair tile N is 256 (its halves are 128)");
@@ -451,8 +459,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer (leader CTA) ----------------
     if (leader && lane == 0) {
-      constexpr uint32_t idesc_full = idesc_bf16_f32(TM, TN, false, true);
-      constexpr uint32_t idesc_half = idesc_bf16_f32(TM, TN / 2, false, true);
+      constexpr uint32_t idesc_full = idesc_f16kind<TIn>(TM, TN, false, true);
+      constexpr uint32_t idesc_half = idesc_f16kind<TIn>(TM, TN / 2, false, true);
       const uint32_t empty0 = smem_u32(&s.empty[0]);
       const uint32_t tfull0 = smem_u32(&s.tfull[0]);
       const uint32_t empty0_peer = mapa_shared(empty0, 1);
@@ -498,7 +506,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // XOR-swizzled by row) and are read back so that 8 lanes cover 128
     // contiguous bytes of one row: every store writes 16 bytes, every
     // 8 lanes a whole 128-byte line, local or across NVLink.
-    //   bf16 C: blocks of 64 columns (32 rows x 128 B); fp32 C: 32 columns.
+    //   16-bit C: blocks of 64 columns (32 rows x 128 B); fp32 C: 32 columns.
     constexpr int kBlk = sizeof(TOut) == 2 ? 64 : 32;  // columns per staged block
     const int quarter = warp & 3;
     uint4* stage = reinterpret_cast<uint4*>(s.epi[quarter]);  // [32 rows][8 chunks of 16 B]
@@ -517,8 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t t_warp = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * TN;
       const int my_row = m0 + lane;  // row of this lane in the TMEM layout
-      const __nv_bfloat16* rrow =
-          residual ? residual + (size_t)(my_row < M ? my_row : 0) * N : nullptr;
+      const TIn* rrow = residual ? residual + (size_t)(my_row < M ? my_row : 0) * N : nullptr;
       const float2 rs = ln_stats && my_row < M ? ln_stats[my_row] : make_float2(0.0f, 1.0f);
 #pragma unroll 1
       for (int cb = 0; cb < pu.cols; cb += kBlk) {
@@ -561,10 +568,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int j = 0; j < 32; j += 8) {
                 if (c0 + j < N) {
                   const uint4 rv = *reinterpret_cast<const uint4*>(rrow + c0 + j);
-                  const __nv_bfloat162* rp = reinterpret_cast<const __nv_bfloat162*>(&rv);
+                  const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
                   for (int q = 0; q < 4; ++q) {
-                    const float2 f = __bfloat1622float2(rp[q]);
+                    const float2 f = unpack2<TIn>(rw[q]);
                     v[j + 2 * q] += f.x;
                     v[j + 2 * q + 1] += f.y;
                   }
@@ -577,8 +584,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int q = 0; q < 4; ++q)
               stage[lane * 8 + ((h * 4 + q) ^ (lane & 7))] =
-                  make_uint4(pack_bf16x2(v[8 * q], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
-                             pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+                  make_uint4(pack2<TOut>(v[8 * q], v[8 * q + 1]), pack2<TOut>(v[8 * q + 2], v[8 * q + 3]),
+                             pack2<TOut>(v[8 * q + 4], v[8 * q + 5]), pack2<TOut>(v[8 * q + 6], v[8 * q + 7]));
           } else {
 #pragma unroll
             for (int q = 0; q < 8; ++q)

@@ -9,8 +9,11 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <type_traits>
 
 namespace jb {
 
@@ -275,6 +278,22 @@ __device__ __forceinline__ void umma8_ss(uint32_t d_tmem, const uint64_t (&a)[8]
       : "memory");
 }
 
+#define JB_MMA_SS4(ai, bi, pr) \
+  "tcgen05.mma.cta_group::1.kind::f16 [%0], %" #ai ", %" #bi ", %10, " pr ";\n\t"
+// D (+)= sum over 4 K-steps of A[smem] * B[smem].
+__device__ __forceinline__ void umma4_ss(uint32_t d_tmem, const uint64_t (&a)[4],
+                                         const uint64_t (&b)[4], uint32_t acc_first,
+                                         uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %9, 0;\n\t"
+      "setp.eq.b32 q, %9, %9;\n\t"
+      JB_MMA_SS4(1, 5, "p") JB_MMA_SS4(2, 6, "q") JB_MMA_SS4(3, 7, "q") JB_MMA_SS4(4, 8, "q")
+      "}" ::"r"(d_tmem), "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(b[0]), "l"(b[1]),
+      "l"(b[2]), "l"(b[3]), "r"(acc_first), "r"(idesc)
+      : "memory");
+}
+
 #define JB_MMA_TS(ai, bi, pr) \
   "tcgen05.mma.cta_group::1.kind::f16 [%0], [%" #ai "], %" #bi ", %18, " pr ";\n\t"
 
@@ -347,6 +366,16 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn, bool b_mn) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) |
          ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// kind::f16 instruction descriptor for A and B of one 16-bit type (f16 or
+// bf16; the two operands always share it): the A/B format fields are 0 for
+// f16, 1 for bf16.
+template <typename T>
+__host__ __device__ constexpr uint32_t idesc_f16kind(int M, int N, bool a_mn, bool b_mn) {
+  return std::is_same<T, __half>::value
+             ? (idesc_bf16_f32(M, N, a_mn, b_mn) & ~((7u << 7) | (7u << 10)))
+             : idesc_bf16_f32(M, N, a_mn, b_mn);
 }
 
 // Shared-memory matrix descriptor for a 128-byte-swizzled operand.
@@ -444,6 +473,31 @@ __device__ __forceinline__ float ex2_approx(float x) {
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Two floats as one 32-bit pair of the 16-bit element type T (round to
+// nearest even), and back.
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) { return pack_bf16x2(lo, hi); }
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) { return pack_f16x2(lo, hi); }
+
+template <typename T>
+__device__ __forceinline__ float2 unpack2(uint32_t v);
+template <>
+__device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t v) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v));
+}
+template <>
+__device__ __forceinline__ float2 unpack2<__half>(uint32_t v) {
+  return __half22float2(*reinterpret_cast<const __half2*>(&v));
 }
 
 }  // namespace jb

@@ -13,12 +13,19 @@ def bf16_np(x):
     return oracle.bf16_round(np.ascontiguousarray(x, np.float32))
 
 
+def f16_np(x):
+    """float32 array rounded to IEEE half (RNE), kept as float32."""
+    return np.ascontiguousarray(x, np.float32).astype(np.float16).astype(np.float32)
+
+
 def to_dev(x, dtype="bf16"):
-    """numpy float32 -> CUDA tensor (bf16 keeps the exact RNE-rounded bits)."""
+    """numpy float32 -> CUDA tensor (bf16 / f16 keep the exact RNE-rounded bits)."""
     import torch
     t = torch.from_numpy(np.ascontiguousarray(x, np.float32))
     if dtype == "bf16":
         t = t.to(torch.bfloat16)
+    elif dtype == "f16":
+        t = t.to(torch.float16)
     return t.cuda()
 
 

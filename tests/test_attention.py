@@ -109,3 +109,41 @@ def test_attention_config_c5_sampled(jb, orc):
     """Config C5: [4, Hq=64, Hkv=8, 16384, 128] causal bf16 (grouped-query)."""
     _sampled_check(jb, orc, 4, 64, 8, 16384, units=[0, 71, 255],
                    q_windows=[(16256, 16384), (5000, 5064)], seed=5)
+
+
+# --- fp16 operands and head dim 64 on tcgen05 ------------------------------
+@pytest.mark.parametrize("D", [128, 64])
+@pytest.mark.parametrize("B,Hq,Hkv,S", [(1, 2, 2, 256), (1, 8, 2, 384), (1, 3, 3, 333), (1, 4, 1, 129)])
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_f16_tc(jb, orc, D, B, Hq, Hkv, S, causal):
+    from helpers import f16_np
+    Q, K, V = (f16_np(x) for x in attn_inputs(B, Hq, Hkv, S, D, seed=B * 7 + S + D, bf16=False))
+    want, lse_want = orc.flash_attention(Q, K, V, causal=causal)
+    got, lse = _gpu_attn(jb, Q, K, V, causal, "f16")
+    assert max_abs(got, want) <= BF16_MAX_ABS
+    assert rel_l2(got, want) <= BF16_REL_L2
+    assert max_abs(lse, lse_want) <= 2e-3
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,S", [(1, 2, 2, 128), (2, 4, 4, 384), (1, 8, 2, 300),
+                                        (4, 4, 4, 512), (1, 1, 1, 1)])
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_bf16_d64_tc(jb, orc, B, Hq, Hkv, S, causal):
+    """Head dim 64 (the reference benchmark's shapes, benchmarks/bench_kernel.cpp:509-512)
+    on the tensor-core kernel."""
+    Q, K, V = attn_inputs(B, Hq, Hkv, S, 64, seed=B * 100 + S + 64)
+    want, lse_want = orc.flash_attention(Q, K, V, causal=causal)
+    got, lse = _gpu_attn(jb, Q, K, V, causal)
+    assert max_abs(got, want) <= BF16_MAX_ABS
+    assert rel_l2(got, want) <= BF16_REL_L2
+    assert max_abs(lse, lse_want) <= 2e-3
+
+
+def test_attention_f16_other_head_dims(jb, orc):
+    """fp16 with head dim 96: the CUDA-core kernel."""
+    from helpers import f16_np
+    Q, K, V = (f16_np(x) for x in attn_inputs(1, 4, 2, 200, 96, seed=96, bf16=False))
+    want, _ = orc.flash_attention(Q, K, V, causal=True)
+    got, _ = _gpu_attn(jb, Q, K, V, True, "f16")
+    assert max_abs(got, want) <= BF16_MAX_ABS
+    assert rel_l2(got, want) <= BF16_REL_L2

@@ -156,3 +156,41 @@ def test_sgemm_vs_reference_blas(jb, ref, ta, tb):
         r = ref.blas_matmul(A, B)
         got2 = jb.sgemm(torch.from_numpy(A).cuda(), torch.from_numpy(B).cuda())
         assert rel_l2(to_np(got2), r) <= F32_REL_L2
+
+
+# --- fp16 operands (tcgen05 kind::f16 with the f16 format; the reference's
+# mixed-precision pass treats f16 like bf16, MixedPrecisionPass.cpp:76) ----
+@pytest.mark.parametrize("M,N,K", [(256, 512, 256), (129, 264, 72), (640, 1024, 1024), (7, 40, 24)])
+@pytest.mark.parametrize("act", ["none", "gelu"])
+def test_gemm_f16(jb, orc, M, N, K, act):
+    import torch
+    from helpers import f16_np
+    g = np.random.default_rng(M + 3 * N + K)
+    s = 1.0 / np.sqrt(K)
+    A = f16_np(g.uniform(-1, 1, (M, K)).astype(np.float32) * s)
+    W = f16_np(g.uniform(-1, 1, (K, N)).astype(np.float32) * s)
+    b = (g.standard_normal(N) * 0.02).astype(np.float32)
+    R = f16_np(g.standard_normal((M, N)).astype(np.float32))
+    bias = torch.from_numpy(b).cuda()
+    C = jb.gemm_bias_act(to_dev(A, "f16"), to_dev(W, "f16"), bias, to_dev(R, "f16"), act=act)
+    C32 = jb.gemm_bias_act(to_dev(A, "f16"), to_dev(W, "f16"), bias, to_dev(R, "f16"), act=act,
+                           out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert jb.device_error() == 0
+    assert C.dtype == torch.float16
+    want = orc.gemm_bias_act(A, W, b, R, act)
+    assert max_abs(to_np(C), want) <= BF16_MAX_ABS
+    assert rel_l2(to_np(C), want) <= BF16_REL_L2
+    assert max_abs(to_np(C32), want) <= 2e-3
+    assert torch.equal(C, C32.to(torch.float16))  # one rounding, at the store
+
+
+def test_gemm_f16_rejects_mixed_dtypes(jb):
+    import torch
+    a = torch.zeros((256, 256), dtype=torch.float16, device="cuda")
+    w = torch.zeros((256, 256), dtype=torch.bfloat16, device="cuda")
+    c = torch.empty((256, 256), dtype=torch.bfloat16, device="cuda")
+    rc = jb.lib().jules_gemm_bias_act(jb._ptr(a), jb._ptr(a), None, None, jb._ptr(c), 256, 256, 256,
+                                      0, jb.DT_F16, jb.DT_BF16, jb._stream(None))
+    assert rc == 3  # JULES_ERR_DTYPE: f16 operands give f16 or fp32 C
+    del w
