@@ -51,7 +51,7 @@ def parse():
     p.add_argument("--impl", choices=["jules", "reference"], default="jules")
     p.add_argument("--workload", choices=["headline", "gemm", "attn", "attn_gqa", "mlp",
                                           "attn_fp32", "softmax", "xent", "int8", "fp8",
-                                          "attn_bwd"],
+                                          "attn_bwd", "gemm_f32", "gelu_f32"],
                    default="headline")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
@@ -101,7 +101,7 @@ def roofline(wl, achieved, peak, peak_kind, traffic):
                 "frac": round(achieved / NOMINAL_FP8_TFLOPS, 4),
                 "peak_kind": "nominal dense fp8 (datasheet; no measured fp8 figure)",
                 "traffic": traffic, "traffic_unit": "DRAM bytes per launch (ncu, profiles/)"}
-    fp32 = isinstance(wl, AttentionF32)
+    fp32 = isinstance(wl, (AttentionF32, GemmF32))
     p = NOMINAL_FP32_TFLOPS if fp32 else peak
     return {"bound": "fp32_cuda_cores" if fp32 else "tensor", "kernel": wl.dominant,
             "achieved": round(achieved, 2), "peak": round(p, 1), "unit": "TFLOP/s",
@@ -117,7 +117,7 @@ def profiled_traffic(workload):
     name = {"gemm": "gemm_tc_c2", "attn": "attn_tc_c3", "attn_gqa": "attn_tc_c5",
             "mlp": "gemm_tc_c4", "attn_fp32": "attn_simt_c1", "softmax": "rows_softmax",
             "xent": "rows_xent", "int8": "gemm_s8_int8", "fp8": "gemm_f8_fp8",
-            "attn_bwd": "attn_bwd_c3"}[workload]
+            "attn_bwd": "attn_bwd_c3", "gemm_f32": "gemm_simt_f32", "gelu_f32": "gelu_f32"}[workload]
     path = os.path.join(HERE, "profiles", f"{name}.md")
     try:
         with open(path) as f:
@@ -179,6 +179,12 @@ def describe(workload, world, extra_l2=None):
         c = {"workload": "fused softmax + cross-entropy (fusedCrossEntropyLoss), fp32 logits",
              "M_per_rank": 4096, "N": 32768, "global_M": 4096 * world, "sharding": "rows",
              "bytes_convention": "logits read + grad written + targets read"}
+    elif workload == "gemm_f32":
+        c = {"workload": "fp32 GEMM + bias + GELU (tiledMatmulWithActivation's float* path)",
+             "M_per_rank": 2048, "N": 2048, "K": 2048, "sharding": "rows of M"}
+    elif workload == "gelu_f32":
+        c = {"workload": "fp32 GELU (fusedGelu)", "n_per_rank": 64 << 20,
+             "bytes_convention": "n*4 read + n*4 written"}
     else:
         c = {"workload": "C1 fp32 flash-attention fwd, non-causal", "B_per_rank": 1, "H": 8,
              "S": 512, "D": 64, "sharding": "batch"}
@@ -814,6 +820,81 @@ class RowWise(Workload):
         return h_in, h_out, lambda d, o: self._run(d[0], o[0], d[1] if self.xent else None)
 
 
+class GemmF32(Workload):
+    """The reference's float* GEMM path (tiledMatmulWithActivation with GELU,
+    fp32 in and out): the fp32 CUDA-core kernel its 1e-5 rel-L2 bar needs.
+    M = N = K = 2048 per rank."""
+    dtype = "f32"
+    dominant = "simt::gemm_kernel<float, float> (fp32 CUDA cores)"
+
+    def __init__(self, jb, torch, rank, world, M=2048, N=2048, K=2048):
+        self.jb, self.torch = jb, torch
+        dev = torch.device("cuda")
+        g = torch.Generator(device=dev).manual_seed(21 + rank)
+        per_set = (M * K + K * N + M * N) * 4
+        self.nsets = self.sets_for(per_set)
+        s = 1.0 / K ** 0.5
+        self.A = [(torch.rand((M, K), generator=g, device=dev) * 2 - 1) * s for _ in range(self.nsets)]
+        self.W = [(torch.rand((K, N), generator=g, device=dev) * 2 - 1) * s for _ in range(self.nsets)]
+        self.b = torch.randn(N, generator=g, device=dev) * 0.02
+        self.C = [torch.empty((M, N), device=dev) for _ in range(self.nsets)]
+        self.flops_per_step = 2.0 * M * N * K
+        self.flops_dominant = self.flops_per_step
+        self.config = {"l2": f"{self.nsets} rotating input sets ({self.nsets * per_set / 2**20:.0f} MiB > L2)"}
+
+    def step(self, i, ev=None):
+        k = i % self.nsets
+        if ev:
+            ev[0].record()
+        self.jb.gemm_bias_act(self.A[k], self.W[k], self.b, act="gelu", out=self.C[k])
+        if ev:
+            ev[1].record()
+
+    def output(self, i):
+        return self.C[i % self.nsets]
+
+    def e2e_spec(self):
+        jb = self.jb
+        h_in = [self.A[0].cpu().pin_memory(), self.W[0].cpu().pin_memory()]
+        h_out = [self.torch.empty_like(self.C[0], device="cpu").pin_memory()]
+        return h_in, h_out, lambda d, o: jb.gemm_bias_act(d[0], d[1], self.b, act="gelu", out=o[0])
+
+
+class GeluF32(Workload):
+    """The reference's fusedGelu over 64 Mi fp32 elements (HBM-bound, GB/s)."""
+    unit = "GB/s"
+    unit_scale = 1e9
+    dtype = "f32"
+    dominant = "simt::gelu_kernel<float>"
+
+    def __init__(self, jb, torch, rank, world, n=64 << 20):
+        self.jb, self.torch = jb, torch
+        dev = torch.device("cuda")
+        g = torch.Generator(device=dev).manual_seed(22 + rank)
+        self.X = [torch.randn(n, generator=g, device=dev) * 3 for _ in range(2)]
+        self.Y = [torch.empty_like(x) for x in self.X]
+        self.nsets = 2
+        self.flops_per_step = 2.0 * n * 4  # bytes read + written
+        self.flops_dominant = self.flops_per_step
+        self.config = {"l2": "inputs 256 MiB per step (> L2)"}
+
+    def step(self, i, ev=None):
+        k = i % self.nsets
+        if ev:
+            ev[0].record()
+        self.jb.gelu(self.X[k], out=self.Y[k])
+        if ev:
+            ev[1].record()
+
+    def output(self, i):
+        return self.Y[i % self.nsets]
+
+    def e2e_spec(self):
+        h_in = [self.X[0].cpu().pin_memory()]
+        h_out = [self.torch.empty_like(h_in[0]).pin_memory()]
+        return h_in, h_out, lambda d, o: self.jb.gelu(d[0], out=o[0])
+
+
 METRIC = "Flash-attn fwd & fused-GEMM TFLOP/s at 1/2/4/8 B200; % of tensor peak"
 # Extra (non-headline) workloads of the row-wise kernels report HBM bytes per second.
 ROWS_METRIC = "Row softmax / fused cross-entropy GB/s (HBM bytes moved) per B200"
@@ -822,9 +903,17 @@ FP8_METRIC = "fp8 GEMM + bias + GELU TFLOP/s (mixed-precision matmul at fp8) per
 BWD_METRIC = "Flash-attention backward (dQ, dK, dV) TFLOP/s per B200; % of tensor peak"
 
 
+F32_GEMM_METRIC = "fp32 GEMM + bias + GELU TFLOP/s (the reference's float* API) per B200"
+GELU_METRIC = "fp32 GELU GB/s (HBM bytes moved) per B200"
+
+
 def metric_for(workload):
     if workload in ("softmax", "xent"):
         return ROWS_METRIC
+    if workload == "gemm_f32":
+        return F32_GEMM_METRIC
+    if workload == "gelu_f32":
+        return GELU_METRIC
     return {"int8": INT8_METRIC, "fp8": FP8_METRIC, "attn_bwd": BWD_METRIC}.get(workload, METRIC)
 # B200 datasheet dense int8 / fp8 tensor throughput (no measured figures on this pool).
 NOMINAL_INT8_TOPS = 4500.0
@@ -921,6 +1010,28 @@ def cpu_reference_sample(workload, reps=3, warm=1):
             fn()
         dt = (time.perf_counter() - t0) / reps
         return flops / dt / 1e9, desc + f"; {reps} timed reps, {dt * 1e3:.1f} ms each", threads
+    elif workload == "gemm_f32":
+        Ms, N, K = 512, 2048, 2048
+        A = (g.uniform(-1, 1, (Ms, K)) / np.sqrt(K)).astype(np.float32)
+        W = (g.uniform(-1, 1, (K, N)) / np.sqrt(K)).astype(np.float32)
+        b = (0.02 * g.standard_normal(N)).astype(np.float32)
+        fn = lambda: ref.gemm_bias_gelu(A, W, b)
+        flops = 2.0 * Ms * N * K
+        desc = (f"reference tiledMatmulWithActivation + bias + fusedGelu (FusedKernels.h:378-458,"
+                f"606-627) on {Ms} of the 2048 rows")
+    elif workload == "gelu_f32":
+        n = 16 << 20
+        X = (3 * g.standard_normal(n)).astype(np.float32)
+        fn = lambda: ref.gelu(X)
+        for _ in range(warm):
+            fn()
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        dt = (time.perf_counter() - t0) / reps
+        return (2.0 * n * 4 / dt / 1e9,
+                f"reference fusedGelu (FusedKernels.h:606-627) on 16 Mi of the 64 Mi elements; "
+                f"{reps} timed reps, {dt * 1e3:.1f} ms each", threads)
     elif workload == "attn_fp32":
         Q, K_, V = (g.standard_normal((1, 8, 512, 64), dtype=np.float32) for _ in range(3))
         fn = lambda: ref.flash_attention(Q, K_, V)
@@ -968,7 +1079,7 @@ def run_reference_arm(args):
         return statistics.mean(vals), (time.perf_counter() - t0) / steps, desc, threads
 
     value, step_s, desc, threads = timed(workload, args.steps, args.warmup)
-    rowwise = workload in ("softmax", "xent")
+    rowwise = workload in ("softmax", "xent", "gelu_f32")
     unit = "GB/s" if rowwise else ("TOPS" if workload == "int8" else "TFLOP/s")
     line = {"metric": metric_for(args.workload), "value": round(value, 6), "unit": unit,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -1045,7 +1156,9 @@ def main():
                 "xent": lambda: RowWise(jb, torch, rank, world, xent=True),
                 "int8": lambda: Int8Gemm(jb, torch, rank, world),
                 "fp8": lambda: Fp8Gemm(jb, torch, rank, world),
-                "attn_bwd": lambda: AttentionBwd(jb, torch, rank, world)}[workload]()
+                "attn_bwd": lambda: AttentionBwd(jb, torch, rank, world),
+                "gemm_f32": lambda: GemmF32(jb, torch, rank, world),
+                "gelu_f32": lambda: GeluF32(jb, torch, rank, world)}[workload]()
 
     def measure(workload):
         """Warm-up, the K timed steps, the gather, e2e and the CPU leg of one
@@ -1193,7 +1306,8 @@ def main():
             "config": describe(workload, world, wl.config.get("l2")),
             "roofline": roofline(wl, achieved, peak, peak_kind, traffic),
             **({"pct_of_dense_bf16_peak_2250": round(100 * tflops_total / world / 2250.0, 2)}
-               if wl.unit == "TFLOP/s" and not isinstance(wl, (Fp8Gemm, AttentionF32)) else {}),
+               if wl.unit == "TFLOP/s" and not isinstance(wl, (Fp8Gemm, AttentionF32, GemmF32))
+               else {}),
             "clocks": clocks,
             "e2e": e2e,
             "gpu_launches": K * wl.launches_per_step,
