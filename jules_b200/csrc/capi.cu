@@ -222,7 +222,7 @@ int gemm_tc2(const TIn* A, const TIn* W, const float* bias,
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(jb::gemm::kThreads);
+  cfg.blockDim = dim3(jb::gemm::kThreads2);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cfg.attrs = attr;

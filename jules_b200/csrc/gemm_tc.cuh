@@ -46,7 +46,8 @@ namespace gemm {
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // one 128-byte swizzle row of bf16
-constexpr int kThreads = 192;
+constexpr int kThreads = 192;   // 1-CTA kernel: TMA, MMA, 4 epilogue warps
+constexpr int kThreads2 = 320;  // pair kernel: TMA, MMA, 8 epilogue warps
 
 // Tile order shared by both GEMM kernels: groups of kGroupM tile rows; inside
 // a group m runs fastest and n advances once per group height, so the tiles
@@ -295,8 +296,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 //                       the leader CTA's full barrier.
 //   warp 1 (leader)     MMA issue; commits free the stage in both CTAs and
 //                       mark the accumulator ready in both CTAs.
-//   warps 2-5 (both)    epilogue of the CTA's 128 rows; they release the
-//                       accumulator on the leader's barrier (256 arrivals).
+//   warps 2-9 (both)    epilogue of the CTA's 128 rows, two warps per TMEM
+//                       lane quarter; they release the accumulator on the
+//                       leader's barrier (512 arrivals).
 //
 // Tail split.  With T tiles on P resident pairs, the last round holds only
 // r = T mod P tiles (all T when T < P).  When 2r <= P, those r tiles are run
@@ -312,7 +314,7 @@ struct Smem2 {
   alignas(1024) uint8_t b[STAGES][kBBytes];
   // Epilogue staging: 4 KB per epilogue warp (32 rows of 128 bytes, their
   // 16-byte chunks XOR-swizzled by row & 7).
-  alignas(128) float epi[4][32][32];
+  alignas(128) float epi[8][32][32];
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
   uint64_t tfull[2];
@@ -385,7 +387,7 @@ __device__ __forceinline__ void epilogue8(float (&v)[8], const float* bias,
 // whole_units: tiles run at full width; num_units: whole_units + 2 x the
 // number of tail tiles run as halves (== whole_units when nothing is split).
 template <int STAGES, int TN, typename TIn, typename TOut>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads2, 1)
     gemm_bf16_tc2_kernel(const __grid_constant__ CUtensorMap tmA,
                          const __grid_constant__ CUtensorMap tmW, const float* __restrict__ bias,
                          const TIn* __restrict__ residual, const OutDest<TOut> out,
@@ -415,7 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.tfull[i], 1);
-      mbar_init(&s.tempty[i], 2 * 128);
+      mbar_init(&s.tempty[i], 2 * 256);
     }
     s.abort_flag = 0;
     fence_mbar_init();
@@ -499,7 +501,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..5, both CTAs) ----------------
+    // ---------------- epilogue (warps 2..9, both CTAs) ----------------
     // Each warp owns 32 rows (its TMEM lane quarter).  tcgen05.ld gives lane t
     // row t; bias, activation and residual are applied in that layout, the
     // results go through shared memory (4 KB per warp, 16-byte chunks
@@ -507,9 +509,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // contiguous bytes of one row: every store writes 16 bytes, every
     // 8 lanes a whole 128-byte line, local or across NVLink.
     //   16-bit C: blocks of 64 columns (32 rows x 128 B); fp32 C: 32 columns.
+    // Eight epilogue warps: two per TMEM lane quarter (warp & 3), each taking
+    // half of the unit's columns (chalf).
     constexpr int kBlk = sizeof(TOut) == 2 ? 64 : 32;  // columns per staged block
+    const int ew = warp - 2;
     const int quarter = warp & 3;
-    uint4* stage = reinterpret_cast<uint4*>(s.epi[quarter]);  // [32 rows][8 chunks of 16 B]
+    const int chalf = ew >> 2;
+    uint4* stage = reinterpret_cast<uint4*>(s.epi[ew]);  // [32 rows][8 chunks of 16 B]
     const int g = lane & 7;      // chunk (8 bf16 / 4 fp32 columns) this lane stores
     const int rsub = lane >> 3;  // first row this lane stores
     const uint32_t tempty0_leader = mapa_shared(smem_u32(&s.tempty[0]), 0);
@@ -528,7 +534,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const TIn* rrow = residual ? residual + (size_t)(my_row < M ? my_row : 0) * N : nullptr;
       const float2 rs = ln_stats && my_row < M ? ln_stats[my_row] : make_float2(0.0f, 1.0f);
 #pragma unroll 1
-      for (int cb = 0; cb < pu.cols; cb += kBlk) {
+      for (int cb = chalf * (pu.cols / 2); cb < (chalf + 1) * (pu.cols / 2); cb += kBlk) {
 #pragma unroll
         for (int h = 0; h < kBlk / 32; ++h) {
           const int c0 = n0 + cb + h * 32;  // first column of these 32

@@ -194,3 +194,37 @@ def test_gemm_f16_rejects_mixed_dtypes(jb):
                                       0, jb.DT_F16, jb.DT_BF16, jb._stream(None))
     assert rc == 3  # JULES_ERR_DTYPE: f16 operands give f16 or fp32 C
     del w
+
+
+# --- more 256 x 256 tiles than the 74 CTA pairs, with a partial last round
+# (run as half-width units when it is at most half full) ---------------------
+@pytest.mark.parametrize("M,N,K", [(2560, 2048, 128),   # 80 tiles: last round 6 -> 12 halves
+                                   (4096, 4096, 320),   # 256 tiles: 34 -> 68 halves
+                                   (2600, 2056, 200),   # ragged rows / columns / K, 99 tiles
+                                   (4096, 2048, 1024)]) # 128 tiles: last round 54, whole
+def test_gemm_multi_round(jb, orc, M, N, K):
+    import torch
+    A, W, b = gemm_inputs(M, N, K, seed=M + N + 3 * K)
+    g = np.random.default_rng(K)
+    R = bf16_np(g.standard_normal((M, N)).astype(np.float32))
+    rows = np.linspace(0, M - 1, 64).astype(np.int64)
+    Ad, Wd, Rd, bd = to_dev(A), to_dev(W), to_dev(R), torch.from_numpy(b).cuda()
+    C = jb.gemm_bias_act(Ad, Wd, bd, Rd, act="gelu")
+    C32 = jb.gemm_bias_act(Ad, Wd, bd, Rd, act="gelu", out_dtype=torch.float32)
+    C_again = jb.gemm_bias_act(Ad, Wd, bd, Rd, act="gelu")
+    torch.cuda.synchronize()
+    assert jb.device_error() == 0
+    want = orc.gemm_bias_act(A[rows], W, b, R[rows], "gelu")
+    got = to_np(C32[torch.from_numpy(rows).cuda()])
+    assert max_abs(got, want) <= 2e-3
+    assert rel_l2(got, want) <= 1e-3
+    assert torch.equal(C, C32.to(torch.bfloat16))   # one rounding, at the store
+    assert torch.equal(C, C_again)                   # deterministic across launches
+    # the last tiles (the half-width units): whole columns against the oracle
+    cols = np.arange(N - 256, N)
+    tail_rows = np.arange(max(0, M - 256), M)
+    want_t = orc.gemm_bias_act(np.ascontiguousarray(A[tail_rows]), np.ascontiguousarray(W[:, cols]),
+                               np.ascontiguousarray(b[cols]),
+                               np.ascontiguousarray(R[np.ix_(tail_rows, cols)]), "gelu")
+    got_t = to_np(C32[torch.from_numpy(tail_rows).cuda()][:, torch.from_numpy(cols).cuda()])
+    assert max_abs(got_t, want_t) <= 2e-3
