@@ -63,9 +63,11 @@ def test_attention_bf16_other_head_dims(jb, orc, D):
     assert rel_l2(got, want) <= BF16_REL_L2
 
 
-def _sampled_check(jb, orc, B, Hq, Hkv, S, units, q_windows, seed):
+def _sampled_check(jb, orc, B, Hq, Hkv, S, units, q_windows, seed, every_row=False):
     """Full-size run on the GPU; oracle on sampled (b, h) units and query
-    windows (inputs generated on the GPU, sampled slices copied back)."""
+    windows (inputs generated on the GPU, sampled slices copied back).
+    every_row: also every row of every head against a plain fp32 torch
+    computation of softmax(scale Q K^T, causal) V (no tf32)."""
     import torch
     g = torch.Generator(device="cuda").manual_seed(seed)
     D = 128
@@ -95,20 +97,46 @@ def _sampled_check(jb, orc, B, Hq, Hkv, S, units, q_windows, seed):
     vmax = vmax.repeat_interleave(group, dim=1)
     assert bool((O.float().abs() <= vmax * (1 + 1e-2) + 1e-2).all())
     assert bool(torch.isfinite(lse).all())
+    if every_row:
+        prev = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = False
+        try:
+            mask = torch.triu(torch.full((S, S), float("-inf"), device="cuda"), 1)
+            err2 = ref2 = 0.0
+            worst = 0.0
+            for b in range(B):
+                for h0 in range(0, Hq, 4):
+                    hs = slice(h0, h0 + 4)
+                    q = Q[b, hs].float()
+                    kk = K[b, [h // group for h in range(h0, h0 + 4)]].float()
+                    vv = V[b, [h // group for h in range(h0, h0 + 4)]].float()
+                    sc = q @ kk.transpose(-1, -2) / D ** 0.5 + mask
+                    want = torch.softmax(sc, -1) @ vv
+                    got = O[b, hs].float()
+                    worst = max(worst, float((got - want).abs().max()))
+                    err2 += float(((got - want) ** 2).sum())
+                    ref2 += float((want ** 2).sum())
+                    lw = torch.logsumexp(sc, -1)
+                    assert float((lse[b, hs] - lw).abs().max()) <= 2e-3
+            assert worst <= BF16_MAX_ABS
+            assert (err2 / ref2) ** 0.5 <= BF16_REL_L2
+        finally:
+            torch.backends.cuda.matmul.allow_tf32 = prev
 
 
 @pytest.mark.slow
 def test_attention_config_c3_sampled(jb, orc):
     """Config C3: [8,32,4096,128] causal bf16 + lse."""
-    _sampled_check(jb, orc, 8, 32, 32, 4096, units=[0, 37, 255],
-                   q_windows=[(0, 130), (2000, 2100), (3968, 4096)], seed=3)
+    _sampled_check(jb, orc, 8, 32, 32, 4096, units=[0, 37, 100, 163, 200, 255],
+                   q_windows=[(0, 130), (1024, 1152), (2000, 2100), (3968, 4096)], seed=3,
+                   every_row=True)
 
 
 @pytest.mark.slow
 def test_attention_config_c5_sampled(jb, orc):
     """Config C5: [4, Hq=64, Hkv=8, 16384, 128] causal bf16 (grouped-query)."""
-    _sampled_check(jb, orc, 4, 64, 8, 16384, units=[0, 71, 255],
-                   q_windows=[(16256, 16384), (5000, 5064)], seed=5)
+    _sampled_check(jb, orc, 4, 64, 8, 16384, units=[0, 71, 100, 190, 255],
+                   q_windows=[(16256, 16384), (5000, 5064), (0, 64), (9000, 9128)], seed=5)
 
 
 # --- fp16 operands and head dim 64 on tcgen05 ------------------------------
