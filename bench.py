@@ -129,8 +129,13 @@ def profiled_traffic(workload):
     return None
 
 
-def describe(workload, world, extra_l2=None):
-    """The config object of the JSON line (shared by both arms)."""
+def describe(workload, world, extra_l2=None, multicast=None):
+    """The config object of the JSON line (shared by both arms).  multicast:
+    whether the library's communicator stores the fused gather through
+    NVLink multicast addresses (None: no communicator)."""
+    how = (" through NVLink multicast (each chunk stored once, the NVSwitch writes it to "
+           "every rank)" if multicast else " as peer stores to each rank" if multicast is not None
+           else "")
     if workload in ("gemm", "headline"):
         c = {"workload": "C2 fused GEMM+bias+GELU(tanh)", "M": 4096, "N": 4096, "K": 4096,
              "M_per_rank": 4096 // world, "sharding": "rows of M (strong scaling: the global "
@@ -138,7 +143,7 @@ def describe(workload, world, extra_l2=None):
              "dtype_out": "bf16"}
         if world > 1:
             c["gather"] = ("C gathered into every rank inside the timed step: fused into the GEMM "
-                           "epilogue as NVLink stores to each rank's C (jules_dist_gemm_bias_act)")
+                           "epilogue" + how + " (jules_dist_gemm_bias_act)")
     elif workload in ("attn", "attn_gqa"):
         gqa = workload == "attn_gqa"
         B, Hq, Hkv, S = (4, 64, 8, 16384) if gqa else (8, 32, 32, 4096)
@@ -151,8 +156,7 @@ def describe(workload, world, extra_l2=None):
              "flop_convention": "causal = 2*B*Hq*S^2*D"}
         if world > 1:
             c["gather"] = ("O and lse gathered into every rank inside the timed step: fused into "
-                           "the attention epilogue as NVLink stores to each rank's O and lse "
-                           "(jules_dist_flash_attention_fwd)")
+                           "the attention epilogue" + how + " (jules_dist_flash_attention_fwd)")
     elif workload == "mlp":
         c = {"workload": "C4 MLP block LN->GEMM+b+GELU->GEMM+b+residual", "T_per_rank": 16384,
              "d": 4096, "dff": 16384, "global_T": 16384 * world, "sharding": "token rows",
@@ -1305,7 +1309,8 @@ def main():
             "value": round(tflops_total, 3), "unit": wl.unit,
             "ms_per_step": round(ms_total / K, 5),
             "dtype": "f32" if workload == "attn_fp32" else wl.dtype,
-            "config": describe(workload, world, wl.config.get("l2")),
+            "config": describe(workload, world, wl.config.get("l2"),
+                               multicast=dist_comm.multicast if dist_comm is not None else None),
             "roofline": roofline(wl, achieved, peak, peak_kind, traffic),
             **({"pct_of_dense_bf16_peak_2250": round(100 * tflops_total / world / 2250.0, 2)}
                if wl.unit == "TFLOP/s" and not isinstance(wl, (Fp8Gemm, AttentionF32, GemmF32))

@@ -403,10 +403,20 @@ int jules_dist_destroy(void* comm);
 int jules_dist_barrier(void* comm, void* stream);
 
 /* Output buffer that every rank can write: each rank allocates `bytes`, and
- * the peers' buffers are mapped into every process (CUDA IPC, handles
- * exchanged over the communicator).  Collective.  The memory is zeroed. */
+ * the peers' buffers are mapped into every process.  With NVLink multicast
+ * (below) it is an NCCL symmetric window bound to the communicator's
+ * multicast object; otherwise cudaMalloc + CUDA IPC (handles exchanged over
+ * the communicator).  Both calls are collective (same buffers, same order on
+ * every rank).  The memory is zeroed. */
 int jules_dist_alloc_shared(void* comm, size_t bytes, void** local);
 int jules_dist_free_shared(void* comm, void* local);
+
+/* *on = 1 when this communicator's shared buffers have an NVLink multicast
+ * address (NVSwitch multicast, NCCL >= 2.28 with its device API): the fused
+ * gathers then store each chunk once and the switch replicates it to every
+ * rank.  Chosen at jules_dist_init by all ranks together; the environment
+ * variable JULES_DIST_MULTICAST=0 (or NCCL_NVLS_ENABLE=0) turns it off. */
+int jules_dist_multicast(void* comm, int* on);
 
 /*
  * Sharded jules_gemm_bias_act: rank r computes rows jules_dist_shard(M) of

@@ -78,6 +78,7 @@ _SIGNATURES = {
     "jules_dist_init": ([ctypes.POINTER(_c_vp), _c_int, _c_int, _c_vp], _c_int),
     "jules_dist_destroy": ([_c_vp], _c_int),
     "jules_dist_barrier": ([_c_vp, _c_vp], _c_int),
+    "jules_dist_multicast": ([_c_vp, ctypes.POINTER(_c_int)], _c_int),
     "jules_dist_alloc_shared": ([_c_vp, ctypes.c_size_t, ctypes.POINTER(_c_vp)], _c_int),
     "jules_dist_free_shared": ([_c_vp, _c_vp], _c_int),
     "jules_dist_gemm_bias_act": ([_c_vp] * 6 + [_c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int,
@@ -567,6 +568,14 @@ class Dist:
             lib().jules_dist_destroy(self.h)
             self.h = _c_vp()
             self._shared.clear()
+
+    @property
+    def multicast(self):
+        """True when shared buffers have an NVLink multicast address (the
+        fused gathers store each chunk once; the NVSwitch replicates it)."""
+        on = _c_int(0)
+        _check(lib().jules_dist_multicast(self.h, ctypes.byref(on)), "jules_dist_multicast")
+        return bool(on.value)
 
     def barrier(self, stream=None):
         _check(lib().jules_dist_barrier(self.h, _stream(stream)), "jules_dist_barrier")

@@ -25,6 +25,25 @@ NVCC_FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC,-O3"
                      "-I" + os.path.join(ROOT, "include")]
 
 
+def nccl_include() -> list:
+    """-I for an NCCL include directory that has the device API headers
+    (nccl_device.h, NCCL >= 2.28: symmetric windows, multicast pointers), if
+    one is installed; without it the library builds with the multicast
+    gather compiled out.  $JULES_NCCL_INCLUDE overrides the search."""
+    cands = [os.environ.get("JULES_NCCL_INCLUDE")]
+    try:
+        import importlib.util
+        spec = importlib.util.find_spec("nvidia")
+        for loc in (spec.submodule_search_locations or []) if spec else []:
+            cands.append(os.path.join(loc, "nccl", "include"))
+    except Exception:
+        pass
+    for d in cands:
+        if d and os.path.exists(os.path.join(d, "nccl_device.h")):
+            return ["-I" + d]
+    return []
+
+
 def nvcc() -> str:
     for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
         if cand and os.path.exists(cand):
@@ -54,7 +73,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     objs = []
     for src in SOURCES:
         obj = os.path.join(LIB_DIR, os.path.splitext(src)[0] + ".o")
-        cmd = [nvcc()] + NVCC_FLAGS + ["-c", os.path.join(CSRC, src), "-o", obj]
+        cmd = [nvcc()] + NVCC_FLAGS + nccl_include() + ["-c", os.path.join(CSRC, src), "-o", obj]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

@@ -68,6 +68,11 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 struct AttnOut {
   __nv_bfloat16* o[kMaxPeers];
   float* lse[kMaxPeers];
+  // NVLink multicast addresses of O and lse (all ranks' buffers behind one
+  // address, the switch replicating each store), or null: then o[] / lse[]
+  // are stored one by one.
+  __nv_bfloat16* o_mc;
+  float* lse_mc;
   int n;
 };
 
@@ -521,9 +526,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (row0 + rr < S) {
             const uint4 v = stg[rr * 4 + ((lane & 3) ^ ((rr >> 1) & 3))];
             const size_t off = ((size_t)bh * S + row0 + rr) * HDIM + c + (lane & 3) * 8;
+            if (out.o_mc) {
+              multimem_st16(out.o_mc + off, v);
+            } else {
 #pragma unroll
-            for (int p = 0; p < kMaxPeers; ++p)
-              if (p < out.n) *reinterpret_cast<uint4*>(out.o[p] + off) = v;
+              for (int p = 0; p < kMaxPeers; ++p)
+                if (p < out.n) *reinterpret_cast<uint4*>(out.o[p] + off) = v;
+            }
           }
         }
         __syncwarp();
@@ -531,9 +540,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (out.lse[0] && row_ok) {
         const float l = (m_run + log2f(l_run)) * 0.69314718055994531f;
+        if (kGather && out.lse_mc) {
+          multimem_st_f32(out.lse_mc + (size_t)bh * S + q, l);
+        } else {
 #pragma unroll
-        for (int p = 0; p < kMaxPeers; ++p)
-          if (p < out.n) out.lse[p][(size_t)bh * S + q] = l;
+          for (int p = 0; p < kMaxPeers; ++p)
+            if (p < out.n) out.lse[p][(size_t)bh * S + q] = l;
+        }
       }
       tc_fence_before();
       mbar_arrive(&s.o_empty[t]);
@@ -543,6 +556,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // Peer stores must be visible system-wide before this rank signals the
   // others that its units are in place (dist_signal_wait_kernel).
+  if (kGather && out.o_mc) fence_proxy_alias();
   if (kGather) __threadfence_system();
   __syncwarp();
   tc_fence_before();

@@ -1382,7 +1382,7 @@ int jules_dist_unique_id(void* id) {
   if (!id) return fail(JULES_ERR_ARG, "dist_unique_id: NULL");
   if (int rc = need_nccl()) return rc;
   ncclUniqueId u;
-  ncclResult_t r = nccl().get_unique_id(&u);
+  ncclResult_t r = nccl_lib().get_unique_id(&u);
   if (r != ncclSuccess) return nccl_fail(r, "ncclGetUniqueId");
   static_assert(sizeof(u) == JULES_DIST_ID_BYTES, "NCCL unique id size");
   std::memcpy(id, &u, sizeof(u));
@@ -1405,7 +1405,7 @@ int jules_dist_init(void** comm, int world, int rank, const void* id) {
   }
   ncclUniqueId u;
   std::memcpy(&u, id, sizeof(u));
-  ncclResult_t r = nccl().comm_init_rank(&c->comm, world, u, rank);
+  ncclResult_t r = nccl_lib().comm_init_rank(&c->comm, world, u, rank);
   if (r != ncclSuccess) {
     delete c;
     return nccl_fail(r, "ncclCommInitRank");
@@ -1422,6 +1422,9 @@ int jules_dist_init(void** comm, int world, int rank, const void* id) {
     jules_dist_destroy(c);
     return rc;
   }
+#if JULES_NCCL_DEVICE_API
+  multicast_setup(c);
+#endif
   *comm = c;
   return ok();
 }
@@ -1433,8 +1436,20 @@ int jules_dist_destroy(void* comm) {
   for (auto& b : c->shared) shared_release(c, b);
   shared_release(c, c->flags);
   if (c->d_counters) cudaFree(c->d_counters);
-  if (c->comm) nccl().comm_destroy(c->comm);
+#if JULES_NCCL_DEVICE_API
+  if (c->has_devcomm) nccl_lib().devcomm_destroy(c->comm, &c->devcomm);
+#endif
+  if (c->comm) nccl_lib().comm_destroy(c->comm);
   delete c;
+  return ok();
+}
+
+int jules_dist_multicast(void* comm, int* on) {
+  if (!on) return fail(JULES_ERR_ARG, "dist_multicast: NULL");
+  *on = 0;
+  DistComm* c;
+  if (int rc = dist_check(comm, &c)) return rc;
+  *on = c->mc_stores ? 1 : 0;
   return ok();
 }
 
@@ -1444,7 +1459,7 @@ int jules_dist_barrier(void* comm, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // one in-place all-reduce of the spare word after the counter
   auto* w = reinterpret_cast<unsigned long long*>(static_cast<char*>(c->flags.local) + 64);
-  ncclResult_t r = nccl().all_reduce(w, w, 1, ncclUint64, ncclSum, c->comm, st);
+  ncclResult_t r = nccl_lib().all_reduce(w, w, 1, ncclUint64, ncclSum, c->comm, st);
   return r == ncclSuccess ? ok() : nccl_fail(r, "ncclAllReduce(barrier)");
 }
 
@@ -1455,6 +1470,11 @@ int jules_dist_alloc_shared(void* comm, size_t bytes, void** local) {
   if (int rc = dist_check(comm, &c)) return rc;
   if (bytes == 0) return fail(JULES_ERR_ARG, "dist_alloc_shared: 0 bytes");
   SharedBuf b;
+#if JULES_NCCL_DEVICE_API
+  if (c->multicast) {
+    if (int rc = shared_alloc_window(c, bytes, &b)) return rc;
+  } else
+#endif
   if (int rc = shared_alloc(c, bytes, &b)) return rc;
   std::lock_guard<std::mutex> lk(c->mu);
   c->shared.push_back(b);
@@ -1515,6 +1535,7 @@ int jules_dist_gemm_bias_act(void* comm, const void* A, const void* W, const flo
       od.n = c->world;
       od.row_off = (int)b;
       od.c[0] = static_cast<__nv_bfloat16*>(C);
+      od.mc = c->mc_stores ? static_cast<__nv_bfloat16*>(shared_c.mc) : nullptr;
       for (int q = 1; q < c->world; ++q)
         od.c[q] = static_cast<__nv_bfloat16*>(shared_c.peers[(c->rank + q) % c->world]);
       rc = gemm_tc2<256>(a, w, bias, r, od, e - b, N, K, act, st);
@@ -1523,6 +1544,7 @@ int jules_dist_gemm_bias_act(void* comm, const void* A, const void* W, const flo
       od.n = c->world;
       od.row_off = (int)b;
       od.c[0] = static_cast<float*>(C);
+      od.mc = c->mc_stores ? static_cast<float*>(shared_c.mc) : nullptr;
       for (int q = 1; q < c->world; ++q)
         od.c[q] = static_cast<float*>(shared_c.peers[(c->rank + q) % c->world]);
       rc = gemm_tc2<256>(a, w, bias, r, od, e - b, N, K, act, st);
@@ -1596,6 +1618,12 @@ int jules_dist_flash_attention_fwd(void* comm, const void* Q, const void* K, con
                                                    ((size_t)b0 * Hq + (size_t)g0 * G) * S * 4)
                         : nullptr;
     }
+    if (c->mc_stores && so.mc && (!lse || sl.mc)) {  // both through multicast, or neither
+      out.o_mc = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(so.mc) + q_off * elt);
+      out.lse_mc = lse ? reinterpret_cast<float*>(static_cast<char*>(sl.mc) +
+                                                  ((size_t)b0 * Hq + (size_t)g0 * G) * S * 4)
+                       : nullptr;
+    }
     if (!(scale > 0.0f)) scale = 1.0f / sqrtf((float)D);
     if (int rc = attn_tc(q, k, v, out, Bl, Hql, Hkvl, S, D, scale, causal ? 1 : 0,
                          dtype == JULES_DTYPE_F16, st))
@@ -1610,11 +1638,11 @@ int jules_dist_flash_attention_fwd(void* comm, const void* Q, const void* K, con
     return rc;
   ncclDataType_t t;
   if (int rc = nccl_type(dtype, &t)) return rc;
-  ncclResult_t r = nccl().group_start();
+  ncclResult_t r = nccl_lib().group_start();
   if (r != ncclSuccess) return nccl_fail(r, "ncclGroupStart");
   int rc = gather_in_place(c, O, units, (int64_t)G * S * D, t, elt, st);
   if (!rc && lse) rc = gather_in_place(c, lse, units, (int64_t)G * S, ncclFloat32, 4, st);
-  r = nccl().group_end();
+  r = nccl_lib().group_end();
   if (rc) return rc;
   return r == ncclSuccess ? ok() : nccl_fail(r, "ncclGroupEnd");
 }

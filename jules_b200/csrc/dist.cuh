@@ -17,17 +17,36 @@
 // spin, until all ranks have signalled: after it, every rank's output holds
 // the whole result.  Outputs that are not shared fall back to computing the
 // local share and an in-place ncclAllGather.
+//
+// NVLink multicast: when the loaded NCCL has the symmetric-memory device API
+// (NCCL 2.28, the version of the headers this file is compiled against) and
+// the node's NVSwitch supports multicast (NVLS), shared buffers are NCCL
+// symmetric windows (ncclMemAlloc + ncclCommWindowRegister) and the
+// communicator carries a multicast handle (ncclDevCommCreate with
+// lsaMultimem): the epilogues then store each 16-byte chunk once, to the
+// buffer's multicast address, and the switch writes it into every rank's
+// buffer.  Otherwise (another NCCL, NVLS off, JULES_DIST_MULTICAST=0) the
+// buffers are cudaMalloc + CUDA IPC and the epilogues store to each rank.
 #pragma once
 
 #include <dlfcn.h>
 #include <nccl.h>
 
+#if __has_include(<nccl_device.h>)
+#include <nccl_device.h>
+#define JULES_NCCL_DEVICE_API 1
+#else
+#define JULES_NCCL_DEVICE_API 0
+#endif
+
+#include <cstdlib>
 #include <vector>
 
 namespace jb {
 namespace dist {
 
 constexpr int kMaxRanks = 8;  // == gemm::kMaxOutDest
+constexpr int kMulticastMinWorld = 4;
 constexpr uint32_t kSiteSignalWait = 251;
 
 // Adds one to every rank's completion counter, then waits until this rank's
@@ -54,6 +73,16 @@ __global__ void dist_signal_wait_kernel(unsigned long long* const* counters, int
   __threadfence_system();
 }
 
+#if JULES_NCCL_DEVICE_API
+// A symmetric window's multicast address (out[0]) and every rank's unicast
+// address of it (out[1 + r]), resolved by NCCL's own device functions.
+__global__ void window_ptrs_kernel(ncclWindow_t w, ncclDevComm dc, int world, void** out) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  out[0] = ncclGetLsaMultimemPointer(w, 0, dc);
+  for (int r = 0; r < world; ++r) out[1 + r] = ncclGetLsaPointer(w, 0, r);
+}
+#endif
+
 }  // namespace dist
 }  // namespace jb
 
@@ -72,11 +101,23 @@ struct NcclApi {
   decltype(&ncclGroupStart) group_start = nullptr;
   decltype(&ncclGroupEnd) group_end = nullptr;
   decltype(&ncclGetErrorString) error_string = nullptr;
+  decltype(&ncclGetVersion) get_version = nullptr;
+#if JULES_NCCL_DEVICE_API
+  // Symmetric windows and the device communicator (optional).
+  decltype(&ncclMemAlloc) mem_alloc = nullptr;
+  decltype(&ncclMemFree) mem_free = nullptr;
+  decltype(&ncclCommWindowRegister) win_register = nullptr;
+  decltype(&ncclCommWindowDeregister) win_deregister = nullptr;
+  decltype(&ncclDevCommCreate) devcomm_create = nullptr;
+  decltype(&ncclDevCommDestroy) devcomm_destroy = nullptr;
+#endif
+  bool device_api = false;  // all of those, from a library of the headers' version
+  int version = 0;
   bool loaded = false;
   std::string why;
 };
 
-NcclApi& nccl() {
+NcclApi& nccl_lib() {
   static NcclApi api;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -103,16 +144,32 @@ NcclApi& nccl() {
     sym(api.error_string, "ncclGetErrorString");
     api.loaded = ok;
     if (!ok) api.why = "libnccl.so.2 lacks an expected symbol";
+    auto opt = [&](auto& fn, const char* name) {
+      fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(h, name));
+      return fn != nullptr;
+    };
+    if (opt(api.get_version, "ncclGetVersion")) api.get_version(&api.version);
+#if JULES_NCCL_DEVICE_API
+    bool dev = opt(api.mem_alloc, "ncclMemAlloc");
+    dev = opt(api.mem_free, "ncclMemFree") && dev;
+    dev = opt(api.win_register, "ncclCommWindowRegister") && dev;
+    dev = opt(api.win_deregister, "ncclCommWindowDeregister") && dev;
+    dev = opt(api.devcomm_create, "ncclDevCommCreate") && dev;
+    dev = opt(api.devcomm_destroy, "ncclDevCommDestroy") && dev;
+    // The device communicator and window structs are read by code compiled
+    // from this version's headers.
+    api.device_api = ok && dev && api.version == NCCL_VERSION_CODE;
+#endif
   });
   return api;
 }
 
 int nccl_fail(ncclResult_t r, const char* what) {
-  return fail(JULES_ERR_COMM, "%s: %s", what, nccl().error_string ? nccl().error_string(r) : "?");
+  return fail(JULES_ERR_COMM, "%s: %s", what, nccl_lib().error_string ? nccl_lib().error_string(r) : "?");
 }
 
 int need_nccl() {
-  if (!nccl().loaded) return fail(JULES_ERR_COMM, "NCCL unavailable: %s", nccl().why.c_str());
+  if (!nccl_lib().loaded) return fail(JULES_ERR_COMM, "NCCL unavailable: %s", nccl_lib().why.c_str());
   return JULES_OK;
 }
 
@@ -123,11 +180,19 @@ struct SharedBuf {
   void* local = nullptr;
   size_t bytes = 0;
   void* peers[jb::dist::kMaxRanks] = {};  // peers[rank] == local
+  void* mc = nullptr;   // multicast address of the whole buffer (symmetric window), or null
+  void* win = nullptr;  // ncclWindow_t of a symmetric window, or null (cudaMalloc + IPC)
 };
 
 struct DistComm {
   ncclComm_t comm = nullptr;
   int world = 1, rank = 0, dev = 0;
+  bool multicast = false;  // shared buffers are multicast windows
+  bool mc_stores = false;  // the fused gathers store through the multicast address
+#if JULES_NCCL_DEVICE_API
+  bool has_devcomm = false;
+  ncclDevComm devcomm{};
+#endif
   unsigned long long calls = 0;             // signal/wait rounds issued (same on every rank)
   SharedBuf flags;                          // one u64 completion counter per rank
   unsigned long long** d_counters = nullptr;  // device array: every rank's counter
@@ -135,12 +200,105 @@ struct DistComm {
   std::mutex mu;
 };
 
+// Collective for symmetric windows (the deregistration is), local for IPC
+// buffers.
 void shared_release(DistComm* c, SharedBuf& b) {
+#if JULES_NCCL_DEVICE_API
+  if (b.win) {
+    nccl_lib().win_deregister(c->comm, static_cast<ncclWindow_t>(b.win));
+    nccl_lib().mem_free(b.local);
+    b = SharedBuf{};
+    return;
+  }
+#endif
   for (int r = 0; r < c->world; ++r)
     if (r != c->rank && b.peers[r]) cudaIpcCloseMemHandle(b.peers[r]);
   if (b.local) cudaFree(b.local);
   b = SharedBuf{};
 }
+
+#if JULES_NCCL_DEVICE_API
+// Collective: a symmetric window of `bytes` (rounded up to 4 KiB) on every
+// rank, zeroed, with its multicast address and every rank's unicast address.
+int shared_alloc_window(DistComm* c, size_t bytes, SharedBuf* out) {
+  SharedBuf b;
+  b.bytes = bytes;
+  const size_t sz = (bytes + 4095) & ~size_t(4095);
+  ncclResult_t r = nccl_lib().mem_alloc(&b.local, sz);
+  if (r != ncclSuccess) return nccl_fail(r, "ncclMemAlloc");
+  cudaError_t e = cudaMemset(b.local, 0, sz);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    nccl_lib().mem_free(b.local);
+    return cuda_fail(e, "cudaMemset(shared window)");
+  }
+  ncclWindow_t w = nullptr;
+  r = nccl_lib().win_register(c->comm, b.local, sz, &w, NCCL_WIN_COLL_SYMMETRIC);
+  if (r != ncclSuccess) {
+    nccl_lib().mem_free(b.local);
+    return nccl_fail(r, "ncclCommWindowRegister");
+  }
+  b.win = w;
+  void** d = nullptr;
+  void* h[1 + jb::dist::kMaxRanks] = {};
+  const size_t hb = sizeof(void*) * (1 + c->world);
+  e = cudaMalloc(&d, hb);
+  if (e == cudaSuccess) {
+    jb::dist::window_ptrs_kernel<<<1, 32>>>(w, c->devcomm, c->world, d);
+    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaMemcpy(h, d, hb, cudaMemcpyDeviceToHost);
+    cudaFree(d);
+  }
+  if (e != cudaSuccess || !h[0]) {
+    shared_release(c, b);
+    return e != cudaSuccess ? cuda_fail(e, "symmetric window addresses")
+                            : fail(JULES_ERR_COMM, "symmetric window without a multicast address");
+  }
+  b.mc = h[0];
+  for (int q = 0; q < c->world; ++q) b.peers[q] = q == c->rank ? b.local : h[1 + q];
+  *out = b;
+  return JULES_OK;
+}
+
+// Collective: the device communicator with a multicast handle, when every
+// rank can have one.  c->multicast says whether shared buffers are windows,
+// c->mc_stores whether the fused gathers store through their multicast
+// address (else through the windows' per-rank addresses).
+// JULES_DIST_MULTICAST: "0" off, "1" on at every world size; unset: on from
+// kMulticastMinWorld ranks.  A multicast store also sends this rank's own
+// share out through the switch and back, so each GPU receives the whole
+// output instead of (world-1)/world of it; it pays only where the per-rank
+// fan-out of peer stores is the slower side.
+void multicast_setup(DistComm* c) {
+  if (c->world < 2) return;
+  const char* env = std::getenv("JULES_DIST_MULTICAST");
+  const bool off = env && env[0] == '0', forced = env && env[0] == '1';
+  int want = nccl_lib().device_api && !off && (forced || c->world >= jb::dist::kMulticastMinWorld) ? 1 : 0;
+  // Every rank must take the same allocation route: agree on the flag first.
+  int* d = nullptr;
+  if (cudaMalloc(&d, sizeof(int)) != cudaSuccess) return;
+  int agreed = 0;
+  if (cudaMemcpy(d, &want, sizeof(int), cudaMemcpyHostToDevice) == cudaSuccess &&
+      nccl_lib().all_reduce(d, d, 1, ncclInt32, ncclMin, c->comm, nullptr) == ncclSuccess &&
+      cudaMemcpy(&agreed, d, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess && agreed) {
+    ncclDevCommRequirements reqs{};
+    reqs.lsaMultimem = true;
+    int have = 0;
+    if (nccl_lib().devcomm_create(c->comm, &reqs, &c->devcomm) == ncclSuccess) {
+      c->has_devcomm = true;
+      have = c->devcomm.lsaMultimem.mcBasePtr != nullptr && c->devcomm.lsaSize == c->world &&
+             c->devcomm.lsaRank == c->rank;
+    }
+    int all = 0;
+    if (cudaMemcpy(d, &have, sizeof(int), cudaMemcpyHostToDevice) == cudaSuccess &&
+        nccl_lib().all_reduce(d, d, 1, ncclInt32, ncclMin, c->comm, nullptr) == ncclSuccess &&
+        cudaMemcpy(&all, d, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess)
+      c->multicast = all != 0;
+  }
+  c->mc_stores = c->multicast;
+  cudaFree(d);
+}
+#endif
 
 // Collective: every rank allocates `bytes`, exports a CUDA IPC handle, the
 // handles are all-gathered over NCCL and each rank maps the others'.
@@ -172,7 +330,7 @@ int shared_alloc(DistComm* c, size_t bytes, SharedBuf* out) {
   } else if ((e = cudaMemcpy(d_handles + hb * c->rank, &mine, hb, cudaMemcpyHostToDevice)) != cudaSuccess) {
     rc = cuda_fail(e, "copy IPC handle");
   } else {
-    ncclResult_t r = nccl().all_gather(d_handles + hb * c->rank, d_handles, hb, ncclUint8, c->comm, st);
+    ncclResult_t r = nccl_lib().all_gather(d_handles + hb * c->rank, d_handles, hb, ncclUint8, c->comm, st);
     if (r != ncclSuccess) rc = nccl_fail(r, "ncclAllGather(IPC handles)");
     else if ((e = cudaStreamSynchronize(st)) != cudaSuccess) rc = cuda_fail(e, "handle exchange");
     else if ((e = cudaMemcpy(all.data(), d_handles, hb * c->world, cudaMemcpyDeviceToHost)) != cudaSuccess)
@@ -245,17 +403,17 @@ int gather_in_place(DistComm* c, void* buf, int64_t units, int64_t unit_elems, n
   char* base = static_cast<char*>(buf);
   if (units % w == 0) {
     const size_t cnt = (size_t)(units / w) * unit_elems;
-    ncclResult_t r = nccl().all_gather(base + (size_t)c->rank * cnt * elt, base, cnt, t, c->comm, st);
+    ncclResult_t r = nccl_lib().all_gather(base + (size_t)c->rank * cnt * elt, base, cnt, t, c->comm, st);
     return r == ncclSuccess ? JULES_OK : nccl_fail(r, "ncclAllGather");
   }
-  ncclResult_t r = nccl().group_start();
+  ncclResult_t r = nccl_lib().group_start();
   for (int q = 0; q < w && r == ncclSuccess; ++q) {
     int64_t b, e;
     jules_dist_shard(units, w, q, &b, &e);
     void* p = base + (size_t)b * unit_elems * elt;
-    r = nccl().broadcast(p, p, (size_t)(e - b) * unit_elems, t, q, c->comm, st);
+    r = nccl_lib().broadcast(p, p, (size_t)(e - b) * unit_elems, t, q, c->comm, st);
   }
-  ncclResult_t r2 = nccl().group_end();
+  ncclResult_t r2 = nccl_lib().group_end();
   if (r != ncclSuccess) return nccl_fail(r, "ncclBroadcast");
   return r2 == ncclSuccess ? JULES_OK : nccl_fail(r2, "ncclGroupEnd");
 }

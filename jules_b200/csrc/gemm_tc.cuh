@@ -326,11 +326,15 @@ struct Smem2 {
 // Where the pair kernel's epilogue writes C: the local C (c[0]) and, for the
 // sharded GEMM with the gather fused in, the same rows of every other rank's
 // C mapped into this process (c[1..n-1]).  Local row r of the tile grid is
-// row row_off + r of every C; A and the residual use local rows.
+// row row_off + r of every C; A and the residual use local rows.  mc, when
+// set, is C's NVLink multicast address (all ranks' C behind one address):
+// each 16-byte chunk is then stored once and the switch writes it into every
+// rank's C, instead of n stores over n links.
 constexpr int kMaxOutDest = kMaxPeers;
 template <typename TOut>
 struct OutDest {
   TOut* c[kMaxOutDest];
+  TOut* mc;
   int n;
   int row_off;
 };
@@ -610,9 +614,13 @@ __global__ void __launch_bounds__(kThreads2, 1)
             if (row >= M) break;  // rows only grow with i
             const uint4 val = stage[rr * 8 + (g ^ (rr & 7))];
             const size_t off = (size_t)(out.row_off + row) * N + col;
+            if (out.mc) {
+              multimem_st16(out.mc + off, val);
+            } else {
 #pragma unroll
-            for (int p = 0; p < kMaxOutDest; ++p)
-              if (p < out.n) *reinterpret_cast<uint4*>(out.c[p] + off) = val;
+              for (int p = 0; p < kMaxOutDest; ++p)
+                if (p < out.n) *reinterpret_cast<uint4*>(out.c[p] + off) = val;
+            }
           }
         }
         __syncwarp();
@@ -623,6 +631,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
     }
     // Peer stores must be visible system-wide before this rank signals the
     // others that its rows are in place (dist_signal_wait_kernel).
+    if (out.mc) fence_proxy_alias();
     if (out.n > 1) __threadfence_system();
   }
 

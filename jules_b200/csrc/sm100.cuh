@@ -500,4 +500,21 @@ __device__ __forceinline__ float2 unpack2<__half>(uint32_t v) {
   return __half22float2(*reinterpret_cast<const __half2*>(&v));
 }
 
+// NVLink multicast stores (NVLS): one store to a multicast address is
+// replicated by the NVSwitch into the same offset of every member GPU's
+// buffer, this GPU's included.  16 bytes (four 32-bit words, bit patterns
+// of any 16-bit or 32-bit type) or one fp32 word.
+__device__ __forceinline__ void multimem_st16(void* mc, const uint4& v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x),
+               "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void multimem_st_f32(float* mc, float v) {
+  asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(mc), "f"(v) : "memory");
+}
+// Orders this thread's accesses through the multicast alias of a buffer
+// before its later accesses through other aliases (the signal that follows
+// the stores goes through unicast addresses).
+__device__ __forceinline__ void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
+
 }  // namespace jb

@@ -130,6 +130,7 @@ def _worker(rank, world, port, q, case):
                 out["site"] = (w.value >> 8) & 0xff
             tdist.barrier()  # rank 1 stays alive (its C stays mapped) until rank 0 is done
         assert jb.device_error() == 0
+        out["multicast"] = dist.multicast
         q.put((rank, out))
     except Exception as ex:  # reported to the parent
         q.put((rank, {"error": repr(ex)}))
@@ -139,15 +140,30 @@ def _worker(rank, world, port, q, case):
         tdist.destroy_process_group()
 
 
-def _run2(case):
+def _run2(case, multicast=False):
+    """Two ranks on GPUs 0 and 1.  multicast=False: NVLS off in NCCL and in
+    the library (peer stores over CUDA IPC mappings); True: both on."""
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    os.environ["NCCL_NVLS_ENABLE"] = "0"
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, case)) for r in range(2)]
-    for p in procs:
-        p.start()
+    saved = {k: os.environ.get(k) for k in ("NCCL_NVLS_ENABLE", "JULES_DIST_MULTICAST")}
+    if multicast:
+        os.environ.pop("NCCL_NVLS_ENABLE", None)
+        os.environ["JULES_DIST_MULTICAST"] = "1"
+    else:
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        os.environ["JULES_DIST_MULTICAST"] = "0"
+    try:
+        procs = [ctx.Process(target=_worker, args=(r, 2, port, q, case)) for r in range(2)]
+        for p in procs:
+            p.start()
+    finally:
+        for k, v in saved.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
     res = dict(q.get(timeout=300) for _ in procs)
     for p in procs:
         p.join(timeout=120)
@@ -163,6 +179,7 @@ def test_dist_gemm_matches_single_gpu():
     res = _run2("gemm")
     for r in (0, 1):
         assert "error" not in res[r], res[r]
+        assert not res[r].pop("multicast")  # peer stores over IPC mappings
         assert all(res[r].values()), res[r]
 
 
@@ -172,6 +189,28 @@ def test_dist_attention_matches_single_gpu():
     res = _run2("attn")
     for r in (0, 1):
         assert "error" not in res[r], res[r]
+        assert not res[r].pop("multicast")
+        assert all(res[r].values()), res[r]
+
+
+@pytest.mark.gpu
+@needs2
+def test_dist_gemm_multicast_matches_single_gpu():
+    """The fused gather through NVLink multicast stores (NVLS on)."""
+    res = _run2("gemm", multicast=True)
+    for r in (0, 1):
+        assert "error" not in res[r], res[r]
+        assert res[r]["multicast"], "no multicast address on this node"
+        assert all(res[r].values()), res[r]
+
+
+@pytest.mark.gpu
+@needs2
+def test_dist_attention_multicast_matches_single_gpu():
+    res = _run2("attn", multicast=True)
+    for r in (0, 1):
+        assert "error" not in res[r], res[r]
+        assert res[r]["multicast"], "no multicast address on this node"
         assert all(res[r].values()), res[r]
 
 
