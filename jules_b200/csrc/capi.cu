@@ -1618,7 +1618,9 @@ int jules_dist_flash_attention_fwd(void* comm, const void* Q, const void* K, con
                                                    ((size_t)b0 * Hq + (size_t)g0 * G) * S * 4)
                         : nullptr;
     }
-    if (c->mc_stores && so.mc && (!lse || sl.mc)) {  // both through multicast, or neither
+    const size_t share = (size_t)upr * G * S * D * elt;  // this rank's O bytes
+    if (c->mc_stores && so.mc && (!lse || sl.mc) &&
+        (c->mc_forced || share <= jb::dist::kAttnMulticastMaxBytes)) {  // O and lse alike
       out.o_mc = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(so.mc) + q_off * elt);
       out.lse_mc = lse ? reinterpret_cast<float*>(static_cast<char*>(sl.mc) +
                                                   ((size_t)b0 * Hq + (size_t)g0 * G) * S * 4)

@@ -46,7 +46,16 @@ namespace jb {
 namespace dist {
 
 constexpr int kMaxRanks = 8;  // == gemm::kMaxOutDest
-constexpr int kMulticastMinWorld = 4;
+// When the fused gathers store through NVLink multicast (measured on 4 and 8
+// B200s of one NVSwitch node, against peer stores): from 8 ranks, where the
+// end-of-kernel fan-out to 7 peers is the slower side (C2 GEMM 1200 vs 1075
+// TFLOP/s, C3 attention 2096 vs 1783); not at 4 (C2 1105 vs 1466).  For
+// attention only while this rank's output share is at most
+// kAttnMulticastMaxBytes: a long kernel streaming a large output (C5, 134 MB
+// per rank at 8) ran at 4062 vs 6467 TFLOP/s, the switch's sustained
+// multicast throughput being below that of peer stores.
+constexpr int kMulticastMinWorld = 8;
+constexpr size_t kAttnMulticastMaxBytes = size_t(64) << 20;
 constexpr uint32_t kSiteSignalWait = 251;
 
 // Adds one to every rank's completion counter, then waits until this rank's
@@ -189,6 +198,7 @@ struct DistComm {
   int world = 1, rank = 0, dev = 0;
   bool multicast = false;  // shared buffers are multicast windows
   bool mc_stores = false;  // the fused gathers store through the multicast address
+  bool mc_forced = false;  // ... at every size (JULES_DIST_MULTICAST=1)
 #if JULES_NCCL_DEVICE_API
   bool has_devcomm = false;
   ncclDevComm devcomm{};
@@ -264,11 +274,12 @@ int shared_alloc_window(DistComm* c, size_t bytes, SharedBuf* out) {
 // rank can have one.  c->multicast says whether shared buffers are windows,
 // c->mc_stores whether the fused gathers store through their multicast
 // address (else through the windows' per-rank addresses).
-// JULES_DIST_MULTICAST: "0" off, "1" on at every world size; unset: on from
-// kMulticastMinWorld ranks.  A multicast store also sends this rank's own
-// share out through the switch and back, so each GPU receives the whole
-// output instead of (world-1)/world of it; it pays only where the per-rank
-// fan-out of peer stores is the slower side.
+// JULES_DIST_MULTICAST: "0" off, "1" on at every world size (and for every
+// attention output size); unset: on from kMulticastMinWorld ranks.  A
+// multicast store also sends this rank's own share out through the switch
+// and back, so each GPU receives the whole output instead of (world-1)/world
+// of it; it pays only where the per-rank fan-out of peer stores is the
+// slower side.
 void multicast_setup(DistComm* c) {
   if (c->world < 2) return;
   const char* env = std::getenv("JULES_DIST_MULTICAST");
@@ -296,6 +307,7 @@ void multicast_setup(DistComm* c) {
       c->multicast = all != 0;
   }
   c->mc_stores = c->multicast;
+  c->mc_forced = forced;
   cudaFree(d);
 }
 #endif
