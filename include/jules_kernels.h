@@ -414,10 +414,9 @@ int jules_dist_free_shared(void* comm, void* local);
 /* *on = 1 when this communicator's shared buffers have an NVLink multicast
  * address (NVSwitch multicast, NCCL >= 2.28 with its device API): the fused
  * gathers then store each chunk once and the switch replicates it to every
- * rank.  Chosen at jules_dist_init by all ranks together: by default from 8
- * ranks (and, for attention, while a rank's output share is at most 64 MiB),
- * where it measured faster than peer stores; JULES_DIST_MULTICAST=1 uses it
- * at every size, JULES_DIST_MULTICAST=0 (or NCCL_NVLS_ENABLE=0) never. */
+ * rank.  Opt-in: set JULES_DIST_MULTICAST=1 in every rank before
+ * jules_dist_init (it measured no reproducible gain over peer stores on 2-8
+ * B200s; it needs NVLS, so NCCL_NVLS_ENABLE=0 also keeps it off). */
 int jules_dist_multicast(void* comm, int* on);
 
 /*

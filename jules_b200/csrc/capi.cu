@@ -1449,7 +1449,7 @@ int jules_dist_multicast(void* comm, int* on) {
   *on = 0;
   DistComm* c;
   if (int rc = dist_check(comm, &c)) return rc;
-  *on = c->mc_stores ? 1 : 0;
+  *on = c->multicast ? 1 : 0;
   return ok();
 }
 
@@ -1535,7 +1535,7 @@ int jules_dist_gemm_bias_act(void* comm, const void* A, const void* W, const flo
       od.n = c->world;
       od.row_off = (int)b;
       od.c[0] = static_cast<__nv_bfloat16*>(C);
-      od.mc = c->mc_stores ? static_cast<__nv_bfloat16*>(shared_c.mc) : nullptr;
+      od.mc = static_cast<__nv_bfloat16*>(shared_c.mc);
       for (int q = 1; q < c->world; ++q)
         od.c[q] = static_cast<__nv_bfloat16*>(shared_c.peers[(c->rank + q) % c->world]);
       rc = gemm_tc2<256>(a, w, bias, r, od, e - b, N, K, act, st);
@@ -1544,7 +1544,7 @@ int jules_dist_gemm_bias_act(void* comm, const void* A, const void* W, const flo
       od.n = c->world;
       od.row_off = (int)b;
       od.c[0] = static_cast<float*>(C);
-      od.mc = c->mc_stores ? static_cast<float*>(shared_c.mc) : nullptr;
+      od.mc = static_cast<float*>(shared_c.mc);
       for (int q = 1; q < c->world; ++q)
         od.c[q] = static_cast<float*>(shared_c.peers[(c->rank + q) % c->world]);
       rc = gemm_tc2<256>(a, w, bias, r, od, e - b, N, K, act, st);
@@ -1618,9 +1618,7 @@ int jules_dist_flash_attention_fwd(void* comm, const void* Q, const void* K, con
                                                    ((size_t)b0 * Hq + (size_t)g0 * G) * S * 4)
                         : nullptr;
     }
-    const size_t share = (size_t)upr * G * S * D * elt;  // this rank's O bytes
-    if (c->mc_stores && so.mc && (!lse || sl.mc) &&
-        (c->mc_forced || share <= jb::dist::kAttnMulticastMaxBytes)) {  // O and lse alike
+    if (c->multicast && so.mc && (!lse || sl.mc)) {  // O and lse alike
       out.o_mc = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(so.mc) + q_off * elt);
       out.lse_mc = lse ? reinterpret_cast<float*>(static_cast<char*>(sl.mc) +
                                                   ((size_t)b0 * Hq + (size_t)g0 * G) * S * 4)

@@ -25,8 +25,9 @@
 // communicator carries a multicast handle (ncclDevCommCreate with
 // lsaMultimem): the epilogues then store each 16-byte chunk once, to the
 // buffer's multicast address, and the switch writes it into every rank's
-// buffer.  Otherwise (another NCCL, NVLS off, JULES_DIST_MULTICAST=0) the
-// buffers are cudaMalloc + CUDA IPC and the epilogues store to each rank.
+// buffer.  Opt-in (JULES_DIST_MULTICAST=1); otherwise, and without that NCCL
+// or NVLS, the buffers are cudaMalloc + CUDA IPC and the epilogues store to
+// each rank.
 #pragma once
 
 #include <dlfcn.h>
@@ -46,16 +47,6 @@ namespace jb {
 namespace dist {
 
 constexpr int kMaxRanks = 8;  // == gemm::kMaxOutDest
-// When the fused gathers store through NVLink multicast (measured on 4 and 8
-// B200s of one NVSwitch node, against peer stores): from 8 ranks, where the
-// end-of-kernel fan-out to 7 peers is the slower side (C2 GEMM 1200 vs 1075
-// TFLOP/s, C3 attention 2096 vs 1783); not at 4 (C2 1105 vs 1466).  For
-// attention only while this rank's output share is at most
-// kAttnMulticastMaxBytes: a long kernel streaming a large output (C5, 134 MB
-// per rank at 8) ran at 4062 vs 6467 TFLOP/s, the switch's sustained
-// multicast throughput being below that of peer stores.
-constexpr int kMulticastMinWorld = 8;
-constexpr size_t kAttnMulticastMaxBytes = size_t(64) << 20;
 constexpr uint32_t kSiteSignalWait = 251;
 
 // Adds one to every rank's completion counter, then waits until this rank's
@@ -196,9 +187,8 @@ struct SharedBuf {
 struct DistComm {
   ncclComm_t comm = nullptr;
   int world = 1, rank = 0, dev = 0;
-  bool multicast = false;  // shared buffers are multicast windows
-  bool mc_stores = false;  // the fused gathers store through the multicast address
-  bool mc_forced = false;  // ... at every size (JULES_DIST_MULTICAST=1)
+  bool multicast = false;  // shared buffers are multicast windows, stored through their
+                           // multicast address
 #if JULES_NCCL_DEVICE_API
   bool has_devcomm = false;
   ncclDevComm devcomm{};
@@ -271,20 +261,20 @@ int shared_alloc_window(DistComm* c, size_t bytes, SharedBuf* out) {
 }
 
 // Collective: the device communicator with a multicast handle, when every
-// rank can have one.  c->multicast says whether shared buffers are windows,
-// c->mc_stores whether the fused gathers store through their multicast
-// address (else through the windows' per-rank addresses).
-// JULES_DIST_MULTICAST: "0" off, "1" on at every world size (and for every
-// attention output size); unset: on from kMulticastMinWorld ranks.  A
-// multicast store also sends this rank's own share out through the switch
-// and back, so each GPU receives the whole output instead of (world-1)/world
-// of it; it pays only where the per-rank fan-out of peer stores is the
-// slower side.
+// rank can have one and JULES_DIST_MULTICAST=1 asks for it.  c->multicast
+// says whether shared buffers are windows and the fused gathers store
+// through their multicast address.  Off by default: a multicast store also
+// sends this rank's own share out through the switch and back (each GPU
+// receives the whole output instead of (world-1)/world of it), and on 2, 4
+// and 8 B200s of one NVSwitch node it measured no reproducible gain over
+// peer stores (8 ranks: C2 GEMM 1200 and 1054 TFLOP/s on two boxes against
+// 1075, C3 attention 2096 and 1741 against 1783; a long C5 attention 4062
+// against 6467; 4 ranks: C2 1105 against 1466; 2 ranks: C2 1197 against
+// 1499).
 void multicast_setup(DistComm* c) {
   if (c->world < 2) return;
   const char* env = std::getenv("JULES_DIST_MULTICAST");
-  const bool off = env && env[0] == '0', forced = env && env[0] == '1';
-  int want = nccl_lib().device_api && !off && (forced || c->world >= jb::dist::kMulticastMinWorld) ? 1 : 0;
+  int want = nccl_lib().device_api && env && env[0] == '1' ? 1 : 0;
   // Every rank must take the same allocation route: agree on the flag first.
   int* d = nullptr;
   if (cudaMalloc(&d, sizeof(int)) != cudaSuccess) return;
@@ -306,8 +296,6 @@ void multicast_setup(DistComm* c) {
         cudaMemcpy(&all, d, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess)
       c->multicast = all != 0;
   }
-  c->mc_stores = c->multicast;
-  c->mc_forced = forced;
   cudaFree(d);
 }
 #endif
