@@ -129,21 +129,25 @@ def profiled_traffic(workload):
     return None
 
 
-def describe(workload, world, extra_l2=None, multicast=None):
-    """The config object of the JSON line (shared by both arms).  multicast:
-    whether the library's communicator stores the fused gather through
-    NVLink multicast addresses (None: no communicator)."""
-    how = (" through NVLink multicast (each chunk stored once, the NVSwitch writes it to "
-           "every rank)" if multicast else " as peer stores to each rank" if multicast is not None
-           else "")
+def describe(workload, world, extra_l2=None, comm=None):
+    """The config object of the JSON line (shared by both arms).  comm: the
+    library's communicator, asked which gather route the workload's output
+    takes (None: the reference arm)."""
+    def how(out_bytes, kernel, what):
+        route = comm.gather_route(out_bytes) if comm is not None else "stores"
+        return {"stores": f"fused into the {kernel} epilogue as NVLink stores to each rank's {what}",
+                "multicast": f"fused into the {kernel} epilogue as NVLink multicast stores (the "
+                             f"NVSwitch writes each chunk into every rank's {what})",
+                "pull": f"the {kernel} stores this rank's share, then the copy engines pull the "
+                        f"other ranks' shares of {what} over NVLink"}[route]
     if workload in ("gemm", "headline"):
         c = {"workload": "C2 fused GEMM+bias+GELU(tanh)", "M": 4096, "N": 4096, "K": 4096,
              "M_per_rank": 4096 // world, "sharding": "rows of M (strong scaling: the global "
              "config split over the ranks)", "dtype_in": "bf16", "accumulate": "fp32",
              "dtype_out": "bf16"}
         if world > 1:
-            c["gather"] = ("C gathered into every rank inside the timed step: fused into the GEMM "
-                           "epilogue" + how + " (jules_dist_gemm_bias_act)")
+            c["gather"] = ("C gathered into every rank inside the timed step: "
+                           + how(4096 * 4096 * 2, "GEMM", "C") + " (jules_dist_gemm_bias_act)")
     elif workload in ("attn", "attn_gqa"):
         gqa = workload == "attn_gqa"
         B, Hq, Hkv, S = (4, 64, 8, 16384) if gqa else (8, 32, 32, 4096)
@@ -155,8 +159,9 @@ def describe(workload, world, extra_l2=None, multicast=None):
                          "the ranks)",
              "flop_convention": "causal = 2*B*Hq*S^2*D"}
         if world > 1:
-            c["gather"] = ("O and lse gathered into every rank inside the timed step: fused into "
-                           "the attention epilogue" + how + " (jules_dist_flash_attention_fwd)")
+            c["gather"] = ("O and lse gathered into every rank inside the timed step: "
+                           + how(B * Hq * S * 128 * 2, "attention", "O and lse")
+                           + " (jules_dist_flash_attention_fwd)")
     elif workload == "mlp":
         c = {"workload": "C4 MLP block LN->GEMM+b+GELU->GEMM+b+residual", "T_per_rank": 16384,
              "d": 4096, "dff": 16384, "global_T": 16384 * world, "sharding": "token rows",
@@ -1309,8 +1314,7 @@ def main():
             "value": round(tflops_total, 3), "unit": wl.unit,
             "ms_per_step": round(ms_total / K, 5),
             "dtype": "f32" if workload == "attn_fp32" else wl.dtype,
-            "config": describe(workload, world, wl.config.get("l2"),
-                               multicast=dist_comm.multicast if dist_comm is not None else None),
+            "config": describe(workload, world, wl.config.get("l2"), comm=dist_comm),
             "roofline": roofline(wl, achieved, peak, peak_kind, traffic),
             **({"pct_of_dense_bf16_peak_2250": round(100 * tflops_total / world / 2250.0, 2)}
                if wl.unit == "TFLOP/s" and not isinstance(wl, (Fp8Gemm, AttentionF32, GemmF32))

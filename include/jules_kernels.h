@@ -419,6 +419,22 @@ int jules_dist_free_shared(void* comm, void* local);
  * B200s; it needs NVLS, so NCCL_NVLS_ENABLE=0 also keeps it off). */
 int jules_dist_multicast(void* comm, int* on);
 
+/* How the sharded calls gather an output of out_bytes (total, all ranks)
+ * held in a shared buffer:
+ *   JULES_GATHER_STORES     the kernel's epilogue stores every finished tile
+ *                           into every rank's buffer over NVLink;
+ *   JULES_GATHER_MULTICAST  the same through the buffer's multicast address;
+ *   JULES_GATHER_PULL       the kernel stores this rank's share locally and,
+ *                           once every rank has signalled, the copy engines
+ *                           fetch the other ranks' shares (one transfer per
+ *                           peer on its own stream).
+ * Chosen from the world size and out_bytes (the same on every rank);
+ * JULES_DIST_GATHER=stores or pull in the environment forces one. */
+#define JULES_GATHER_STORES 0
+#define JULES_GATHER_MULTICAST 1
+#define JULES_GATHER_PULL 2
+int jules_dist_gather_route(void* comm, size_t out_bytes, int* route);
+
 /*
  * Sharded jules_gemm_bias_act: rank r computes rows jules_dist_shard(M) of
  * C = act(A . W + bias) (+ residual) from its rows of A (and residual); W and

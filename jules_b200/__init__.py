@@ -79,6 +79,7 @@ _SIGNATURES = {
     "jules_dist_destroy": ([_c_vp], _c_int),
     "jules_dist_barrier": ([_c_vp, _c_vp], _c_int),
     "jules_dist_multicast": ([_c_vp, ctypes.POINTER(_c_int)], _c_int),
+    "jules_dist_gather_route": ([_c_vp, ctypes.c_size_t, ctypes.POINTER(_c_int)], _c_int),
     "jules_dist_alloc_shared": ([_c_vp, ctypes.c_size_t, ctypes.POINTER(_c_vp)], _c_int),
     "jules_dist_free_shared": ([_c_vp, _c_vp], _c_int),
     "jules_dist_gemm_bias_act": ([_c_vp] * 6 + [_c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int,
@@ -576,6 +577,14 @@ class Dist:
         on = _c_int(0)
         _check(lib().jules_dist_multicast(self.h, ctypes.byref(on)), "jules_dist_multicast")
         return bool(on.value)
+
+    def gather_route(self, out_bytes):
+        """"stores", "multicast" or "pull": how a sharded call gathers a
+        shared output of out_bytes (jules_dist_gather_route)."""
+        r = _c_int(0)
+        _check(lib().jules_dist_gather_route(self.h, int(out_bytes), ctypes.byref(r)),
+               "jules_dist_gather_route")
+        return ("stores", "multicast", "pull")[r.value]
 
     def barrier(self, stream=None):
         _check(lib().jules_dist_barrier(self.h, _stream(stream)), "jules_dist_barrier")

@@ -1425,6 +1425,10 @@ int jules_dist_init(void** comm, int world, int rank, const void* id) {
 #if JULES_NCCL_DEVICE_API
   multicast_setup(c);
 #endif
+  if (const char* g = std::getenv("JULES_DIST_GATHER")) {
+    if (!std::strcmp(g, "stores") || !std::strcmp(g, "fused")) c->gather_mode = 1;
+    if (!std::strcmp(g, "pull")) c->gather_mode = 2;
+  }
   *comm = c;
   return ok();
 }
@@ -1433,6 +1437,7 @@ int jules_dist_destroy(void* comm) {
   if (!comm) return ok();
   auto* c = static_cast<DistComm*>(comm);
   cudaDeviceSynchronize();
+  side_release(c);
   for (auto& b : c->shared) shared_release(c, b);
   shared_release(c, c->flags);
   if (c->d_counters) cudaFree(c->d_counters);
@@ -1450,6 +1455,16 @@ int jules_dist_multicast(void* comm, int* on) {
   DistComm* c;
   if (int rc = dist_check(comm, &c)) return rc;
   *on = c->multicast ? 1 : 0;
+  return ok();
+}
+
+int jules_dist_gather_route(void* comm, size_t out_bytes, int* route) {
+  if (!route) return fail(JULES_ERR_ARG, "dist_gather_route: NULL");
+  *route = JULES_GATHER_STORES;
+  DistComm* c;
+  if (int rc = dist_check(comm, &c)) return rc;
+  *route = c->multicast ? JULES_GATHER_MULTICAST
+                        : use_pull_gather(c, out_bytes) ? JULES_GATHER_PULL : JULES_GATHER_STORES;
   return ok();
 }
 
@@ -1529,10 +1544,14 @@ int jules_dist_gemm_bias_act(void* comm, const void* A, const void* W, const flo
     const auto* a = reinterpret_cast<const __nv_bfloat16*>(A_l);
     const auto* w = static_cast<const __nv_bfloat16*>(W);
     const auto* r = reinterpret_cast<const __nv_bfloat16*>(R_l);
+    // pull: the kernel stores this rank's rows locally; the copy engines
+    // fetch the other ranks' rows after the signal/wait round.
+    const bool pull = use_pull_gather(c, (size_t)M * N * eout) && !c->multicast;
+    const int n_dest = pull ? 1 : c->world;
     int rc;
     if (out_dtype == JULES_DTYPE_BF16) {
       jb::gemm::OutDest<__nv_bfloat16> od{};
-      od.n = c->world;
+      od.n = n_dest;
       od.row_off = (int)b;
       od.c[0] = static_cast<__nv_bfloat16*>(C);
       od.mc = static_cast<__nv_bfloat16*>(shared_c.mc);
@@ -1541,7 +1560,7 @@ int jules_dist_gemm_bias_act(void* comm, const void* A, const void* W, const flo
       rc = gemm_tc2<256>(a, w, bias, r, od, e - b, N, K, act, st);
     } else {
       jb::gemm::OutDest<float> od{};
-      od.n = c->world;
+      od.n = n_dest;
       od.row_off = (int)b;
       od.c[0] = static_cast<float*>(C);
       od.mc = static_cast<float*>(shared_c.mc);
@@ -1554,7 +1573,8 @@ int jules_dist_gemm_bias_act(void* comm, const void* A, const void* W, const flo
     jb::dist::dist_signal_wait_kernel<<<1, 32, 0, st>>>(
         c->d_counters, c->world, static_cast<const unsigned long long*>(c->flags.local), target,
         jb::kWaitLimitNs);
-    return check_launch("dist_signal_wait_kernel launch");
+    if (int rc2 = check_launch("dist_signal_wait_kernel launch")) return rc2;
+    return pull ? pull_gather(c, shared_c, M, (size_t)N * eout, nullptr, 0, st) : ok();
   }
   if (e > b) {
     char* C_l = static_cast<char*>(C) + (size_t)b * N * eout;
@@ -1609,8 +1629,9 @@ int jules_dist_flash_attention_fwd(void* comm, const void* Q, const void* K, con
       aligned16(K) && aligned16(V) && aligned16(O)) {
     // Gather fused into the attention epilogue: each finished O tile (and
     // its lse) is stored into every rank's buffers.
+    const bool pull = use_pull_gather(c, (size_t)B * Hq * S * D * elt) && !c->multicast;
     jb::attn::AttnOut out{};
-    out.n = w;
+    out.n = pull ? 1 : w;  // pull: local stores, the copy engines fetch the rest
     for (int qq = 0; qq < w; ++qq) {
       const int peer = (c->rank + qq) % w;
       out.o[qq] = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(so.peers[peer]) + q_off * elt);
@@ -1632,7 +1653,10 @@ int jules_dist_flash_attention_fwd(void* comm, const void* Q, const void* K, con
     jb::dist::dist_signal_wait_kernel<<<1, 32, 0, st>>>(
         c->d_counters, w, static_cast<const unsigned long long*>(c->flags.local), target,
         jb::kWaitLimitNs);
-    return check_launch("dist_signal_wait_kernel launch");
+    if (int rc = check_launch("dist_signal_wait_kernel launch")) return rc;
+    return pull ? pull_gather(c, so, units, (size_t)G * S * D * elt, lse ? &sl : nullptr,
+                              (size_t)G * S * 4, st)
+                : ok();
   }
   if (int rc = jules_flash_attention_fwd(q, k, v, o, l, Bl, Hql, Hkvl, S, D, scale, causal, dtype, stream))
     return rc;

@@ -140,14 +140,20 @@ def _worker(rank, world, port, q, case):
         tdist.destroy_process_group()
 
 
-def _run2(case, multicast=False):
+def _run2(case, multicast=False, gather=None):
     """Two ranks on GPUs 0 and 1.  multicast=False: NVLS off in NCCL and in
-    the library (peer stores over CUDA IPC mappings); True: both on."""
+    the library (peer stores over CUDA IPC mappings); True: both on.
+    gather: JULES_DIST_GATHER for the ranks ("fused", "pull") or None."""
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    saved = {k: os.environ.get(k) for k in ("NCCL_NVLS_ENABLE", "JULES_DIST_MULTICAST")}
+    saved = {k: os.environ.get(k) for k in ("NCCL_NVLS_ENABLE", "JULES_DIST_MULTICAST",
+                                             "JULES_DIST_GATHER")}
+    if gather:
+        os.environ["JULES_DIST_GATHER"] = gather
+    else:
+        os.environ.pop("JULES_DIST_GATHER", None)
     if multicast:
         os.environ.pop("NCCL_NVLS_ENABLE", None)
         os.environ["JULES_DIST_MULTICAST"] = "1"
@@ -191,6 +197,20 @@ def test_dist_attention_matches_single_gpu():
         assert "error" not in res[r], res[r]
         assert not res[r].pop("multicast")
         assert all(res[r].values()), res[r]
+
+
+@pytest.mark.gpu
+@needs2
+@pytest.mark.parametrize("gather", ["fused", "pull"])
+def test_dist_gather_routes_match_single_gpu(gather):
+    """Both gather routes, forced: the epilogue's stores to every rank, and
+    local stores plus copy-engine pulls of the peers' shares."""
+    for case in ("gemm", "attn"):
+        res = _run2(case, gather=gather)
+        for r in (0, 1):
+            assert "error" not in res[r], (case, res[r])
+            assert not res[r].pop("multicast")
+            assert all(res[r].values()), (case, res[r])
 
 
 @pytest.mark.gpu
