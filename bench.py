@@ -213,9 +213,10 @@ class ClockSampler:
         "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
     }
 
-    def __init__(self, device_index, interval=0.001):
+    def __init__(self, device_index, interval=0.0005):
         self.ok = False
         self.samples = []
+        self.timed_from = None  # index of the first sample inside the timed region
         self.reasons = set()
         self.max_mhz = None
         try:
@@ -249,13 +250,20 @@ class ClockSampler:
             self._t = threading.Thread(target=self._run, daemon=True)
             self._t.start()
 
+    def mark_timed(self):
+        """The timed region starts now (warm-up samples come before it)."""
+        self.timed_from = len(self.samples)
+
     def stop(self):
         if self._t:
             self._stop.set()
             self._t.join()
+        timed = self.samples[self.timed_from:] if self.timed_from is not None else []
         return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_mhz_timed": statistics.median(timed) if timed else None,
                 "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
-                "samples": len(self.samples), "source": "nvml" if self.ok else "unavailable"}
+                "samples": len(self.samples), "samples_timed": len(timed),
+                "window": "warm-up and timed steps", "source": "nvml" if self.ok else "unavailable"}
 
 
 # ---------------------------------------------------------------------------
@@ -1176,21 +1184,25 @@ def main():
         workload; returns the fields of its JSON object."""
         wl = make(workload)
         stream = torch.cuda.current_stream()
+        # clocks: sampled from the first warm-up step to the end of the timed
+        # steps (a short timed region alone gets one or two NVML samples)
+        sampler = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
+                               else local_rank)
+        sampler.start()
         for i in range(args.warmup):
             wl.step(i)
         torch.cuda.synchronize()
         if jb.device_error() != 0:
+            sampler.stop()
             raise RuntimeError(f"device error during warm-up ({workload})")
 
         # ---------------- timed region (device) ----------------
         K = args.steps
         dom = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in range(K)]
-        sampler = ClockSampler(torch.cuda.current_device() if "CUDA_VISIBLE_DEVICES" not in os.environ
-                               else local_rank)
         barrier()
         torch.cuda.synchronize()
-        sampler.start()
+        sampler.mark_timed()
         t_begin = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
         t_begin.record(stream)
