@@ -101,6 +101,13 @@ def roofline(wl, achieved, peak, peak_kind, traffic):
                 "frac": round(achieved / NOMINAL_FP8_TFLOPS, 4),
                 "peak_kind": "nominal dense fp8 (datasheet; no measured fp8 figure)",
                 "traffic": traffic, "traffic_unit": "DRAM bytes per launch (ncu, profiles/)"}
+    if getattr(wl, "tf32x3", False):
+        p = peak / 2  # dense tf32 runs at half the bf16 rate per flop
+        return {"bound": "tensor (tf32)", "kernel": wl.dominant, "achieved": round(achieved, 2),
+                "peak": round(p, 1), "unit": "TFLOP/s", "frac": round(achieved / p, 4),
+                "peak_kind": f"{peak_kind} cuBLAS bf16 burst / 2 (tf32 dense rate); achieved = "
+                             "executed tf32 MMA flops (3 x 2MNK) per step",
+                "traffic": traffic, "traffic_unit": "DRAM bytes per launch (ncu, profiles/)"}
     fp32 = isinstance(wl, (AttentionF32, GemmF32))
     p = NOMINAL_FP32_TFLOPS if fp32 else peak
     return {"bound": "fp32_cuda_cores" if fp32 else "tensor", "kernel": wl.dominant,
@@ -117,7 +124,7 @@ def profiled_traffic(workload):
     name = {"gemm": "gemm_tc_c2", "attn": "attn_tc_c3", "attn_gqa": "attn_tc_c5",
             "mlp": "gemm_tc_c4", "attn_fp32": "attn_simt_c1", "softmax": "rows_softmax",
             "xent": "rows_xent", "int8": "gemm_s8_int8", "fp8": "gemm_f8_fp8",
-            "attn_bwd": "attn_bwd_c3", "gemm_f32": "gemm_simt_f32", "gelu_f32": "gelu_f32"}[workload]
+            "attn_bwd": "attn_bwd_c3", "gemm_f32": "gemm_tf32x3_f32", "gelu_f32": "gelu_f32"}[workload]
     path = os.path.join(HERE, "profiles", f"{name}.md")
     try:
         with open(path) as f:
@@ -189,7 +196,8 @@ def describe(workload, world, extra_l2=None, comm=None):
              "M_per_rank": 4096, "N": 32768, "global_M": 4096 * world, "sharding": "rows",
              "bytes_convention": "logits read + grad written + targets read"}
     elif workload == "gemm_f32":
-        c = {"workload": "fp32 GEMM + bias + GELU (tiledMatmulWithActivation's float* path)",
+        c = {"workload": "fp32 GEMM + bias + GELU (tiledMatmulWithActivation's float* path), "
+                         "3xTF32 on tensor cores (rel-L2 <= 1e-5 against the reference)",
              "M_per_rank": 2048, "N": 2048, "K": 2048, "sharding": "rows of M"}
     elif workload == "gelu_f32":
         c = {"workload": "fp32 GELU (fusedGelu)", "n_per_rank": 64 << 20,
@@ -841,10 +849,15 @@ class RowWise(Workload):
 
 class GemmF32(Workload):
     """The reference's float* GEMM path (tiledMatmulWithActivation with GELU,
-    fp32 in and out): the fp32 CUDA-core kernel its 1e-5 rel-L2 bar needs.
-    M = N = K = 2048 per rank."""
+    fp32 in and out) at its 1e-5 rel-L2 bar: 3xTF32 on tensor cores
+    (jules_gemm_f32_tc: operand split, then the tcgen05 pair GEMM on
+    kind::tf32 over K' = 3K).  M = N = K = 2048 per rank.  The exact fp32
+    CUDA-core kernel is timed beside it (cuda_core_exact)."""
     dtype = "f32"
-    dominant = "simt::gemm_kernel<float, float> (fp32 CUDA cores)"
+    dominant = ("split3_a/w_kernel + gemm_bf16_tc2_kernel<float> (tcgen05 kind::tf32, 3xTF32; "
+                "events bracket the split and the GEMM)")
+    tf32x3 = True
+    launches_per_step = 3  # two split kernels and the GEMM
 
     def __init__(self, jb, torch, rank, world, M=2048, N=2048, K=2048):
         self.jb, self.torch = jb, torch
@@ -857,17 +870,37 @@ class GemmF32(Workload):
         self.W = [(torch.rand((K, N), generator=g, device=dev) * 2 - 1) * s for _ in range(self.nsets)]
         self.b = torch.randn(N, generator=g, device=dev) * 0.02
         self.C = [torch.empty((M, N), device=dev) for _ in range(self.nsets)]
+        self.ws = torch.empty(jb.gemm_f32_tc_workspace_bytes(M, N, K), dtype=torch.uint8, device=dev)
         self.flops_per_step = 2.0 * M * N * K
-        self.flops_dominant = self.flops_per_step
+        # executed tf32 MMA work: three products over K
+        self.flops_dominant = 3 * self.flops_per_step
         self.config = {"l2": f"{self.nsets} rotating input sets ({self.nsets * per_set / 2**20:.0f} MiB > L2)"}
 
     def step(self, i, ev=None):
         k = i % self.nsets
         if ev:
             ev[0].record()
-        self.jb.gemm_bias_act(self.A[k], self.W[k], self.b, act="gelu", out=self.C[k])
+        self.jb.gemm_f32_tc(self.A[k], self.W[k], self.b, act="gelu", out=self.C[k], workspace=self.ws)
         if ev:
             ev[1].record()
+
+    def extra_measure(self):
+        """The exact fp32 CUDA-core GEMM on the same inputs (fp32 FMA
+        products), for comparison: TFLOP/s over 10 calls after 3."""
+        torch = self.torch
+        for i in range(3):
+            self.jb.gemm_bias_act(self.A[i % self.nsets], self.W[i % self.nsets], self.b, act="gelu",
+                                  out=self.C[i % self.nsets])
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(10):
+            self.jb.gemm_bias_act(self.A[i % self.nsets], self.W[i % self.nsets], self.b, act="gelu",
+                                  out=self.C[i % self.nsets])
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / 10
+        return {"kernel": "simt::gemm_kernel<float, float> (fp32 CUDA cores, exact products)",
+                "ms": round(ms, 4), "tflops": round(self.flops_per_step / (ms * 1e-3) / 1e12, 2)}
 
     def output(self, i):
         return self.C[i % self.nsets]
@@ -876,7 +909,8 @@ class GemmF32(Workload):
         jb = self.jb
         h_in = [self.A[0].cpu().pin_memory(), self.W[0].cpu().pin_memory()]
         h_out = [self.torch.empty_like(self.C[0], device="cpu").pin_memory()]
-        return h_in, h_out, lambda d, o: jb.gemm_bias_act(d[0], d[1], self.b, act="gelu", out=o[0])
+        return h_in, h_out, lambda d, o: jb.gemm_f32_tc(d[0], d[1], self.b, act="gelu", out=o[0],
+                                                        workspace=self.ws)
 
 
 class GeluF32(Workload):
@@ -1341,6 +1375,8 @@ def main():
             res["gather"] = gather
         if compute_only:
             res["compute_only"] = compute_only
+        if hasattr(wl, "extra_measure"):
+            res["cuda_core_exact"] = wl.extra_measure()
         if hasattr(wl, "release"):
             torch.cuda.synchronize()
             barrier()
@@ -1393,7 +1429,7 @@ def main():
                 "dtype": main_res["dtype"],
                 "data": "synthetic (seeded; config shapes and distributions)"}
         for k in ("config", "roofline", "pct_of_dense_bf16_peak_2250", "clocks", "e2e",
-                  "gpu_launches", "cpu_baseline", "gather", "compute_only"):
+                  "gpu_launches", "cpu_baseline", "gather", "compute_only", "cuda_core_exact"):
             if k in main_res:
                 line[k] = main_res[k]
         if attn_res:

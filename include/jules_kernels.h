@@ -108,6 +108,26 @@ int jules_gemm_bias_act(const void* A, const void* W, const float* bias, const v
                         int out_dtype, void* stream);
 
 /*
+ * fp32 C = act(A . W + bias) on tensor cores with fp32-level accuracy
+ * (3xTF32): each operand is split into tf32 hi + lo parts (one HBM pass into
+ * the caller's workspace) and the tcgen05 pair GEMM (kind::tf32, fp32
+ * accumulation in TMEM) computes hiA.hiW + hiA.loW + loA.hiW, dropping only
+ * loA.loW (relative size <= 2^-22).  Activations in the accurate fp32 forms.
+ *   A [M,K], W [K,N], C [M,N], bias [N] (nullable), all fp32, row-major.
+ * Tensor cores for M >= 256, N >= 256, N % 8 == 0, K % 4 == 0 and 16-byte
+ * aligned buffers; other shapes run the fp32 CUDA-core GEMM (no workspace
+ * used).  workspace: jules_gemm_f32_tc_workspace_bytes(M, N, K) bytes of
+ * device memory, 16-byte aligned (JULES_ERR_WORKSPACE when smaller).
+ * Replaces tiledMatmulWithActivation (FusedKernels.h:378-458) and, through
+ * the C++ API, blasMatmul / fusedMLPForward's GEMMs (:633-644, :650-760) on
+ * the reference's float* path.
+ */
+size_t jules_gemm_f32_tc_workspace_bytes(int64_t M, int64_t N, int64_t K);
+int jules_gemm_f32_tc(const float* A, const float* W, const float* bias, float* C, int64_t M,
+                      int64_t N, int64_t K, int act, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/*
  * Row-major fp32 SGEMM, C = alpha op(A) op(B) + beta C, with op = transpose
  * when transA / transB != 0; lda/ldb/ldc in elements.  The cblas_sgemm
  * contract the reference relies on (FusedKernels.h:633-644,

@@ -38,6 +38,9 @@ _SIGNATURES = {
     "jules_status_string": ([_c_int], ctypes.c_char_p),
     "jules_device_error": ([ctypes.POINTER(ctypes.c_uint32), _c_int], _c_int),
     "jules_selftest_bounded_wait": ([ctypes.c_uint64, _c_vp], _c_int),
+    "jules_gemm_f32_tc_workspace_bytes": ([_c_i64, _c_i64, _c_i64], ctypes.c_size_t),
+    "jules_gemm_f32_tc": ([_c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_vp,
+                           ctypes.c_size_t, _c_vp], _c_int),
     "jules_gemm_bias_act": ([_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_int,
                              _c_int, _c_int, _c_vp], _c_int),
     "jules_sgemm": ([_c_int, _c_int, _c_i64, _c_i64, _c_i64, _c_f, _c_vp, _c_i64, _c_vp, _c_i64,
@@ -192,6 +195,36 @@ def gemm_bias_act(A, W, bias=None, residual=None, act="none", out=None, out_dtyp
                                    _dtype_code(A), _dtype_code(out), _stream(stream))
     _check(rc, "jules_gemm_bias_act")
     return out
+
+
+def gemm_f32_tc(A, W, bias=None, act="none", out=None, workspace=None, stream=None):
+    """fp32 C = act(A @ W + bias) on tensor cores with fp32-level accuracy
+    (3xTF32, jules_gemm_f32_tc).  workspace: a uint8 CUDA tensor of at least
+    gemm_f32_tc_workspace_bytes(M, N, K) bytes (allocated here if None)."""
+    import torch
+    _dense(A, "A"), _dense(W, "W")
+    M, K = A.shape
+    K2, N = W.shape
+    if K2 != K or A.dtype != torch.float32 or W.dtype != torch.float32:
+        raise ValueError("A [M,K] and W [K,N] must be fp32")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=A.device)
+    if bias is not None:
+        _dense(bias, "bias")
+        if bias.dtype != torch.float32 or bias.numel() != N:
+            raise ValueError("bias must be fp32 with N elements")
+    need = gemm_f32_tc_workspace_bytes(M, N, K)
+    if workspace is None:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=A.device)
+    rc = lib().jules_gemm_f32_tc(_ptr(A), _ptr(W), _ptr(bias), _ptr(out), M, N, K,
+                                 ACT[act] if isinstance(act, str) else int(act), _ptr(workspace),
+                                 workspace.numel() * workspace.element_size(), _stream(stream))
+    _check(rc, "jules_gemm_f32_tc")
+    return out
+
+
+def gemm_f32_tc_workspace_bytes(M, N, K):
+    return int(lib().jules_gemm_f32_tc_workspace_bytes(M, N, K))
 
 
 def sgemm(A, B, C=None, alpha=1.0, beta=0.0, transA=False, transB=False, stream=None):

@@ -156,8 +156,9 @@ constexpr int kGemmStages = 4;
 
 template <typename TIn>
 constexpr CUtensorMapDataType tmap_dtype() {
-  return std::is_same<TIn, __half>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                                          : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  return std::is_same<TIn, __half>::value   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+         : std::is_same<TIn, float>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                           : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
 }
 
 // TIn: __nv_bfloat16 or __half operands (and residual); TOut: TIn or float.
@@ -201,16 +202,17 @@ int gemm_tc2(const TIn* A, const TIn* W, const float* bias,
   int dev;
   if (int rc = current_device(&dev)) return rc;
   CUtensorMap ta, tw;
+  constexpr uint32_t kE = sizeof(TIn), kRow = 128 / kE;  // elements per 128-byte row
   {
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
-    const uint64_t strides[1] = {(uint64_t)K * 2};
-    const uint32_t box[2] = {64, 128};
+    const uint64_t strides[1] = {(uint64_t)K * kE};
+    const uint32_t box[2] = {kRow, 128};
     if (int rc = make_tmap_bf16(&ta, A, 2, dims, strides, box, tmap_dtype<TIn>())) return rc;
   }
   {
     const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
-    const uint64_t strides[1] = {(uint64_t)N * 2};
-    const uint32_t box[2] = {64, 64};
+    const uint64_t strides[1] = {(uint64_t)N * kE};
+    const uint32_t box[2] = {kRow, kRow};
     if (int rc = make_tmap_bf16(&tw, W, 2, dims, strides, box, tmap_dtype<TIn>())) return rc;
   }
   constexpr int kStages = TN == 256 ? 6 : 8;
@@ -824,6 +826,48 @@ int jules_gemm_bias_act(const void* A, const void* W, const float* bias, const v
   if (in_bf) return gemm_simt<__nv_bfloat16, float>(A, W, bias, residual, C, M, N, K, act, 1, st);
   if (out_bf) return gemm_simt<float, __nv_bfloat16>(A, W, bias, residual, C, M, N, K, act, 0, st);
   return gemm_simt<float, float>(A, W, bias, residual, C, M, N, K, act, 1, st);
+}
+
+size_t jules_gemm_f32_tc_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  return align256((size_t)M * 3 * (size_t)K * 4) + (size_t)3 * K * N * 4;
+}
+
+int jules_gemm_f32_tc(const float* A, const float* W, const float* bias, float* C, int64_t M,
+                      int64_t N, int64_t K, int act, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  if (!A || !W || !C) return fail(JULES_ERR_ARG, "gemm_f32_tc: NULL A, W or C");
+  if (M < 0 || N <= 0 || K <= 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+    return fail(JULES_ERR_SHAPE, "gemm_f32_tc: M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
+  if (act < JULES_ACT_NONE || act > JULES_ACT_GELU) return fail(JULES_ERR_ARG, "gemm_f32_tc: act=%d", act);
+  if (M == 0) return ok();
+  const bool tc = M >= 256 && N >= 256 && N % 8 == 0 && K % 4 == 0 && 3 * K <= INT32_MAX &&
+                  aligned16(A) && aligned16(W) && aligned16(C) && (!bias || aligned16(bias));
+  if (!tc)  // the fp32 CUDA-core GEMM (exact fp32 products)
+    return jules_gemm_bias_act(A, W, bias, nullptr, C, M, N, K, act, JULES_DTYPE_F32, JULES_DTYPE_F32, stream);
+  const size_t need = jules_gemm_f32_tc_workspace_bytes(M, N, K);
+  if (!workspace || workspace_bytes < need)
+    return fail(JULES_ERR_WORKSPACE, "gemm_f32_tc: workspace %zu bytes, need %zu", workspace_bytes, need);
+  if (!aligned16(workspace)) return fail(JULES_ERR_ALIGN, "gemm_f32_tc: workspace not 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int dev;
+  if (int rc = current_device(&dev)) return rc;
+  float* A3 = static_cast<float*>(workspace);
+  float* W3 = reinterpret_cast<float*>(static_cast<char*>(workspace) + align256((size_t)M * 3 * K * 4));
+  const int64_t na = M * (K / 4), nw = K * (N / 4);
+  const int cap = device_sms(dev) * 8;
+  auto blocks = [cap](int64_t n) { return (int)std::min<int64_t>((n + 255) / 256, cap); };
+  jb::simt::split3_a_kernel<<<blocks(na), 256, 0, st>>>(reinterpret_cast<const float4*>(A),
+                                                        reinterpret_cast<float4*>(A3), M, K / 4);
+  if (int rc = check_launch("split3_a_kernel launch")) return rc;
+  jb::simt::split3_w_kernel<<<blocks(nw), 256, 0, st>>>(reinterpret_cast<const float4*>(W),
+                                                        reinterpret_cast<float4*>(W3), nw);
+  if (int rc = check_launch("split3_w_kernel launch")) return rc;
+  jb::gemm::OutDest<float> out{};
+  out.c[0] = C;
+  out.n = 1;
+  return gemm_tc2<256>(static_cast<const float*>(A3), static_cast<const float*>(W3), bias,
+                       static_cast<const float*>(nullptr), out, M, N, 3 * K, act, st);
 }
 
 int jules_sgemm(int transA, int transB, int64_t M, int64_t N, int64_t K, float alpha,

@@ -42,6 +42,18 @@ __device__ __forceinline__ float act_fast(float v, int act) {
   }
 }
 
+// Accurate activations (fp32 outputs): the scalar forms of
+// include/jules/Kernel/FusedKernels.h:425-428, 616.
+__device__ __forceinline__ float act_exact(float v, int act) {
+  switch (act) {
+    case 1: return fmaxf(v, 0.0f);
+    case 2: return 1.0f / (1.0f + expf(-v));
+    case 3: return tanhf(v);
+    case 4: return 0.5f * v * (1.0f + tanhf(0.7978845608f * (v + 0.044715f * v * v * v)));
+    default: return v;
+  }
+}
+
 namespace gemm {
 
 constexpr int BM = 128;
@@ -401,6 +413,13 @@ __global__ void __launch_bounds__(kThreads2, 1)
   constexpr int TM = 256;
   constexpr uint32_t kTmemCols = 2 * TN;  // two accumulators
   using S = Smem2<STAGES, TN>;
+  // Operand bytes: 2 (bf16 / f16, kind::f16) or 4 (fp32 read as tf32,
+  // kind::tf32).  A k-block is one 128-byte swizzle row of K (BKe elements);
+  // a W box is one 128-byte row of N (also BKe elements); the stage sizes in
+  // bytes are the same for both.
+  constexpr int kE = (int)sizeof(TIn);
+  constexpr int BKe = 128 / kE;
+  static_assert(S::kABytes == 128 * BKe * kE && S::kBBytes == BKe * (TN / 2) * kE, "stage layout");
   extern __shared__ uint8_t smem_raw[];
   S& s = *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -412,7 +431,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
   const int num_pairs = gridDim.x >> 1;
   const int num_m = (M + TM - 1) / TM;
   const int num_n = (N + TN - 1) / TN;
-  const int num_k = (K + BK - 1) / BK;
+  const int num_k = (K + BKe - 1) / BKe;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -451,13 +470,13 @@ __global__ void __launch_bounds__(kThreads2, 1)
         const int cta_cols = pu.cols / 2;  // this CTA's share of the unit's W columns
         const int m0 = mi * TM + (int)rank * 128;
         const int n0 = ni * TN + pu.n_off + (int)rank * cta_cols;
-        const uint32_t tx = 2u * (uint32_t)(S::kABytes + BK * cta_cols * 2);
+        const uint32_t tx = 2u * (uint32_t)(S::kABytes + BKe * cta_cols * kE);
         for (int kb = 0; kb < num_k; ++kb) {
           if (!mbar_wait(&s.empty[stage], phase ^ 1u, 41, abort_flag)) { ok = false; break; }
           if (leader) mbar_arrive_expect_tx(&s.full[stage], tx);
-          tma_load_2d_pair(s.a[stage], &tmA, &s.full[stage], kb * BK, m0);
-          for (int j = 0; j < cta_cols / 64; ++j)
-            tma_load_2d_pair(s.b[stage] + j * (BK * 64 * 2), &tmW, &s.full[stage], n0 + j * 64, kb * BK);
+          tma_load_2d_pair(s.a[stage], &tmA, &s.full[stage], kb * BKe, m0);
+          for (int j = 0; j < cta_cols / BKe; ++j)
+            tma_load_2d_pair(s.b[stage] + j * (BKe * 128), &tmW, &s.full[stage], n0 + j * BKe, kb * BKe);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
       }
@@ -486,14 +505,17 @@ __global__ void __launch_bounds__(kThreads2, 1)
           if (!mbar_wait(&s.full[stage], phase, 43, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint64_t a0 = sdesc_sw128(smem_u32(s.a[stage]), 16, 1024);
-          const uint64_t b0 = sdesc_sw128(smem_u32(s.b[stage]), BK * 64 * 2, 1024);
+          const uint64_t b0 = sdesc_sw128(smem_u32(s.b[stage]), BKe * 128, 1024);
           uint64_t ad[4], bd[4];
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            ad[kk] = a0 + kk * 2;    // +32 bytes inside the swizzle row
-            bd[kk] = b0 + kk * 128;  // +16 K rows of 128 bytes
+            ad[kk] = a0 + kk * 2;           // +32 bytes (one MMA's K) inside the swizzle row
+            bd[kk] = b0 + kk * (256 / kE);  // +32/kE K rows of 128 bytes
           }
-          umma4_pair_ss(d_tmem, ad, bd, kb > 0 ? 1u : 0u, idesc);
+          if constexpr (kE == 4)
+            umma4_pair_ss_tf32(d_tmem, ad, bd, kb > 0 ? 1u : 0u, idesc);
+          else
+            umma4_pair_ss(d_tmem, ad, bd, kb > 0 ? 1u : 0u, idesc);
           umma_commit_pair(empty0 + stage * 8);
           umma_commit_pair(empty0_peer + stage * 8);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -571,19 +593,26 @@ __global__ void __launch_bounds__(kThreads2, 1)
                 }
               }
             }
+            if constexpr (kE == 4) {  // fp32 operands (3xTF32): fp32-accurate activations
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = act_fast(v[j], act);
-            if (rrow) {
+              for (int j = 0; j < 32; ++j) v[j] = act_exact(v[j], act);
+            } else {
 #pragma unroll
-              for (int j = 0; j < 32; j += 8) {
-                if (c0 + j < N) {
-                  const uint4 rv = *reinterpret_cast<const uint4*>(rrow + c0 + j);
-                  const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+              for (int j = 0; j < 32; ++j) v[j] = act_fast(v[j], act);
+            }
+            if constexpr (kE == 2) {  // residual: 16-bit operands only
+              if (rrow) {
 #pragma unroll
-                  for (int q = 0; q < 4; ++q) {
-                    const float2 f = unpack2<TIn>(rw[q]);
-                    v[j + 2 * q] += f.x;
-                    v[j + 2 * q + 1] += f.y;
+                for (int j = 0; j < 32; j += 8) {
+                  if (c0 + j < N) {
+                    const uint4 rv = *reinterpret_cast<const uint4*>(rrow + c0 + j);
+                    const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                      const float2 f = unpack2<TIn>(rw[q]);
+                      v[j + 2 * q] += f.x;
+                      v[j + 2 * q + 1] += f.y;
+                    }
                   }
                 }
               }

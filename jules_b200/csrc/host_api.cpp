@@ -80,22 +80,24 @@ void d2h(void* h, const void* d, size_t n) {
   if (n) check(cudaMemcpy(h, d, n, cudaMemcpyDeviceToHost), "cudaMemcpy D2H");
 }
 
-// act(X.W + bias), host pointers, fp32.
+// act(X.W + bias), host pointers, fp32: the 3xTF32 tensor-core GEMM (its
+// operand-split workspace in the staging area) where the shape allows, the
+// fp32 CUDA-core GEMM otherwise.
 void gemm_host(const float* X, const float* W, const float* bias, float* out, int M, int K, int N,
                int act) {
   if (M <= 0 || N <= 0 || K <= 0) return;
   const size_t bx = (size_t)M * K * 4, bw = (size_t)K * N * 4, bb = bias ? (size_t)N * 4 : 0,
-               bo = (size_t)M * N * 4;
-  const size_t sizes[4] = {bx, bw, bb ? bb : 4, bo};
-  char* d[4];
-  staging().reserve(sizes, 4, d);
+               bo = (size_t)M * N * 4, bws = jules_gemm_f32_tc_workspace_bytes(M, N, K);
+  const size_t sizes[5] = {bx, bw, bb ? bb : 4, bo, bws};
+  char* d[5];
+  staging().reserve(sizes, 5, d);
   h2d(d[0], X, bx);
   h2d(d[1], W, bw);
   if (bias) h2d(d[2], bias, bb);
-  check_status(jules_gemm_bias_act(d[0], d[1], bias ? reinterpret_cast<float*>(d[2]) : nullptr,
-                                   nullptr, d[3], M, N, K, act, JULES_DTYPE_F32, JULES_DTYPE_F32,
-                                   nullptr),
-               "jules_gemm_bias_act");
+  check_status(jules_gemm_f32_tc(reinterpret_cast<float*>(d[0]), reinterpret_cast<float*>(d[1]),
+                                 bias ? reinterpret_cast<float*>(d[2]) : nullptr,
+                                 reinterpret_cast<float*>(d[3]), M, N, K, act, d[4], bws, nullptr),
+               "jules_gemm_f32_tc");
   d2h(out, d[3], bo);
 }
 
@@ -300,17 +302,27 @@ InterleavedMLPResult interleavedMLPForwardBackward(const float* X, const float* 
 void blasMatmul(const float* A, const float* B, float* C, int M, int N, int K, float alpha,
                 float beta, bool transA, bool transB) {
   if (M <= 0 || N <= 0) return;
-  const size_t ba = (size_t)M * K * 4, bb = (size_t)K * N * 4, bc = (size_t)M * N * 4;
-  const size_t sizes[3] = {ba ? ba : 4, bb ? bb : 4, bc};
-  char* d[3];
-  staging().reserve(sizes, 3, d);
+  // The plain product (no transposes, alpha 1, beta 0) runs the 3xTF32
+  // tensor-core GEMM; everything else the fp32 SGEMM kernel.
+  const bool plain = !transA && !transB && alpha == 1.0f && beta == 0.0f && K > 0;
+  const size_t ba = (size_t)M * K * 4, bb = (size_t)K * N * 4, bc = (size_t)M * N * 4,
+               bws = plain ? jules_gemm_f32_tc_workspace_bytes(M, N, K) : 0;
+  const size_t sizes[4] = {ba ? ba : 4, bb ? bb : 4, bc, bws ? bws : 4};
+  char* d[4];
+  staging().reserve(sizes, 4, d);
   h2d(d[0], A, ba);
   h2d(d[1], B, bb);
   if (beta != 0.0f) h2d(d[2], C, bc);
-  check_status(jules_sgemm(transA, transB, M, N, K, alpha, reinterpret_cast<float*>(d[0]),
-                           transA ? M : K, reinterpret_cast<float*>(d[1]), transB ? K : N, beta,
-                           reinterpret_cast<float*>(d[2]), N, nullptr),
-               "jules_sgemm");
+  if (plain)
+    check_status(jules_gemm_f32_tc(reinterpret_cast<float*>(d[0]), reinterpret_cast<float*>(d[1]),
+                                   nullptr, reinterpret_cast<float*>(d[2]), M, N, K, JULES_ACT_NONE,
+                                   d[3], bws, nullptr),
+                 "jules_gemm_f32_tc");
+  else
+    check_status(jules_sgemm(transA, transB, M, N, K, alpha, reinterpret_cast<float*>(d[0]),
+                             transA ? M : K, reinterpret_cast<float*>(d[1]), transB ? K : N, beta,
+                             reinterpret_cast<float*>(d[2]), N, nullptr),
+                 "jules_sgemm");
   d2h(C, d[2], bc);
 }
 
@@ -333,11 +345,16 @@ void fusedMLPForward(float* output, const float* X, const MLPParams& p, Executio
   h2d(db1, p.b1, (size_t)N1 * 4);
   h2d(dW2, p.W2, (size_t)N1 * N2 * 4);
   h2d(db2, p.b2, (size_t)N2 * 4);
-  check_status(jules_gemm_bias_act(dX, dW1, db1, nullptr, dH, M, N1, K1, JULES_ACT_RELU,
-                                   JULES_DTYPE_F32, JULES_DTYPE_F32, nullptr),
+  // The GEMMs' operand-split workspace lives in the staging area, not the
+  // caller's arena (which is sized for the reference's own buffers).
+  const size_t ws1 = jules_gemm_f32_tc_workspace_bytes(M, N1, K1),
+               ws2 = jules_gemm_f32_tc_workspace_bytes(M, N2, N1);
+  const size_t wsb[1] = {ws1 > ws2 ? ws1 : ws2};
+  char* ws[1];
+  staging().reserve(wsb, 1, ws);
+  check_status(jules_gemm_f32_tc(dX, dW1, db1, dH, M, N1, K1, JULES_ACT_RELU, ws[0], wsb[0], nullptr),
                "mlp gemm1");
-  check_status(jules_gemm_bias_act(dH, dW2, db2, nullptr, dO, M, N2, N1, JULES_ACT_NONE,
-                                   JULES_DTYPE_F32, JULES_DTYPE_F32, nullptr),
+  check_status(jules_gemm_f32_tc(dH, dW2, db2, dO, M, N2, N1, JULES_ACT_NONE, ws[0], wsb[0], nullptr),
                "mlp gemm2");
   d2h(output, dO, (size_t)M * N2 * 4);
   arena.reset();

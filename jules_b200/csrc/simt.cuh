@@ -5,7 +5,7 @@
 // All are GPU kernels; none falls back to the host.
 #pragma once
 
-#include "gemm_tc.cuh"  // act_fast
+#include "gemm_tc.cuh"  // act_fast, act_exact
 #include "sm100.cuh"
 
 namespace jb {
@@ -32,17 +32,6 @@ __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(
 template <>
 __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
 
-// Accurate activations (fp32 outputs): the scalar forms of
-// include/jules/Kernel/FusedKernels.h:425-428, 616.
-__device__ __forceinline__ float act_exact(float v, int act) {
-  switch (act) {
-    case 1: return fmaxf(v, 0.0f);
-    case 2: return 1.0f / (1.0f + expf(-v));
-    case 3: return tanhf(v);
-    case 4: return 0.5f * v * (1.0f + tanhf(0.7978845608f * (v + 0.044715f * v * v * v)));
-    default: return v;
-  }
-}
 
 // ---------------------------------------------------------------------------
 // GEMM: C = act(A.W + bias) (+ residual).  128x128 block tile, 8x8 per
@@ -759,6 +748,56 @@ __global__ void gelu_kernel(const T* __restrict__ in, T* __restrict__ out, int64
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     out[i] = from_f32<T>(act_exact(to_f32(in[i]), 4));
+}
+
+// ---------------------------------------------------------------------------
+// 3xTF32 operand split for the fp32 GEMM on tensor cores.  Each fp32 x is
+// hi + lo + r with hi = tf32(x), lo = tf32(x - hi) (x - hi is exact in fp32)
+// and |r| <= 2^-22 |x|; the tf32 pair GEMM then runs over K' = 3K
+//   A [M,K] -> A3 [M,3K] = [hi | hi | lo]
+//   W [K,N] -> W3 [3K,N] = [hi ; lo ; hi]
+// so that A3 . W3 = hiA hiW + hiA loW + loA hiW, which drops only loA loW
+// (<= 2^-22 |a w|).  Four elements per thread (K % 4 == 0 for A, N % 4 == 0
+// for W, 16-byte aligned buffers).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+  hi = to_tf32(x);
+  lo = to_tf32(x - hi);
+}
+
+__device__ __forceinline__ void split_tf32x4(const float4& x, float4& hi, float4& lo) {
+  split_tf32(x.x, hi.x, lo.x);
+  split_tf32(x.y, hi.y, lo.y);
+  split_tf32(x.z, hi.z, lo.z);
+  split_tf32(x.w, hi.w, lo.w);
+}
+
+// rows x k4 float4s of A -> A3 (row stride 3 k4 float4s).
+__global__ void split3_a_kernel(const float4* __restrict__ A, float4* __restrict__ A3, int64_t rows,
+                                int64_t k4) {
+  const int64_t n = rows * k4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / k4, c = i - r * k4;
+    float4 hi, lo;
+    split_tf32x4(A[i], hi, lo);
+    float4* row = A3 + r * 3 * k4;
+    row[c] = hi;
+    row[k4 + c] = hi;
+    row[2 * k4 + c] = lo;
+  }
+}
+
+// K x n4 float4s of W -> W3 = three K-row blocks (hi, lo, hi).
+__global__ void split3_w_kernel(const float4* __restrict__ W, float4* __restrict__ W3, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    float4 hi, lo;
+    split_tf32x4(W[i], hi, lo);
+    W3[i] = hi;
+    W3[n + i] = lo;
+    W3[2 * n + i] = hi;
+  }
 }
 
 }  // namespace simt

@@ -130,7 +130,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
 // ---------------------------------------------------------------------------
 // TMA (tiled, no cluster features).  Coordinates are element indices,
 // innermost first.  The innermost coordinate times the element size must be
-// a multiple of 16 bytes; callers only pass multiples of 64 elements.
+// a multiple of 16 bytes; callers only pass multiples of 128 bytes.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int x, int y) {
@@ -328,6 +328,22 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
 
 #define JB_MMA2_SS(ai, bi, pr) \
   "tcgen05.mma.cta_group::2.kind::f16 [%0], %" #ai ", %" #bi ", %10, " pr ";\n\t"
+#define JB_MMA2_SS_TF32(ai, bi, pr) \
+  "tcgen05.mma.cta_group::2.kind::tf32 [%0], %" #ai ", %" #bi ", %10, " pr ";\n\t"
+// Four K=8 steps of the pair MMA on tf32 operands: D (+)= A[smem] * B[smem].
+__device__ __forceinline__ void umma4_pair_ss_tf32(uint32_t d_tmem, const uint64_t (&a)[4],
+                                                   const uint64_t (&b)[4], uint32_t acc_first,
+                                                   uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %9, 0;\n\t"
+      "setp.eq.b32 q, %9, %9;\n\t"
+      JB_MMA2_SS_TF32(1, 5, "p") JB_MMA2_SS_TF32(2, 6, "q") JB_MMA2_SS_TF32(3, 7, "q")
+      JB_MMA2_SS_TF32(4, 8, "q")
+      "}" ::"r"(d_tmem), "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(b[0]), "l"(b[1]),
+      "l"(b[2]), "l"(b[3]), "r"(acc_first), "r"(idesc)
+      : "memory");
+}
 // Four K=16 steps of the pair MMA: D (+)= A[smem] * B[smem].
 __device__ __forceinline__ void umma4_pair_ss(uint32_t d_tmem, const uint64_t (&a)[4],
                                               const uint64_t (&b)[4], uint32_t acc_first,
@@ -368,14 +384,24 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn, b
          ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
-// kind::f16 instruction descriptor for A and B of one 16-bit type (f16 or
-// bf16; the two operands always share it): the A/B format fields are 0 for
-// f16, 1 for bf16.
+// Instruction descriptor for A and B of one type (the two operands always
+// share it): kind::f16 with format 0 for f16, 1 for bf16; kind::tf32 (fp32
+// operands read as tf32) with format 2.
 template <typename T>
 __host__ __device__ constexpr uint32_t idesc_f16kind(int M, int N, bool a_mn, bool b_mn) {
   return std::is_same<T, __half>::value
              ? (idesc_bf16_f32(M, N, a_mn, b_mn) & ~((7u << 7) | (7u << 10)))
+         : std::is_same<T, float>::value
+             ? ((idesc_bf16_f32(M, N, a_mn, b_mn) & ~((7u << 7) | (7u << 10))) | (2u << 7) | (2u << 10))
              : idesc_bf16_f32(M, N, a_mn, b_mn);
+}
+
+// fp32 -> tf32 (round to nearest, ties away from zero): the low 13 mantissa
+// bits of the result are zero.
+__device__ __forceinline__ float to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
 }
 
 // Shared-memory matrix descriptor for a 128-byte-swizzled operand.

@@ -63,6 +63,17 @@ int main(int argc, char** argv) {
   save(d + "/out_relu.bin", C);
   blasMatmul(A.data(), W.data(), C.data(), M, N, Kd);
   save(d + "/out_blas.bin", C);
+  // [320,200]x[200,264]: M, N >= 256, the 3xTF32 tensor-core path
+  {
+    const int Mt = 320, Nt = 264;
+    auto At = load(d + "/in_a_tc.bin", Mt * Kd), Wt = load(d + "/in_w_tc.bin", Kd * Nt);
+    std::vector<float> Ct(Mt * Nt);
+    TileConfig cfg_t = planner.getTileConfig(Mt, Nt, Kd);
+    tiledMatmulWithActivation(At.data(), Wt.data(), Ct.data(), Mt, Nt, Kd, cfg_t, ActivationType::Gelu);
+    save(d + "/out_tiled_gelu_tc.bin", Ct);
+    blasMatmul(At.data(), Wt.data(), Ct.data(), Mt, Nt, Kd);
+    save(d + "/out_blas_tc.bin", Ct);
+  }
   // layernorm [96,200] and gelu
   std::vector<float> g(Kd, 1.0f), be(Kd, 0.0f), L(M * Kd);
   fusedLayerNorm(L.data(), A.data(), g.data(), be.data(), M, Kd);

@@ -41,14 +41,19 @@ def test_drop_in_matches_reference(tmp_path, jb, ref):
     A9 = g.integers(-128, 128, (256, 256)).astype(np.int8)
     B9 = g.integers(-128, 128, (256, 512)).astype(np.int8)
     b9 = g.standard_normal(512).astype(np.float32)
+    A_tc = g.uniform(-1, 1, (320, 200)).astype(np.float32)
+    W_tc = g.uniform(-1, 1, (200, 264)).astype(np.float32)
     for name, arr in dict(q=Q, k=K, v=V, a=A, w=W, bias=bias, w2=W2, b2=b2, a8=A8, b8=B8, a9=A9,
-                          b9=B9, b9bias=b9).items():
+                          b9=B9, b9bias=b9, a_tc=A_tc, w_tc=W_tc).items():
         arr.tofile(os.path.join(d, f"in_{name}.bin"))
     subprocess.run([exe, d], check=True)
     out = lambda n, shape: np.fromfile(os.path.join(d, f"out_{n}.bin"), np.float32).reshape(shape)
     assert rel_l2(out("flash", Q.shape), ref.flash_attention(Q, K, V)) <= F32_REL_L2
     assert rel_l2(out("attention", Q.shape), ref.attention(Q, K, V)) <= F32_REL_L2
     assert rel_l2(out("tiled_gelu", (96, 136)), ref.tiled_matmul_act(A, W, "gelu")) <= F32_REL_L2
+    # M, N >= 256: the float* API on the 3xTF32 tensor-core GEMM
+    assert rel_l2(out("tiled_gelu_tc", (320, 264)), ref.tiled_matmul_act(A_tc, W_tc, "gelu")) <= F32_REL_L2
+    assert rel_l2(out("blas_tc", (320, 264)), ref.blas_matmul(A_tc, W_tc)) <= F32_REL_L2
     assert rel_l2(out("bias_relu", (96, 136)), ref.fused_matmul_bias_relu(A, W, bias)) <= F32_REL_L2
     assert rel_l2(out("standard", Q.shape), ref.standard_attention(Q, K, V)) <= F32_REL_L2
     # fusedMatmulRelu takes (M, K, N); a swapped order would not match (M, K, N all differ)

@@ -127,6 +127,68 @@ def test_gemm_fp32_vs_reference(jb, ref, M, N, K, act):
     assert rel_l2(to_np(got), want) <= F32_REL_L2
 
 
+@pytest.mark.parametrize("M,N,K", [(256, 256, 256), (512, 768, 1000), (300, 264, 4096)])
+@pytest.mark.parametrize("act", ["none", "gelu"])
+def test_gemm_f32_tc_vs_reference(jb, ref, M, N, K, act):
+    """3xTF32 tensor-core fp32 GEMM vs the reference's own tiled kernel, at
+    the fp32 bar (rel-L2 1e-5); ragged K (3K not a multiple of the 32-wide
+    k-block) and partial tiles included."""
+    import torch
+    g = np.random.default_rng(M + 3 * N + K)
+    A = g.uniform(-1, 1, (M, K)).astype(np.float32)
+    W = g.uniform(-1, 1, (K, N)).astype(np.float32)
+    want = ref.tiled_matmul_act(A, W, act)
+    got = jb.gemm_f32_tc(torch.from_numpy(A).cuda(), torch.from_numpy(W).cuda(), act=act)
+    torch.cuda.synchronize()
+    assert jb.device_error() == 0
+    assert rel_l2(to_np(got), want) <= F32_REL_L2
+    # against float64: fp32 accumulation over 3K/8 MMA steps costs ~sqrt(3K/8)
+    # 2^-24 (2.3e-6 at K = 4096); tf32 alone (~5e-4) would fail this by far
+    exact = A.astype(np.float64) @ W.astype(np.float64)
+    if act == "none":
+        assert rel_l2(to_np(got), exact) <= 5e-6
+
+
+def test_gemm_f32_tc_bias_and_tail_split(jb):
+    """Bias + GELU at a shape whose last round runs as half-width units (80
+    tiles on 74 pairs), vs float64."""
+    import torch
+    g = np.random.default_rng(17)
+    M, N, K = 2560, 2048, 96
+    A = g.standard_normal((M, K)).astype(np.float32)
+    W = (g.standard_normal((K, N)) / 8).astype(np.float32)
+    b = g.standard_normal(N).astype(np.float32)
+    got = to_np(jb.gemm_f32_tc(torch.from_numpy(A).cuda(), torch.from_numpy(W).cuda(),
+                               torch.from_numpy(b).cuda(), act="gelu"))
+    z = A.astype(np.float64) @ W + b
+    want = 0.5 * z * (1 + np.tanh(0.7978845608 * (z + 0.044715 * z ** 3)))
+    assert rel_l2(got, want) <= 2e-6
+    assert np.abs(got - want).max() <= 1e-4
+
+
+def test_gemm_f32_tc_fallback_and_workspace(jb):
+    """Shapes the tensor cores do not take (N % 8 != 0, M < 256) run the fp32
+    CUDA-core GEMM; a workspace below the size query is refused."""
+    import torch
+    g = np.random.default_rng(3)
+    for (M, N, K) in ((300, 260, 64), (100, 512, 64)):
+        A = g.uniform(-1, 1, (M, K)).astype(np.float32)
+        W = g.uniform(-1, 1, (K, N)).astype(np.float32)
+        got = jb.gemm_f32_tc(torch.from_numpy(A).cuda(), torch.from_numpy(W).cuda(),
+                             workspace=torch.empty(16, dtype=torch.uint8, device="cuda"))
+        assert rel_l2(to_np(got), A.astype(np.float64) @ W) <= F32_REL_L2
+    M, N, K = 512, 512, 128
+    need = jb.gemm_f32_tc_workspace_bytes(M, N, K)
+    assert need == ((M * 3 * K * 4 + 255) // 256) * 256 + 3 * K * N * 4
+    A = torch.zeros((M, K), device="cuda")
+    W = torch.zeros((K, N), device="cuda")
+    C = torch.empty((M, N), device="cuda")
+    ws = torch.empty(need - 256, dtype=torch.uint8, device="cuda")
+    rc = jb.lib().jules_gemm_f32_tc(jb._ptr(A), jb._ptr(W), None, jb._ptr(C), M, N, K, 0,
+                                    jb._ptr(ws), ws.numel(), None)
+    assert rc == 8  # JULES_ERR_WORKSPACE
+
+
 def test_gemm_fp32_bias_relu_vs_reference(jb, ref):
     import torch
     g = np.random.default_rng(11)
