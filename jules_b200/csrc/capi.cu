@@ -198,18 +198,27 @@ template <int TN, typename TIn, typename TOut>
 int gemm_tc2(const TIn* A, const TIn* W, const float* bias,
              const TIn* res, const jb::gemm::OutDest<TOut>& out, int64_t M, int64_t N,
              int64_t K, int act, cudaStream_t st, const float2* ln_stats = nullptr,
-             const float* ln_colsum = nullptr) {
+             const float* ln_colsum = nullptr, int64_t ld_a = 0, int64_t ld_w = 0) {
+  // ld_a: A's row stride in elements (0: K).  ld_w: the transposed fp32 W's
+  // row stride (0: K); 16-bit W is [K,N] with row stride N.
+  if (ld_a == 0) ld_a = K;
+  if (ld_w == 0) ld_w = K;
   int dev;
   if (int rc = current_device(&dev)) return rc;
   CUtensorMap ta, tw;
   constexpr uint32_t kE = sizeof(TIn), kRow = 128 / kE;  // elements per 128-byte row
   {
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
-    const uint64_t strides[1] = {(uint64_t)K * kE};
+    const uint64_t strides[1] = {(uint64_t)ld_a * kE};
     const uint32_t box[2] = {kRow, 128};
     if (int rc = make_tmap_bf16(&ta, A, 2, dims, strides, box, tmap_dtype<TIn>())) return rc;
   }
-  {
+  if constexpr (kE == 4) {  // fp32 (tf32) W comes transposed: [N,K], boxes of 64 N rows
+    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)N};
+    const uint64_t strides[1] = {(uint64_t)ld_w * kE};
+    const uint32_t box[2] = {kRow, 64};
+    if (int rc = make_tmap_bf16(&tw, W, 2, dims, strides, box, tmap_dtype<TIn>())) return rc;
+  } else {
     const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
     const uint64_t strides[1] = {(uint64_t)N * kE};
     const uint32_t box[2] = {kRow, kRow};
@@ -828,9 +837,19 @@ int jules_gemm_bias_act(const void* A, const void* W, const float* bias, const v
   return gemm_simt<float, float>(A, W, bias, residual, C, M, N, K, act, 1, st);
 }
 
+// 3xTF32 chunking: K is accumulated on the tensor cores in chunks of at most
+// kF32Chunk columns (each 3 x kF32Chunk tf32 columns, at most 128 MMA steps
+// at full magnitude), whose fp32 partial products are then summed with
+// round-to-nearest adds.
+constexpr int64_t kF32Chunk = 1024;
+
+int64_t f32_chunks(int64_t K) { return (K + kF32Chunk - 1) / kF32Chunk; }
+
 size_t jules_gemm_f32_tc_workspace_bytes(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
-  return align256((size_t)M * 3 * (size_t)K * 4) + (size_t)3 * K * N * 4;
+  const int64_t chunks = f32_chunks(K);
+  return align256((size_t)M * 3 * (size_t)K * 4) + align256((size_t)3 * K * N * 4) +
+         (chunks > 1 ? (size_t)chunks * M * N * 4 : 0);
 }
 
 int jules_gemm_f32_tc(const float* A, const float* W, const float* bias, float* C, int64_t M,
@@ -842,7 +861,8 @@ int jules_gemm_f32_tc(const float* A, const float* W, const float* bias, float* 
   if (act < JULES_ACT_NONE || act > JULES_ACT_GELU) return fail(JULES_ERR_ARG, "gemm_f32_tc: act=%d", act);
   if (M == 0) return ok();
   const bool tc = M >= 256 && N >= 256 && N % 8 == 0 && K % 4 == 0 && 3 * K <= INT32_MAX &&
-                  aligned16(A) && aligned16(W) && aligned16(C) && (!bias || aligned16(bias));
+                  (K + 31) / 32 <= 65535 && aligned16(A) && aligned16(W) && aligned16(C) &&
+                  (!bias || aligned16(bias));
   if (!tc)  // the fp32 CUDA-core GEMM (exact fp32 products)
     return jules_gemm_bias_act(A, W, bias, nullptr, C, M, N, K, act, JULES_DTYPE_F32, JULES_DTYPE_F32, stream);
   const size_t need = jules_gemm_f32_tc_workspace_bytes(M, N, K);
@@ -852,22 +872,41 @@ int jules_gemm_f32_tc(const float* A, const float* W, const float* bias, float* 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int dev;
   if (int rc = current_device(&dev)) return rc;
-  float* A3 = static_cast<float*>(workspace);
-  float* W3 = reinterpret_cast<float*>(static_cast<char*>(workspace) + align256((size_t)M * 3 * K * 4));
-  const int64_t na = M * (K / 4), nw = K * (N / 4);
+  char* ws = static_cast<char*>(workspace);
+  float* A3 = reinterpret_cast<float*>(ws);
+  float* W3T = reinterpret_cast<float*>(ws + align256((size_t)M * 3 * K * 4));
+  float* P = reinterpret_cast<float*>(ws + align256((size_t)M * 3 * K * 4) + align256((size_t)3 * K * N * 4));
+  const int Kc = (int)std::min<int64_t>(K, kF32Chunk);
+  const int64_t chunks = f32_chunks(K);
   const int cap = device_sms(dev) * 8;
-  auto blocks = [cap](int64_t n) { return (int)std::min<int64_t>((n + 255) / 256, cap); };
-  jb::simt::split3_a_kernel<<<blocks(na), 256, 0, st>>>(reinterpret_cast<const float4*>(A),
-                                                        reinterpret_cast<float4*>(A3), M, K / 4);
+  const int64_t na = M * (K / 4);
+  jb::simt::split3_a_kernel<<<(int)std::min<int64_t>((na + 255) / 256, cap), 256, 0, st>>>(
+      reinterpret_cast<const float4*>(A), A3, M, (int)K, Kc);
   if (int rc = check_launch("split3_a_kernel launch")) return rc;
-  jb::simt::split3_w_kernel<<<blocks(nw), 256, 0, st>>>(reinterpret_cast<const float4*>(W),
-                                                        reinterpret_cast<float4*>(W3), nw);
-  if (int rc = check_launch("split3_w_kernel launch")) return rc;
-  jb::gemm::OutDest<float> out{};
-  out.c[0] = C;
-  out.n = 1;
-  return gemm_tc2<256>(static_cast<const float*>(A3), static_cast<const float*>(W3), bias,
-                       static_cast<const float*>(nullptr), out, M, N, 3 * K, act, st);
+  jb::simt::split3_wt_kernel<<<dim3((unsigned)((N + 31) / 32), (unsigned)((K + 31) / 32)), dim3(32, 8), 0, st>>>(
+      W, W3T, (int)K, (int)N, Kc);
+  if (int rc = check_launch("split3_wt_kernel launch")) return rc;
+  const float* none = nullptr;
+  if (chunks == 1) {
+    jb::gemm::OutDest<float> out{};
+    out.c[0] = C;
+    out.n = 1;
+    return gemm_tc2<256>(static_cast<const float*>(A3), static_cast<const float*>(W3T), bias, none, out,
+                         M, N, 3 * K, act, st);
+  }
+  for (int64_t c = 0; c < chunks; ++c) {  // partial products, no bias, no activation
+    const int64_t k0 = c * kF32Chunk, L = std::min<int64_t>(kF32Chunk, K - k0);
+    jb::gemm::OutDest<float> out{};
+    out.c[0] = P + c * M * N;
+    out.n = 1;
+    if (int rc = gemm_tc2<256>(static_cast<const float*>(A3 + 3 * k0), static_cast<const float*>(W3T + 3 * k0),
+                               none, none, out, M, N, 3 * L, JULES_ACT_NONE, st, nullptr, nullptr, 3 * K, 3 * K))
+      return rc;
+  }
+  const int64_t n4 = M * N / 4;
+  jb::simt::chunk_combine_kernel<<<(int)std::min<int64_t>((n4 + 255) / 256, cap), 256, 0, st>>>(
+      reinterpret_cast<const float4*>(P), (int)chunks, n4, (int)N, bias, act, reinterpret_cast<float4*>(C));
+  return check_launch("chunk_combine_kernel launch");
 }
 
 int jules_sgemm(int transA, int transB, int64_t M, int64_t N, int64_t K, float alpha,

@@ -420,6 +420,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
   constexpr int kE = (int)sizeof(TIn);
   constexpr int BKe = 128 / kE;
   static_assert(S::kABytes == 128 * BKe * kE && S::kBBytes == BKe * (TN / 2) * kE, "stage layout");
+  // B operand: 16-bit W is read MN-major straight from [K,N]; the tf32 MMAs
+  // take B K-major, so fp32 W comes transposed ([N,K], rows of K like A) in
+  // boxes of 64 N rows.
+  constexpr bool kBKMajor = kE == 4;
   extern __shared__ uint8_t smem_raw[];
   S& s = *reinterpret_cast<S*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 
@@ -475,8 +479,13 @@ __global__ void __launch_bounds__(kThreads2, 1)
           if (!mbar_wait(&s.empty[stage], phase ^ 1u, 41, abort_flag)) { ok = false; break; }
           if (leader) mbar_arrive_expect_tx(&s.full[stage], tx);
           tma_load_2d_pair(s.a[stage], &tmA, &s.full[stage], kb * BKe, m0);
-          for (int j = 0; j < cta_cols / BKe; ++j)
-            tma_load_2d_pair(s.b[stage] + j * (BKe * 128), &tmW, &s.full[stage], n0 + j * BKe, kb * BKe);
+          if constexpr (kBKMajor) {
+            for (int j = 0; j < cta_cols / 64; ++j)
+              tma_load_2d_pair(s.b[stage] + j * (64 * 128), &tmW, &s.full[stage], kb * BKe, n0 + j * 64);
+          } else {
+            for (int j = 0; j < cta_cols / BKe; ++j)
+              tma_load_2d_pair(s.b[stage] + j * (BKe * 128), &tmW, &s.full[stage], n0 + j * BKe, kb * BKe);
+          }
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
       }
@@ -484,8 +493,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer (leader CTA) ----------------
     if (leader && lane == 0) {
-      constexpr uint32_t idesc_full = idesc_f16kind<TIn>(TM, TN, false, true);
-      constexpr uint32_t idesc_half = idesc_f16kind<TIn>(TM, TN / 2, false, true);
+      constexpr uint32_t idesc_full = idesc_f16kind<TIn>(TM, TN, false, !kBKMajor);
+      constexpr uint32_t idesc_half = idesc_f16kind<TIn>(TM, TN / 2, false, !kBKMajor);
       const uint32_t empty0 = smem_u32(&s.empty[0]);
       const uint32_t tfull0 = smem_u32(&s.tfull[0]);
       const uint32_t empty0_peer = mapa_shared(empty0, 1);
@@ -505,12 +514,14 @@ __global__ void __launch_bounds__(kThreads2, 1)
           if (!mbar_wait(&s.full[stage], phase, 43, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint64_t a0 = sdesc_sw128(smem_u32(s.a[stage]), 16, 1024);
-          const uint64_t b0 = sdesc_sw128(smem_u32(s.b[stage]), BKe * 128, 1024);
+          const uint64_t b0 = kBKMajor ? sdesc_sw128(smem_u32(s.b[stage]), 16, 1024)
+                                       : sdesc_sw128(smem_u32(s.b[stage]), BKe * 128, 1024);
           uint64_t ad[4], bd[4];
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            ad[kk] = a0 + kk * 2;           // +32 bytes (one MMA's K) inside the swizzle row
-            bd[kk] = b0 + kk * (256 / kE);  // +32/kE K rows of 128 bytes
+            ad[kk] = a0 + kk * 2;  // +32 bytes (one MMA's K) inside the swizzle row
+            // K-major B like A; MN-major B: +16 K rows of 128 bytes
+            bd[kk] = kBKMajor ? b0 + kk * 2 : b0 + kk * 128;
           }
           if constexpr (kE == 4)
             umma4_pair_ss_tf32(d_tmem, ad, bd, kb > 0 ? 1u : 0u, idesc);

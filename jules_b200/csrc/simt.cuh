@@ -753,50 +753,104 @@ __global__ void gelu_kernel(const T* __restrict__ in, T* __restrict__ out, int64
 // ---------------------------------------------------------------------------
 // 3xTF32 operand split for the fp32 GEMM on tensor cores.  Each fp32 x is
 // hi + lo + r with hi = tf32(x), lo = tf32(x - hi) (x - hi is exact in fp32)
-// and |r| <= 2^-22 |x|; the tf32 pair GEMM then runs over K' = 3K
-//   A [M,K] -> A3 [M,3K] = [hi | hi | lo]
-//   W [K,N] -> W3 [3K,N] = [hi ; lo ; hi]
-// so that A3 . W3 = hiA hiW + hiA loW + loA hiW, which drops only loA loW
-// (<= 2^-22 |a w|).  Four elements per thread (K % 4 == 0 for A, N % 4 == 0
-// for W, 16-byte aligned buffers).
+// and |r| <= 2^-22 |x|.  K is cut into chunks of Kc (the last one shorter);
+// chunk c of length L becomes 3L columns of the tf32 operands:
+//   A  [M,K] -> A3  [M,3K]: per chunk [lo | hi | hi]
+//   W  [K,N] -> W3T [N,3K]: per chunk [hi | lo | hi] of W's columns (W
+//               transposed: the tf32 MMAs take B K-major)
+// so that one chunk's product is loA hiW + hiA loW + hiA hiW, dropping only
+// loA loW (<= 2^-22 |a w|).  The small terms come first, while the
+// accumulator is still small: the MMAs' fp32 accumulation truncates toward
+// zero, so each step costs up to an ulp of the running sum.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
   hi = to_tf32(x);
   lo = to_tf32(x - hi);
 }
 
-__device__ __forceinline__ void split_tf32x4(const float4& x, float4& hi, float4& lo) {
-  split_tf32(x.x, hi.x, lo.x);
-  split_tf32(x.y, hi.y, lo.y);
-  split_tf32(x.z, hi.z, lo.z);
-  split_tf32(x.w, hi.w, lo.w);
+// Column k of the K columns -> offsets of its three copies in a 3K row.
+__device__ __forceinline__ void chunk_cols(int k, int K, int Kc, int& o_first, int& L) {
+  const int c = k / Kc;
+  const int base = c * Kc;
+  L = min(Kc, K - base);
+  o_first = 3 * base + (k - base);  // first copy; the others at +L and +2L
 }
 
-// rows x k4 float4s of A -> A3 (row stride 3 k4 float4s).
-__global__ void split3_a_kernel(const float4* __restrict__ A, float4* __restrict__ A3, int64_t rows,
-                                int64_t k4) {
+// A [rows, K] -> A3 [rows, 3K].  Four columns per thread (K, Kc multiples of
+// 4: a group never straddles a chunk; 16-byte aligned rows).
+__global__ void split3_a_kernel(const float4* __restrict__ A, float* __restrict__ A3, int64_t rows,
+                                int K, int Kc) {
+  const int k4 = K / 4;
   const int64_t n = rows * k4;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / k4, c = i - r * k4;
+    const int64_t r = i / k4;
+    const int k = (int)(i - r * k4) * 4;
+    const float4 x = A[i];
     float4 hi, lo;
-    split_tf32x4(A[i], hi, lo);
-    float4* row = A3 + r * 3 * k4;
-    row[c] = hi;
-    row[k4 + c] = hi;
-    row[2 * k4 + c] = lo;
+    split_tf32(x.x, hi.x, lo.x);
+    split_tf32(x.y, hi.y, lo.y);
+    split_tf32(x.z, hi.z, lo.z);
+    split_tf32(x.w, hi.w, lo.w);
+    int o, L;
+    chunk_cols(k, K, Kc, o, L);
+    float* row = A3 + r * 3 * (int64_t)K;
+    *reinterpret_cast<float4*>(row + o) = lo;
+    *reinterpret_cast<float4*>(row + o + L) = hi;
+    *reinterpret_cast<float4*>(row + o + 2 * L) = hi;
   }
 }
 
-// K x n4 float4s of W -> W3 = three K-row blocks (hi, lo, hi).
-__global__ void split3_w_kernel(const float4* __restrict__ W, float4* __restrict__ W3, int64_t n) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+// W [K,N] -> W3T [N,3K].  Block (32, 8) per 32 x 32 tile: reads along N,
+// writes along K (both coalesced).  Grid (ceil(N/32), ceil(K/32)).
+__global__ void __launch_bounds__(256)
+    split3_wt_kernel(const float* __restrict__ W, float* __restrict__ W3T, int K, int N, int Kc) {
+  __shared__ float hi_s[32][33], lo_s[32][33];
+  const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int k = k0 + i, n = n0 + threadIdx.x;
+    float h = 0.0f, l = 0.0f;
+    if (k < K && n < N) split_tf32(W[(size_t)k * N + n], h, l);
+    hi_s[i][threadIdx.x] = h;
+    lo_s[i][threadIdx.x] = l;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    const int n = n0 + i, k = k0 + threadIdx.x;
+    if (n < N && k < K) {
+      int o, L;
+      chunk_cols(k, K, Kc, o, L);
+      float* row = W3T + (size_t)n * 3 * K;
+      const float h = hi_s[threadIdx.x][i], l = lo_s[threadIdx.x][i];
+      row[o] = h;
+      row[o + L] = l;
+      row[o + 2 * L] = h;
+    }
+  }
+}
+
+// C = act(sum_c P[c] + bias) in fp32 (round to nearest): the chunks' partial
+// products, each accumulated on the tensor cores, combined.  Four elements
+// per thread (N % 4 == 0, 16-byte aligned).
+__global__ void chunk_combine_kernel(const float4* __restrict__ P, int chunks, int64_t n4, int N,
+                                     const float* __restrict__ bias, int act, float4* __restrict__ C) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
        i += (int64_t)gridDim.x * blockDim.x) {
-    float4 hi, lo;
-    split_tf32x4(W[i], hi, lo);
-    W3[i] = hi;
-    W3[n + i] = lo;
-    W3[2 * n + i] = hi;
+    float4 s = P[i];
+    for (int c = 1; c < chunks; ++c) {
+      const float4 p = P[(int64_t)c * n4 + i];
+      s.x += p.x; s.y += p.y; s.z += p.z; s.w += p.w;
+    }
+    if (bias) {
+      const int col = (int)((i * 4) % N);
+      const float4 b = *reinterpret_cast<const float4*>(bias + col);
+      s.x += b.x; s.y += b.y; s.z += b.z; s.w += b.w;
+    }
+    s.x = act_exact(s.x, act);
+    s.y = act_exact(s.y, act);
+    s.z = act_exact(s.z, act);
+    s.w = act_exact(s.w, act);
+    C[i] = s;
   }
 }
 
