@@ -7,8 +7,10 @@
 // so any number of translation units may include this header.
 //
 // float* arguments are HOST pointers, as in the reference: each call stages
-// its operands to the current GPU, runs an fp32 CUDA kernel and copies the
-// result back before returning.  The device-pointer C ABI in
+// its operands to the current GPU, runs fp32-accurate CUDA kernels (the
+// GEMMs of tiledMatmulWithActivation, the plain blasMatmul and
+// fusedMLPForward on tensor cores as 3xTF32 when M and N are at least 256)
+// and copies the result back before returning.  The device-pointer C ABI in
 // jules_kernels.h is the fast path (bf16 tensor cores, no copies).
 //
 //===----------------------------------------------------------------------===//
