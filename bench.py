@@ -857,7 +857,6 @@ class GemmF32(Workload):
     dominant = ("split3_a/w_kernel + gemm_bf16_tc2_kernel<float> (tcgen05 kind::tf32, 3xTF32; "
                 "events bracket the split and the GEMM)")
     tf32x3 = True
-    launches_per_step = 3  # two split kernels and the GEMM
 
     def __init__(self, jb, torch, rank, world, M=2048, N=2048, K=2048):
         self.jb, self.torch = jb, torch
@@ -871,6 +870,8 @@ class GemmF32(Workload):
         self.b = torch.randn(N, generator=g, device=dev) * 0.02
         self.C = [torch.empty((M, N), device=dev) for _ in range(self.nsets)]
         self.ws = torch.empty(jb.gemm_f32_tc_workspace_bytes(M, N, K), dtype=torch.uint8, device=dev)
+        # two split kernels and one GEMM per 1024-column K chunk
+        self.launches_per_step = 2 + (K + 1023) // 1024
         self.flops_per_step = 2.0 * M * N * K
         # executed tf32 MMA work: three products over K
         self.flops_dominant = 3 * self.flops_per_step

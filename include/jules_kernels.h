@@ -112,10 +112,10 @@ int jules_gemm_bias_act(const void* A, const void* W, const float* bias, const v
  * (3xTF32): each operand is split into tf32 hi + lo parts (one HBM pass into
  * the caller's workspace, W transposed) and the tcgen05 pair GEMM (kind::tf32,
  * fp32 accumulation in TMEM) computes loA.hiW + hiA.loW + hiA.hiW, dropping
- * only loA.loW (relative size <= 2^-22).  K runs in chunks of 1024 whose
- * partial products are summed in fp32 with round-to-nearest adds (the MMA
- * accumulation truncates, so long accumulations would drift).  Activations
- * in the accurate fp32 forms.
+ * only loA.loW (relative size <= 2^-22).  K runs in chunks of 1024, each
+ * chunk's epilogue adding the sum of the earlier ones in fp32 with a
+ * round-to-nearest add (the MMA accumulation truncates, so long
+ * accumulations would drift).  Activations in the accurate fp32 forms.
  *   A [M,K], W [K,N], C [M,N], bias [N] (nullable), all fp32, row-major.
  * Tensor cores for M >= 256, N >= 256, N % 8 == 0, K % 4 == 0 and 16-byte
  * aligned buffers; other shapes run the fp32 CUDA-core GEMM (no workspace

@@ -839,17 +839,16 @@ int jules_gemm_bias_act(const void* A, const void* W, const float* bias, const v
 
 // 3xTF32 chunking: K is accumulated on the tensor cores in chunks of at most
 // kF32Chunk columns (each 3 x kF32Chunk tf32 columns, at most 128 MMA steps
-// at full magnitude), whose fp32 partial products are then summed with
-// round-to-nearest adds.
+// at full magnitude); each chunk's epilogue adds the fp32 sum of the earlier
+// chunks (held in C) with a round-to-nearest add, the last one then bias and
+// activation.
 constexpr int64_t kF32Chunk = 1024;
 
 int64_t f32_chunks(int64_t K) { return (K + kF32Chunk - 1) / kF32Chunk; }
 
 size_t jules_gemm_f32_tc_workspace_bytes(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
-  const int64_t chunks = f32_chunks(K);
-  return align256((size_t)M * 3 * (size_t)K * 4) + align256((size_t)3 * K * N * 4) +
-         (chunks > 1 ? (size_t)chunks * M * N * 4 : 0);
+  return align256((size_t)M * 3 * (size_t)K * 4) + (size_t)3 * K * N * 4;
 }
 
 int jules_gemm_f32_tc(const float* A, const float* W, const float* bias, float* C, int64_t M,
@@ -875,7 +874,6 @@ int jules_gemm_f32_tc(const float* A, const float* W, const float* bias, float* 
   char* ws = static_cast<char*>(workspace);
   float* A3 = reinterpret_cast<float*>(ws);
   float* W3T = reinterpret_cast<float*>(ws + align256((size_t)M * 3 * K * 4));
-  float* P = reinterpret_cast<float*>(ws + align256((size_t)M * 3 * K * 4) + align256((size_t)3 * K * N * 4));
   const int Kc = (int)std::min<int64_t>(K, kF32Chunk);
   const int64_t chunks = f32_chunks(K);
   const int cap = device_sms(dev) * 8;
@@ -886,27 +884,18 @@ int jules_gemm_f32_tc(const float* A, const float* W, const float* bias, float* 
   jb::simt::split3_wt_kernel<<<dim3((unsigned)((N + 31) / 32), (unsigned)((K + 31) / 32)), dim3(32, 8), 0, st>>>(
       W, W3T, (int)K, (int)N, Kc);
   if (int rc = check_launch("split3_wt_kernel launch")) return rc;
-  const float* none = nullptr;
-  if (chunks == 1) {
+  for (int64_t c = 0; c < chunks; ++c) {
+    const int64_t k0 = c * kF32Chunk, L = std::min<int64_t>(kF32Chunk, K - k0);
+    const bool last = c == chunks - 1;
     jb::gemm::OutDest<float> out{};
     out.c[0] = C;
     out.n = 1;
-    return gemm_tc2<256>(static_cast<const float*>(A3), static_cast<const float*>(W3T), bias, none, out,
-                         M, N, 3 * K, act, st);
-  }
-  for (int64_t c = 0; c < chunks; ++c) {  // partial products, no bias, no activation
-    const int64_t k0 = c * kF32Chunk, L = std::min<int64_t>(kF32Chunk, K - k0);
-    jb::gemm::OutDest<float> out{};
-    out.c[0] = P + c * M * N;
-    out.n = 1;
     if (int rc = gemm_tc2<256>(static_cast<const float*>(A3 + 3 * k0), static_cast<const float*>(W3T + 3 * k0),
-                               none, none, out, M, N, 3 * L, JULES_ACT_NONE, st, nullptr, nullptr, 3 * K, 3 * K))
+                               last ? bias : nullptr, c == 0 ? nullptr : static_cast<const float*>(C), out,
+                               M, N, 3 * L, last ? act : JULES_ACT_NONE, st, nullptr, nullptr, 3 * K, 3 * K))
       return rc;
   }
-  const int64_t n4 = M * N / 4;
-  jb::simt::chunk_combine_kernel<<<(int)std::min<int64_t>((n4 + 255) / 256, cap), 256, 0, st>>>(
-      reinterpret_cast<const float4*>(P), (int)chunks, n4, (int)N, bias, act, reinterpret_cast<float4*>(C));
-  return check_launch("chunk_combine_kernel launch");
+  return JULES_OK;
 }
 
 int jules_sgemm(int transA, int transB, int64_t M, int64_t N, int64_t K, float alpha,

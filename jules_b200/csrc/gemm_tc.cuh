@@ -582,6 +582,20 @@ __global__ void __launch_bounds__(kThreads2, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
           if (c0 < N) {  // N is a multiple of 8: a 32-column group is all in or starts past N
+            if constexpr (kE == 4) {
+              // fp32 operands (3xTF32 by K chunks): `residual` is the fp32
+              // sum of the earlier chunks (C itself, read here before this
+              // warp's stores write it), added before bias and activation
+              if (rrow) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                  if (c0 + j < N) {
+                    const float4 p = *reinterpret_cast<const float4*>(rrow + c0 + j);
+                    v[j] += p.x; v[j + 1] += p.y; v[j + 2] += p.z; v[j + 3] += p.w;
+                  }
+                }
+              }
+            }
             if (ln_stats) {
 #pragma unroll
               for (int j = 0; j < 32; j += 8) {

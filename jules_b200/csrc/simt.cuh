@@ -829,30 +829,5 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// C = act(sum_c P[c] + bias) in fp32 (round to nearest): the chunks' partial
-// products, each accumulated on the tensor cores, combined.  Four elements
-// per thread (N % 4 == 0, 16-byte aligned).
-__global__ void chunk_combine_kernel(const float4* __restrict__ P, int chunks, int64_t n4, int N,
-                                     const float* __restrict__ bias, int act, float4* __restrict__ C) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    float4 s = P[i];
-    for (int c = 1; c < chunks; ++c) {
-      const float4 p = P[(int64_t)c * n4 + i];
-      s.x += p.x; s.y += p.y; s.z += p.z; s.w += p.w;
-    }
-    if (bias) {
-      const int col = (int)((i * 4) % N);
-      const float4 b = *reinterpret_cast<const float4*>(bias + col);
-      s.x += b.x; s.y += b.y; s.z += b.z; s.w += b.w;
-    }
-    s.x = act_exact(s.x, act);
-    s.y = act_exact(s.y, act);
-    s.z = act_exact(s.z, act);
-    s.w = act_exact(s.w, act);
-    C[i] = s;
-  }
-}
-
 }  // namespace simt
 }  // namespace jb

@@ -142,8 +142,8 @@ def test_gemm_f32_tc_vs_reference(jb, ref, M, N, K, act):
     torch.cuda.synchronize()
     assert jb.device_error() == 0
     assert rel_l2(to_np(got), want) <= F32_REL_L2
-    # against float64 too (K = 4096 runs as four 1024-column chunks combined
-    # in fp32); tf32 alone (~5e-4) would fail this by far
+    # against float64 too (K = 4096 runs as four 1024-column chunks, each
+    # adding the running sum in fp32); tf32 alone (~5e-4) would fail this by far
     exact = A.astype(np.float64) @ W.astype(np.float64)
     if act == "none":
         assert rel_l2(to_np(got), exact) <= F32_REL_L2
@@ -180,9 +180,8 @@ def test_gemm_f32_tc_fallback_and_workspace(jb):
     M, N, K = 512, 512, 128
     need = jb.gemm_f32_tc_workspace_bytes(M, N, K)
     a256 = lambda n: (n + 255) // 256 * 256
-    assert need == a256(M * 3 * K * 4) + a256(3 * K * N * 4)  # one chunk: no partials
-    assert jb.gemm_f32_tc_workspace_bytes(M, N, 3000) == (
-        a256(M * 9000 * 4) + a256(9000 * N * 4) + 3 * M * N * 4)  # three chunks
+    assert need == a256(M * 3 * K * 4) + 3 * K * N * 4  # A3 and W3T
+    assert jb.gemm_f32_tc_workspace_bytes(M, N, 3000) == a256(M * 9000 * 4) + 9000 * N * 4
     A = torch.zeros((M, K), device="cuda")
     W = torch.zeros((K, N), device="cuda")
     C = torch.empty((M, N), device="cuda")
