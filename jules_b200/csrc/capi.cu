@@ -860,7 +860,7 @@ int jules_gemm_f32_tc(const float* A, const float* W, const float* bias, float* 
   if (act < JULES_ACT_NONE || act > JULES_ACT_GELU) return fail(JULES_ERR_ARG, "gemm_f32_tc: act=%d", act);
   if (M == 0) return ok();
   const bool tc = M >= 256 && N >= 256 && N % 8 == 0 && K % 4 == 0 && 3 * K <= INT32_MAX &&
-                  (K + 31) / 32 <= 65535 && aligned16(A) && aligned16(W) && aligned16(C) &&
+                  (K + 63) / 64 <= 65535 && aligned16(A) && aligned16(W) && aligned16(C) &&
                   (!bias || aligned16(bias));
   if (!tc)  // the fp32 CUDA-core GEMM (exact fp32 products)
     return jules_gemm_bias_act(A, W, bias, nullptr, C, M, N, K, act, JULES_DTYPE_F32, JULES_DTYPE_F32, stream);
@@ -881,7 +881,8 @@ int jules_gemm_f32_tc(const float* A, const float* W, const float* bias, float* 
   jb::simt::split3_a_kernel<<<(int)std::min<int64_t>((na + 255) / 256, cap), 256, 0, st>>>(
       reinterpret_cast<const float4*>(A), A3, M, (int)K, Kc);
   if (int rc = check_launch("split3_a_kernel launch")) return rc;
-  jb::simt::split3_wt_kernel<<<dim3((unsigned)((N + 31) / 32), (unsigned)((K + 31) / 32)), dim3(32, 8), 0, st>>>(
+  constexpr int64_t T = jb::simt::kSplitTile;
+  jb::simt::split3_wt_kernel<<<dim3((unsigned)((N + T - 1) / T), (unsigned)((K + T - 1) / T)), dim3(32, 8), 0, st>>>(
       W, W3T, (int)K, (int)N, Kc);
   if (int rc = check_launch("split3_wt_kernel launch")) return rc;
   for (int64_t c = 0; c < chunks; ++c) {

@@ -801,30 +801,45 @@ __global__ void split3_a_kernel(const float4* __restrict__ A, float* __restrict_
   }
 }
 
-// W [K,N] -> W3T [N,3K].  Block (32, 8) per 32 x 32 tile: reads along N,
-// writes along K (both coalesced).  Grid (ceil(N/32), ceil(K/32)).
+// W [K,N] -> W3T [N,3K].  Block (32, 8) per 64 x 64 tile (16 loads in
+// flight per thread): reads along N, 16-byte writes along K (both
+// coalesced).
+// Grid (ceil(N/64), ceil(K/64)).
+constexpr int kSplitTile = 64;
 __global__ void __launch_bounds__(256)
     split3_wt_kernel(const float* __restrict__ W, float* __restrict__ W3T, int K, int N, int Kc) {
-  __shared__ float hi_s[32][33], lo_s[32][33];
-  const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
-  for (int i = threadIdx.y; i < 32; i += 8) {
-    const int k = k0 + i, n = n0 + threadIdx.x;
-    float h = 0.0f, l = 0.0f;
-    if (k < K && n < N) split_tf32(W[(size_t)k * N + n], h, l);
-    hi_s[i][threadIdx.x] = h;
-    lo_s[i][threadIdx.x] = l;
+  constexpr int T = kSplitTile;
+  __shared__ float hi_s[T][T + 1], lo_s[T][T + 1];
+  const int k0 = blockIdx.y * T, n0 = blockIdx.x * T;
+#pragma unroll
+  for (int i = threadIdx.y; i < T; i += 8) {
+#pragma unroll
+    for (int h = 0; h < T; h += 32) {
+      const int k = k0 + i, n = n0 + h + threadIdx.x;
+      float hv = 0.0f, lv = 0.0f;
+      if (k < K && n < N) split_tf32(W[(size_t)k * N + n], hv, lv);
+      hi_s[i][h + threadIdx.x] = hv;
+      lo_s[i][h + threadIdx.x] = lv;
+    }
   }
   __syncthreads();
-  for (int i = threadIdx.y; i < 32; i += 8) {
-    const int n = n0 + i, k = k0 + threadIdx.x;
+  // Stores: 16 bytes (4 consecutive k of one n) per thread and copy; a warp
+  // covers two rows of 64 k.  K and Kc are multiples of 4, so a group of 4
+  // never straddles a chunk and every store is 16-byte aligned.
+  const int tid = threadIdx.y * 32 + threadIdx.x;
+#pragma unroll
+  for (int it = tid; it < T * (T / 4); it += 256) {
+    const int nl = it / (T / 4), kg = (it % (T / 4)) * 4;
+    const int n = n0 + nl, k = k0 + kg;
     if (n < N && k < K) {
       int o, L;
       chunk_cols(k, K, Kc, o, L);
       float* row = W3T + (size_t)n * 3 * K;
-      const float h = hi_s[threadIdx.x][i], l = lo_s[threadIdx.x][i];
-      row[o] = h;
-      row[o + L] = l;
-      row[o + 2 * L] = h;
+      const float4 hv = make_float4(hi_s[kg][nl], hi_s[kg + 1][nl], hi_s[kg + 2][nl], hi_s[kg + 3][nl]);
+      const float4 lv = make_float4(lo_s[kg][nl], lo_s[kg + 1][nl], lo_s[kg + 2][nl], lo_s[kg + 3][nl]);
+      *reinterpret_cast<float4*>(row + o) = hv;
+      *reinterpret_cast<float4*>(row + o + L) = lv;
+      *reinterpret_cast<float4*>(row + o + 2 * L) = hv;
     }
   }
 }
