@@ -86,6 +86,24 @@ def test_gemm_argument_errors(jb, FAKE):
     assert b"NULL" in h.jules_last_error_string() or h.jules_last_error_string() == b""
 
 
+def test_gemm_f32_tc_argument_errors(jb, FAKE):
+    """The 3xTF32 entry point validates before touching the device; its
+    workspace query is host arithmetic (A3 [M,3K] padded to 256 bytes, then
+    W3T [N,3K])."""
+    h = jb.lib()
+    f = h.jules_gemm_f32_tc
+    assert f(None, FAKE, None, FAKE, 4, 4, 4, 0, None, 0, None) == 6      # NULL A
+    assert f(FAKE, FAKE, None, FAKE, 4, 0, 4, 0, None, 0, None) == 1      # N = 0
+    assert f(FAKE, FAKE, None, FAKE, 4, 4, 4, 9, None, 0, None) == 6      # act
+    assert f(FAKE, FAKE, None, FAKE, 1 << 32, 4, 4, 0, None, 0, None) == 1
+    assert f(FAKE, FAKE, None, FAKE, 0, 4, 4, 0, None, 0, None) == 0      # empty
+    q = h.jules_gemm_f32_tc_workspace_bytes
+    assert q(0, 4, 4) == 0 and q(4, 4, -1) == 0
+    a256 = lambda n: (n + 255) // 256 * 256
+    for (M, N, K) in ((256, 256, 256), (300, 264, 4096), (2048, 2048, 2048), (3, 5, 7)):
+        assert q(M, N, K) == a256(M * 3 * K * 4) + 3 * K * N * 4
+
+
 def test_attention_argument_errors(jb, FAKE):
     h = jb.lib()
     f = h.jules_flash_attention_fwd
